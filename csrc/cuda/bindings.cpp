@@ -1,0 +1,377 @@
+// PyTorch bindings of the device runtime (module nexar_b200._cuda).
+//
+// Every entry point validates shapes and dtypes, splits messages that exceed
+// the staging slot into slot-sized pieces, and launches on the caller's
+// current CUDA stream.
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+
+#include <atomic>
+#include <memory>
+
+#include "coll_api.h"
+#include "device_comm.h"
+#include "ops_api.h"
+
+namespace nexar {
+
+std::atomic<unsigned long long> g_launches{0};
+void count_launch(unsigned long long n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
+
+int dtype_code(at::ScalarType t) {
+  switch (t) {
+    case at::kFloat: return kF32;
+    case at::kDouble: return kF64;
+    case at::kHalf: return kF16;
+    case at::kBFloat16: return kBF16;
+    case at::kChar: return kI8;
+    case at::kInt: return kI32;
+    case at::kLong: return kI64;
+    case at::kByte: return kU8;
+    case at::kUInt32: return kU32;
+    case at::kUInt64: return kU64;
+    case at::kFloat8_e4m3fn: return kF8E4M3;
+    case at::kFloat8_e5m2: return kF8E5M2;
+    default: TORCH_CHECK(false, "nexar_b200: unsupported dtype ", t);
+  }
+}
+
+at::ScalarType scalar_type_of(int code) {
+  switch (code) {
+    case kF32: return at::kFloat;
+    case kF64: return at::kDouble;
+    case kF16: return at::kHalf;
+    case kBF16: return at::kBFloat16;
+    case kI8: return at::kChar;
+    case kI32: return at::kInt;
+    case kI64: return at::kLong;
+    case kU8: return at::kByte;
+    case kU32: return at::kUInt32;
+    case kU64: return at::kUInt64;
+    case kF8E4M3: return at::kFloat8_e4m3fn;
+    case kF8E5M2: return at::kFloat8_e5m2;
+    default: TORCH_CHECK(false, "nexar_b200: unknown dtype code ", code);
+  }
+}
+
+static void check_dev_tensor(const DeviceComm& c, const at::Tensor& t, const char* name) {
+  TORCH_CHECK(t.is_cuda(), "nexar_b200: ", name, " must be a CUDA tensor");
+  TORCH_CHECK(t.get_device() == c.device(), "nexar_b200: ", name, " is on cuda:", t.get_device(),
+              " but the communicator is on cuda:", c.device());
+  TORCH_CHECK(t.is_contiguous(), "nexar_b200: ", name, " must be contiguous");
+}
+
+static void check_launch(cudaError_t e, const char* what) {
+  TORCH_CHECK(e == cudaSuccess, "nexar_b200: ", what, " launch failed: ", cudaGetErrorString(e));
+}
+
+static cudaStream_t cur_stream(const DeviceComm& c) {
+  return at::cuda::getCurrentCUDAStream(c.device()).stream();
+}
+
+static unsigned long long round_down(unsigned long long v, unsigned long long m) { return v / m * m; }
+
+using CommPtr = std::shared_ptr<DeviceComm>;
+
+// ---------------------------------------------------------------- collectives
+void all_reduce(const CommPtr& c, const at::Tensor& in, const at::Tensor& out, int op, double scale,
+                int algo, long long oneshot_max_bytes) {
+  check_dev_tensor(*c, in, "input");
+  check_dev_tensor(*c, out, "output");
+  TORCH_CHECK(in.numel() == out.numel(), "all_reduce: input and output sizes differ");
+  TORCH_CHECK(c->connected(), "communicator is not connected");
+  c10::cuda::CUDAGuard g(c->device());
+  const int dti = dtype_code(in.scalar_type()), dto = dtype_code(out.scalar_type());
+  const unsigned long long n = in.numel();
+  const int esi = in.element_size(), eso = out.element_size();
+  const unsigned long long bytes = n * esi;
+  if (n == 0) return;
+  cudaStream_t s = cur_stream(*c);
+  if (c->world() == 1) {
+    // A single rank: the result is the (scaled, cast) input.
+    check_launch(launch_all_reduce(c->dev(), in.data_ptr(), out.data_ptr(), dti, dto, op, n,
+                                   (float)scale, kAlgoOneShot, -1, c->max_blocks, s), "all_reduce");
+    count_launch(1);
+    return;
+  }
+  long long sym = -1;
+  if (in.data_ptr() == out.data_ptr() && dti == dto) sym = c->symmetric_offset(in.data_ptr(), bytes);
+  if (algo == kAlgoAuto) algo = (long long)bytes <= oneshot_max_bytes ? kAlgoOneShot : kAlgoTwoShot;
+  if (sym >= 0) {
+    check_launch(launch_all_reduce(c->dev(), in.data_ptr(), out.data_ptr(), dti, dto, op, n,
+                                   (float)scale, algo, sym, c->max_blocks, s), "all_reduce");
+    count_launch(1);
+    return;
+  }
+  const unsigned long long per = round_down(c->slot_bytes() / std::max(esi, eso), 256);
+  for (unsigned long long off = 0; off < n; off += per) {
+    const unsigned long long m = std::min(per, n - off);
+    check_launch(launch_all_reduce(c->dev(), (const char*)in.data_ptr() + off * esi,
+                                   (char*)out.data_ptr() + off * eso, dti, dto, op, m, (float)scale,
+                                   algo, -1, c->max_blocks, s),
+                 "all_reduce");
+    count_launch(1);
+  }
+}
+
+void reduce_scatter(const CommPtr& c, const at::Tensor& in, const at::Tensor& out, int op,
+                    double scale) {
+  check_dev_tensor(*c, in, "input");
+  check_dev_tensor(*c, out, "output");
+  const int N = c->world();
+  TORCH_CHECK(in.numel() == out.numel() * N, "reduce_scatter: input must hold world_size * output elements");
+  c10::cuda::CUDAGuard g(c->device());
+  const int dti = dtype_code(in.scalar_type()), dto = dtype_code(out.scalar_type());
+  const unsigned long long count = out.numel();
+  const int esi = in.element_size(), eso = out.element_size();
+  const unsigned long long per = round_down(c->slot_bytes() / ((unsigned long long)N * std::max(esi, eso)), 256);
+  cudaStream_t s = cur_stream(*c);
+  for (unsigned long long off = 0; off < count; off += per) {
+    const unsigned long long m = std::min(per, count - off);
+    check_launch(launch_reduce_scatter(c->dev(), (const char*)in.data_ptr() + off * esi,
+                                       (char*)out.data_ptr() + off * eso, dti, dto, op, m, count,
+                                       (float)scale, c->max_blocks, s),
+                 "reduce_scatter");
+    count_launch(1);
+  }
+}
+
+void all_gather(const CommPtr& c, const at::Tensor& in, const at::Tensor& out) {
+  check_dev_tensor(*c, in, "input");
+  check_dev_tensor(*c, out, "output");
+  const int N = c->world();
+  TORCH_CHECK(out.numel() == in.numel() * N, "all_gather: output must hold world_size * input elements");
+  TORCH_CHECK(in.scalar_type() == out.scalar_type(), "all_gather: dtype mismatch");
+  c10::cuda::CUDAGuard g(c->device());
+  const int dt = dtype_code(in.scalar_type());
+  const unsigned long long count = in.numel();
+  const int es = in.element_size();
+  const unsigned long long per = round_down(c->slot_bytes() / es, 256);
+  cudaStream_t s = cur_stream(*c);
+  for (unsigned long long off = 0; off < count; off += per) {
+    const unsigned long long m = std::min(per, count - off);
+    check_launch(launch_all_gather(c->dev(), (const char*)in.data_ptr() + off * es,
+                                   (char*)out.data_ptr() + off * es, dt, m, count, c->max_blocks, s),
+                 "all_gather");
+    count_launch(1);
+  }
+}
+
+void all_to_all(const CommPtr& c, const at::Tensor& in, const at::Tensor& out) {
+  check_dev_tensor(*c, in, "input");
+  check_dev_tensor(*c, out, "output");
+  const int N = c->world();
+  TORCH_CHECK(in.numel() == out.numel() && in.numel() % N == 0,
+              "all_to_all: input and output must both hold world_size * count elements");
+  TORCH_CHECK(in.scalar_type() == out.scalar_type(), "all_to_all: dtype mismatch");
+  c10::cuda::CUDAGuard g(c->device());
+  const int dt = dtype_code(in.scalar_type());
+  const unsigned long long count = in.numel() / N;
+  const int es = in.element_size();
+  const unsigned long long per = round_down(c->slot_bytes() / ((unsigned long long)N * es), 256);
+  cudaStream_t s = cur_stream(*c);
+  for (unsigned long long off = 0; off < count; off += per) {
+    const unsigned long long m = std::min(per, count - off);
+    check_launch(launch_all_to_all(c->dev(), (const char*)in.data_ptr() + off * es,
+                                   (char*)out.data_ptr() + off * es, dt, m, count, count,
+                                   c->max_blocks, s),
+                 "all_to_all");
+    count_launch(1);
+  }
+}
+
+void broadcast(const CommPtr& c, const at::Tensor& in, const at::Tensor& out, int root) {
+  check_dev_tensor(*c, in, "input");
+  check_dev_tensor(*c, out, "output");
+  TORCH_CHECK(in.numel() == out.numel() && in.scalar_type() == out.scalar_type(), "broadcast: shape/dtype mismatch");
+  TORCH_CHECK(root >= 0 && root < c->world(), "broadcast: root out of range");
+  c10::cuda::CUDAGuard g(c->device());
+  const int dt = dtype_code(in.scalar_type());
+  const unsigned long long n = in.numel();
+  const int es = in.element_size();
+  const unsigned long long per = round_down(c->slot_bytes() / es, 256);
+  cudaStream_t s = cur_stream(*c);
+  for (unsigned long long off = 0; off < n; off += per) {
+    const unsigned long long m = std::min(per, n - off);
+    check_launch(launch_broadcast(c->dev(), (const char*)in.data_ptr() + off * es,
+                                  (char*)out.data_ptr() + off * es, dt, m, root, c->max_blocks, s),
+                 "broadcast");
+    count_launch(1);
+  }
+}
+
+void reduce(const CommPtr& c, const at::Tensor& in, const at::Tensor& out, int root, int op,
+            double scale) {
+  check_dev_tensor(*c, in, "input");
+  check_dev_tensor(*c, out, "output");
+  TORCH_CHECK(in.numel() == out.numel(), "reduce: size mismatch");
+  TORCH_CHECK(root >= 0 && root < c->world(), "reduce: root out of range");
+  c10::cuda::CUDAGuard g(c->device());
+  const int dti = dtype_code(in.scalar_type()), dto = dtype_code(out.scalar_type());
+  const unsigned long long n = in.numel();
+  const int esi = in.element_size(), eso = out.element_size();
+  const unsigned long long per = round_down(c->slot_bytes() / std::max(esi, eso), 256);
+  cudaStream_t s = cur_stream(*c);
+  for (unsigned long long off = 0; off < n; off += per) {
+    const unsigned long long m = std::min(per, n - off);
+    check_launch(launch_reduce(c->dev(), (const char*)in.data_ptr() + off * esi,
+                               (char*)out.data_ptr() + off * eso, dti, dto, op, m, root,
+                               (float)scale, c->max_blocks, s),
+                 "reduce");
+    count_launch(1);
+  }
+}
+
+void gather(const CommPtr& c, const at::Tensor& in, const at::Tensor& out, int root) {
+  check_dev_tensor(*c, in, "input");
+  check_dev_tensor(*c, out, "output");
+  const int N = c->world();
+  TORCH_CHECK(out.numel() == in.numel() * N, "gather: output must hold world_size * input elements");
+  TORCH_CHECK(in.scalar_type() == out.scalar_type(), "gather: dtype mismatch");
+  TORCH_CHECK(root >= 0 && root < N, "gather: root out of range");
+  c10::cuda::CUDAGuard g(c->device());
+  const int dt = dtype_code(in.scalar_type());
+  const unsigned long long count = in.numel();
+  const int es = in.element_size();
+  const unsigned long long per = round_down(c->slot_bytes() / es, 256);
+  cudaStream_t s = cur_stream(*c);
+  for (unsigned long long off = 0; off < count; off += per) {
+    const unsigned long long m = std::min(per, count - off);
+    check_launch(launch_gather(c->dev(), (const char*)in.data_ptr() + off * es,
+                               (char*)out.data_ptr() + off * es, dt, m, count, root, c->max_blocks, s),
+                 "gather");
+    count_launch(1);
+  }
+}
+
+void scatter(const CommPtr& c, const at::Tensor& in, const at::Tensor& out, int root) {
+  check_dev_tensor(*c, in, "input");
+  check_dev_tensor(*c, out, "output");
+  const int N = c->world();
+  TORCH_CHECK(in.numel() == out.numel() * N, "scatter: input must hold world_size * output elements");
+  TORCH_CHECK(in.scalar_type() == out.scalar_type(), "scatter: dtype mismatch");
+  TORCH_CHECK(root >= 0 && root < N, "scatter: root out of range");
+  c10::cuda::CUDAGuard g(c->device());
+  const int dt = dtype_code(in.scalar_type());
+  const unsigned long long count = out.numel();
+  const int es = in.element_size();
+  const unsigned long long per = round_down(c->slot_bytes() / ((unsigned long long)N * es), 256);
+  cudaStream_t s = cur_stream(*c);
+  for (unsigned long long off = 0; off < count; off += per) {
+    const unsigned long long m = std::min(per, count - off);
+    check_launch(launch_scatter(c->dev(), (const char*)in.data_ptr() + off * es,
+                                (char*)out.data_ptr() + off * es, dt, m, count, root, c->max_blocks, s),
+                 "scatter");
+    count_launch(1);
+  }
+}
+
+void scan(const CommPtr& c, const at::Tensor& in, const at::Tensor& out, int op, bool exclusive) {
+  check_dev_tensor(*c, in, "input");
+  check_dev_tensor(*c, out, "output");
+  TORCH_CHECK(in.numel() == out.numel() && in.scalar_type() == out.scalar_type(), "scan: shape/dtype mismatch");
+  c10::cuda::CUDAGuard g(c->device());
+  const int dt = dtype_code(in.scalar_type());
+  const unsigned long long n = in.numel();
+  const int es = in.element_size();
+  const unsigned long long per = round_down(c->slot_bytes() / es, 256);
+  cudaStream_t s = cur_stream(*c);
+  for (unsigned long long off = 0; off < n; off += per) {
+    const unsigned long long m = std::min(per, n - off);
+    check_launch(launch_scan(c->dev(), (const char*)in.data_ptr() + off * es,
+                             (char*)out.data_ptr() + off * es, dt, op, m, exclusive, c->max_blocks, s),
+                 "scan");
+    count_launch(1);
+  }
+}
+
+void barrier(const CommPtr& c) {
+  c10::cuda::CUDAGuard g(c->device());
+  check_launch(launch_barrier(c->dev(), cur_stream(*c)), "barrier");
+  count_launch(1);
+}
+
+void reduce_inplace(const at::Tensor& dst, const at::Tensor& src, int op) {
+  TORCH_CHECK(dst.is_cuda() && src.is_cuda() && dst.is_contiguous() && src.is_contiguous(),
+              "reduce_inplace: contiguous CUDA tensors required");
+  TORCH_CHECK(dst.numel() == src.numel() && dst.scalar_type() == src.scalar_type(),
+              "reduce_inplace: shape/dtype mismatch");
+  c10::cuda::CUDAGuard g(dst.get_device());
+  check_launch(launch_reduce_inplace(dst.data_ptr(), src.data_ptr(), dtype_code(dst.scalar_type()), op,
+                                     dst.numel(), at::cuda::getCurrentCUDAStream().stream()),
+               "reduce_inplace");
+  count_launch(1);
+}
+
+at::Tensor symmetric_tensor(const CommPtr& c, unsigned long long offset, std::vector<int64_t> shape,
+                            int dtype) {
+  at::ScalarType st = scalar_type_of(dtype);
+  int64_t numel = 1;
+  for (auto d : shape) numel *= d;
+  TORCH_CHECK(offset + numel * c10::elementSize(st) <= c->heap_bytes(), "symmetric_tensor out of heap range");
+  CommPtr keep = c;
+  auto opts = at::TensorOptions().dtype(st).device(at::kCUDA, c->device());
+  return torch::from_blob(c->local_base() + offset, shape, [keep](void*) {}, opts);
+}
+
+py::dict status_dict(const CommPtr& c) {
+  DeviceStatus s = c->status();
+  py::dict d;
+  d["code"] = s.code;
+  d["rank"] = s.rank;
+  d["op"] = s.op;
+  d["block"] = s.block;
+  d["epoch"] = s.epoch;
+  return d;
+}
+
+void register_ops(py::module& m);
+
+}  // namespace nexar
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  using namespace nexar;
+  m.doc() = "nexar_b200 device runtime: symmetric heap, peer-memory collectives, fused kernels (sm_100a)";
+  py::class_<DeviceComm, std::shared_ptr<DeviceComm>>(m, "DeviceComm")
+      .def(py::init<int, int, int, uint64_t, uint64_t, uint64_t>(), py::arg("rank"), py::arg("world"),
+           py::arg("device"), py::arg("heap_bytes"), py::arg("slot_bytes"), py::arg("timeout_us"))
+      .def("export_handle", [](const DeviceComm& c) { return py::bytes(c.export_handle()); })
+      .def("connect", [](DeviceComm& c, const std::vector<py::bytes>& hs) {
+        std::vector<std::string> v;
+        for (auto& h : hs) v.push_back(std::string(h));
+        c.connect(v);
+      })
+      .def("alloc_symmetric", &DeviceComm::alloc_symmetric, py::arg("bytes"), py::arg("align") = 256)
+      .def("reset_symmetric", &DeviceComm::reset_symmetric)
+      .def("symmetric_offset", [](const DeviceComm& c, const at::Tensor& t) {
+        return c.symmetric_offset(t.data_ptr(), t.numel() * t.element_size());
+      })
+      .def("status", &status_dict)
+      .def("clear_status", &DeviceComm::clear_status)
+      .def_property_readonly("rank", &DeviceComm::rank)
+      .def_property_readonly("world", &DeviceComm::world)
+      .def_property_readonly("device", &DeviceComm::device)
+      .def_property_readonly("heap_bytes", &DeviceComm::heap_bytes)
+      .def_property_readonly("slot_bytes", &DeviceComm::slot_bytes)
+      .def_property_readonly("user_bytes_free", &DeviceComm::user_bytes_free)
+      .def_property_readonly("connected", &DeviceComm::connected)
+      .def_property("timeout_us", &DeviceComm::timeout_us, &DeviceComm::set_timeout_us)
+      .def_readwrite("max_blocks", &DeviceComm::max_blocks)
+      .def("peer_ptr", [](const DeviceComm& c, int p) { return (uint64_t)c.peer_base(p); })
+      .def("local_ptr", [](const DeviceComm& c) { return (uint64_t)c.local_base(); });
+  m.def("all_reduce", &all_reduce);
+  m.def("reduce_scatter", &reduce_scatter);
+  m.def("all_gather", &all_gather);
+  m.def("all_to_all", &all_to_all);
+  m.def("broadcast", &broadcast);
+  m.def("reduce", &reduce);
+  m.def("gather", &gather);
+  m.def("scatter", &scatter);
+  m.def("scan", &scan);
+  m.def("barrier", &barrier);
+  m.def("reduce_inplace", &reduce_inplace);
+  m.def("symmetric_tensor", &symmetric_tensor);
+  m.def("launch_count", []() { return g_launches.load(); });
+  register_ops(m);
+}

@@ -1,0 +1,179 @@
+// Data-movement collectives: all-gather, all-to-all, broadcast, gather, scatter, barrier.
+#include "coll_impl.cuh"
+
+namespace nexar {
+
+// ============================================================ all-gather
+template <typename T>
+__global__ void __launch_bounds__(kThreads) k_all_gather(CommDev c, const T* in, T* out,
+                                                         unsigned long long count,
+                                                         unsigned long long out_ld, bool vec) {
+  const unsigned long long call = call_index(c);
+  constexpr int V = PackOf<T>::V;
+  const int N = c.world;
+  unsigned long long lo, hi;
+  block_range(count, gridDim.x, blockIdx.x, V, &lo, &hi);
+  const int slot = (int)(call & 1ull);
+  copy_range<T>(stage_ptr<T>(c, c.rank, slot), in, lo, hi, vec, false);
+  if (block_barrier(c, epoch_of(call, 0), kOpAllGather)) {
+    for (int q = 0; q < N; ++q) {
+      const int p = (c.rank + q) % N;
+      copy_range<T>(out + p * out_ld, stage_ptr<T>(c, p, slot), lo, hi, vec, p != c.rank);
+    }
+  }
+  finish_call(c, call);
+}
+
+// ============================================================ all-to-all
+// in: [N][count] (block p goes to rank p), out: [N][count] (block p came from p)
+template <typename T>
+__global__ void __launch_bounds__(kThreads) k_all_to_all(CommDev c, const T* in, T* out,
+                                                         unsigned long long count,
+                                                         unsigned long long in_ld,
+                                                         unsigned long long out_ld, bool vec) {
+  const unsigned long long call = call_index(c);
+  constexpr int V = PackOf<T>::V;
+  const int N = c.world;
+  unsigned long long lo, hi;
+  block_range(count, gridDim.x, blockIdx.x, V, &lo, &hi);
+  const int slot = (int)(call & 1ull);
+  T* a = stage_ptr<T>(c, c.rank, slot);
+  for (int p = 0; p < N; ++p) copy_range<T>(a + p * count, in + p * in_ld, lo, hi, vec, false);
+  if (block_barrier(c, epoch_of(call, 0), kOpAllToAll)) {
+    for (int q = 0; q < N; ++q) {
+      const int p = (c.rank + q) % N;
+      copy_range<T>(out + p * out_ld, stage_ptr<T>(c, p, slot) + (unsigned long long)c.rank * count,
+                    lo, hi, vec, p != c.rank);
+    }
+  }
+  finish_call(c, call);
+}
+
+// ============================================================ broadcast
+template <typename T>
+__global__ void __launch_bounds__(kThreads) k_broadcast(CommDev c, const T* in, T* out,
+                                                        unsigned long long n, int root, bool vec) {
+  const unsigned long long call = call_index(c);
+  constexpr int V = PackOf<T>::V;
+  unsigned long long lo, hi;
+  block_range(n, gridDim.x, blockIdx.x, V, &lo, &hi);
+  const int slot = (int)(call & 1ull);
+  if (c.rank == root) {
+    copy_range<T>(stage_ptr<T>(c, c.rank, slot), in, lo, hi, vec, false);
+    if (out != in) copy_range<T>(out, in, lo, hi, vec, false);
+  }
+  if (block_barrier(c, epoch_of(call, 0), kOpBroadcast)) {
+    if (c.rank != root) copy_range<T>(out, stage_ptr<T>(c, root, slot), lo, hi, vec, true);
+  }
+  finish_call(c, call);
+}
+
+// ============================================================ gather / scatter
+template <typename T>
+__global__ void __launch_bounds__(kThreads) k_gather(CommDev c, const T* in, T* out,
+                                                     unsigned long long count,
+                                                     unsigned long long out_ld, int root, bool vec) {
+  const unsigned long long call = call_index(c);
+  constexpr int V = PackOf<T>::V;
+  unsigned long long lo, hi;
+  block_range(count, gridDim.x, blockIdx.x, V, &lo, &hi);
+  const int slot = (int)(call & 1ull);
+  copy_range<T>(stage_ptr<T>(c, c.rank, slot), in, lo, hi, vec, false);
+  if (block_barrier(c, epoch_of(call, 0), kOpGather) && c.rank == root) {
+    for (int q = 0; q < c.world; ++q) {
+      const int p = (c.rank + q) % c.world;
+      copy_range<T>(out + p * out_ld, stage_ptr<T>(c, p, slot), lo, hi, vec, p != c.rank);
+    }
+  }
+  finish_call(c, call);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads) k_scatter(CommDev c, const T* in, T* out,
+                                                      unsigned long long count,
+                                                      unsigned long long in_ld, int root, bool vec) {
+  const unsigned long long call = call_index(c);
+  constexpr int V = PackOf<T>::V;
+  unsigned long long lo, hi;
+  block_range(count, gridDim.x, blockIdx.x, V, &lo, &hi);
+  const int slot = (int)(call & 1ull);
+  if (c.rank == root) {
+    T* a = stage_ptr<T>(c, c.rank, slot);
+    for (int p = 0; p < c.world; ++p) copy_range<T>(a + p * count, in + p * in_ld, lo, hi, vec, false);
+  }
+  if (block_barrier(c, epoch_of(call, 0), kOpScatter)) {
+    copy_range<T>(out, stage_ptr<T>(c, root, slot) + (unsigned long long)c.rank * count, lo, hi, vec,
+                  c.rank != root);
+  }
+  finish_call(c, call);
+}
+
+// ============================================================ barrier
+__global__ void k_barrier(CommDev c) {
+  const unsigned long long call = call_index(c);
+  block_barrier(c, epoch_of(call, 0), kOpBarrier);
+  finish_call(c, call);
+}
+
+cudaError_t launch_all_gather(const CommDev& c, const void* in, void* out, int dt,
+                              unsigned long long count, unsigned long long out_ld,
+                              unsigned int max_blocks, cudaStream_t s) {
+  if (count == 0) return cudaSuccess;
+  const int es = dtype_size(dt);
+  const bool vec = aligned16(in) && aligned16(out) && (count * es) % 16 == 0 && (out_ld * es) % 16 == 0;
+  const unsigned int g = pick_blocks(count * es, max_blocks);
+  NEXAR_DISPATCH_ALL(dt, k_all_gather<T><<<g, kThreads, 0, s>>>(c, (const T*)in, (T*)out, count, out_ld, vec));
+  return cudaGetLastError();
+}
+
+cudaError_t launch_all_to_all(const CommDev& c, const void* in, void* out, int dt,
+                              unsigned long long count, unsigned long long in_ld,
+                              unsigned long long out_ld, unsigned int max_blocks, cudaStream_t s) {
+  if (count == 0) return cudaSuccess;
+  const int es = dtype_size(dt);
+  const bool vec = aligned16(in) && aligned16(out) && (count * es) % 16 == 0 &&
+                   (in_ld * es) % 16 == 0 && (out_ld * es) % 16 == 0;
+  const unsigned int g = pick_blocks(count * es, max_blocks);
+  NEXAR_DISPATCH_ALL(dt, k_all_to_all<T><<<g, kThreads, 0, s>>>(c, (const T*)in, (T*)out, count, in_ld, out_ld, vec));
+  return cudaGetLastError();
+}
+
+cudaError_t launch_broadcast(const CommDev& c, const void* in, void* out, int dt,
+                             unsigned long long n, int root, unsigned int max_blocks,
+                             cudaStream_t s) {
+  if (n == 0) return cudaSuccess;
+  const int es = dtype_size(dt);
+  const bool vec = aligned16(in) && aligned16(out) && (n * es) % 16 == 0;
+  const unsigned int g = pick_blocks(n * es, max_blocks);
+  NEXAR_DISPATCH_ALL(dt, k_broadcast<T><<<g, kThreads, 0, s>>>(c, (const T*)in, (T*)out, n, root, vec));
+  return cudaGetLastError();
+}
+
+cudaError_t launch_gather(const CommDev& c, const void* in, void* out, int dt,
+                          unsigned long long count, unsigned long long out_ld, int root,
+                          unsigned int max_blocks, cudaStream_t s) {
+  if (count == 0) return cudaSuccess;
+  const int es = dtype_size(dt);
+  const bool vec = aligned16(in) && aligned16(out) && (count * es) % 16 == 0 && (out_ld * es) % 16 == 0;
+  const unsigned int g = pick_blocks(count * es, max_blocks);
+  NEXAR_DISPATCH_ALL(dt, k_gather<T><<<g, kThreads, 0, s>>>(c, (const T*)in, (T*)out, count, out_ld, root, vec));
+  return cudaGetLastError();
+}
+
+cudaError_t launch_scatter(const CommDev& c, const void* in, void* out, int dt,
+                           unsigned long long count, unsigned long long in_ld, int root,
+                           unsigned int max_blocks, cudaStream_t s) {
+  if (count == 0) return cudaSuccess;
+  const int es = dtype_size(dt);
+  const bool vec = aligned16(in) && aligned16(out) && (count * es) % 16 == 0 && (in_ld * es) % 16 == 0;
+  const unsigned int g = pick_blocks(count * es, max_blocks);
+  NEXAR_DISPATCH_ALL(dt, k_scatter<T><<<g, kThreads, 0, s>>>(c, (const T*)in, (T*)out, count, in_ld, root, vec));
+  return cudaGetLastError();
+}
+
+cudaError_t launch_barrier(const CommDev& c, cudaStream_t s) {
+  k_barrier<<<1, 32, 0, s>>>(c);
+  return cudaGetLastError();
+}
+
+}  // namespace nexar

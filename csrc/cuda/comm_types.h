@@ -1,0 +1,52 @@
+// Host- and device-visible types shared by the runtime and the kernels.
+//
+// Element codes follow the reference wire format (nexar/src/types.rs:13-24,
+// `DataType` repr(u8) 0..9); FP8 E4M3 = 10 and E5M2 = 11 are additions for the
+// block-scaled fp8 paths and do not renumber the reference codes.
+#pragma once
+#include <cstddef>
+
+namespace nexar {
+
+enum DType : int {
+  kF32 = 0, kF64 = 1, kF16 = 2, kBF16 = 3, kI8 = 4, kI32 = 5, kI64 = 6,
+  kU8 = 7, kU32 = 8, kU64 = 9, kF8E4M3 = 10, kF8E5M2 = 11,
+};
+
+// Reduce operator codes follow nexar/src/types.rs:62-71 (Sum, Prod, Min, Max).
+enum RedOp : int { kSum = 0, kProd = 1, kMin = 2, kMax = 3 };
+
+// Device status word layout (host-mapped; written with plain stores and a
+// system-scope fence, the code field last).
+// A kernel that gives up waiting on a peer writes these and returns normally,
+// so the context stays usable and the host can map the code to an error.
+struct DeviceStatus {
+  unsigned int code;      // 0 = ok, otherwise a StatusCode below
+  unsigned int rank;      // rank whose flag never arrived
+  unsigned int op;        // collective op id
+  unsigned int block;     // block index that observed the timeout
+  unsigned long long epoch;
+};
+enum StatusCode : unsigned int {
+  kStatusOk = 0,
+  kStatusWaitTimeout = 1,
+  kStatusBadArgument = 2,
+};
+
+constexpr int kMaxRanks = 8;
+constexpr int kMaxBlocks = 256;
+constexpr size_t kFlagBytes = 64 * 1024;   // >= kMaxBlocks*kMaxRanks*8 * 4 phases
+constexpr int kThreads = 512;
+
+struct CommDev {
+  char* peer_base[kMaxRanks];
+  unsigned long long* ctrl;     // local: [0] call counter, [1] finished-block count
+  DeviceStatus* status;         // host-mapped status word
+  unsigned long long timeout_ns;
+  unsigned long long stage_off;
+  unsigned long long slot_bytes;
+  int rank;
+  int world;
+};
+
+}  // namespace nexar

@@ -1,0 +1,81 @@
+// Device communicator: the symmetric heap shared by the ranks of one box and
+// the host state that the peer-memory kernels need.
+//
+// This is the on-box replacement for `NcclGroup` (nexar-nccl/src/group.rs:16-326)
+// and for the host staging `CudaAdapter` (nexar-rdma/src/cuda_adapter.rs:14-139):
+// device pointers never leave the device; kernels move them over NVLink.
+#pragma once
+#include <cstdint>
+#include <string>
+#include <vector>
+#include <mutex>
+#include <stdexcept>
+
+#include <cuda_runtime.h>
+#include "comm_types.h"
+
+namespace nexar {
+
+struct HeapHandle {
+  uint32_t magic;
+  int32_t device;
+  uint64_t pid;
+  uint64_t base;          // raw device VA in the exporting process
+  uint64_t bytes;
+  cudaIpcMemHandle_t ipc;  // 64 bytes
+};
+
+class DeviceComm {
+ public:
+  DeviceComm(int rank, int world, int device, uint64_t heap_bytes, uint64_t slot_bytes,
+             uint64_t timeout_us);
+  ~DeviceComm();
+  DeviceComm(const DeviceComm&) = delete;
+  DeviceComm& operator=(const DeviceComm&) = delete;
+
+  // Serialized handle of this rank's heap, to be exchanged out of band.
+  std::string export_handle() const;
+  // Map every peer's heap. `handles[p]` is rank p's export_handle().
+  void connect(const std::vector<std::string>& handles);
+  bool connected() const { return connected_; }
+
+  const CommDev& dev() const { return dev_; }
+  int rank() const { return rank_; }
+  int world() const { return world_; }
+  int device() const { return device_; }
+  uint64_t heap_bytes() const { return heap_bytes_; }
+  uint64_t slot_bytes() const { return slot_bytes_; }
+  uint64_t user_bytes_free() const { return heap_bytes_ - user_next_; }
+  char* local_base() const { return base_; }
+  char* peer_base(int p) const { return dev_.peer_base[p]; }
+
+  // Bump-allocate `bytes` of symmetric memory; every rank must call this in
+  // the same order with the same sizes. Returns the heap offset.
+  uint64_t alloc_symmetric(uint64_t bytes, uint64_t align);
+  void reset_symmetric();
+  // Heap offset of `ptr` if it lies in the user region of the local heap, else -1.
+  long long symmetric_offset(const void* ptr, uint64_t bytes) const;
+
+  // Device status word (host-mapped).
+  DeviceStatus status() const;
+  void clear_status();
+  void set_timeout_us(uint64_t us) { dev_.timeout_ns = us * 1000ull; }
+  uint64_t timeout_us() const { return dev_.timeout_ns / 1000ull; }
+
+  unsigned int max_blocks = 148;
+
+ private:
+  int rank_, world_, device_;
+  uint64_t heap_bytes_, slot_bytes_;
+  uint64_t user_off_ = 0, user_next_ = 0;
+  char* base_ = nullptr;
+  unsigned long long* ctrl_ = nullptr;
+  DeviceStatus* status_host_ = nullptr;
+  std::vector<char*> opened_;  // IPC-opened peer bases (to close)
+  bool connected_ = false;
+  CommDev dev_{};
+};
+
+void check_cuda(cudaError_t e, const char* what);
+
+}  // namespace nexar

@@ -1,0 +1,206 @@
+// PyTorch bindings of the model-side kernels.
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+
+#include "ops_api.h"
+
+namespace nexar {
+
+void count_launch(unsigned long long n);
+
+namespace {
+cudaStream_t stream_of(const at::Tensor& t) {
+  return at::cuda::getCurrentCUDAStream(t.get_device()).stream();
+}
+void chk(cudaError_t e, const char* what) {
+  TORCH_CHECK(e == cudaSuccess, "nexar_b200: ", what, " failed: ", cudaGetErrorString(e));
+}
+void need_bf16(const at::Tensor& t, const char* name) {
+  TORCH_CHECK(t.is_cuda() && t.scalar_type() == at::kBFloat16 && t.is_contiguous(), "nexar_b200: ", name,
+              " must be a contiguous bf16 CUDA tensor");
+}
+void need_f32(const at::Tensor& t, const char* name) {
+  TORCH_CHECK(t.is_cuda() && t.scalar_type() == at::kFloat && t.is_contiguous(), "nexar_b200: ", name,
+              " must be a contiguous fp32 CUDA tensor");
+}
+__nv_bfloat16* bf(const at::Tensor& t) { return reinterpret_cast<__nv_bfloat16*>(t.data_ptr()); }
+const __nv_bfloat16* bfc(const c10::optional<at::Tensor>& t) {
+  return t ? reinterpret_cast<const __nv_bfloat16*>(t->data_ptr()) : nullptr;
+}
+}  // namespace
+
+// LayerNorm forward; x: [R, C]. Returns nothing; writes y, mean, rstd (and
+// sum_out = x + res when res is given).
+void op_ln_fwd(const at::Tensor& x, const c10::optional<at::Tensor>& res,
+               const c10::optional<at::Tensor>& sum_out, const at::Tensor& w, const at::Tensor& b,
+               const at::Tensor& y, const at::Tensor& mean, const at::Tensor& rstd, double eps) {
+  need_bf16(x, "x");
+  need_bf16(y, "y");
+  need_bf16(w, "weight");
+  need_bf16(b, "bias");
+  need_f32(mean, "mean");
+  need_f32(rstd, "rstd");
+  const int C = x.size(-1);
+  const int R = x.numel() / C;
+  TORCH_CHECK(res.has_value() == sum_out.has_value(), "ln_fwd: res and sum_out go together");
+  c10::cuda::CUDAGuard g(x.get_device());
+  chk(ln_fwd(bf(x), bfc(res), sum_out ? bf(*sum_out) : nullptr, bf(w), bf(b), bf(y),
+             mean.data_ptr<float>(), rstd.data_ptr<float>(), R, C, (float)eps, stream_of(x)),
+      "ln_fwd");
+  count_launch(1);
+}
+
+int64_t op_ln_bwd_scratch_floats(int64_t R, int64_t C) {
+  return (int64_t)ln_bwd_scratch_floats((int)C, ln_bwd_blocks((int)R));
+}
+
+void op_ln_bwd(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& mean, const at::Tensor& rstd,
+               const at::Tensor& w, const c10::optional<at::Tensor>& dres, const at::Tensor& dx,
+               const at::Tensor& dw, const at::Tensor& db, const at::Tensor& scratch,
+               const at::Tensor& counter) {
+  need_bf16(dy, "dy");
+  need_bf16(x, "x");
+  need_bf16(dx, "dx");
+  need_bf16(dw, "dw");
+  need_bf16(db, "db");
+  need_f32(scratch, "scratch");
+  const int C = x.size(-1);
+  const int R = x.numel() / C;
+  const int blocks = ln_bwd_blocks(R);
+  TORCH_CHECK((size_t)scratch.numel() >= ln_bwd_scratch_floats(C, blocks), "ln_bwd: scratch too small");
+  TORCH_CHECK(counter.numel() >= 1 && counter.element_size() == 4, "ln_bwd: counter must be a 4-byte tensor");
+  c10::cuda::CUDAGuard g(x.get_device());
+  chk(ln_bwd(bf(dy), bf(x), mean.data_ptr<float>(), rstd.data_ptr<float>(), bf(w), bfc(dres), bf(dx),
+             bf(dw), bf(db), scratch.data_ptr<float>(), reinterpret_cast<unsigned int*>(counter.data_ptr()),
+             R, C, blocks, stream_of(x)),
+      "ln_bwd");
+  count_launch(1);
+}
+
+void op_gelu_fwd(const at::Tensor& x, const at::Tensor& y) {
+  need_bf16(x, "x");
+  need_bf16(y, "y");
+  c10::cuda::CUDAGuard g(x.get_device());
+  chk(gelu_fwd(bf(x), bf(y), x.numel(), stream_of(x)), "gelu_fwd");
+  count_launch(1);
+}
+void op_gelu_bwd(const at::Tensor& x, const at::Tensor& dy, const at::Tensor& dx) {
+  need_bf16(x, "x");
+  need_bf16(dy, "dy");
+  need_bf16(dx, "dx");
+  c10::cuda::CUDAGuard g(x.get_device());
+  chk(gelu_bwd(bf(x), bf(dy), bf(dx), x.numel(), stream_of(x)), "gelu_bwd");
+  count_launch(1);
+}
+void op_swiglu_fwd(const at::Tensor& gu, const at::Tensor& y) {
+  need_bf16(gu, "gu");
+  need_bf16(y, "y");
+  const int F = y.size(-1);
+  const int R = y.numel() / F;
+  TORCH_CHECK(gu.numel() == 2LL * R * F, "swiglu: gu must be [R, 2F]");
+  c10::cuda::CUDAGuard g(gu.get_device());
+  chk(swiglu_fwd(bf(gu), bf(y), R, F, stream_of(gu)), "swiglu_fwd");
+  count_launch(1);
+}
+void op_swiglu_bwd(const at::Tensor& gu, const at::Tensor& dy, const at::Tensor& dgu) {
+  need_bf16(gu, "gu");
+  need_bf16(dy, "dy");
+  need_bf16(dgu, "dgu");
+  const int F = dy.size(-1);
+  const int R = dy.numel() / F;
+  c10::cuda::CUDAGuard g(gu.get_device());
+  chk(swiglu_bwd(bf(gu), bf(dy), bf(dgu), R, F, stream_of(gu)), "swiglu_bwd");
+  count_launch(1);
+}
+
+void op_xent(const at::Tensor& logits, const at::Tensor& targets, const at::Tensor& losses,
+             const c10::optional<at::Tensor>& dlogits, int64_t V, double grad_scale) {
+  need_bf16(logits, "logits");
+  TORCH_CHECK(targets.scalar_type() == at::kLong && targets.is_contiguous(), "xent: targets must be int64");
+  need_f32(losses, "losses");
+  const int Vp = logits.size(-1);
+  const int R = logits.numel() / Vp;
+  TORCH_CHECK(targets.numel() == R && losses.numel() == R, "xent: one target/loss per row");
+  c10::cuda::CUDAGuard g(logits.get_device());
+  chk(xent_fwd_bwd(bf(logits), targets.data_ptr<int64_t>(), losses.data_ptr<float>(),
+                   dlogits ? bf(*dlogits) : nullptr, R, (int)V, Vp, (float)grad_scale, stream_of(logits)),
+      "xent");
+  count_launch(1);
+}
+
+void op_embed_fwd(const at::Tensor& tok, const at::Tensor& wte, const at::Tensor& wpe, const at::Tensor& out,
+                  int64_t T) {
+  TORCH_CHECK(tok.scalar_type() == at::kLong && tok.is_contiguous(), "embed: tokens must be int64");
+  need_bf16(wte, "wte");
+  need_bf16(wpe, "wpe");
+  need_bf16(out, "out");
+  const int C = wte.size(-1);
+  c10::cuda::CUDAGuard g(wte.get_device());
+  chk(embed_fwd(tok.data_ptr<int64_t>(), bf(wte), bf(wpe), bf(out), tok.numel(), (int)T, C, stream_of(wte)),
+      "embed_fwd");
+  count_launch(1);
+}
+void op_embed_bwd(const at::Tensor& tok, const at::Tensor& dout, const at::Tensor& dwte, const at::Tensor& dwpe,
+                  int64_t B, int64_t T) {
+  need_bf16(dout, "dout");
+  need_bf16(dwte, "dwte");
+  need_bf16(dwpe, "dwpe");
+  const int C = dout.size(-1);
+  c10::cuda::CUDAGuard g(dout.get_device());
+  chk(embed_bwd(tok.data_ptr<int64_t>(), bf(dout), bf(dwte), bf(dwpe), (int)B, (int)T, C, stream_of(dout)),
+      "embed_bwd");
+  count_launch(2);
+}
+
+int64_t op_grad_norm_blocks(int64_t n) { return grad_norm_blocks(n); }
+void op_grad_norm_clip(const at::Tensor& g, double max_norm, const at::Tensor& scratch, const at::Tensor& counter,
+                       const at::Tensor& norm_out, const at::Tensor& coef) {
+  need_bf16(g, "grads");
+  const int blocks = grad_norm_blocks(g.numel());
+  TORCH_CHECK(scratch.numel() >= blocks, "grad_norm: scratch too small");
+  c10::cuda::CUDAGuard gd(g.get_device());
+  chk(grad_norm_clip(bf(g), g.numel(), (float)max_norm, scratch.data_ptr<float>(),
+                     reinterpret_cast<unsigned int*>(counter.data_ptr()), norm_out.data_ptr<float>(),
+                     coef.data_ptr<float>(), blocks, stream_of(g)),
+      "grad_norm");
+  count_launch(1);
+}
+
+void op_adamw(const at::Tensor& p, const at::Tensor& m, const at::Tensor& v, const at::Tensor& g,
+              const at::Tensor& pb, int64_t decay_end, double lr, double b1, double b2, double eps, double wd,
+              int64_t step, const c10::optional<at::Tensor>& gscale, const c10::optional<at::Tensor>& step_dev,
+              const c10::optional<at::Tensor>& lr_dev) {
+  need_f32(p, "param");
+  need_f32(m, "exp_avg");
+  need_f32(v, "exp_avg_sq");
+  need_bf16(g, "grad");
+  need_bf16(pb, "param_bf16");
+  TORCH_CHECK(p.numel() == m.numel() && p.numel() == v.numel() && p.numel() == g.numel() && p.numel() == pb.numel(),
+              "adamw: size mismatch");
+  c10::cuda::CUDAGuard gd(p.get_device());
+  chk(adamw_step(p.data_ptr<float>(), m.data_ptr<float>(), v.data_ptr<float>(), bf(g), bf(pb), p.numel(),
+                 decay_end, (float)lr, (float)b1, (float)b2, (float)eps, (float)wd, (int)step,
+                 gscale ? gscale->data_ptr<float>() : nullptr, step_dev ? step_dev->data_ptr<int>() : nullptr,
+                 lr_dev ? lr_dev->data_ptr<float>() : nullptr, stream_of(p)),
+      "adamw");
+  count_launch(1);
+}
+
+void register_ops(py::module& m) {
+  m.def("ln_fwd", &op_ln_fwd);
+  m.def("ln_bwd", &op_ln_bwd);
+  m.def("ln_bwd_scratch_floats", &op_ln_bwd_scratch_floats);
+  m.def("gelu_fwd", &op_gelu_fwd);
+  m.def("gelu_bwd", &op_gelu_bwd);
+  m.def("swiglu_fwd", &op_swiglu_fwd);
+  m.def("swiglu_bwd", &op_swiglu_bwd);
+  m.def("xent", &op_xent);
+  m.def("embed_fwd", &op_embed_fwd);
+  m.def("embed_bwd", &op_embed_bwd);
+  m.def("grad_norm_blocks", &op_grad_norm_blocks);
+  m.def("grad_norm_clip", &op_grad_norm_clip);
+  m.def("adamw", &op_adamw);
+}
+
+}  // namespace nexar

@@ -1,0 +1,304 @@
+"""DeviceCommunicator: device-pointer collectives over NVLink peer memory.
+
+One process (or one thread) per GPU. Each rank allocates a symmetric heap of
+the same size; handles are exchanged out of band (``torch.distributed`` or a
+``nexar_b200`` host client) and every rank maps every peer's heap. All the
+collectives below then run as single sm_100a kernels that load and store peer
+HBM directly, with the reduction, scaling and dtype cast fused in.
+
+This is the on-box device path that the reference delegates to NCCL
+(nexar-nccl/src/comm.rs:122-181, nexar-nccl/src/group.rs:72-225), widened to
+every collective of the host API (nexar/src/client/collectives.rs:12-262):
+all_reduce, reduce_scatter, all_gather, all_to_all, broadcast, reduce, gather,
+scatter, scan, exclusive_scan and barrier, plus ``*_nb`` variants returning a
+handle (nexar/src/collective/handle.rs:12-91).
+
+Semantics that differ from the reference's host ring, on purpose:
+  * reduce_scatter gives rank r the reduction of chunk r (NCCL/MPI), not chunk
+    (r+1) mod N (nexar/src/collective/reduce_scatter.rs:73-77).
+Every device wait is bounded (``NEXAR_DEVICE_WAIT_TIMEOUT_US``); a kernel that
+times out records it in a host-mapped status word and returns, and
+:meth:`check` raises :class:`~nexar_b200.core.CollectiveFailed`.
+"""
+from __future__ import annotations
+
+import os
+from typing import Callable, List, Optional, Sequence
+
+import torch
+
+from .. import _native
+from ..core import CollectiveFailed, DataType, ReduceOp
+
+_ALGOS = {"auto": 0, "oneshot": 1, "one_shot": 1, "twoshot": 2, "two_shot": 2, "nvls": 3}
+_OP_NAMES = {1: "all_reduce", 2: "reduce_scatter", 3: "all_gather", 4: "all_to_all",
+             5: "broadcast", 6: "reduce", 7: "gather", 8: "scatter", 9: "scan",
+             10: "barrier", 11: "moe_dispatch", 12: "moe_combine", 13: "gemm_reduce_scatter",
+             14: "all_gather_gemm", 15: "compressed_all_reduce"}
+
+
+def _env_int(name: str, default: int) -> int:
+    v = os.environ.get(name)
+    return int(v) if v not in (None, "") else default
+
+
+class DeviceHandle:
+    """Completion handle of a non-blocking device collective.
+
+    ``wait()`` makes the caller's current stream wait for the collective
+    (no host block), ``synchronize()`` blocks the host, ``is_finished()``
+    polls. Mirrors ``CollectiveHandle`` (nexar/src/collective/handle.rs).
+    """
+
+    def __init__(self, event: torch.cuda.Event, keep: tuple, comm: "DeviceCommunicator"):
+        self._event = event
+        self._keep = keep
+        self._comm = comm
+
+    def wait(self):
+        torch.cuda.current_stream(self._comm.device).wait_event(self._event)
+        return self._keep[-1] if self._keep else None
+
+    def synchronize(self):
+        self._event.synchronize()
+        self._comm.check()
+        return self._keep[-1] if self._keep else None
+
+    def is_finished(self) -> bool:
+        return self._event.query()
+
+
+class DeviceCommunicator:
+    """Symmetric-memory communicator over the GPUs of one box."""
+
+    def __init__(self, rank: int, world_size: int, device: int,
+                 exchange: Callable[[bytes], List[bytes]],
+                 heap_bytes: Optional[int] = None, slot_bytes: Optional[int] = None,
+                 timeout_us: Optional[int] = None, barrier: Optional[Callable[[], None]] = None):
+        C = _native.cuda()
+        self.rank = rank
+        self.world_size = world_size
+        self.device = device
+        slot = slot_bytes or _env_int("NEXAR_SLOT_BYTES", 256 << 20)
+        user = _env_int("NEXAR_SYMM_USER_BYTES", 1 << 30)
+        heap = heap_bytes or (64 << 10) + 2 * slot + user
+        tmo = timeout_us if timeout_us is not None else _env_int("NEXAR_DEVICE_WAIT_TIMEOUT_US", 10_000_000)
+        self.oneshot_max_bytes = _env_int(
+            "NEXAR_AR_ONESHOT_MAX", 512 << 10 if world_size <= 4 else 256 << 10)
+        self._comm = C.DeviceComm(rank, world_size, device, heap, slot, tmo)
+        self._comm.max_blocks = _env_int("NEXAR_MAX_BLOCKS", 148)
+        handles = exchange(self._comm.export_handle())
+        if world_size > 1:
+            self._comm.connect(list(handles))
+        self._barrier = barrier
+        if barrier is not None:
+            barrier()  # every rank has mapped its peers before any kernel runs
+        self._side_stream = None
+        self._C = C
+
+    # ----------------------------------------------------------- construction
+    @classmethod
+    def from_torch(cls, group=None, device: Optional[int] = None, **kw) -> "DeviceCommunicator":
+        """Build from an initialised ``torch.distributed`` process group."""
+        import torch.distributed as dist
+        rank = dist.get_rank(group)
+        world = dist.get_world_size(group)
+        dev = torch.cuda.current_device() if device is None else device
+
+        def exchange(h: bytes) -> List[bytes]:
+            out: List = [None] * world
+            dist.all_gather_object(out, h, group=group)
+            return out
+
+        def barrier():
+            dist.barrier(group=group)
+
+        return cls(rank, world, dev, exchange, barrier=barrier, **kw)
+
+    @classmethod
+    def from_client(cls, client, device: Optional[int] = None, **kw) -> "DeviceCommunicator":
+        """Build from a ``nexar_b200`` host client (handles travel over its TCP mesh)."""
+        dev = torch.cuda.current_device() if device is None else device
+
+        def exchange(h: bytes) -> List[bytes]:
+            return client.all_gather_bytes(h)
+
+        return cls(client.rank, client.world_size, dev, exchange, barrier=client.barrier, **kw)
+
+    # ----------------------------------------------------------- memory
+    def symmetric_empty(self, shape: Sequence[int], dtype=torch.bfloat16, align: int = 256) -> torch.Tensor:
+        """Allocate a tensor inside the symmetric heap (collective: same order on all ranks).
+
+        Collectives on such tensors run in place with no staging copies.
+        """
+        numel = 1
+        for d in shape:
+            numel *= int(d)
+        nbytes = numel * torch.empty((), dtype=dtype).element_size()
+        off = self._comm.alloc_symmetric(nbytes, align)
+        return self._C.symmetric_tensor(self._comm, off, list(shape), int(DataType.from_torch(dtype)))
+
+    def is_symmetric(self, t: torch.Tensor) -> bool:
+        return self._comm.symmetric_offset(t) >= 0
+
+    @property
+    def native(self):
+        return self._comm
+
+    # ----------------------------------------------------------- status
+    def check(self):
+        """Raise CollectiveFailed if any device wait of this communicator timed out."""
+        st = self._comm.status()
+        if st["code"] != 0:
+            op = _OP_NAMES.get(st["op"], str(st["op"]))
+            raise CollectiveFailed(
+                f"{op} failed at rank {self.rank}: device wait for rank {st['rank']} timed out "
+                f"(block {st['block']}, epoch {st['epoch']})")
+
+    def status(self) -> dict:
+        return self._comm.status()
+
+    def clear_status(self):
+        self._comm.clear_status()
+
+    # ----------------------------------------------------------- collectives
+    def all_reduce(self, t: torch.Tensor, op="sum", out: Optional[torch.Tensor] = None,
+                   scale: Optional[float] = None, algo: str = "auto") -> torch.Tensor:
+        """Reduce ``t`` across ranks. In place unless ``out`` is given.
+
+        ``out`` may have a different dtype (fused cast, Sum only); ``scale``
+        multiplies the result (e.g. 1/world for gradient averaging).
+        """
+        out = t if out is None else out
+        self._C.all_reduce(self._comm, t, out, int(ReduceOp.parse(op)),
+                           1.0 if scale is None else float(scale), _ALGOS[algo], self.oneshot_max_bytes)
+        return out
+
+    def reduce_scatter(self, inp: torch.Tensor, out: Optional[torch.Tensor] = None, op="sum",
+                       scale: Optional[float] = None) -> torch.Tensor:
+        """``inp`` holds world*count elements; rank r receives the reduction of chunk r."""
+        if out is None:
+            if inp.numel() % self.world_size:
+                from ..core import IndivisibleCount
+                raise IndivisibleCount(f"count {inp.numel()} is not divisible by world size {self.world_size}")
+            out = torch.empty(inp.numel() // self.world_size, dtype=inp.dtype, device=inp.device)
+        self._C.reduce_scatter(self._comm, inp, out, int(ReduceOp.parse(op)), 1.0 if scale is None else float(scale))
+        return out
+
+    def all_gather(self, inp: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        if out is None:
+            out = torch.empty(inp.numel() * self.world_size, dtype=inp.dtype, device=inp.device)
+        self._C.all_gather(self._comm, inp, out)
+        return out
+
+    def all_to_all(self, inp: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        out = torch.empty_like(inp) if out is None else out
+        self._C.all_to_all(self._comm, inp, out)
+        return out
+
+    def broadcast(self, t: torch.Tensor, root: int = 0, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        out = t if out is None else out
+        self._C.broadcast(self._comm, t, out, int(root))
+        return out
+
+    def reduce(self, t: torch.Tensor, root: int = 0, op="sum", out: Optional[torch.Tensor] = None,
+               scale: Optional[float] = None) -> torch.Tensor:
+        out = t if out is None else out
+        self._C.reduce(self._comm, t, out, int(root), int(ReduceOp.parse(op)), 1.0 if scale is None else float(scale))
+        return out
+
+    def gather(self, inp: torch.Tensor, root: int = 0, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        if out is None:
+            out = torch.empty(inp.numel() * self.world_size, dtype=inp.dtype, device=inp.device)
+        self._C.gather(self._comm, inp, out, int(root))
+        return out
+
+    def scatter(self, inp: torch.Tensor, root: int = 0, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        if out is None:
+            out = torch.empty(inp.numel() // self.world_size, dtype=inp.dtype, device=inp.device)
+        self._C.scatter(self._comm, inp, out, int(root))
+        return out
+
+    def scan(self, inp: torch.Tensor, op="sum", out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        out = torch.empty_like(inp) if out is None else out
+        self._C.scan(self._comm, inp, out, int(ReduceOp.parse(op)), False)
+        return out
+
+    def exclusive_scan(self, inp: torch.Tensor, op="sum", out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        out = torch.empty_like(inp) if out is None else out
+        self._C.scan(self._comm, inp, out, int(ReduceOp.parse(op)), True)
+        return out
+
+    def barrier(self):
+        self._C.barrier(self._comm)
+
+    # ----------------------------------------------------------- non-blocking
+    def side_stream(self) -> torch.cuda.Stream:
+        if self._side_stream is None:
+            self._side_stream = torch.cuda.Stream(device=self.device, priority=-1)
+        return self._side_stream
+
+    def _nb(self, fn, tensors, result):
+        cur = torch.cuda.current_stream(self.device)
+        side = self.side_stream()
+        side.wait_stream(cur)
+        with torch.cuda.stream(side):
+            fn()
+        for t in tensors:
+            if t is not None and t.is_cuda:
+                t.record_stream(side)
+        ev = torch.cuda.Event()
+        ev.record(side)
+        return DeviceHandle(ev, tuple(tensors) + (result,), self)
+
+    def all_reduce_nb(self, t, op="sum", out=None, scale=None, algo="auto") -> DeviceHandle:
+        out_ = t if out is None else out
+        return self._nb(lambda: self.all_reduce(t, op, out_, scale, algo), (t, out_), out_)
+
+    def reduce_scatter_nb(self, inp, out, op="sum", scale=None) -> DeviceHandle:
+        return self._nb(lambda: self.reduce_scatter(inp, out, op, scale), (inp, out), out)
+
+    def all_gather_nb(self, inp, out) -> DeviceHandle:
+        return self._nb(lambda: self.all_gather(inp, out), (inp, out), out)
+
+    def all_to_all_nb(self, inp, out) -> DeviceHandle:
+        return self._nb(lambda: self.all_to_all(inp, out), (inp, out), out)
+
+    def broadcast_nb(self, t, root=0) -> DeviceHandle:
+        return self._nb(lambda: self.broadcast(t, root), (t,), t)
+
+    def reduce_nb(self, t, root=0, op="sum") -> DeviceHandle:
+        return self._nb(lambda: self.reduce(t, root, op), (t,), t)
+
+    def gather_nb(self, inp, out, root=0) -> DeviceHandle:
+        return self._nb(lambda: self.gather(inp, root, out), (inp, out), out)
+
+    def scatter_nb(self, inp, out, root=0) -> DeviceHandle:
+        return self._nb(lambda: self.scatter(inp, root, out), (inp, out), out)
+
+    def scan_nb(self, inp, out, op="sum") -> DeviceHandle:
+        return self._nb(lambda: self.scan(inp, op, out), (inp, out), out)
+
+    def exclusive_scan_nb(self, inp, out, op="sum") -> DeviceHandle:
+        return self._nb(lambda: self.exclusive_scan(inp, op, out), (inp, out), out)
+
+    def barrier_nb(self) -> DeviceHandle:
+        return self._nb(self.barrier, (), None)
+
+    # ----------------------------------------------------------- p2p (NCCL)
+    def send(self, t: torch.Tensor, dst: int, group=None):
+        """Pipeline-style device send; stays on NCCL p2p (torch.distributed)."""
+        import torch.distributed as dist
+        dist.send(t, dst, group=group)
+
+    def recv(self, t: torch.Tensor, src: int, group=None):
+        import torch.distributed as dist
+        dist.recv(t, src, group=group)
+
+    def isend(self, t: torch.Tensor, dst: int, group=None):
+        import torch.distributed as dist
+        return dist.isend(t, dst, group=group)
+
+    def irecv(self, t: torch.Tensor, src: int, group=None):
+        import torch.distributed as dist
+        return dist.irecv(t, src, group=group)

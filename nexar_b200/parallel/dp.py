@@ -1,0 +1,159 @@
+"""Data-parallel training entry point.
+
+One process per GPU. Gradients live in one flat bf16 buffer inside the
+symmetric heap, split into ~25 MB buckets (contiguous ranges). A
+post-accumulate hook counts finished parameters per bucket; when a bucket is
+complete its all-reduce (two-shot over NVLink, averaging scale 1/world fused
+into the kernel, in place, no staging copies) is launched on the
+communicator's side stream, overlapping the rest of backward. The optimizer
+step (global-norm clip + fused AdamW over flat fp32 master weights) runs
+after the last bucket joins. The whole step can be captured in one CUDA graph.
+
+The reference offers only the primitives for this (all_reduce_nb +
+CollectiveGroup, nexar/src/client/collectives_nb.rs:33-47; host-only bucketed
+all-reduce, nexar/src/collective/bucketed_allreduce.rs:23-75).
+"""
+from __future__ import annotations
+
+import time
+from typing import List, Optional
+
+import torch
+
+from .. import _native
+from ..models.gpt2 import GPT2, GPT2Config
+
+
+class DataParallelTrainer:
+    def __init__(self, cfg: GPT2Config, micro_batch: int, seq_len: int, comm=None, device=None,
+                 lr: float = 6e-4, betas=(0.9, 0.95), eps: float = 1e-8, weight_decay: float = 0.1,
+                 grad_clip: float = 1.0, bucket_bytes: int = 25 << 20, seed: int = 0,
+                 use_cuda_graph: bool = True):
+        self.cfg = cfg
+        self.B, self.T = micro_batch, seq_len
+        self.comm = comm
+        self.world = comm.world_size if comm is not None else 1
+        self.device = torch.device("cuda", torch.cuda.current_device() if device is None else device)
+        grad_alloc = None
+        if self.world > 1:
+            grad_alloc = lambda n: comm.symmetric_empty([n], torch.bfloat16)  # noqa: E731
+        self.model = GPT2(cfg, self.device, grad_alloc=grad_alloc, seed=seed)
+        flat = self.model.flat
+        if self.world > 1:
+            # identical start on every rank (ranks share the seed; this makes it exact)
+            comm.broadcast(flat.master, root=0)
+            flat.param_bf16.copy_(flat.master)
+        self.lr, self.betas, self.eps, self.wd, self.clip = lr, betas, eps, weight_decay, grad_clip
+        self.step_dev = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self.lr_dev = torch.full((1,), lr, dtype=torch.float32, device=self.device)
+        C = _native.cuda()
+        self._C = C
+        self.norm_scratch = torch.empty(C.grad_norm_blocks(flat.numel), dtype=torch.float32, device=self.device)
+        self.norm_counter = torch.zeros(4, dtype=torch.int32, device=self.device)
+        self.grad_norm = torch.zeros(1, dtype=torch.float32, device=self.device)
+        self.clip_coef = torch.ones(1, dtype=torch.float32, device=self.device)
+        # buckets + hooks
+        self.buckets = flat.buckets(bucket_bytes) if self.world > 1 else []
+        self._bucket_of = {}
+        self._bucket_need: List[int] = []
+        for bi, (_, _, names) in enumerate(self.buckets):
+            for n in names:
+                self._bucket_of[n] = bi
+            self._bucket_need.append(len(names))
+        self._bucket_left: List[int] = list(self._bucket_need)
+        self._launched: List[bool] = [False] * len(self.buckets)
+        if self.world > 1:
+            for name, par in self.model.p.items():
+                par.register_post_accumulate_grad_hook(self._make_hook(name))
+        self.static_idx = torch.zeros(self.B, self.T, dtype=torch.int64, device=self.device)
+        self.static_tgt = torch.zeros(self.B, self.T, dtype=torch.int64, device=self.device)
+        self.static_loss = torch.zeros((), dtype=torch.float32, device=self.device)
+        self.use_cuda_graph = use_cuda_graph
+        self.graph: Optional[torch.cuda.CUDAGraph] = None
+        self.graph_launches = 0
+        self._host_loss = torch.zeros((), dtype=torch.float32).pin_memory()
+
+    # ---------------------------------------------------------------- hooks
+    def _make_hook(self, name):
+        bi = self._bucket_of[name]
+
+        def hook(_param):
+            self._bucket_left[bi] -= 1
+            if self._bucket_left[bi] == 0:
+                self._launch_bucket(bi)
+        return hook
+
+    def _launch_bucket(self, bi):
+        start, end, _ = self.buckets[bi]
+        side = self.comm.side_stream()
+        side.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(side):
+            self.comm.all_reduce(self.model.flat.grad[start:end], scale=1.0 / self.world)
+        self._launched[bi] = True
+
+    # ---------------------------------------------------------------- step
+    def _step_body(self):
+        flat = self.model.flat
+        self._bucket_left = list(self._bucket_need)
+        self._launched = [False] * len(self.buckets)
+        flat.grad.zero_()
+        loss = self.model(self.static_idx, self.static_tgt, unit_grad=True)
+        loss.backward()
+        if self.world > 1:
+            for bi, done in enumerate(self._launched):
+                if not done:  # parameters without gradient (none in GPT-2) still need averaging
+                    self._launch_bucket(bi)
+            torch.cuda.current_stream(self.device).wait_stream(self.comm.side_stream())
+        C = self._C
+        C.grad_norm_clip(flat.grad, self.clip, self.norm_scratch, self.norm_counter, self.grad_norm,
+                         self.clip_coef)
+        self.step_dev.add_(1)
+        C.adamw(flat.master, flat.exp_avg, flat.exp_avg_sq, flat.grad, flat.param_bf16, flat.decay_end,
+                self.lr, self.betas[0], self.betas[1], self.eps, self.wd, 1, self.clip_coef,
+                self.step_dev, self.lr_dev)
+        self.static_loss.copy_(loss.detach())
+
+    def capture(self, warmup: int = 3):
+        """Warm up eagerly on a side stream, then capture one whole step."""
+        s = torch.cuda.Stream(device=self.device)
+        s.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(s):
+            for _ in range(warmup):
+                self._step_body()
+        torch.cuda.current_stream(self.device).wait_stream(s)
+        torch.cuda.synchronize(self.device)
+        if not self.use_cuda_graph:
+            return
+        g = torch.cuda.CUDAGraph()
+        before = _native.launch_count()
+        with torch.cuda.graph(g):
+            self._step_body()
+        self.graph_launches = _native.launch_count() - before
+        self.graph = g
+        torch.cuda.synchronize(self.device)
+
+    def run_step(self):
+        """One training step on the static device inputs (device-side only)."""
+        if self.graph is not None:
+            self.graph.replay()
+        else:
+            self._step_body()
+
+    def set_batch(self, idx: torch.Tensor, tgt: torch.Tensor, non_blocking: bool = True):
+        self.static_idx.copy_(idx, non_blocking=non_blocking)
+        self.static_tgt.copy_(tgt, non_blocking=non_blocking)
+
+    def step(self, idx_host: torch.Tensor, tgt_host: torch.Tensor) -> float:
+        """Public end-to-end step: H2D of the batch, fwd/bwd/all-reduce/AdamW, D2H of the loss."""
+        self.set_batch(idx_host, tgt_host)
+        self.run_step()
+        self._host_loss.copy_(self.static_loss, non_blocking=True)
+        torch.cuda.current_stream(self.device).synchronize()
+        return float(self._host_loss.item())
+
+    def tokens_per_step(self) -> int:
+        return self.B * self.T * self.world
+
+    def release(self):
+        """Drop the captured graph (call before tearing down the process group)."""
+        self.graph = None
