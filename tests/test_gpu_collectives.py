@@ -137,7 +137,8 @@ def _worker(rank, world, port, results):
                 out = comm.scan(xs[rank][:count].to(dev))
                 check(f"scan {dtype} {count}", out, _oracle_reduce([x[:count] for x in xs[:rank + 1]], "sum"), **_tol(dtype, world))
                 out = comm.exclusive_scan(xs[rank][:count].to(dev))
-                want = torch.zeros(count, dtype=torch.float64) if rank == 0 else _oracle_reduce([x[:count] for x in xs[:rank]], "sum")
+                zero = torch.zeros(count, dtype=torch.float64 if dtype.is_floating_point else torch.int64)
+                want = zero if rank == 0 else _oracle_reduce([x[:count] for x in xs[:rank]], "sum")
                 check(f"exscan {dtype} {count}", out, want, **_tol(dtype, world))
     comm.barrier()
     # non-blocking handle
