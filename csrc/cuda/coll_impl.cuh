@@ -77,11 +77,21 @@ template <typename T>
 NEXAR_D void copy_range(T* dst, const T* src, unsigned long long lo, unsigned long long hi,
                         bool vec, bool src_remote) {
   constexpr int V = PackOf<T>::V;
+  constexpr int U = 4;  // packs in flight per thread (NVLink latency hiding)
   unsigned long long i = lo;
   vec = vec && ((reinterpret_cast<uintptr_t>(dst + lo) | reinterpret_cast<uintptr_t>(src + lo)) & 15u) == 0;
   if (vec) {
     const unsigned long long vhi = lo + (hi - lo) / V * V;
-    for (i = lo + (unsigned long long)threadIdx.x * V; i < vhi; i += (unsigned long long)blockDim.x * V) {
+    const unsigned long long stride = (unsigned long long)blockDim.x * V;
+    i = lo + (unsigned long long)threadIdx.x * V;
+    for (; i + (U - 1) * stride < vhi; i += U * stride) {
+      uint4 r[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) r[u] = src_remote ? ld16_volatile(src + i + u * stride) : ld16(src + i + u * stride);
+#pragma unroll
+      for (int u = 0; u < U; ++u) st16(dst + i + u * stride, r[u]);
+    }
+    for (; i < vhi; i += stride) {
       uint4 r = src_remote ? ld16_volatile(src + i) : ld16(src + i);
       st16(dst + i, r);
     }
@@ -99,28 +109,37 @@ NEXAR_D void reduce_range(TO* dst, const T* const* srcs, int nsrc, unsigned long
                           unsigned long long hi, float scale, bool vec) {
   using A = typename AccOf<T>::type;
   constexpr int V = PackOf<T>::V;
+  constexpr int U = 2;  // packs in flight per source per thread
   unsigned long long i = lo;
   if (vec) {
     const unsigned long long vhi = lo + (hi - lo) / V * V;
-    for (i = lo + (unsigned long long)threadIdx.x * V; i < vhi; i += (unsigned long long)blockDim.x * V) {
-      uint4 raw[kMaxRanks];
+    const unsigned long long stride = (unsigned long long)blockDim.x * V;
+    i = lo + (unsigned long long)threadIdx.x * V;
+    for (; i < vhi; i += U * stride) {
+      uint4 raw[kMaxRanks][U];
 #pragma unroll
       for (int p = 0; p < kMaxRanks; ++p)
-        if (p < nsrc) raw[p] = ld16_volatile(srcs[p] + i);
-      A acc[V];
-      unpack<T, A, V>(raw[0], acc);
 #pragma unroll
-      for (int p = 1; p < kMaxRanks; ++p) {
-        if (p < nsrc) {
-          A x[V];
-          unpack<T, A, V>(raw[p], x);
+        for (int u = 0; u < U; ++u)
+          if (p < nsrc && i + u * stride < vhi) raw[p][u] = ld16_volatile(srcs[p] + i + u * stride);
 #pragma unroll
-          for (int v = 0; v < V; ++v) acc[v] = Red<OP, A>::apply(acc[v], x[v]);
+      for (int u = 0; u < U; ++u) {
+        if (i + u * stride >= vhi) break;
+        A acc[V];
+        unpack<T, A, V>(raw[0][u], acc);
+#pragma unroll
+        for (int p = 1; p < kMaxRanks; ++p) {
+          if (p < nsrc) {
+            A x[V];
+            unpack<T, A, V>(raw[p][u], x);
+#pragma unroll
+            for (int v = 0; v < V; ++v) acc[v] = Red<OP, A>::apply(acc[v], x[v]);
+          }
         }
-      }
 #pragma unroll
-      for (int v = 0; v < V; ++v) acc[v] = scale_acc<A>(acc[v], scale);
-      store_pack<TO, V, A>(dst + i, acc);
+        for (int v = 0; v < V; ++v) acc[v] = scale_acc<A>(acc[v], scale);
+        store_pack<TO, V, A>(dst + i + u * stride, acc);
+      }
     }
     i = vhi;
   }

@@ -1,0 +1,127 @@
+"""Device collective sweep: nexar_b200 peer-memory kernels vs NCCL.
+
+    torchrun --nproc-per-node N --master-addr 127.0.0.1 -m nexar_b200.bench.collectives \
+        [--ops all_reduce,reduce_scatter,all_gather,all_to_all,broadcast] [--dtype bf16]
+        [--min-bytes 1024] [--max-bytes 1073741824] [--iters 100] [--warmup 20] [--out file.jsonl]
+
+The NCCL arm issues the same call sequence as the reference's nexar-nccl
+single-node path (ncclAllReduce / ncclReduceScatter / ncclAllGather /
+ncclBroadcast in place on one stream; all_to_all as grouped send/recv),
+through torch.distributed's NCCL backend. Both arms are timed the same way:
+warm-up iterations, then `iters` back-to-back launches between CUDA events,
+max over ranks. Bus bandwidth follows the nccl-tests convention.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import sys
+
+
+def busbw_factor(op: str, n: int) -> float:
+    if op == "all_reduce":
+        return 2.0 * (n - 1) / n
+    if op in ("reduce_scatter", "all_gather", "all_to_all"):
+        return (n - 1) / n
+    return 1.0
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--ops", default="all_reduce,reduce_scatter,all_gather,all_to_all,broadcast")
+    ap.add_argument("--dtype", default="bf16")
+    ap.add_argument("--min-bytes", type=int, default=1024)
+    ap.add_argument("--max-bytes", type=int, default=1 << 30)
+    ap.add_argument("--step", type=int, default=2, help="size multiplier between points")
+    ap.add_argument("--iters", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impls", default="nexar,nccl")
+    ap.add_argument("--algo", default="auto")
+    ap.add_argument("--out", default=None)
+    args = ap.parse_args(argv)
+
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    rank = int(os.environ["RANK"])
+    world = int(os.environ["WORLD_SIZE"])
+    local = int(os.environ.get("LOCAL_RANK", rank))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=dev)
+    from nexar_b200.device import DeviceCommunicator
+    comm = DeviceCommunicator.from_torch()
+    dtype = {"bf16": torch.bfloat16, "f32": torch.float32, "f16": torch.float16}[args.dtype]
+    es = torch.empty((), dtype=dtype).element_size()
+    out_f = open(args.out, "a") if (args.out and rank == 0) else None
+    g = torch.Generator(device=dev).manual_seed(rank)
+
+    def time_it(fn):
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize()
+        dist.barrier()
+        torch.cuda.synchronize()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(args.iters):
+            fn()
+        e.record()
+        torch.cuda.synchronize()
+        t = torch.tensor([s.elapsed_time(e) / args.iters], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    ops = args.ops.split(",")
+    impls = args.impls.split(",")
+    size = args.min_bytes
+    while size <= args.max_bytes:
+        n = max(world, size // es)
+        n = (n // world) * world
+        big = torch.randn(n, device=dev, generator=g).to(dtype)
+        for op in ops:
+            for impl in impls:
+                if op == "all_reduce":
+                    t = big.clone()
+                    fn = (lambda: comm.all_reduce(t, algo=args.algo)) if impl == "nexar" else (lambda: dist.all_reduce(t))
+                    nbytes = n * es
+                elif op == "reduce_scatter":
+                    out = torch.empty(n // world, dtype=dtype, device=dev)
+                    fn = (lambda: comm.reduce_scatter(big, out)) if impl == "nexar" else (lambda: dist.reduce_scatter_tensor(out, big))
+                    nbytes = n * es
+                elif op == "all_gather":
+                    inp = big[: n // world].clone()
+                    out = torch.empty(n, dtype=dtype, device=dev)
+                    fn = (lambda: comm.all_gather(inp, out)) if impl == "nexar" else (lambda: dist.all_gather_into_tensor(out, inp))
+                    nbytes = n * es
+                elif op == "all_to_all":
+                    out = torch.empty_like(big)
+                    fn = (lambda: comm.all_to_all(big, out)) if impl == "nexar" else (lambda: dist.all_to_all_single(out, big))
+                    nbytes = n * es
+                elif op == "broadcast":
+                    t = big.clone()
+                    fn = (lambda: comm.broadcast(t, 0)) if impl == "nexar" else (lambda: dist.broadcast(t, 0))
+                    nbytes = n * es
+                else:
+                    raise SystemExit(f"unknown op {op}")
+                ms = time_it(fn)
+                algbw = nbytes / (ms / 1e3) / 1e9
+                rec = {"op": op, "impl": impl, "dtype": args.dtype, "bytes": nbytes, "n_gpus": world,
+                       "us": round(ms * 1e3, 2), "algbw_gbs": round(algbw, 2),
+                       "busbw_gbs": round(algbw * busbw_factor(op, world), 2)}
+                if rank == 0:
+                    print(json.dumps(rec), flush=True)
+                    if out_f:
+                        out_f.write(json.dumps(rec) + "\n")
+        del big
+        size *= args.step
+    comm.check()
+    dist.barrier()
+    dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

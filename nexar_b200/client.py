@@ -1,0 +1,457 @@
+"""NexarClient: the host communicator (C++ runtime) with nexar's public API.
+
+Bootstrap (nexar/src/client/bootstrap.rs): ``NexarClient.bootstrap_local(n)``
+builds n ranks in this process over loopback TCP through a real seed/worker
+exchange; ``NexarClient.bootstrap(seed_addr)`` joins a multi-process cluster
+(one process per rank / GPU), with ``SeedNode`` hosting discovery.
+
+Every collective of the reference is available with the reference's pointer
+signature (``all_reduce(ptr, count, dtype, op)``; ``count`` is elements per
+rank-chunk for all_gather / reduce_scatter / all_to_all / gather / scatter and
+total elements otherwise), plus ``*_host`` helpers that take numpy arrays or
+CPU torch tensors, ``*_device`` helpers that take CUDA tensors and run the
+sm_100a peer-memory kernels (the CUDA DeviceAdapter), and ``*_nb`` variants
+returning a :class:`CollectiveHandle`.
+"""
+from __future__ import annotations
+
+from typing import Iterable, List, Optional, Sequence, Tuple
+
+from . import _native
+from .core import DataType, ReduceOp
+
+_H = None
+
+
+def _h():
+    global _H
+    if _H is None:
+        _H = _native.host()
+    return _H
+
+
+def Config(**kw):
+    """NexarConfig with the reference's defaults; override fields by keyword."""
+    c = _h().Config()
+    for k, v in kw.items():
+        setattr(c, k, v)
+    return c
+
+
+def config_from_env():
+    return _h().Config.from_env()
+
+
+def _buf(x) -> Tuple[int, int, DataType]:
+    """(address, numel, dtype) of a contiguous numpy array or torch tensor."""
+    try:
+        import torch
+        if isinstance(x, torch.Tensor):
+            if not x.is_contiguous():
+                raise ValueError("tensor must be contiguous")
+            return x.data_ptr(), x.numel(), DataType.from_torch(x.dtype)
+    except ImportError:  # pragma: no cover
+        pass
+    import numpy as np
+    if isinstance(x, np.ndarray):
+        if not x.flags["C_CONTIGUOUS"]:
+            raise ValueError("array must be C-contiguous")
+        table = {np.dtype(np.float32): DataType.F32, np.dtype(np.float64): DataType.F64,
+                 np.dtype(np.float16): DataType.F16, np.dtype(np.int8): DataType.I8,
+                 np.dtype(np.int32): DataType.I32, np.dtype(np.int64): DataType.I64,
+                 np.dtype(np.uint8): DataType.U8, np.dtype(np.uint32): DataType.U32,
+                 np.dtype(np.uint64): DataType.U64, np.dtype(np.uint16): DataType.BF16}
+        return x.ctypes.data, x.size, table[x.dtype]
+    raise TypeError(f"unsupported buffer type {type(x)}")
+
+
+class CollectiveHandle:
+    """Handle of a non-blocking collective (nexar/src/collective/handle.rs)."""
+
+    def __init__(self, native, keep=()):
+        self._h = native
+        self._keep = keep
+
+    def wait(self):
+        self._h.wait()
+
+    def is_finished(self) -> bool:
+        return self._h.is_finished()
+
+
+class CollectiveGroup:
+    """Wait for several handles; raises the first error (handle.rs:50-91)."""
+
+    def __init__(self):
+        self._handles: List[CollectiveHandle] = []
+
+    def push(self, h: CollectiveHandle):
+        self._handles.append(h)
+
+    def wait_all(self):
+        first = None
+        for h in self._handles:
+            try:
+                h.wait()
+            except Exception as e:  # noqa: BLE001
+                first = first or e
+        if first is not None:
+            raise first
+
+    def __len__(self):
+        return len(self._handles)
+
+
+class NexarClient:
+    """A rank of a communicator (wraps the C++ ``NexarClient``)."""
+
+    def __init__(self, native, device_comm=None):
+        self._c = native
+        self._device = device_comm
+
+    # ------------------------------------------------------------ bootstrap
+    @staticmethod
+    def bootstrap_local(world_size: int, config=None) -> List["NexarClient"]:
+        cfg = config if config is not None else _h().Config()
+        return [NexarClient(c) for c in _h().NexarClient.bootstrap_local(world_size, cfg)]
+
+    bootstrap_local_with_config = bootstrap_local
+
+    @staticmethod
+    def bootstrap(seed_addr: str, token: Optional[bytes] = None, config=None,
+                  bind_host: str = "127.0.0.1") -> "NexarClient":
+        cfg = config if config is not None else _h().Config.from_env()
+        return NexarClient(_h().NexarClient.bootstrap_worker(seed_addr, token, cfg, bind_host))
+
+    # ------------------------------------------------------------ identity
+    @property
+    def rank(self) -> int:
+        return self._c.rank
+
+    @property
+    def world_size(self) -> int:
+        return self._c.world_size
+
+    @property
+    def comm_id(self) -> int:
+        return self._c.comm_id
+
+    @property
+    def native(self):
+        return self._c
+
+    def config(self):
+        return self._c.config()
+
+    def has_direct_peer(self, rank: int) -> bool:
+        return self._c.has_direct_peer(rank)
+
+    def is_sparse(self) -> bool:
+        return self._c.is_sparse()
+
+    def adapter(self) -> str:
+        return "cuda" if self._device is not None else self._c.adapter_name
+
+    # ------------------------------------------------------------ p2p
+    def send(self, ptr: int, size: int, dest: int, tag: int):
+        self._c.send(ptr, size, dest, tag)
+
+    def recv(self, ptr: int, size: int, src: int, tag: int):
+        self._c.recv(ptr, size, src, tag)
+
+    def send_iov(self, iov: Sequence[Tuple[int, int]], dest: int, tag: int):
+        self._c.send_iov(list(iov), dest, tag)
+
+    def recv_iov(self, iov: Sequence[Tuple[int, int]], src: int, tag: int):
+        self._c.recv_iov(list(iov), src, tag)
+
+    def send_bytes(self, dest: int, data: bytes):
+        self._c.send_bytes(dest, data)
+
+    def recv_bytes(self, src: int) -> bytes:
+        return self._c.recv_bytes(src)
+
+    def send_bytes_tagged(self, dest: int, tag: int, data: bytes):
+        self._c.send_bytes_tagged(dest, tag, data)
+
+    def recv_bytes_tagged(self, src: int, tag: int, timeout_s: float = -1.0) -> bytes:
+        return self._c.recv_bytes_tagged(src, tag, timeout_s)
+
+    # ------------------------------------------------------------ rpc
+    def register_rpc(self, fn_id: int, handler):
+        """handler(bytes) -> bytes, served by ``serve_rpc_once`` / ``start_rpc_server``."""
+        self._c.register_rpc(fn_id, handler)
+
+    def rpc(self, target: int, fn_id: int, args: bytes, timeout_s: float = -1.0) -> bytes:
+        return self._c.rpc(target, fn_id, args, timeout_s)
+
+    rpc_with_timeout = rpc
+
+    def recv_rpc_request(self, src: int, timeout_s: float = -1.0) -> dict:
+        return self._c.recv_rpc_request(src, timeout_s)
+
+    def serve_rpc_once(self, src: int, timeout_s: float = -1.0):
+        self._c.serve_rpc_once(src, timeout_s)
+
+    def start_rpc_server(self):
+        self._c.start_rpc_server()
+
+    def stop_rpc_server(self):
+        self._c.stop_rpc_server()
+
+    # ------------------------------------------------------------ collectives (pointer API)
+    def all_reduce(self, ptr: int, count: int, dtype, op=ReduceOp.Sum):
+        self._c.all_reduce(ptr, count, int(dtype), int(ReduceOp.parse(op)))
+
+    def all_reduce_rs_ag(self, ptr: int, count: int, dtype, op=ReduceOp.Sum):
+        self._c.all_reduce_rs_ag(ptr, count, int(dtype), int(ReduceOp.parse(op)))
+
+    def all_reduce_bucketed(self, entries: Sequence[Tuple[int, int]], dtype, op=ReduceOp.Sum):
+        self._c.all_reduce_bucketed(list(entries), int(dtype), int(ReduceOp.parse(op)))
+
+    def all_reduce_compressed(self, ptr: int, count: int, dtype, op, compressor, residual_ptr: int):
+        self._c.all_reduce_compressed(ptr, count, int(dtype), int(ReduceOp.parse(op)), compressor, residual_ptr)
+
+    def broadcast(self, ptr: int, count: int, dtype, root: int):
+        self._c.broadcast(ptr, count, int(dtype), root)
+
+    def all_gather(self, send_ptr: int, recv_ptr: int, count: int, dtype):
+        self._c.all_gather(send_ptr, recv_ptr, count, int(dtype))
+
+    def reduce_scatter(self, send_ptr: int, recv_ptr: int, count: int, dtype, op=ReduceOp.Sum):
+        self._c.reduce_scatter(send_ptr, recv_ptr, count, int(dtype), int(ReduceOp.parse(op)))
+
+    def reduce(self, ptr: int, count: int, dtype, op, root: int):
+        self._c.reduce(ptr, count, int(dtype), int(ReduceOp.parse(op)), root)
+
+    def all_to_all(self, send_ptr: int, recv_ptr: int, count: int, dtype):
+        self._c.all_to_all(send_ptr, recv_ptr, count, int(dtype))
+
+    def gather(self, send_ptr: int, recv_ptr: int, count: int, dtype, root: int):
+        self._c.gather(send_ptr, recv_ptr, count, int(dtype), root)
+
+    def scatter(self, send_ptr: int, recv_ptr: int, count: int, dtype, root: int):
+        self._c.scatter(send_ptr, recv_ptr, count, int(dtype), root)
+
+    def scan(self, ptr: int, count: int, dtype, op=ReduceOp.Sum):
+        self._c.scan(ptr, count, int(dtype), int(ReduceOp.parse(op)))
+
+    def exclusive_scan(self, ptr: int, count: int, dtype, op=ReduceOp.Sum):
+        self._c.exclusive_scan(ptr, count, int(dtype), int(ReduceOp.parse(op)))
+
+    def barrier(self, timeout_s: Optional[float] = None):
+        if timeout_s is None:
+            self._c.barrier()
+        else:
+            self._c.barrier_with_timeout(timeout_s)
+
+    # ------------------------------------------------------------ non-blocking
+    def all_reduce_nb(self, ptr: int, count: int, dtype, op=ReduceOp.Sum) -> CollectiveHandle:
+        return CollectiveHandle(self._c.all_reduce_nb(ptr, count, int(dtype), int(ReduceOp.parse(op))))
+
+    def _nb(self, op: str, *args) -> CollectiveHandle:
+        return CollectiveHandle(self._c.spawn_collective(op, tuple(int(a) for a in args)))
+
+    def broadcast_nb(self, ptr, count, dtype, root):
+        return self._nb("broadcast", ptr, count, dtype, root)
+
+    def all_gather_nb(self, send_ptr, recv_ptr, count, dtype):
+        return self._nb("all_gather", send_ptr, recv_ptr, count, dtype)
+
+    def reduce_scatter_nb(self, send_ptr, recv_ptr, count, dtype, op=ReduceOp.Sum):
+        return self._nb("reduce_scatter", send_ptr, recv_ptr, count, dtype, ReduceOp.parse(op))
+
+    def reduce_nb(self, ptr, count, dtype, op, root):
+        return self._nb("reduce", ptr, count, dtype, ReduceOp.parse(op), root)
+
+    def all_to_all_nb(self, send_ptr, recv_ptr, count, dtype):
+        return self._nb("all_to_all", send_ptr, recv_ptr, count, dtype)
+
+    def gather_nb(self, send_ptr, recv_ptr, count, dtype, root):
+        return self._nb("gather", send_ptr, recv_ptr, count, dtype, root)
+
+    def scatter_nb(self, send_ptr, recv_ptr, count, dtype, root):
+        return self._nb("scatter", send_ptr, recv_ptr, count, dtype, root)
+
+    def scan_nb(self, ptr, count, dtype, op=ReduceOp.Sum):
+        return self._nb("scan", ptr, count, dtype, ReduceOp.parse(op))
+
+    def exclusive_scan_nb(self, ptr, count, dtype, op=ReduceOp.Sum):
+        return self._nb("exclusive_scan", ptr, count, dtype, ReduceOp.parse(op))
+
+    def all_reduce_rs_ag_nb(self, ptr, count, dtype, op=ReduceOp.Sum):
+        return self._nb("all_reduce_rs_ag", ptr, count, dtype, ReduceOp.parse(op))
+
+    def barrier_nb(self):
+        return self._nb("barrier")
+
+    # ------------------------------------------------------------ typed host helpers
+    def all_reduce_host(self, buf, op=ReduceOp.Sum):
+        p, n, dt = _buf(buf)
+        self.all_reduce(p, n, dt, op)
+        return buf
+
+    def broadcast_host(self, buf, root: int):
+        p, n, dt = _buf(buf)
+        self.broadcast(p, n, dt, root)
+        return buf
+
+    def all_gather_host(self, send, recv):
+        ps, n, dt = _buf(send)
+        pr, _, _ = _buf(recv)
+        self.all_gather(ps, pr, n, dt)
+        return recv
+
+    def reduce_scatter_host(self, send, recv, op=ReduceOp.Sum):
+        ps, _, dt = _buf(send)
+        pr, n, _ = _buf(recv)
+        self.reduce_scatter(ps, pr, n, dt, op)
+        return recv
+
+    def reduce_host(self, buf, op, root: int):
+        p, n, dt = _buf(buf)
+        self.reduce(p, n, dt, op, root)
+        return buf
+
+    def all_to_all_host(self, send, recv):
+        ps, n, dt = _buf(send)
+        pr, _, _ = _buf(recv)
+        self.all_to_all(ps, pr, n // self.world_size, dt)
+        return recv
+
+    def gather_host(self, send, recv, root: int):
+        ps, n, dt = _buf(send)
+        pr = _buf(recv)[0] if recv is not None else 0
+        self.gather(ps, pr, n, dt, root)
+        return recv
+
+    def scatter_host(self, send, recv, root: int):
+        pr, n, dt = _buf(recv)
+        ps = _buf(send)[0] if send is not None else 0
+        self.scatter(ps, pr, n, dt, root)
+        return recv
+
+    def scan_host(self, buf, op=ReduceOp.Sum):
+        p, n, dt = _buf(buf)
+        self.scan(p, n, dt, op)
+        return buf
+
+    def exclusive_scan_host(self, buf, op=ReduceOp.Sum):
+        p, n, dt = _buf(buf)
+        self.exclusive_scan(p, n, dt, op)
+        return buf
+
+    def all_reduce_bucketed_host(self, bufs, op=ReduceOp.Sum):
+        entries = [_buf(b) for b in bufs]
+        dts = {e[2] for e in entries}
+        if len(dts) != 1:
+            raise ValueError("all buffers of a bucket need one dtype")
+        self.all_reduce_bucketed([(p, n) for p, n, _ in entries], dts.pop(), op)
+        return bufs
+
+    def all_reduce_compressed_host(self, buf, compressor, residual, op=ReduceOp.Sum):
+        p, n, dt = _buf(buf)
+        r, _, _ = _buf(residual)
+        self.all_reduce_compressed(p, n, dt, op, compressor, r)
+        return buf
+
+    # ------------------------------------------------------------ device (CUDA adapter)
+    def attach_device(self, device: Optional[int] = None, **kw):
+        """Attach the CUDA DeviceAdapter: maps the symmetric heaps of every rank
+        (handles travel over this client's mesh) so ``*_device`` calls run the
+        sm_100a peer-memory kernels."""
+        from .device import DeviceCommunicator
+        self._device = DeviceCommunicator.from_client(self, device=device, **kw)
+        return self._device
+
+    @property
+    def device(self):
+        if self._device is None:
+            raise RuntimeError("no CUDA device attached; call attach_device()")
+        return self._device
+
+    def all_reduce_device(self, t, op=ReduceOp.Sum):
+        return self.device.all_reduce(t, op=str(ReduceOp.parse(op)))
+
+    def broadcast_device(self, t, root: int):
+        return self.device.broadcast(t, root)
+
+    def all_gather_device(self, send, recv):
+        return self.device.all_gather(send, recv)
+
+    def reduce_scatter_device(self, send, recv, op=ReduceOp.Sum):
+        return self.device.reduce_scatter(send, recv, op=str(ReduceOp.parse(op)))
+
+    def reduce_device(self, t, op, root: int):
+        return self.device.reduce(t, root, op=str(ReduceOp.parse(op)))
+
+    def all_to_all_device(self, send, recv):
+        return self.device.all_to_all(send, recv)
+
+    def gather_device(self, send, recv, root: int):
+        return self.device.gather(send, root, recv)
+
+    def scatter_device(self, send, recv, root: int):
+        return self.device.scatter(send, root, recv)
+
+    def scan_device(self, t, op=ReduceOp.Sum):
+        return t.copy_(self.device.scan(t, op=str(ReduceOp.parse(op))))
+
+    def exclusive_scan_device(self, t, op=ReduceOp.Sum):
+        return t.copy_(self.device.exclusive_scan(t, op=str(ReduceOp.parse(op))))
+
+    # ------------------------------------------------------------ helpers for the device layer
+    def all_gather_bytes(self, data: bytes) -> List[bytes]:
+        """All-gather variable-length byte strings (used for handle exchange)."""
+        import numpy as np
+        n = np.array([len(data)], dtype=np.uint64)
+        lens = np.zeros(self.world_size, dtype=np.uint64)
+        self.all_gather_host(n, lens)
+        m = int(lens.max())
+        mine = np.zeros(m, dtype=np.uint8)
+        mine[:len(data)] = np.frombuffer(data, dtype=np.uint8)
+        out = np.zeros(m * self.world_size, dtype=np.uint8)
+        self.all_gather_host(mine, out)
+        return [out[i * m: i * m + int(lens[i])].tobytes() for i in range(self.world_size)]
+
+    # ------------------------------------------------------------ communicators
+    def split(self, color: int, key: int) -> "NexarClient":
+        return NexarClient(self._c.split(color, key))
+
+    def rebuild_excluding(self, dead_ranks: Iterable[int]) -> "NexarClient":
+        return NexarClient(self._c.rebuild_excluding(sorted(set(dead_ranks))))
+
+    def rebuild_adding(self, new_mesh_ranks: Iterable[int], comm_id: int = 0) -> "NexarClient":
+        return NexarClient(self._c.rebuild_adding(list(new_mesh_ranks), comm_id))
+
+    def failure_watch(self) -> List[int]:
+        """Current dead ranks (communicator numbering)."""
+        return self._c.dead_ranks()
+
+    def wait_failure(self, timeout_s: float) -> List[int]:
+        return self._c.wait_failure(timeout_s)
+
+    def close(self):
+        """Shut every connection of this rank (fault injection)."""
+        self._c.close()
+
+
+# The C++ API is synchronous, so the blocking client is the same object.
+SyncClient = NexarClient
+
+
+def SeedNode(addr: str = "127.0.0.1:0", token: Optional[bytes] = None, local: bool = False):
+    h = _h()
+    return h.SeedNode.bind_local() if local else h.SeedNode.bind(addr, token)
+
+
+def TopKCompressor(ratio: float):
+    return _h().TopKCompressor(ratio)
+
+
+def RandomKCompressor(ratio: float):
+    return _h().RandomKCompressor(ratio)
+
+
+def NoCompression():
+    return _h().NoCompression()
