@@ -1,0 +1,102 @@
+// Host side of the tcgen05 GEMM: tensor-map creation and launch.
+#include <mutex>
+
+#include "gemm.cuh"
+#include "gemm_api.h"
+
+namespace nexar {
+
+namespace {
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+unsigned int* err_word() {
+  static unsigned int* w = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    if (cudaMalloc(&w, sizeof(unsigned int) * 64) == cudaSuccess) cudaMemset(w, 0, sizeof(unsigned int) * 64);
+  });
+  return w;
+}
+
+int sm_count() {
+  static int n = 0;
+  if (n == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (n <= 0) n = 148;
+  }
+  return n;
+}
+}  // namespace
+
+// 2D bf16 tensor map over a row-major [rows, cols] matrix with leading
+// dimension ld (elements), box = [box_rows, box_cols], 128-byte swizzle.
+cudaError_t make_tmap_bf16(CUtensorMap* map, const void* base, long long rows, long long cols, long long ld,
+                           int box_rows, int box_cols) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return cudaErrorNotSupported;
+  if ((reinterpret_cast<uintptr_t>(base) & 15u) || (ld * 2) % 16) return cudaErrorInvalidValue;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
+  cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
+template <class Epi>
+static cudaError_t launch_gemm(const void* A, const void* B, int M, int N, int K, long long lda, long long ldb,
+                               const Epi& epi, int max_ctas, cudaStream_t s) {
+  using namespace gemm;
+  if (M <= 0 || N <= 0 || K <= 0) return cudaSuccess;
+  CUtensorMap ta, tb;
+  cudaError_t e = make_tmap_bf16(&ta, A, M, K, lda, BM, BK);
+  if (e != cudaSuccess) return e;
+  e = make_tmap_bf16(&tb, B, N, K, ldb, BN, BK);
+  if (e != cudaSuccess) return e;
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaFuncSetAttribute(k_gemm_bf16<Epi>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    attr_set = true;
+  }
+  const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
+  int grid = sm_count();
+  if (max_ctas > 0 && max_ctas < grid) grid = max_ctas;
+  if (tiles < grid) grid = tiles;
+  k_gemm_bf16<Epi><<<grid, THREADS, SMEM_BYTES, s>>>(ta, tb, M, N, K, epi, err_word());
+  return cudaGetLastError();
+}
+
+cudaError_t gemm_bf16(const __nv_bfloat16* A, const __nv_bfloat16* B, __nv_bfloat16* C, int M, int N, int K,
+                      long long lda, long long ldb, long long ldc, const __nv_bfloat16* bias,
+                      const __nv_bfloat16* residual, long long ldr, __nv_bfloat16* pre_act, int act, float alpha,
+                      cudaStream_t s) {
+  gemm::EpiStore epi{C, ldc, bias, residual, ldr, pre_act, alpha, act};
+  return launch_gemm(A, B, M, N, K, lda, ldb, epi, 0, s);
+}
+
+unsigned int gemm_error_flag() {
+  unsigned int v = 0;
+  if (unsigned int* w = err_word()) cudaMemcpy(&v, w, sizeof(v), cudaMemcpyDeviceToHost);
+  return v;
+}
+
+}  // namespace nexar

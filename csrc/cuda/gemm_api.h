@@ -1,0 +1,23 @@
+// Host API of the tcgen05 GEMMs (plain and fused with collectives).
+#pragma once
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+namespace nexar {
+
+// C[M,N] = act(alpha * A[M,K] . B[N,K]^T + bias) (+ residual), bf16 in/out,
+// fp32 accumulation in TMEM. `pre_act` (optional) receives the value before
+// the activation. Leading dimensions in elements; all must be multiples of 8.
+cudaError_t gemm_bf16(const __nv_bfloat16* A, const __nv_bfloat16* B, __nv_bfloat16* C, int M, int N, int K,
+                      long long lda, long long ldb, long long ldc, const __nv_bfloat16* bias,
+                      const __nv_bfloat16* residual, long long ldr, __nv_bfloat16* pre_act, int act, float alpha,
+                      cudaStream_t s);
+
+// Nonzero if any GEMM launch on this device gave up on a bounded wait.
+unsigned int gemm_error_flag();
+
+cudaError_t make_tmap_bf16(CUtensorMap* map, const void* base, long long rows, long long cols, long long ld,
+                           int box_rows, int box_cols);
+
+}  // namespace nexar

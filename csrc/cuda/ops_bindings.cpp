@@ -187,7 +187,9 @@ void op_adamw(const at::Tensor& p, const at::Tensor& m, const at::Tensor& v, con
   count_launch(1);
 }
 
+void register_gemm_ops(py::module& m);
 void register_ops(py::module& m) {
+  register_gemm_ops(m);
   m.def("ln_fwd", &op_ln_fwd);
   m.def("ln_bwd", &op_ln_bwd);
   m.def("ln_bwd_scratch_floats", &op_ln_bwd_scratch_floats);
@@ -203,4 +205,34 @@ void register_ops(py::module& m) {
   m.def("adamw", &op_adamw);
 }
 
+}  // namespace nexar
+
+// ---------------------------------------------------------------- GEMM (tcgen05)
+#include "gemm_api.h"
+namespace nexar {
+void op_gemm(const at::Tensor& A, const at::Tensor& B, const at::Tensor& C, const c10::optional<at::Tensor>& bias,
+             const c10::optional<at::Tensor>& residual, const c10::optional<at::Tensor>& pre, int64_t act,
+             double alpha) {
+  TORCH_CHECK(A.is_cuda() && B.is_cuda() && C.is_cuda(), "gemm: CUDA tensors required");
+  TORCH_CHECK(A.scalar_type() == at::kBFloat16 && B.scalar_type() == at::kBFloat16 && C.scalar_type() == at::kBFloat16,
+              "gemm: bf16 operands required");
+  TORCH_CHECK(A.dim() == 2 && B.dim() == 2 && C.dim() == 2, "gemm: 2D operands required");
+  TORCH_CHECK(A.stride(1) == 1 && B.stride(1) == 1 && C.stride(1) == 1, "gemm: inner dimension must be contiguous");
+  const int M = A.size(0), K = A.size(1), N = B.size(0);
+  TORCH_CHECK(B.size(1) == K && C.size(0) == M && C.size(1) == N, "gemm: shape mismatch");
+  c10::cuda::CUDAGuard g(A.get_device());
+  const __nv_bfloat16* rp = residual ? reinterpret_cast<const __nv_bfloat16*>(residual->data_ptr()) : nullptr;
+  chk(gemm_bf16(reinterpret_cast<const __nv_bfloat16*>(A.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(B.data_ptr()),
+                reinterpret_cast<__nv_bfloat16*>(C.data_ptr()), M, N, K, A.stride(0), B.stride(0), C.stride(0),
+                bias ? reinterpret_cast<const __nv_bfloat16*>(bias->data_ptr()) : nullptr, rp,
+                residual ? residual->stride(0) : 0, pre ? reinterpret_cast<__nv_bfloat16*>(pre->data_ptr()) : nullptr,
+                (int)act, (float)alpha, stream_of(A)),
+      "gemm");
+  count_launch(1);
+}
+void register_gemm_ops(py::module& m) {
+  m.def("gemm", &op_gemm, py::arg("A"), py::arg("B"), py::arg("C"), py::arg("bias") = py::none(),
+        py::arg("residual") = py::none(), py::arg("pre") = py::none(), py::arg("act") = 0, py::arg("alpha") = 1.0);
+  m.def("gemm_error_flag", &gemm_error_flag);
+}
 }  // namespace nexar
