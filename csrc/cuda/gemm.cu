@@ -62,9 +62,10 @@ cudaError_t make_tmap_bf16(CUtensorMap* map, const void* base, long long rows, l
   return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
-template <class Epi>
-static cudaError_t launch_gemm(const void* A, const void* B, int M, int N, int K, long long lda, long long ldb,
-                               const Epi& epi, int max_ctas, cudaStream_t s) {
+template <class Epi, class Gate>
+cudaError_t launch_gemm_generic(const void* A, const void* B, int M, int N, int K, long long lda, long long ldb,
+                                const CUtensorMap& tout, const CUtensorMap& tpre, int m_rotate, const Epi& epi,
+                                const Gate& gate, int max_ctas, cudaStream_t s) {
   using namespace gemm;
   if (M <= 0 || N <= 0 || K <= 0) return cudaSuccess;
   CUtensorMap ta, tb;
@@ -74,14 +75,15 @@ static cudaError_t launch_gemm(const void* A, const void* B, int M, int N, int K
   if (e != cudaSuccess) return e;
   static bool attr_set = false;
   if (!attr_set) {
-    cudaFuncSetAttribute(k_gemm_bf16<Epi>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    cudaFuncSetAttribute(k_gemm_bf16<Epi, Gate>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
     attr_set = true;
   }
   const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
   int grid = sm_count();
   if (max_ctas > 0 && max_ctas < grid) grid = max_ctas;
   if (tiles < grid) grid = tiles;
-  k_gemm_bf16<Epi><<<grid, THREADS, SMEM_BYTES, s>>>(ta, tb, M, N, K, epi, err_word());
+  k_gemm_bf16<Epi, Gate><<<grid, THREADS, SMEM_BYTES, s>>>(ta, tb, tout, tpre, M, N, K, m_rotate, epi, gate,
+                                                          err_word());
   return cudaGetLastError();
 }
 
@@ -89,8 +91,16 @@ cudaError_t gemm_bf16(const __nv_bfloat16* A, const __nv_bfloat16* B, __nv_bfloa
                       long long lda, long long ldb, long long ldc, const __nv_bfloat16* bias,
                       const __nv_bfloat16* residual, long long ldr, __nv_bfloat16* pre_act, int act, float alpha,
                       cudaStream_t s) {
-  gemm::EpiStore epi{C, ldc, bias, residual, ldr, pre_act, alpha, act};
-  return launch_gemm(A, B, M, N, K, lda, ldb, epi, 0, s);
+  CUtensorMap tout, tpre;
+  cudaError_t e = make_tmap_bf16(&tout, C, M, N, ldc, 32, 64);
+  if (e != cudaSuccess) return e;
+  tpre = tout;
+  if (pre_act) {
+    e = make_tmap_bf16(&tpre, pre_act, M, N, ldc, 32, 64);
+    if (e != cudaSuccess) return e;
+  }
+  gemm::EpiStore epi{bias, residual, ldr, alpha, act, pre_act != nullptr};
+  return launch_gemm_generic(A, B, M, N, K, lda, ldb, tout, tpre, 0, epi, gemm::NoGate{}, 0, s);
 }
 
 unsigned int gemm_error_flag() {

@@ -2,15 +2,24 @@
 //
 //   C[M, N] = epilogue( A[M, K] . B[N, K]^T )      (both operands K-major)
 //
-// CTA = 6 warps: warp 0 lane 0 issues TMA loads of 128x64 A and 256x64 B
-// tiles into a 4-stage ring of 128-byte-swizzled shared memory; warp 1
+// CTA = 6 warps. Warp 0 lane 0 issues TMA loads of 128x64 A and 256x64 B
+// tiles into a 4-stage ring of 128-byte-swizzled shared memory. Warp 1
 // allocates 512 TMEM columns (two 128x256 fp32 accumulators) and its lane 0
-// issues tcgen05.mma (M=128, N=256, K=16) and commits completion to
-// mbarriers; warps 2-5 drain the accumulator of the previous tile from TMEM
-// (tcgen05.ld 32x32b) while the next tile is being multiplied, and apply the
-// epilogue policy. TMA loads use no cluster multicast. Every mbarrier wait is
-// bounded; a wait that gives up sets *err and the kernel unwinds (TMEM is
-// always freed).
+// issues tcgen05.mma (M=128, N=256, K=16), committing completion to
+// mbarriers. Warps 2-5 drain the previous tile's accumulator from TMEM
+// (tcgen05.ld 32x32b.x32, one 32-lane quarter per warp) while the next tile
+// is multiplied, apply the epilogue math in registers, stage 32x64 bf16
+// blocks in 128-byte-swizzled shared memory (bank-conflict free) and write
+// them out with TMA bulk stores (or, for the fused reduce-scatter, with
+// coalesced stores into the owning peer's memory).
+//
+// Hooks let the fused collective kernels reuse this mainloop:
+//   Sched::coords(t, tm, tn)      tile order
+//   Gate::wait_a(tm)              producer waits until A rows of tm are local
+//   Epi (see EpiStore)            tile sink
+// TMA loads use no cluster multicast. Every mbarrier wait is bounded
+// (2 s of %globaltimer); a wait that gives up sets *err, the kernel unwinds
+// and TMEM is always freed.
 #pragma once
 #include "common.cuh"
 #include "sm100.cuh"
@@ -20,11 +29,14 @@ namespace gemm {
 
 constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4, THREADS = 192;
 constexpr int A_BYTES = BM * BK * 2, B_BYTES = BN * BK * 2, STAGE_BYTES = A_BYTES + B_BYTES;
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+constexpr int EPI_WARPS = 4, EPI_BUF_BYTES = 32 * 64 * 2;  // one 32x64 bf16 block
+constexpr int EPI_BYTES = EPI_WARPS * 2 * EPI_BUF_BYTES;   // double-buffered per warp
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + EPI_BYTES + 1024 /*align*/ + 256 /*barriers*/;
 constexpr uint64_t kWaitLimit = 2000000000ull;  // ns: 2 s per wait, far above any legitimate wait
 
 struct TileSched {
   int tiles_m, tiles_n;
+  int m_rotate;  // tile rows start at this M-tile (fused kernels: local shard first)
   __device__ int num() const { return tiles_m * tiles_n; }
   __device__ void coords(int t, int& tm, int& tn) const {
     // Groups of 8 M-tiles walk N together so concurrently running CTAs
@@ -35,22 +47,117 @@ struct TileSched {
     const int first_m = g * group;
     const int gm = min(tiles_m - first_m, group);
     const int r = t % per_group;
-    tm = first_m + r % gm;
+    tm = (first_m + r % gm + m_rotate) % tiles_m;
     tn = r / gm;
   }
 };
 
-// Epilogue policy contract:
-//   __device__ void apply(int row, int col0, float (&v)[32], int M, int N) const;
-// called by each epilogue thread for 32 consecutive columns of one row.
-template <class Epi>
+struct NoGate {
+  __device__ __forceinline__ bool wait_a(int) const { return true; }
+};
+
+__device__ __forceinline__ float gelu_tanh_f(float x) {
+  const float u = 0.7978845608028654f * (x + 0.044715f * x * x * x);
+  return 0.5f * x * (1.f + tanhf(u));
+}
+
+// Pack 64 floats of one row into the 128-byte-swizzled staging block
+// (row `r` of 32, 8 chunks of 16 bytes; chunk j lands at j ^ (r & 7)).
+__device__ __forceinline__ void stage_row64(uint8_t* buf, int r, const float (&v)[64]) {
+  uint8_t* row = buf + r * 128;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    uint4 o;
+    __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) h[e] = __floats2bfloat162_rn(v[j * 8 + 2 * e], v[j * 8 + 2 * e + 1]);
+    *reinterpret_cast<uint4*>(row + ((j ^ (r & 7)) << 4)) = o;
+  }
+}
+
+// Default sink: out = act(alpha * acc + bias) (+ residual), via TMA store;
+// optionally the pre-activation through a second tensor map.
+struct EpiStore {
+  const __nv_bfloat16* bias;      // [N] or null
+  const __nv_bfloat16* residual;  // [M, ldr] or null
+  long long ldr;
+  float alpha;
+  int act;                        // 0 none, 1 gelu(tanh)
+  int has_pre;
+
+  __device__ __forceinline__ bool begin_tile(int, int) const { return true; }
+  // v: 64 accumulators of row `row`, columns col0..col0+63 (in-place math).
+  __device__ __forceinline__ void math(int row, int col0, float (&v)[64], int M, int N, float (&pre)[64]) const {
+#pragma unroll
+    for (int i = 0; i < 64; ++i) v[i] *= alpha;
+    if (bias) {
+      const int valid = min(64, N - col0);
+      if (valid == 64 && ((reinterpret_cast<uintptr_t>(bias + col0) & 15u) == 0)) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          uint4 b = *reinterpret_cast<const uint4*>(bias + col0 + j * 8);
+          const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&b);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            float2 f = __bfloat1622float2(h[e]);
+            v[j * 8 + 2 * e] += f.x;
+            v[j * 8 + 2 * e + 1] += f.y;
+          }
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 64; ++i)
+          if (i < valid) v[i] += __bfloat162float(bias[col0 + i]);
+      }
+    }
+    if (has_pre) {
+#pragma unroll
+      for (int i = 0; i < 64; ++i) pre[i] = v[i];
+    }
+    if (act == 1) {
+#pragma unroll
+      for (int i = 0; i < 64; ++i) v[i] = gelu_tanh_f(v[i]);
+    }
+    if (residual && row < M) {
+      const __nv_bfloat16* rp = residual + (long long)row * ldr + col0;
+      const int valid = min(64, N - col0);
+      if (valid == 64 && ((reinterpret_cast<uintptr_t>(rp) & 15u) == 0)) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          uint4 b = *reinterpret_cast<const uint4*>(rp + j * 8);
+          const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&b);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            float2 f = __bfloat1622float2(h[e]);
+            v[j * 8 + 2 * e] += f.x;
+            v[j * 8 + 2 * e + 1] += f.y;
+          }
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 64; ++i)
+          if (i < valid) v[i] += __bfloat162float(rp[i]);
+      }
+    }
+  }
+  // Called by lane 0 after the 32x64 block is staged and fenced.
+  __device__ __forceinline__ void store_block(const CUtensorMap* out, const CUtensorMap*, const uint8_t* buf,
+                                              const uint8_t*, int row0, int col0) const {
+    sm100::tma_store_2d(out, buf, col0, row0);
+  }
+  __device__ __forceinline__ void end_tile(int, int) const {}
+};
+
+template <class Epi, class Gate = NoGate>
 __global__ void __launch_bounds__(THREADS, 1)
-k_gemm_bf16(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M, int N,
-            int K, Epi epi, unsigned int* err) {
+k_gemm_bf16(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+            const __grid_constant__ CUtensorMap tmOut, const __grid_constant__ CUtensorMap tmPre, int M, int N,
+            int K, int m_rotate, Epi epi, Gate gate, unsigned int* err) {
   using namespace sm100;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  uint8_t* epi_smem = smem + STAGES * STAGE_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(epi_smem + EPI_BYTES);
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
@@ -65,7 +172,7 @@ k_gemm_bf16(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
-      mbar_init(&tempty[b], 4);
+      mbar_init(&tempty[b], EPI_WARPS);
     }
     s_abort = 0;
     mbar_fence_init();
@@ -81,7 +188,7 @@ k_gemm_bf16(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
-  TileSched sched{(M + BM - 1) / BM, (N + BN - 1) / BN};
+  TileSched sched{(M + BM - 1) / BM, (N + BN - 1) / BN, m_rotate};
   const int ntiles = sched.num();
   const int kblocks = (K + BK - 1) / BK;
   constexpr uint32_t idesc = umma_idesc_bf16_f32(BM, BN);
@@ -93,6 +200,11 @@ k_gemm_bf16(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
       for (int t = blockIdx.x; t < ntiles && !s_abort; t += gridDim.x) {
         int tm, tn;
         sched.coords(t, tm, tn);
+        if (!gate.wait_a(tm)) {
+          atomicExch(err, 5u);
+          s_abort = 1;
+          break;
+        }
         for (int kb = 0; kb < kblocks; ++kb) {
           if (!mbar_wait_bounded(&empty[stage], phase ^ 1, kWaitLimit)) {
             atomicExch(err, 1u);
@@ -110,8 +222,8 @@ k_gemm_bf16(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
           }
         }
       }
-      // Wait (bounded) until the MMA warp consumed everything we loaded, so
-      // no TMA write into this CTA's shared memory is outstanding at exit.
+      // Wait (bounded) until the MMA warp consumed everything loaded, so no
+      // TMA write into this CTA's shared memory is outstanding at exit.
       for (int s = 0; s < STAGES; ++s) {
         mbar_wait_bounded(&empty[stage], phase ^ 1, kWaitLimit >> 4);
         if (++stage == STAGES) {
@@ -160,9 +272,12 @@ k_gemm_bf16(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
       }
     }
   } else {
-    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const int ew = warp - 2;  // epilogue warp index 0..3
+    const int q = warp & 3;   // TMEM lane quarter this warp may access
+    uint8_t* bufs = epi_smem + ew * 2 * EPI_BUF_BYTES;
     int acc = 0;
     uint32_t acc_phase = 0;
+    int nb = 0;  // staging buffer toggle
     for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
       int tm, tn;
       sched.coords(t, tm, tn);
@@ -177,24 +292,56 @@ k_gemm_bf16(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
         break;
       }
       tc_fence_after();
-      const int row = tm * BM + q * 32 + lane;
+      epi.begin_tile(tm, tn);
+      const int row0 = tm * BM + q * 32;
+      const int row = row0 + lane;
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
 #pragma unroll 1
-      for (int c0 = 0; c0 < BN; c0 += 32) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(tbase + c0, r);
+      for (int c0 = 0; c0 < BN; c0 += 64) {
+        if (tn * BN + c0 >= N) break;
+        uint32_t r0[32], r1[32];
+        tmem_ld_32x32b_x32(tbase + c0, r0);
+        tmem_ld_32x32b_x32(tbase + c0 + 32, r1);
         tmem_ld_wait();
-        float v[32];
+        float v[64], pre[64];
 #pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-        epi.apply(row, tn * BN + c0, v, M, N);
+        for (int i = 0; i < 32; ++i) {
+          v[i] = __uint_as_float(r0[i]);
+          v[32 + i] = __uint_as_float(r1[i]);
+        }
+        epi.math(row, tn * BN + c0, v, M, N, pre);
+        // Wait until the store that last read this staging buffer is done.
+        if (lane == 0) tma_store_wait_read<1>();
+        __syncwarp();
+        uint8_t* buf = bufs + nb * EPI_BUF_BYTES;
+        stage_row64(buf, lane, v);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) epi.store_block(&tmOut, &tmPre, buf, nullptr, row0, tn * BN + c0);
+        if (epi.has_pre) {
+          if (lane == 0) {
+            tma_store_commit();
+            tma_store_wait_read<0>();
+          }
+          __syncwarp();
+          stage_row64(buf, lane, pre);
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) tma_store_2d(&tmPre, buf, tn * BN + c0, row0);
+        }
+        if (lane == 0) tma_store_commit();
+        nb ^= 1;
       }
+      // The accumulator is in registers / staging now: release TMEM early.
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[acc]);
+      epi.end_tile(tm, tn);
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1;
     }
+    if (lane == 0) tma_store_wait_all<0>();
+    __syncwarp();
   }
   tc_fence_before();
   __syncthreads();
@@ -203,62 +350,6 @@ k_gemm_bf16(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
     tmem_dealloc(tmem_base, 512);
   }
 }
-
-// ---------------------------------------------------------------- epilogues
-__device__ __forceinline__ float gelu_tanh_f(float x) {
-  const float u = 0.7978845608028654f * (x + 0.044715f * x * x * x);
-  return 0.5f * x * (1.f + tanhf(u));
-}
-
-__device__ __forceinline__ void store_row32_bf16(__nv_bfloat16* dst, const float (&v)[32], int valid) {
-  if (valid >= 32 && (reinterpret_cast<uintptr_t>(dst) & 15u) == 0) {
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      uint4 o;
-      __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&o);
-#pragma unroll
-      for (int e = 0; e < 4; ++e) h[e] = __floats2bfloat162_rn(v[k * 8 + 2 * e], v[k * 8 + 2 * e + 1]);
-      reinterpret_cast<uint4*>(dst)[k] = o;
-    }
-  } else {
-    for (int i = 0; i < valid; ++i) dst[i] = __float2bfloat16_rn(v[i]);
-  }
-}
-
-// out = act(alpha * acc + bias) (+ residual); optionally also the
-// pre-activation (for the activation's backward pass).
-struct EpiStore {
-  __nv_bfloat16* out;
-  long long ldo;
-  const __nv_bfloat16* bias;      // [N] or null
-  const __nv_bfloat16* residual;  // [M, ld=ldr] or null
-  long long ldr;
-  __nv_bfloat16* pre;             // [M, ld=ldo] or null
-  float alpha;
-  int act;                        // 0 none, 1 gelu(tanh)
-
-  __device__ __forceinline__ void apply(int row, int col0, float (&v)[32], int M, int N) const {
-    if (row >= M || col0 >= N) return;
-    const int valid = min(32, N - col0);
-#pragma unroll
-    for (int i = 0; i < 32; ++i) v[i] *= alpha;
-    if (bias) {
-#pragma unroll
-      for (int i = 0; i < 32; ++i)
-        if (i < valid) v[i] += __bfloat162float(bias[col0 + i]);
-    }
-    if (pre) store_row32_bf16(pre + (long long)row * ldo + col0, v, valid);
-    if (act == 1) {
-#pragma unroll
-      for (int i = 0; i < 32; ++i) v[i] = gelu_tanh_f(v[i]);
-    }
-    if (residual) {
-      const __nv_bfloat16* rp = residual + (long long)row * ldr + col0;
-      for (int i = 0; i < valid; ++i) v[i] += __bfloat162float(rp[i]);
-    }
-    store_row32_bf16(out + (long long)row * ldo + col0, v, valid);
-  }
-};
 
 }  // namespace gemm
 }  // namespace nexar
