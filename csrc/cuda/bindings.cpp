@@ -13,6 +13,7 @@
 #include "coll_api.h"
 #include "device_comm.h"
 #include "ops_api.h"
+#include "gemm_api.h"
 
 namespace nexar {
 
@@ -326,6 +327,50 @@ py::dict status_dict(const CommPtr& c) {
   return d;
 }
 
+// ---------------------------------------------------------------- fused GEMM + collective
+static const __nv_bfloat16* cbf(const at::Tensor& t) { return reinterpret_cast<const __nv_bfloat16*>(t.data_ptr()); }
+static __nv_bfloat16* mbf(const at::Tensor& t) { return reinterpret_cast<__nv_bfloat16*>(t.data_ptr()); }
+static void need_bf16_2d(const at::Tensor& t, const char* n) {
+  TORCH_CHECK(t.is_cuda() && t.scalar_type() == at::kBFloat16 && t.dim() == 2 && t.stride(1) == 1, "nexar_b200: ", n,
+              " must be a 2D bf16 CUDA tensor with contiguous rows");
+}
+
+void gemm_rs(const CommPtr& c, const at::Tensor& A, const at::Tensor& B, const at::Tensor& out,
+             const c10::optional<at::Tensor>& bias, double alpha) {
+  need_bf16_2d(A, "A");
+  need_bf16_2d(B, "B");
+  need_bf16_2d(out, "out");
+  const int M = A.size(0), K = A.size(1), N = B.size(0);
+  TORCH_CHECK(B.size(1) == K && out.size(0) * c->world() == M && out.size(1) == N, "gemm_reduce_scatter: shape mismatch");
+  c10::cuda::CUDAGuard g(c->device());
+  check_launch(gemm_reduce_scatter(c->dev(), cbf(A), cbf(B), mbf(out), M, N, K, A.stride(0), B.stride(0), out.stride(0),
+                                   bias ? cbf(*bias) : nullptr, (float)alpha, cur_stream(*c)),
+               "gemm_reduce_scatter");
+  count_launch(1);
+}
+
+void ag_gemm(const CommPtr& c, const at::Tensor& x, const at::Tensor& B, const at::Tensor& out, const at::Tensor& afull,
+             const at::Tensor& cnt, const c10::optional<at::Tensor>& bias, int act, const c10::optional<at::Tensor>& pre,
+             double alpha) {
+  need_bf16_2d(x, "x");
+  need_bf16_2d(B, "B");
+  need_bf16_2d(out, "out");
+  TORCH_CHECK(afull.is_cuda() && afull.is_contiguous() && afull.scalar_type() == at::kBFloat16, "afull workspace");
+  TORCH_CHECK(cnt.is_cuda() && cnt.is_contiguous() && cnt.element_size() == 4, "cnt workspace");
+  const int W = c->world();
+  const int M = x.size(0) * W, K = x.size(1), N = B.size(0);
+  TORCH_CHECK(B.size(1) == K && out.size(0) == M && out.size(1) == N && afull.numel() >= (int64_t)M * K,
+              "all_gather_gemm: shape mismatch");
+  TORCH_CHECK(cnt.numel() >= M / 128 + 2, "all_gather_gemm: cnt too small");
+  c10::cuda::CUDAGuard g(c->device());
+  check_launch(all_gather_gemm(c->dev(), cbf(x), x.stride(0), cbf(B), mbf(out), mbf(afull),
+                               reinterpret_cast<unsigned int*>(cnt.data_ptr()), M, N, K, B.stride(0), out.stride(0),
+                               bias ? cbf(*bias) : nullptr, act, pre ? mbf(*pre) : nullptr, (float)alpha,
+                               cur_stream(*c)),
+               "all_gather_gemm");
+  count_launch(1);
+}
+
 void register_ops(py::module& m);
 
 }  // namespace nexar
@@ -373,5 +418,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("reduce_inplace", &reduce_inplace);
   m.def("symmetric_tensor", &symmetric_tensor);
   m.def("launch_count", []() { return g_launches.load(); });
+  m.def("gemm_reduce_scatter", &gemm_rs);
+  m.def("all_gather_gemm", &ag_gemm);
   register_ops(m);
 }

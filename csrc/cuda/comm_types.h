@@ -35,7 +35,15 @@ enum StatusCode : unsigned int {
 
 constexpr int kMaxRanks = 8;
 constexpr int kMaxBlocks = 256;
-constexpr size_t kFlagBytes = 64 * 1024;   // >= kMaxBlocks*kMaxRanks*8 * 4 phases
+// Signal area at the start of every symmetric heap:
+//   [0, 16K)        u64 block flags [kMaxBlocks][kMaxRanks] (collective barriers)
+//   [64K, 64K+64)   u64 ready[kMaxRanks]  (fused GEMM+collective kernels: "rank r
+//                   started call e", written by r into every peer)
+//   [68K, 1M)       u64 tile flags [kMaxRanks][kMaxFusedTiles] (per-tile arrival)
+constexpr size_t kFlagBytes = 1024 * 1024;
+constexpr size_t kFusedReadyOff = 64 * 1024;
+constexpr size_t kFusedTileOff = 68 * 1024;
+constexpr int kMaxFusedTiles = (int)((kFlagBytes - kFusedTileOff) / (8 * kMaxRanks));
 constexpr int kThreads = 512;
 
 struct CommDev {

@@ -1,8 +1,7 @@
 // Host side of the tcgen05 GEMM: tensor-map creation and launch.
 #include <mutex>
 
-#include "gemm.cuh"
-#include "gemm_api.h"
+#include "gemm_launch.cuh"
 
 namespace nexar {
 
@@ -23,8 +22,9 @@ EncodeTiledFn encode_fn() {
   });
   return fn;
 }
+}  // namespace
 
-unsigned int* err_word() {
+unsigned int* gemm_err_word() {
   static unsigned int* w = nullptr;
   static std::once_flag once;
   std::call_once(once, [] {
@@ -33,7 +33,7 @@ unsigned int* err_word() {
   return w;
 }
 
-int sm_count() {
+int gemm_sm_count() {
   static int n = 0;
   if (n == 0) {
     int dev = 0;
@@ -43,7 +43,6 @@ int sm_count() {
   }
   return n;
 }
-}  // namespace
 
 // 2D bf16 tensor map over a row-major [rows, cols] matrix with leading
 // dimension ld (elements), box = [box_rows, box_cols], 128-byte swizzle.
@@ -62,31 +61,6 @@ cudaError_t make_tmap_bf16(CUtensorMap* map, const void* base, long long rows, l
   return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
-template <class Epi, class Gate>
-cudaError_t launch_gemm_generic(const void* A, const void* B, int M, int N, int K, long long lda, long long ldb,
-                                const CUtensorMap& tout, const CUtensorMap& tpre, int m_rotate, const Epi& epi,
-                                const Gate& gate, int max_ctas, cudaStream_t s) {
-  using namespace gemm;
-  if (M <= 0 || N <= 0 || K <= 0) return cudaSuccess;
-  CUtensorMap ta, tb;
-  cudaError_t e = make_tmap_bf16(&ta, A, M, K, lda, BM, BK);
-  if (e != cudaSuccess) return e;
-  e = make_tmap_bf16(&tb, B, N, K, ldb, BN, BK);
-  if (e != cudaSuccess) return e;
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaFuncSetAttribute(k_gemm_bf16<Epi, Gate>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
-    attr_set = true;
-  }
-  const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
-  int grid = sm_count();
-  if (max_ctas > 0 && max_ctas < grid) grid = max_ctas;
-  if (tiles < grid) grid = tiles;
-  k_gemm_bf16<Epi, Gate><<<grid, THREADS, SMEM_BYTES, s>>>(ta, tb, tout, tpre, M, N, K, m_rotate, epi, gate,
-                                                          err_word());
-  return cudaGetLastError();
-}
-
 cudaError_t gemm_bf16(const __nv_bfloat16* A, const __nv_bfloat16* B, __nv_bfloat16* C, int M, int N, int K,
                       long long lda, long long ldb, long long ldc, const __nv_bfloat16* bias,
                       const __nv_bfloat16* residual, long long ldr, __nv_bfloat16* pre_act, int act, float alpha,
@@ -100,12 +74,13 @@ cudaError_t gemm_bf16(const __nv_bfloat16* A, const __nv_bfloat16* B, __nv_bfloa
     if (e != cudaSuccess) return e;
   }
   gemm::EpiStore epi{bias, residual, ldr, alpha, act, pre_act != nullptr};
-  return launch_gemm_generic(A, B, M, N, K, lda, ldb, tout, tpre, 0, epi, gemm::NoGate{}, 0, s);
+  return launch_gemm_generic<gemm::EpiStore, gemm::NoGate, 0>(A, B, M, N, K, lda, ldb, tout, tpre, 0, epi,
+                                                                gemm::NoGate{}, 0, s);
 }
 
 unsigned int gemm_error_flag() {
   unsigned int v = 0;
-  if (unsigned int* w = err_word()) cudaMemcpy(&v, w, sizeof(v), cudaMemcpyDeviceToHost);
+  if (unsigned int* w = gemm_err_word()) cudaMemcpy(&v, w, sizeof(v), cudaMemcpyDeviceToHost);
   return v;
 }
 

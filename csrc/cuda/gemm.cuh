@@ -53,7 +53,10 @@ struct TileSched {
 };
 
 struct NoGate {
+  __device__ __forceinline__ bool prologue() const { return true; }
   __device__ __forceinline__ bool wait_a(int) const { return true; }
+  __device__ __forceinline__ void copy_role(int, int) const {}
+  __device__ __forceinline__ void finalize() const {}
 };
 
 __device__ __forceinline__ float gelu_tanh_f(float x) {
@@ -85,6 +88,7 @@ struct EpiStore {
   int act;                        // 0 none, 1 gelu(tanh)
   int has_pre;
 
+  __device__ __forceinline__ bool prologue() const { return true; }
   __device__ __forceinline__ bool begin_tile(int, int) const { return true; }
   // v: 64 accumulators of row `row`, columns col0..col0+63 (in-place math).
   __device__ __forceinline__ void math(int row, int col0, float (&v)[64], int M, int N, float (&pre)[64]) const {
@@ -140,16 +144,17 @@ struct EpiStore {
       }
     }
   }
-  // Called by lane 0 after the 32x64 block is staged and fenced.
-  __device__ __forceinline__ void store_block(const CUtensorMap* out, const CUtensorMap*, const uint8_t* buf,
-                                              const uint8_t*, int row0, int col0) const {
-    sm100::tma_store_2d(out, buf, col0, row0);
+  // Called by every lane of the warp after the 32x64 block is staged and fenced.
+  __device__ __forceinline__ void store_block(const CUtensorMap* out, const uint8_t* buf, int row0, int col0,
+                                              int lane) const {
+    if (lane == 0) sm100::tma_store_2d(out, buf, col0, row0);
   }
-  __device__ __forceinline__ void end_tile(int, int) const {}
+  __device__ __forceinline__ void end_tile(int, int, int) const {}
+  __device__ __forceinline__ void finalize() const {}
 };
 
-template <class Epi, class Gate = NoGate>
-__global__ void __launch_bounds__(THREADS, 1)
+template <class Epi, class Gate = NoGate, int EXTRA = 0>
+__global__ void __launch_bounds__(THREADS + 32 * EXTRA, 1)
 k_gemm_bf16(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
             const __grid_constant__ CUtensorMap tmOut, const __grid_constant__ CUtensorMap tmPre, int M, int N,
             int K, int m_rotate, Epi epi, Gate gate, unsigned int* err) {
@@ -187,6 +192,15 @@ k_gemm_bf16(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // Fused kernels: stage inputs / signal peers before any role starts.
+  {
+    const bool ok = gate.prologue() && epi.prologue();
+    if (!ok && threadIdx.x == 0) {
+      atomicExch(err, 6u);
+      s_abort = 1;
+    }
+    __syncthreads();
+  }
 
   TileSched sched{(M + BM - 1) / BM, (N + BN - 1) / BN, m_rotate};
   const int ntiles = sched.num();
@@ -271,6 +285,8 @@ k_gemm_bf16(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
         if (acc == 0) acc_phase ^= 1;
       }
     }
+  } else if (warp >= 6) {
+    if (!s_abort) gate.copy_role(warp - 6, lane);
   } else {
     const int ew = warp - 2;  // epilogue warp index 0..3
     const int q = warp & 3;   // TMEM lane quarter this warp may access
@@ -317,7 +333,7 @@ k_gemm_bf16(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
         stage_row64(buf, lane, v);
         fence_proxy_async_smem();
         __syncwarp();
-        if (lane == 0) epi.store_block(&tmOut, &tmPre, buf, nullptr, row0, tn * BN + c0);
+        epi.store_block(&tmOut, buf, row0, tn * BN + c0, lane);
         if (epi.has_pre) {
           if (lane == 0) {
             tma_store_commit();
@@ -336,7 +352,7 @@ k_gemm_bf16(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[acc]);
-      epi.end_tile(tm, tn);
+      epi.end_tile(tm, tn, lane);
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1;
     }
@@ -345,6 +361,8 @@ k_gemm_bf16(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
   }
   tc_fence_before();
   __syncthreads();
+  epi.finalize();
+  gate.finalize();
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, 512);

@@ -1,0 +1,39 @@
+// Launch helper shared by the plain and the fused (collective) GEMMs.
+#pragma once
+#include "gemm.cuh"
+#include "gemm_api.h"
+
+namespace nexar {
+
+unsigned int* gemm_err_word();
+int gemm_sm_count();
+
+template <class Epi, class Gate, int EXTRA>
+cudaError_t launch_gemm_generic(const void* A, const void* B, int M, int N, int K, long long lda, long long ldb,
+                                const CUtensorMap& tout, const CUtensorMap& tpre, int m_rotate, const Epi& epi,
+                                const Gate& gate, int grid_override, cudaStream_t s) {
+  using namespace gemm;
+  if (M <= 0 || N <= 0 || K <= 0) return cudaSuccess;
+  CUtensorMap ta, tb;
+  cudaError_t e = make_tmap_bf16(&ta, A, M, K, lda, BM, BK);
+  if (e != cudaSuccess) return e;
+  e = make_tmap_bf16(&tb, B, N, K, ldb, BN, BK);
+  if (e != cudaSuccess) return e;
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaFuncSetAttribute(k_gemm_bf16<Epi, Gate, EXTRA>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    attr_set = true;
+  }
+  const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
+  int grid = gemm_sm_count();
+  if (grid_override > 0) {
+    grid = grid_override;  // fused kernels: every CTA also has collective work
+  } else if (tiles < grid) {
+    grid = tiles;
+  }
+  k_gemm_bf16<Epi, Gate, EXTRA><<<grid, THREADS + 32 * EXTRA, SMEM_BYTES, s>>>(ta, tb, tout, tpre, M, N, K, m_rotate,
+                                                                              epi, gate, gemm_err_word());
+  return cudaGetLastError();
+}
+
+}  // namespace nexar

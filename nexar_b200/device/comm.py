@@ -232,6 +232,47 @@ class DeviceCommunicator:
     def barrier(self):
         self._C.barrier(self._comm)
 
+    # ----------------------------------------------------------- fused GEMM + collective
+    def gemm_reduce_scatter(self, A: torch.Tensor, B: torch.Tensor, out: Optional[torch.Tensor] = None,
+                            bias: Optional[torch.Tensor] = None, alpha: float = 1.0) -> torch.Tensor:
+        """Row-parallel linear: returns this rank's rows of sum_r (A_r @ B_r^T) (+ bias).
+
+        One persistent tcgen05 kernel: output tiles go straight into the owning
+        rank's memory over NVLink while later tiles are still being multiplied.
+        A: [M, K_local] bf16, B: [N, K_local] bf16 (nn.Linear layout); out: [M/world, N].
+        """
+        M, N = A.shape[0], B.shape[0]
+        if out is None:
+            out = torch.empty(M // self.world_size, N, dtype=A.dtype, device=A.device)
+        self._C.gemm_reduce_scatter(self._comm, A, B, out, bias, float(alpha))
+        return out
+
+    def all_gather_gemm(self, x: torch.Tensor, B: torch.Tensor, out: Optional[torch.Tensor] = None,
+                        bias: Optional[torch.Tensor] = None, act: Optional[str] = None,
+                        pre: Optional[torch.Tensor] = None, alpha: float = 1.0) -> torch.Tensor:
+        """Column-parallel linear on sequence-sharded input: act(all_gather(x) @ B^T + bias).
+
+        One persistent tcgen05 kernel whose copy warps pull the peers' shards over
+        NVLink (each remote row crosses once) while the tensor cores start on the
+        local shard. x: [M/world, K] bf16, B: [N, K]; out: [M, N].
+        """
+        M, K = x.shape[0] * self.world_size, x.shape[1]
+        if out is None:
+            out = torch.empty(M, B.shape[0], dtype=x.dtype, device=x.device)
+        afull, cnt = self._ag_workspace(M, K, x.device)
+        self._C.all_gather_gemm(self._comm, x, B, out, afull, cnt, bias, 1 if act == "gelu" else 0, pre, float(alpha))
+        return out
+
+    def _ag_workspace(self, M: int, K: int, device):
+        key = (M, K)
+        ws = getattr(self, "_ag_ws", None)
+        if ws is None:
+            ws = self._ag_ws = {}
+        if key not in ws:
+            ws[key] = (torch.empty(M * K, dtype=torch.bfloat16, device=device),
+                       torch.zeros(M // 128 + 2, dtype=torch.int32, device=device))
+        return ws[key]
+
     # ----------------------------------------------------------- non-blocking
     def side_stream(self) -> torch.cuda.Stream:
         if self._side_stream is None:

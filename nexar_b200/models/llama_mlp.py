@@ -1,0 +1,70 @@
+"""Llama-style SwiGLU MLP block, tensor parallel over the GPUs of one box
+(d=4096, ffn=14336, TP=8, 8192 tokens, bf16).
+
+Sequence-parallel layout: each rank holds T/W tokens of the input and of the
+output. Column-parallel up projection (gate|up, [2F/W, d] per rank) runs as
+one fused all-gather->GEMM kernel; SwiGLU is one elementwise kernel; the
+row-parallel down projection ([d, F/W] per rank) runs as one fused
+GEMM->reduce-scatter kernel. `forward_baseline` is the same block with NCCL
+collectives and cuBLAS GEMMs (the comparator).
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+
+from .. import ops
+
+
+@dataclass
+class LlamaMLPConfig:
+    d_model: int = 4096
+    ffn: int = 14336
+    tokens: int = 8192
+
+    @staticmethod
+    def small() -> "LlamaMLPConfig":
+        return LlamaMLPConfig(d_model=512, ffn=1024, tokens=1024)
+
+
+class TPLlamaMLP:
+    def __init__(self, cfg: LlamaMLPConfig, comm, seed: int = 0):
+        self.cfg = cfg
+        self.comm = comm
+        W = comm.world_size if comm is not None else 1
+        self.W = W
+        assert cfg.ffn % W == 0 and cfg.tokens % (W * 128) == 0
+        F = cfg.ffn // W
+        dev = torch.device("cuda", torch.cuda.current_device())
+        g = torch.Generator(device=dev).manual_seed(seed + 1000 * (comm.rank if comm is not None else 0))
+        # N(0, 0.02) weights; [gate_r ; up_r] rows for this rank's ffn slice
+        self.w_up = (0.02 * torch.randn(2 * F, cfg.d_model, device=dev, generator=g)).to(torch.bfloat16)
+        self.w_down = (0.02 * torch.randn(cfg.d_model, F, device=dev, generator=g)).to(torch.bfloat16)
+        self.F = F
+
+    def flops(self) -> float:
+        """Forward FLOPs of the whole block (all ranks)."""
+        c = self.cfg
+        return 2.0 * c.tokens * c.d_model * (2 * c.ffn) + 2.0 * c.tokens * c.ffn * c.d_model
+
+    def forward(self, x_shard: torch.Tensor) -> torch.Tensor:
+        """x_shard: [T/W, d] -> y_shard: [T/W, d] (fused kernels)."""
+        gu = self.comm.all_gather_gemm(x_shard, self.w_up)          # [T, 2F/W]
+        h = ops.swiglu(gu)                                          # [T, F/W]
+        return self.comm.gemm_reduce_scatter(h, self.w_down)        # [T/W, d]
+
+    def forward_baseline(self, x_shard: torch.Tensor, group=None) -> torch.Tensor:
+        """Same block with NCCL all_gather / reduce_scatter and cuBLAS GEMMs."""
+        import torch.distributed as dist
+        T, d = self.cfg.tokens, self.cfg.d_model
+        xf = torch.empty(T, d, dtype=x_shard.dtype, device=x_shard.device)
+        dist.all_gather_into_tensor(xf, x_shard, group=group)
+        gu = torch.matmul(xf, self.w_up.t())
+        gate, up = gu[:, :self.F], gu[:, self.F:]
+        h = torch.nn.functional.silu(gate) * up
+        yp = torch.matmul(h, self.w_down.t())
+        y = torch.empty(T // self.W, d, dtype=x_shard.dtype, device=x_shard.device)
+        dist.reduce_scatter_tensor(y, yp, group=group)
+        return y
