@@ -35,7 +35,7 @@ def main():
     comm = DeviceCommunicator.from_torch()
     cfg = LlamaMLPConfig(args.d, args.ffn, args.tokens)
     mlp = TPLlamaMLP(cfg, comm)
-    x = (torch.randn(cfg.tokens // world, cfg.d, device=dev)).to(torch.bfloat16)
+    x = (torch.randn(cfg.tokens // world, cfg.d_model, device=dev)).to(torch.bfloat16)
 
     def timeit(fn):
         for _ in range(args.warmup):
@@ -58,7 +58,7 @@ def main():
     except Exception:
         pass
     link = 770e9
-    T, d, F, W = cfg.tokens, cfg.d, cfg.ffn, world
+    T, d, F, W = cfg.tokens, cfg.d_model, cfg.ffn, world
     ms_fused = timeit(lambda: mlp.forward(x))
     ms_base = timeit(lambda: mlp.forward_baseline(x))
     # per-kernel rooflines
