@@ -14,6 +14,7 @@
 #include "device_comm.h"
 #include "ops_api.h"
 #include "gemm_api.h"
+#include "moe_api.h"
 
 namespace nexar {
 
@@ -371,6 +372,8 @@ void ag_gemm(const CommPtr& c, const at::Tensor& x, const at::Tensor& B, const a
   count_launch(1);
 }
 
+#include "bindings_moe.inc"
+
 void register_ops(py::module& m);
 
 }  // namespace nexar
@@ -419,6 +422,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("symmetric_tensor", &symmetric_tensor);
   m.def("launch_count", []() { return g_launches.load(); });
   m.def("gemm_reduce_scatter", &gemm_rs);
+  m.def("moe_route", &moe_route_op);
+  m.def("moe_dispatch", &moe_dispatch_op);
+  m.def("moe_combine", &moe_combine_op);
   m.def("all_gather_gemm", &ag_gemm);
   register_ops(m);
 }

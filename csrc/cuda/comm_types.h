@@ -42,6 +42,8 @@ constexpr int kMaxBlocks = 256;
 //   [68K, 1M)       u64 tile flags [kMaxRanks][kMaxFusedTiles] (per-tile arrival)
 constexpr size_t kFlagBytes = 1024 * 1024;
 constexpr size_t kFusedReadyOff = 64 * 1024;
+constexpr size_t kMoeDispatchDoneOff = 65 * 1024;  // u64 [kMaxRanks]: "src finished its dispatch writes"
+constexpr size_t kMoeExpertDoneOff = 66 * 1024;    // u64 [kMaxRanks]: "src's expert outputs are ready"
 constexpr size_t kFusedTileOff = 68 * 1024;
 constexpr int kMaxFusedTiles = (int)((kFlagBytes - kFusedTileOff) / (8 * kMaxRanks));
 constexpr int kThreads = 512;

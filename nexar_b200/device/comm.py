@@ -81,7 +81,7 @@ class DeviceCommunicator:
         self.device = device
         slot = slot_bytes or _env_int("NEXAR_SLOT_BYTES", 256 << 20)
         user = _env_int("NEXAR_SYMM_USER_BYTES", 1 << 30)
-        heap = heap_bytes or (64 << 10) + 2 * slot + user
+        heap = heap_bytes or (1 << 20) + 2 * slot + user  # 1 MiB signal area first
         tmo = timeout_us if timeout_us is not None else _env_int("NEXAR_DEVICE_WAIT_TIMEOUT_US", 10_000_000)
         self.oneshot_max_bytes = _env_int(
             "NEXAR_AR_ONESHOT_MAX", 512 << 10 if world_size <= 4 else 256 << 10)

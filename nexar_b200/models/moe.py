@@ -1,0 +1,107 @@
+"""Expert-parallel MoE layer: one SwiGLU expert per GPU,
+top-2 softmax routing, d=4096, expert ffn=14336, 16384 tokens per GPU, bf16.
+
+forward():          route kernel -> device all-gather of the per-expert counts
+                    -> fused dispatch (all-to-all + permutation, peer stores
+                    into the expert's symmetric receive buffer) -> expert
+                    SwiGLU MLP on tcgen05 GEMMs -> fused combine (peer loads,
+                    gate scaling and top-2 sum).
+forward_baseline(): the same layer with torch routing/permutation, NCCL
+                    all_to_all_single and cuBLAS GEMMs (the comparator).
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+from .. import _native, ops
+
+
+@dataclass
+class MoEConfig:
+    d_model: int = 4096
+    ffn: int = 14336
+    tokens_per_gpu: int = 16384
+    capacity_factor: float = 2.0  # receive rows = capacity_factor * 2 * tokens_per_gpu
+
+    @staticmethod
+    def small() -> "MoEConfig":
+        return MoEConfig(d_model=256, ffn=512, tokens_per_gpu=512)
+
+
+class ExpertParallelMoE:
+    def __init__(self, cfg: MoEConfig, comm, seed: int = 0):
+        self.cfg, self.comm = cfg, comm
+        self.E = comm.world_size
+        dev = torch.device("cuda", torch.cuda.current_device())
+        self.dev = dev
+        g = torch.Generator(device=dev).manual_seed(seed + 7919 * comm.rank)
+        F, d = cfg.ffn, cfg.d_model
+        self.w_up = (0.02 * torch.randn(2 * F, d, device=dev, generator=g)).to(torch.bfloat16)   # [gate; up]
+        self.w_down = (0.02 * torch.randn(d, F, device=dev, generator=g)).to(torch.bfloat16)
+        T = cfg.tokens_per_gpu
+        self.capacity = int(cfg.capacity_factor * 2 * T)
+        self.recv = comm.symmetric_empty([self.capacity, d], torch.bfloat16)
+        self.eout = comm.symmetric_empty([self.capacity, d], torch.bfloat16)
+        self.slot_expert = torch.empty(2 * T, dtype=torch.int32, device=dev)
+        self.slot_pos = torch.empty(2 * T, dtype=torch.int32, device=dev)
+        self.slot_gate = torch.empty(2 * T, dtype=torch.float32, device=dev)
+        self.counts = torch.zeros(self.E, dtype=torch.int32, device=dev)
+        self.counts_all = torch.empty(self.E * self.E, dtype=torch.int32, device=dev)
+        self.ticket = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.gu = torch.empty(self.capacity, 2 * F, dtype=torch.bfloat16, device=dev)
+        self.h = torch.empty(self.capacity, F, dtype=torch.bfloat16, device=dev)
+        self._C = _native.cuda()
+        self.last_rows = 0
+
+    def flops(self, rows: int) -> float:
+        c = self.cfg
+        return 2.0 * rows * c.d_model * 2 * c.ffn + 2.0 * rows * c.ffn * c.d_model
+
+    def forward(self, x: torch.Tensor, logits: torch.Tensor) -> torch.Tensor:
+        """x: [T, d] bf16 tokens of this rank; logits: [T, E] router logits."""
+        C, comm = self._C, self.comm
+        T, d = x.shape
+        self.counts.zero_()
+        C.moe_route(logits, self.slot_expert, self.slot_pos, self.slot_gate, self.counts)
+        comm.all_gather(self.counts, self.counts_all)
+        C.moe_dispatch(comm.native, x, self.slot_expert, self.slot_pos, self.counts_all, self.recv, self.ticket)
+        # rows this expert received (host read of E*E ints: sizes the GEMM launches)
+        rows = int(self.counts_all.view(self.E, self.E)[:, comm.rank].sum().item())
+        rows = min(rows, self.capacity)
+        self.last_rows = rows
+        if rows > 0:
+            gu, h = self.gu[:rows], self.h[:rows]
+            C.gemm(self.recv[:rows], self.w_up, gu)
+            C.swiglu_fwd(gu, h)
+            C.gemm(h, self.w_down, self.eout[:rows])
+        out = torch.empty_like(x)
+        C.moe_combine(comm.native, out, self.slot_expert, self.slot_pos, self.slot_gate, self.eout)
+        return out
+
+    def forward_baseline(self, x: torch.Tensor, logits: torch.Tensor, group=None) -> torch.Tensor:
+        import torch.distributed as dist
+        T, d = x.shape
+        E = self.E
+        top_v, top_i = torch.topk(logits.float(), 2, dim=-1)
+        gates = torch.softmax(top_v, dim=-1)
+        flat_e = top_i.reshape(-1)
+        order = torch.argsort(flat_e, stable=True)
+        send = x.repeat_interleave(2, dim=0)[order]                       # permute
+        send_counts = torch.bincount(flat_e, minlength=E)
+        recv_counts = torch.empty_like(send_counts)
+        dist.all_to_all_single(recv_counts, send_counts, group=group)
+        sc, rc = send_counts.tolist(), recv_counts.tolist()
+        recv = torch.empty(sum(rc), d, dtype=x.dtype, device=x.device)
+        dist.all_to_all_single(recv, send, rc, sc, group=group)
+        gu = torch.matmul(recv, self.w_up.t())
+        F = self.cfg.ffn
+        hh = torch.nn.functional.silu(gu[:, :F]) * gu[:, F:]
+        eo = torch.matmul(hh, self.w_down.t())
+        back = torch.empty_like(send)
+        dist.all_to_all_single(back, eo, sc, rc, group=group)
+        unperm = torch.empty_like(back)
+        unperm[order] = back                                             # unpermute
+        unperm = unperm.view(T, 2, d).float()
+        return (unperm * gates.unsqueeze(-1)).sum(1).to(x.dtype)
