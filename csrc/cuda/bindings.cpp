@@ -98,8 +98,12 @@ void all_reduce(const CommPtr& c, const at::Tensor& in, const at::Tensor& out, i
     return;
   }
   long long sym = -1;
-  if (in.data_ptr() == out.data_ptr() && dti == dto) sym = c->symmetric_offset(in.data_ptr(), bytes);
   if (algo == kAlgoAuto) algo = (long long)bytes <= oneshot_max_bytes ? kAlgoOneShot : kAlgoTwoShot;
+  // Zero-copy in place only for two-shot: there rank r alone reads and writes
+  // chunk r. A one-shot rank would overwrite its input while peers still read
+  // it, so one-shot always goes through the staging slot.
+  if (in.data_ptr() == out.data_ptr() && dti == dto && algo == kAlgoTwoShot)
+    sym = c->symmetric_offset(in.data_ptr(), bytes);
   if (sym >= 0) {
     check_launch(launch_all_reduce(c->dev(), in.data_ptr(), out.data_ptr(), dti, dto, op, n,
                                    (float)scale, algo, sym, c->max_blocks, s), "all_reduce");

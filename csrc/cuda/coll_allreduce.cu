@@ -1,4 +1,6 @@
 // All-reduce kernels: one-shot and two-shot over NVLink peer memory.
+#include <type_traits>
+
 #include "coll_impl.cuh"
 
 namespace nexar {
@@ -70,9 +72,20 @@ __global__ void __launch_bounds__(kThreads) k_ar_twoshot(CommDev c, const T* in,
     if (lo < hi) {
       if (sym) {
         reduce_push_range<T, OP>(dsts, N, srcs, N, lo, hi, scale, vec);
+      } else if constexpr (std::is_same<T, TO>::value) {
+        // One pass: pull the chunk from every peer, reduce, and store the
+        // result into our output and every peer's stage B in the same loop,
+        // so NVLink inbound (loads) and outbound (stores) overlap.
+        T* outs[kMaxRanks];
+#pragma unroll
+        for (int p = 0; p < kMaxRanks; ++p)
+          outs[p] = p >= N ? nullptr
+                           : (p == c.rank ? reinterpret_cast<T*>(out)
+                                          : reinterpret_cast<T*>(c.peer_base[p] + c.stage_off + c.slot_bytes));
+        reduce_push_range<T, OP>(outs, N, srcs, N, lo, hi, scale, vec);
       } else {
-        // Reduce once into our output, then push the TO result into every
-        // peer's stage B.
+        // Fused cast: reduce once into our output, then push the TO result
+        // into every peer's stage B.
         reduce_range<T, TO, OP>(out, srcs, N, lo, hi, scale, vec);
         __syncthreads();
         for (int q = 1; q < N; ++q) {

@@ -138,12 +138,72 @@ cudaError_t launch_all_to_all(const CommDev& c, const void* in, void* out, int d
   return cudaGetLastError();
 }
 
+// Large broadcast as scatter + all-gather: every rank pulls its own 1/N chunk
+// from the root (the root's helper, rank root+1, also pulls the root's chunk)
+// and then pulls the other chunks from the ranks that hold them. The root
+// sends each byte once instead of N-1 times (flat pull).
+template <typename T>
+__global__ void __launch_bounds__(kThreads) k_broadcast_sag(CommDev c, const T* in, T* out,
+                                                            unsigned long long n, int root, bool vec) {
+  const unsigned long long call = call_index(c);
+  constexpr int V = PackOf<T>::V;
+  const int N = c.world;
+  unsigned long long chunk = (n + N - 1) / N;
+  chunk = (chunk + V - 1) / V * V;
+  unsigned long long slo, shi;
+  block_range(chunk, gridDim.x, blockIdx.x, V, &slo, &shi);
+  const int slot = (int)(call & 1ull);
+  T* mine = stage_ptr<T>(c, c.rank, slot);
+  const int helper = (root + 1) % N;
+  auto rng = [&](int q, unsigned long long* lo, unsigned long long* hi) {
+    *lo = q * chunk + slo;
+    *hi = q * chunk + shi;
+    if (*hi > n) *hi = n;
+    return *lo < *hi;
+  };
+  unsigned long long lo, hi;
+  if (c.rank == root) {
+    for (int q = 0; q < N; ++q)
+      if (rng(q, &lo, &hi)) {
+        copy_range<T>(mine, in, lo, hi, vec, false);
+        if (out != in) copy_range<T>(out, in, lo, hi, vec, false);
+      }
+  }
+  bool ok = block_barrier(c, epoch_of(call, 0), kOpBroadcast);
+  if (ok && c.rank != root) {
+    const T* rs = stage_ptr<T>(c, root, slot);
+    for (int q = 0; q < N; ++q) {
+      if (!(q == c.rank || (c.rank == helper && q == root))) continue;
+      if (rng(q, &lo, &hi)) {
+        copy_range<T>(mine, rs, lo, hi, vec, true);
+        __syncthreads();
+        copy_range<T>(out, mine, lo, hi, vec, false);
+      }
+    }
+  }
+  ok = ok && block_barrier(c, epoch_of(call, 1), kOpBroadcast);
+  if (ok && c.rank != root) {
+    for (int d = 1; d < N; ++d) {
+      const int q = (c.rank + d) % N;
+      if (q == c.rank || (c.rank == helper && q == root)) continue;
+      const int owner = q == root ? helper : q;
+      if (rng(q, &lo, &hi)) copy_range<T>(out, stage_ptr<T>(c, owner, slot), lo, hi, vec, true);
+    }
+  }
+  finish_call(c, call);
+}
+
 cudaError_t launch_broadcast(const CommDev& c, const void* in, void* out, int dt,
                              unsigned long long n, int root, unsigned int max_blocks,
                              cudaStream_t s) {
   if (n == 0) return cudaSuccess;
   const int es = dtype_size(dt);
   const bool vec = aligned16(in) && aligned16(out) && (n * es) % 16 == 0;
+  if (c.world >= 3 && n * es >= (256ull << 10)) {
+    const unsigned int g = pick_blocks(n * es / c.world, max_blocks);
+    NEXAR_DISPATCH_ALL(dt, k_broadcast_sag<T><<<g, kThreads, 0, s>>>(c, (const T*)in, (T*)out, n, root, vec));
+    return cudaGetLastError();
+  }
   const unsigned int g = pick_blocks(n * es, max_blocks);
   NEXAR_DISPATCH_ALL(dt, k_broadcast<T><<<g, kThreads, 0, s>>>(c, (const T*)in, (T*)out, n, root, vec));
   return cudaGetLastError();

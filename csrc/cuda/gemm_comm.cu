@@ -125,7 +125,9 @@ struct EpiPeerRS {
   __device__ void end_tile(int tm, int tn, int lane) const {
     __syncwarp();
     if (lane == 0) {
-      __threadfence_system();
+      // CTA-scope release is enough here: the flag writer below issues the
+      // system-scope fence, and release is cumulative over what it observed.
+      __threadfence_block();
       atomicAdd(&s_tile_arrivals(), 1u);
     }
     if (threadIdx.x == 64) {
@@ -287,15 +289,18 @@ struct GateAG {
       const int pr = cols / 8;               // 16-byte packs per row
       const int n = BM * pr;
       int i = lane;
-      for (; i + 3 * 32 < n; i += 4 * 32) {
-        uint4 v[4];
+      // 16 loads of 16 bytes in flight per lane (8 KiB per warp): NVLink
+      // latency x bandwidth needs ~2 MiB in flight across the GPU.
+      constexpr int U = 16;
+      for (; i + (U - 1) * 32 < n; i += U * 32) {
+        uint4 v[U];
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
+        for (int u = 0; u < U; ++u) {
           const int k = i + u * 32;
           v[u] = ld16_volatile(src + (long long)(k / pr) * K + (k % pr) * 8);
         }
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
+        for (int u = 0; u < U; ++u) {
           const int k = i + u * 32;
           st16(dst + (long long)(k / pr) * K + (k % pr) * 8, v[u]);
         }
