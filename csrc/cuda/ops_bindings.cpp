@@ -209,6 +209,7 @@ void register_ops(py::module& m) {
 
 // ---------------------------------------------------------------- GEMM (tcgen05)
 #include "gemm_api.h"
+#include "compress_api.h"
 namespace nexar {
 void op_gemm(const at::Tensor& A, const at::Tensor& B, const at::Tensor& C, const c10::optional<at::Tensor>& bias,
              const c10::optional<at::Tensor>& residual, const c10::optional<at::Tensor>& pre, int64_t act,
@@ -234,5 +235,30 @@ void register_gemm_ops(py::module& m) {
   m.def("gemm", &op_gemm, py::arg("A"), py::arg("B"), py::arg("C"), py::arg("bias") = py::none(),
         py::arg("residual") = py::none(), py::arg("pre") = py::none(), py::arg("act") = 0, py::arg("alpha") = 1.0);
   m.def("gemm_error_flag", &gemm_error_flag);
+  m.def("compress_workspace_bytes", [](int64_t n) { return (int64_t)compress_workspace_bytes(n, nullptr); });
+  m.def("compress_blob_bytes", [](int64_t k) { return (int64_t)((compress_blob_bytes(k) + 15) / 16 * 16); });
+  m.def("topk_fp8_compress", [](const at::Tensor& grad, const at::Tensor& residual, int64_t k, const at::Tensor& blob,
+                                const at::Tensor& ws) {
+    TORCH_CHECK(grad.is_cuda() && grad.is_contiguous() && grad.scalar_type() == at::kBFloat16, "grad: contiguous bf16");
+    TORCH_CHECK(residual.is_cuda() && residual.is_contiguous() && residual.scalar_type() == at::kFloat &&
+                    residual.numel() == grad.numel(), "residual: contiguous fp32 like grad");
+    TORCH_CHECK(blob.numel() * blob.element_size() >= (int64_t)compress_blob_bytes(k), "blob too small");
+    TORCH_CHECK(ws.numel() * ws.element_size() >= (int64_t)compress_workspace_bytes(grad.numel(), nullptr),
+                "workspace too small");
+    c10::cuda::CUDAGuard g(grad.get_device());
+    chk(topk_fp8_compress(reinterpret_cast<const __nv_bfloat16*>(grad.data_ptr()), residual.data_ptr<float>(),
+                          grad.numel(), k, reinterpret_cast<unsigned char*>(blob.data_ptr()), ws.data_ptr(),
+                          stream_of(grad)),
+        "topk_fp8_compress");
+    count_launch(compress_kernel_launches());
+  });
+  m.def("decompress_accumulate", [](const at::Tensor& blob, int64_t k, const at::Tensor& out, double scale) {
+    need_bf16(out, "out");
+    c10::cuda::CUDAGuard g(out.get_device());
+    chk(decompress_accumulate(reinterpret_cast<const unsigned char*>(blob.data_ptr()), k, bf(out), (float)scale,
+                              stream_of(out)),
+        "decompress_accumulate");
+    count_launch(1);
+  });
 }
 }  // namespace nexar

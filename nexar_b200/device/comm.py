@@ -232,6 +232,42 @@ class DeviceCommunicator:
     def barrier(self):
         self._C.barrier(self._comm)
 
+    # ----------------------------------------------------------- compressed all-reduce
+    def all_reduce_compressed(self, t: torch.Tensor, ratio: float, residual: torch.Tensor,
+                              out: Optional[torch.Tensor] = None, scale: float = 1.0) -> torch.Tensor:
+        """Sum over ranks of each rank's top-k (by |residual + t|) entries, fp8-quantised.
+
+        Error feedback as in the reference's TopKCompressor
+        (nexar/src/compression/topk.rs): ``residual`` (fp32, same shape) keeps
+        everything this rank has not sent yet, including the fp8 rounding error.
+        k = ceil(numel * ratio). Every rank's (index, e4m3) blob is exchanged
+        with the device all-gather and added into ``out`` (bf16) in rank
+        order, so all ranks produce identical results. ``scale`` multiplies
+        the result (e.g. 1/world for gradient averaging).
+        """
+        import math
+        n = t.numel()
+        k = max(1, min(n, math.ceil(n * ratio)))
+        out = torch.empty_like(t) if out is None else out
+        bb = self._C.compress_blob_bytes(k)
+        ws = getattr(self, "_cmp_ws", {})
+        self._cmp_ws = ws
+        key = (n, k)
+        if key not in ws:
+            ws[key] = (torch.empty(self._C.compress_workspace_bytes(n), dtype=torch.uint8, device=t.device),
+                       torch.empty(bb, dtype=torch.uint8, device=t.device),
+                       torch.empty(bb * self.world_size, dtype=torch.uint8, device=t.device))
+        work, blob, gathered = ws[key]
+        self._C.topk_fp8_compress(t.reshape(-1), residual.reshape(-1), k, blob, work)
+        if self.world_size > 1:
+            self.all_gather(blob, gathered)
+        else:
+            gathered.copy_(blob)
+        out.zero_()
+        for p in range(self.world_size):
+            self._C.decompress_accumulate(gathered[p * bb:(p + 1) * bb], k, out.reshape(-1), float(scale))
+        return out
+
     # ----------------------------------------------------------- fused GEMM + collective
     def gemm_reduce_scatter(self, A: torch.Tensor, B: torch.Tensor, out: Optional[torch.Tensor] = None,
                             bias: Optional[torch.Tensor] = None, alpha: float = 1.0) -> torch.Tensor:
