@@ -61,10 +61,136 @@ cudaError_t make_tmap_bf16(CUtensorMap* map, const void* base, long long rows, l
   return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
-cudaError_t gemm_bf16(const __nv_bfloat16* A, const __nv_bfloat16* B, __nv_bfloat16* C, int M, int N, int K,
-                      long long lda, long long ldb, long long ldc, const __nv_bfloat16* bias,
-                      const __nv_bfloat16* residual, long long ldr, __nv_bfloat16* pre_act, int act, float alpha,
-                      cudaStream_t s) {
+// 3-D fp32 tensor map over [splits, rows, cols] (contiguous), box 1 x 32 x 32,
+// 128-byte swizzle: the split-K partial sink.
+cudaError_t make_tmap_f32_3d(CUtensorMap* map, void* base, long long splits, long long rows, long long cols) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return cudaErrorNotSupported;
+  if ((reinterpret_cast<uintptr_t>(base) & 15u) || (cols * 4) % 16) return cudaErrorInvalidValue;
+  cuuint64_t dims[3] = {(cuuint64_t)cols, (cuuint64_t)rows, (cuuint64_t)splits};
+  cuuint64_t strides[2] = {(cuuint64_t)cols * 4, (cuuint64_t)(rows * cols * 4)};
+  cuuint32_t box[3] = {32, 32, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, base, dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
+namespace {
+// out = act(sum_s part[s] + bias) (+ residual) (+ out if accumulate), fixed
+// summation order over the splits; 4 columns per thread.
+__global__ void __launch_bounds__(256) k_splitk_reduce(const float* __restrict__ part, int splits, int M, int N,
+                                                       const __nv_bfloat16* __restrict__ bias,
+                                                       const __nv_bfloat16* __restrict__ residual, long long ldr,
+                                                       __nv_bfloat16* out, long long ldc, __nv_bfloat16* pre,
+                                                       int act, int accumulate) {
+  const long long n4 = (long long)M * (N / 4);
+  const long long plane = (long long)M * N;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n4; i += (long long)gridDim.x * blockDim.x) {
+    const long long m = i / (N / 4);
+    const int n = (int)(i % (N / 4)) * 4;
+    float4 a = *reinterpret_cast<const float4*>(part + m * N + n);
+    for (int sidx = 1; sidx < splits; ++sidx) {
+      const float4 b = *reinterpret_cast<const float4*>(part + sidx * plane + m * N + n);
+      a.x += b.x; a.y += b.y; a.z += b.z; a.w += b.w;
+    }
+    float v[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      if (bias) v[e] += __bfloat162float(bias[n + e]);
+    }
+    if (pre) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) pre[m * ldc + n + e] = __float2bfloat16_rn(v[e]);
+    }
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      if (act == 1) v[e] = gemm::gelu_tanh_f(v[e]);
+      if (residual) v[e] += __bfloat162float(residual[m * ldr + n + e]);
+      if (accumulate) v[e] += __bfloat162float(out[m * ldc + n + e]);
+    }
+    __nv_bfloat162* o = reinterpret_cast<__nv_bfloat162*>(out + m * ldc + n);
+    o[0] = __floats2bfloat162_rn(v[0], v[1]);
+    o[1] = __floats2bfloat162_rn(v[2], v[3]);
+  }
+}
+
+template <class Epi, int AMN, int BMN>
+cudaError_t launch_major(const void* A, const void* B, int M, int N, int K, long long lda, long long ldb,
+                         const CUtensorMap& tout, const CUtensorMap& tpre, const Epi& epi, int splits,
+                         cudaStream_t s) {
+  return launch_gemm_generic<Epi, gemm::NoGate, 0, AMN, BMN>(A, B, M, N, K, lda, ldb, tout, tpre, 0, epi,
+                                                              gemm::NoGate{}, 0, s, splits);
+}
+
+template <class Epi>
+cudaError_t launch_any_major(bool a_mn, bool b_mn, const void* A, const void* B, int M, int N, int K, long long lda,
+                             long long ldb, const CUtensorMap& tout, const CUtensorMap& tpre, const Epi& epi,
+                             int splits, cudaStream_t s) {
+  if (!a_mn && !b_mn) return launch_major<Epi, 0, 0>(A, B, M, N, K, lda, ldb, tout, tpre, epi, splits, s);
+  if (!a_mn && b_mn) return launch_major<Epi, 0, 1>(A, B, M, N, K, lda, ldb, tout, tpre, epi, splits, s);
+  if (a_mn && !b_mn) return launch_major<Epi, 1, 0>(A, B, M, N, K, lda, ldb, tout, tpre, epi, splits, s);
+  return launch_major<Epi, 1, 1>(A, B, M, N, K, lda, ldb, tout, tpre, epi, splits, s);
+}
+}  // namespace
+
+int gemm_choose_splits(int M, int N, int K) {
+  // Model: time = k-blocks per split x waves x (one 128x256x64 block at the
+  // per-SM tensor rate, ~0.43 us) + the fp32 partial round trip through HBM.
+  const int sm = gemm_sm_count();
+  const long long tiles = (long long)((M + gemm::BM - 1) / gemm::BM) * ((N + gemm::BN - 1) / gemm::BN);
+  const int kb = (K + gemm::BK - 1) / gemm::BK;
+  int best = 1;
+  double best_t = 1e30;
+  for (int sp = 1; sp <= 16; ++sp) {
+    if (sp > 1 && kb / sp < 4) break;
+    const int kps = (kb + sp - 1) / sp;
+    const int eff = (kb + kps - 1) / kps;
+    const long long waves = (tiles * eff + sm - 1) / sm;
+    double t = (double)kps * (double)waves * 0.43;
+    if (eff > 1) t += ((double)eff * M * N * 8.0 + (double)M * N * 2.0) / 6.0e6;
+    if (t < best_t * 0.97) {
+      best_t = t;
+      best = eff;
+    }
+  }
+  return best;
+}
+
+size_t gemm_split_workspace_bytes(int M, int N, int splits) {
+  return splits > 1 ? (size_t)splits * M * N * sizeof(float) : 0;
+}
+
+cudaError_t gemm_bf16_ex(const __nv_bfloat16* A, const __nv_bfloat16* B, __nv_bfloat16* C, int M, int N, int K,
+                         long long lda, long long ldb, long long ldc, bool a_mn, bool b_mn,
+                         const __nv_bfloat16* bias, const __nv_bfloat16* residual, long long ldr,
+                         __nv_bfloat16* pre_act, int act, float alpha, bool accumulate, int splits, float* ws,
+                         size_t ws_bytes, cudaStream_t s) {
+  if (M <= 0 || N <= 0 || K <= 0) return cudaSuccess;
+  if (splits <= 0) splits = gemm_choose_splits(M, N, K);
+  const int kb = (K + gemm::BK - 1) / gemm::BK;
+  if (splits > kb) splits = kb;
+  if (splits > 1) {
+    const int kps = (kb + splits - 1) / splits;
+    splits = (kb + kps - 1) / kps;  // no empty split
+  }
+  if (splits > 1 && (N % 4 != 0 || ws == nullptr || ws_bytes < gemm_split_workspace_bytes(M, N, splits)))
+    splits = 1;
+  if (splits > 1) {
+    CUtensorMap tpart;
+    cudaError_t e = make_tmap_f32_3d(&tpart, ws, splits, M, N);
+    if (e != cudaSuccess) return e;
+    gemm::EpiSplitF32 epi{alpha};
+    e = launch_any_major(a_mn, b_mn, A, B, M, N, K, lda, ldb, tpart, tpart, epi, splits, s);
+    if (e != cudaSuccess) return e;
+    const long long n4 = (long long)M * (N / 4);
+    long long g = (n4 + 255) / 256;
+    if (g > gemm_sm_count() * 8) g = gemm_sm_count() * 8;
+    k_splitk_reduce<<<(int)g, 256, 0, s>>>(ws, splits, M, N, bias, residual, ldr, C, ldc, pre_act, act,
+                                           accumulate ? 1 : 0);
+    return cudaGetLastError();
+  }
   CUtensorMap tout, tpre;
   cudaError_t e = make_tmap_bf16(&tout, C, M, N, ldc, 32, 64);
   if (e != cudaSuccess) return e;
@@ -73,9 +199,21 @@ cudaError_t gemm_bf16(const __nv_bfloat16* A, const __nv_bfloat16* B, __nv_bfloa
     e = make_tmap_bf16(&tpre, pre_act, M, N, ldc, 32, 64);
     if (e != cudaSuccess) return e;
   }
+  if (accumulate) {
+    if (residual) return cudaErrorInvalidValue;  // one addend at a time
+    residual = C;  // each element is read by the thread that then overwrites it
+    ldr = ldc;
+  }
   gemm::EpiStore epi{bias, residual, ldr, alpha, act, pre_act != nullptr};
-  return launch_gemm_generic<gemm::EpiStore, gemm::NoGate, 0>(A, B, M, N, K, lda, ldb, tout, tpre, 0, epi,
-                                                                gemm::NoGate{}, 0, s);
+  return launch_any_major(a_mn, b_mn, A, B, M, N, K, lda, ldb, tout, tpre, epi, 1, s);
+}
+
+cudaError_t gemm_bf16(const __nv_bfloat16* A, const __nv_bfloat16* B, __nv_bfloat16* C, int M, int N, int K,
+                      long long lda, long long ldb, long long ldc, const __nv_bfloat16* bias,
+                      const __nv_bfloat16* residual, long long ldr, __nv_bfloat16* pre_act, int act, float alpha,
+                      cudaStream_t s) {
+  return gemm_bf16_ex(A, B, C, M, N, K, lda, ldb, ldc, false, false, bias, residual, ldr, pre_act, act, alpha,
+                      false, 1, nullptr, 0, s);
 }
 
 unsigned int gemm_error_flag() {

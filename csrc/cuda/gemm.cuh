@@ -1,6 +1,14 @@
 // Persistent warp-specialised bf16 GEMM for sm_100a (tcgen05 + TMEM + TMA).
 //
-//   C[M, N] = epilogue( A[M, K] . B[N, K]^T )      (both operands K-major)
+//   C[M, N] = epilogue( A[M, K] . B[N, K]^T )
+//
+// Operands are K-major (row-major [M, K] / [N, K]) by default; AMN / BMN
+// select MN-major operands (A stored as row-major [K, M], B as [K, N]), which
+// is how the backward pass of a linear layer reads dY^T, X^T and W without
+// transposing anything: the tensor cores take the transposed layout directly.
+// SPLIT > 0 splits K across CTAs; each split writes an fp32 partial tile
+// (TMA store into [splits, M, N]) and a separate pass sums the splits in a
+// fixed order (deterministic).
 //
 // CTA = 6 warps. Warp 0 lane 0 issues TMA loads of 128x64 A and 256x64 B
 // tiles into a 4-stage ring of 128-byte-swizzled shared memory. Warp 1
@@ -37,8 +45,11 @@ constexpr uint64_t kWaitLimit = 2000000000ull;  // ns: 2 s per wait, far above a
 struct TileSched {
   int tiles_m, tiles_n;
   int m_rotate;  // tile rows start at this M-tile (fused kernels: local shard first)
-  __device__ int num() const { return tiles_m * tiles_n; }
+  int splits;    // K splits; the split index varies slowest so co-resident CTAs share K ranges
+  __device__ int num() const { return tiles_m * tiles_n * splits; }
+  __device__ int split_of(int t) const { return t / (tiles_m * tiles_n); }
   __device__ void coords(int t, int& tm, int& tn) const {
+    t %= tiles_m * tiles_n;
     // Groups of 8 M-tiles walk N together so concurrently running CTAs
     // share B tiles and A rows in L2.
     const int group = 8;
@@ -75,6 +86,19 @@ __device__ __forceinline__ void stage_row64(uint8_t* buf, int r, const float (&v
 #pragma unroll
     for (int e = 0; e < 4; ++e) h[e] = __floats2bfloat162_rn(v[j * 8 + 2 * e], v[j * 8 + 2 * e + 1]);
     *reinterpret_cast<uint4*>(row + ((j ^ (r & 7)) << 4)) = o;
+  }
+}
+
+// 32 fp32 values (columns h*32 .. h*32+31 of v) of row `r` into a 128-byte
+// swizzled staging row (8 chunks of 4 floats; chunk j lands at j ^ (r & 7)).
+template <int H>
+__device__ __forceinline__ void stage_row32f(uint8_t* buf, int r, const float (&v)[64]) {
+  uint8_t* row = buf + r * 128;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const float4 o = make_float4(v[H * 32 + 4 * j], v[H * 32 + 4 * j + 1], v[H * 32 + 4 * j + 2],
+                                 v[H * 32 + 4 * j + 3]);
+    *reinterpret_cast<float4*>(row + ((j ^ (r & 7)) << 4)) = o;
   }
 }
 
@@ -153,11 +177,31 @@ struct EpiStore {
   __device__ __forceinline__ void finalize() const {}
 };
 
-template <class Epi, class Gate = NoGate, int EXTRA = 0>
+// Split-K partial sink: alpha * acc as fp32 into [splits, M, N] (3-D tensor
+// map, so rows past M are clipped per split).
+struct EpiSplitF32 {
+  float alpha;
+  static constexpr int has_pre = 0;
+  __device__ __forceinline__ bool prologue() const { return true; }
+  __device__ __forceinline__ bool begin_tile(int, int) const { return true; }
+  __device__ __forceinline__ void math(int, int, float (&v)[64], int, int, float (&)[64]) const {
+#pragma unroll
+    for (int i = 0; i < 64; ++i) v[i] *= alpha;
+  }
+  // Unused: the mainloop stores fp32 partials itself (EpiTraits::f32_split).
+  __device__ __forceinline__ void store_block(const CUtensorMap*, const uint8_t*, int, int, int) const {}
+  __device__ __forceinline__ void end_tile(int, int, int) const {}
+  __device__ __forceinline__ void finalize() const {}
+};
+
+template <class Epi> struct EpiTraits { static constexpr bool f32_split = false; };
+template <> struct EpiTraits<EpiSplitF32> { static constexpr bool f32_split = true; };
+
+template <class Epi, class Gate = NoGate, int EXTRA = 0, int AMN = 0, int BMN = 0>
 __global__ void __launch_bounds__(THREADS + 32 * EXTRA, 1)
 k_gemm_bf16(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
             const __grid_constant__ CUtensorMap tmOut, const __grid_constant__ CUtensorMap tmPre, int M, int N,
-            int K, int m_rotate, Epi epi, Gate gate, unsigned int* err) {
+            int K, int m_rotate, int splits, Epi epi, Gate gate, unsigned int* err) {
   using namespace sm100;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -202,10 +246,11 @@ k_gemm_bf16(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
     __syncthreads();
   }
 
-  TileSched sched{(M + BM - 1) / BM, (N + BN - 1) / BN, m_rotate};
+  TileSched sched{(M + BM - 1) / BM, (N + BN - 1) / BN, m_rotate, splits};
   const int ntiles = sched.num();
   const int kblocks = (K + BK - 1) / BK;
-  constexpr uint32_t idesc = umma_idesc_bf16_f32(BM, BN);
+  const int kb_per_split = (kblocks + splits - 1) / splits;
+  constexpr uint32_t idesc = umma_idesc_bf16_f32(BM, BN, AMN != 0, BMN != 0);
 
   if (warp == 0) {
     if (lane == 0) {
@@ -219,7 +264,9 @@ k_gemm_bf16(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
           s_abort = 1;
           break;
         }
-        for (int kb = 0; kb < kblocks; ++kb) {
+        const int kb0 = sched.split_of(t) * kb_per_split;
+        const int kb1 = min(kblocks, kb0 + kb_per_split);
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait_bounded(&empty[stage], phase ^ 1, kWaitLimit)) {
             atomicExch(err, 1u);
             s_abort = 1;
@@ -228,8 +275,18 @@ k_gemm_bf16(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
           uint8_t* a = smem + stage * STAGE_BYTES;
           uint8_t* b = a + A_BYTES;
           mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
-          tma_load_2d(a, &tmA, &full[stage], kb * BK, tm * BM);
-          tma_load_2d(b, &tmB, &full[stage], kb * BK, tn * BN);
+          if constexpr (AMN) {
+#pragma unroll
+            for (int j = 0; j < BM / 64; ++j) tma_load_2d(a + j * 8192, &tmA, &full[stage], tm * BM + 64 * j, kb * BK);
+          } else {
+            tma_load_2d(a, &tmA, &full[stage], kb * BK, tm * BM);
+          }
+          if constexpr (BMN) {
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j) tma_load_2d(b + j * 8192, &tmB, &full[stage], tn * BN + 64 * j, kb * BK);
+          } else {
+            tma_load_2d(b, &tmB, &full[stage], kb * BK, tn * BN);
+          }
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1;
@@ -260,7 +317,9 @@ k_gemm_bf16(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
         }
         tc_fence_after();
         const uint32_t d = tmem_base + (uint32_t)(acc * BN);
-        for (int kb = 0; kb < kblocks; ++kb) {
+        const int kb0 = sched.split_of(t) * kb_per_split;
+        const int kb1 = min(kblocks, kb0 + kb_per_split);
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait_bounded(&full[stage], phase, kWaitLimit)) {
             atomicExch(err, 3u);
             s_abort = 1;
@@ -271,8 +330,11 @@ k_gemm_bf16(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
           const uint32_t b = a + A_BYTES;
 #pragma unroll
           for (int k = 0; k < BK / 16; ++k) {
-            umma_f16(d, umma_desc_sw128_kmajor(a + k * 32), umma_desc_sw128_kmajor(b + k * 32), idesc,
-                     (kb | k) != 0 ? 1u : 0u);
+            // K step of 16: 32 bytes inside the swizzle atom (K-major) or
+            // two 8-row groups = 2048 bytes (MN-major).
+            const uint64_t da = AMN ? umma_desc_sw128_mnmajor(a + k * 2048) : umma_desc_sw128_kmajor(a + k * 32);
+            const uint64_t db = BMN ? umma_desc_sw128_mnmajor(b + k * 2048) : umma_desc_sw128_kmajor(b + k * 32);
+            umma_f16(d, da, db, idesc, ((kb - kb0) | k) != 0 ? 1u : 0u);
           }
           umma_commit(&empty[stage]);
           if (++stage == STAGES) {
@@ -326,6 +388,25 @@ k_gemm_bf16(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
           v[32 + i] = __uint_as_float(r1[i]);
         }
         epi.math(row, tn * BN + c0, v, M, N, pre);
+        if constexpr (EpiTraits<Epi>::f32_split) {
+          const int ks = sched.split_of(t);
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            if (lane == 0) tma_store_wait_read<1>();
+            __syncwarp();
+            uint8_t* buf = bufs + nb * EPI_BUF_BYTES;
+            if (h == 0) stage_row32f<0>(buf, lane, v);
+            else stage_row32f<1>(buf, lane, v);
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              tma_store_3d(&tmOut, buf, tn * BN + c0 + 32 * h, row0, ks);
+              tma_store_commit();
+            }
+            nb ^= 1;
+          }
+          continue;
+        }
         // Wait until the store that last read this staging buffer is done.
         if (lane == 0) tma_store_wait_read<1>();
         __syncwarp();

@@ -14,6 +14,18 @@ cudaError_t gemm_bf16(const __nv_bfloat16* A, const __nv_bfloat16* B, __nv_bfloa
                       const __nv_bfloat16* residual, long long ldr, __nv_bfloat16* pre_act, int act, float alpha,
                       cudaStream_t s);
 
+// General form. a_mn: A is stored MN-major as row-major [K, M] (lda >= M);
+// b_mn: B is stored as row-major [K, N]. accumulate: C += result.
+// splits: 1 = no split-K, 0 = choose (uses ws), > 1 = forced (needs ws of
+// gemm_split_workspace_bytes; falls back to 1 when ws is too small).
+cudaError_t gemm_bf16_ex(const __nv_bfloat16* A, const __nv_bfloat16* B, __nv_bfloat16* C, int M, int N, int K,
+                         long long lda, long long ldb, long long ldc, bool a_mn, bool b_mn,
+                         const __nv_bfloat16* bias, const __nv_bfloat16* residual, long long ldr,
+                         __nv_bfloat16* pre_act, int act, float alpha, bool accumulate, int splits, float* ws,
+                         size_t ws_bytes, cudaStream_t s);
+int gemm_choose_splits(int M, int N, int K);
+size_t gemm_split_workspace_bytes(int M, int N, int splits);
+
 // Nonzero if any GEMM launch on this device gave up on a bounded wait.
 unsigned int gemm_error_flag();
 

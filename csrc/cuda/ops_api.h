@@ -12,15 +12,33 @@ namespace nexar {
 cudaError_t ln_fwd(const __nv_bfloat16* x, const __nv_bfloat16* res, __nv_bfloat16* sum_out,
                    const __nv_bfloat16* w, const __nv_bfloat16* b, __nv_bfloat16* y, float* mean,
                    float* rstd, int R, int C, float eps, cudaStream_t s);
+// As ln_fwd with the residual branch's bias folded in: s = x + res + rb.
+cudaError_t ln_fwd_ex(const __nv_bfloat16* x, const __nv_bfloat16* res, const __nv_bfloat16* rb,
+                      __nv_bfloat16* sum_out, const __nv_bfloat16* w, const __nv_bfloat16* b, __nv_bfloat16* y,
+                      float* mean, float* rstd, int R, int C, float eps, cudaStream_t s);
 // LayerNorm backward. dx = dLN/dx (+ dres if non-null). dw/db receive the
-// column sums; `scratch` holds ln_bwd_scratch_floats(C, blocks) floats and
-// `counter` one zero-initialised uint32 (left at zero on exit).
+// column sums; `scratch` holds ln_bwd_scratch_floats(C, blocks) floats;
+// `counter` is unused (kept for the C ABI). Two launches: rows, then a
+// column reduction of the per-CTA partials.
 int ln_bwd_blocks(int R);
 size_t ln_bwd_scratch_floats(int C, int blocks);
 cudaError_t ln_bwd(const __nv_bfloat16* dy, const __nv_bfloat16* x, const float* mean,
                    const float* rstd, const __nv_bfloat16* w, const __nv_bfloat16* dres,
                    __nv_bfloat16* dx, __nv_bfloat16* dw, __nv_bfloat16* db, float* scratch,
                    unsigned int* counter, int R, int C, int blocks, cudaStream_t s);
+// As ln_bwd, plus (if dsum is non-null) the column sums of dx: the bias
+// gradient of the layer whose output was added into the residual stream.
+// scratch: ln_bwd_scratch_floats_ex(C, blocks, dsum != nullptr) floats.
+size_t ln_bwd_scratch_floats_ex(int C, int blocks, bool dsum);
+cudaError_t ln_bwd_ex(const __nv_bfloat16* dy, const __nv_bfloat16* x, const float* mean, const float* rstd,
+                      const __nv_bfloat16* w, const __nv_bfloat16* dres, __nv_bfloat16* dx, __nv_bfloat16* dw,
+                      __nv_bfloat16* db, __nv_bfloat16* dsum, float* scratch, int R, int C, int blocks,
+                      cudaStream_t s);
+// out[c] (+)= sum_r x[r, c] for a bf16 [R, C] matrix (row stride ldx), fp32
+// accumulation in a fixed order; scratch holds colsum_slabs(R) * C floats.
+int colsum_slabs(int R);
+cudaError_t colsum_bf16(const __nv_bfloat16* x, long long ldx, int R, int C, __nv_bfloat16* out, bool accumulate,
+                        float* scratch, cudaStream_t s);
 
 // GELU (tanh approximation, as GPT-2) forward and backward, bf16.
 cudaError_t gelu_fwd(const __nv_bfloat16* x, __nv_bfloat16* y, long long n, cudaStream_t s);

@@ -34,7 +34,8 @@ const __nv_bfloat16* bfc(const c10::optional<at::Tensor>& t) {
 // sum_out = x + res when res is given).
 void op_ln_fwd(const at::Tensor& x, const c10::optional<at::Tensor>& res,
                const c10::optional<at::Tensor>& sum_out, const at::Tensor& w, const at::Tensor& b,
-               const at::Tensor& y, const at::Tensor& mean, const at::Tensor& rstd, double eps) {
+               const at::Tensor& y, const at::Tensor& mean, const at::Tensor& rstd, double eps,
+               const c10::optional<at::Tensor>& rbias) {
   need_bf16(x, "x");
   need_bf16(y, "y");
   need_bf16(w, "weight");
@@ -44,21 +45,22 @@ void op_ln_fwd(const at::Tensor& x, const c10::optional<at::Tensor>& res,
   const int C = x.size(-1);
   const int R = x.numel() / C;
   TORCH_CHECK(res.has_value() == sum_out.has_value(), "ln_fwd: res and sum_out go together");
+  TORCH_CHECK(!rbias || (res && rbias->numel() == C), "ln_fwd: rbias needs res and C elements");
   c10::cuda::CUDAGuard g(x.get_device());
-  chk(ln_fwd(bf(x), bfc(res), sum_out ? bf(*sum_out) : nullptr, bf(w), bf(b), bf(y),
-             mean.data_ptr<float>(), rstd.data_ptr<float>(), R, C, (float)eps, stream_of(x)),
+  chk(ln_fwd_ex(bf(x), bfc(res), bfc(rbias), sum_out ? bf(*sum_out) : nullptr, bf(w), bf(b), bf(y),
+                mean.data_ptr<float>(), rstd.data_ptr<float>(), R, C, (float)eps, stream_of(x)),
       "ln_fwd");
   count_launch(1);
 }
 
-int64_t op_ln_bwd_scratch_floats(int64_t R, int64_t C) {
-  return (int64_t)ln_bwd_scratch_floats((int)C, ln_bwd_blocks((int)R));
+int64_t op_ln_bwd_scratch_floats(int64_t R, int64_t C, bool dsum) {
+  return (int64_t)ln_bwd_scratch_floats_ex((int)C, ln_bwd_blocks((int)R), dsum);
 }
 
 void op_ln_bwd(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& mean, const at::Tensor& rstd,
                const at::Tensor& w, const c10::optional<at::Tensor>& dres, const at::Tensor& dx,
                const at::Tensor& dw, const at::Tensor& db, const at::Tensor& scratch,
-               const at::Tensor& counter) {
+               const at::Tensor& counter, const c10::optional<at::Tensor>& dsum) {
   need_bf16(dy, "dy");
   need_bf16(x, "x");
   need_bf16(dx, "dx");
@@ -68,14 +70,30 @@ void op_ln_bwd(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& mean
   const int C = x.size(-1);
   const int R = x.numel() / C;
   const int blocks = ln_bwd_blocks(R);
-  TORCH_CHECK((size_t)scratch.numel() >= ln_bwd_scratch_floats(C, blocks), "ln_bwd: scratch too small");
-  TORCH_CHECK(counter.numel() >= 1 && counter.element_size() == 4, "ln_bwd: counter must be a 4-byte tensor");
+  TORCH_CHECK((size_t)scratch.numel() >= ln_bwd_scratch_floats_ex(C, blocks, dsum.has_value()),
+              "ln_bwd: scratch too small");
+  if (dsum) need_bf16(*dsum, "dsum");
   c10::cuda::CUDAGuard g(x.get_device());
-  chk(ln_bwd(bf(dy), bf(x), mean.data_ptr<float>(), rstd.data_ptr<float>(), bf(w), bfc(dres), bf(dx),
-             bf(dw), bf(db), scratch.data_ptr<float>(), reinterpret_cast<unsigned int*>(counter.data_ptr()),
-             R, C, blocks, stream_of(x)),
+  chk(ln_bwd_ex(bf(dy), bf(x), mean.data_ptr<float>(), rstd.data_ptr<float>(), bf(w), bfc(dres), bf(dx),
+                bf(dw), bf(db), dsum ? bf(*dsum) : nullptr, scratch.data_ptr<float>(), R, C, blocks, stream_of(x)),
       "ln_bwd");
-  count_launch(1);
+  count_launch(2);
+}
+
+int64_t op_colsum_scratch_floats(int64_t R, int64_t C) { return (int64_t)colsum_slabs((int)R) * C; }
+
+// out[c] (+)= sum over rows of x[:, c] (bias gradient), fp32 accumulation.
+void op_colsum(const at::Tensor& x, const at::Tensor& out, const at::Tensor& scratch, bool accumulate) {
+  need_bf16(x, "x");
+  need_bf16(out, "out");
+  need_f32(scratch, "scratch");
+  TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1, "colsum: 2-D x with contiguous rows");
+  const int R = x.size(0), C = x.size(1);
+  TORCH_CHECK(out.numel() == C, "colsum: out must have C elements");
+  TORCH_CHECK(scratch.numel() >= op_colsum_scratch_floats(R, C), "colsum: scratch too small");
+  c10::cuda::CUDAGuard g(x.get_device());
+  chk(colsum_bf16(bf(x), x.stride(0), R, C, bf(out), accumulate, scratch.data_ptr<float>(), stream_of(x)), "colsum");
+  count_launch(2);
 }
 
 void op_gelu_fwd(const at::Tensor& x, const at::Tensor& y) {
@@ -190,9 +208,14 @@ void op_adamw(const at::Tensor& p, const at::Tensor& m, const at::Tensor& v, con
 void register_gemm_ops(py::module& m);
 void register_ops(py::module& m) {
   register_gemm_ops(m);
-  m.def("ln_fwd", &op_ln_fwd);
-  m.def("ln_bwd", &op_ln_bwd);
-  m.def("ln_bwd_scratch_floats", &op_ln_bwd_scratch_floats);
+  m.def("ln_fwd", &op_ln_fwd, py::arg("x"), py::arg("res"), py::arg("sum_out"), py::arg("w"), py::arg("b"),
+        py::arg("y"), py::arg("mean"), py::arg("rstd"), py::arg("eps"), py::arg("rbias") = py::none());
+  m.def("ln_bwd", &op_ln_bwd, py::arg("dy"), py::arg("x"), py::arg("mean"), py::arg("rstd"), py::arg("w"),
+        py::arg("dres"), py::arg("dx"), py::arg("dw"), py::arg("db"), py::arg("scratch"), py::arg("counter"),
+        py::arg("dsum") = py::none());
+  m.def("ln_bwd_scratch_floats", &op_ln_bwd_scratch_floats, py::arg("R"), py::arg("C"), py::arg("dsum") = false);
+  m.def("colsum", &op_colsum, py::arg("x"), py::arg("out"), py::arg("scratch"), py::arg("accumulate") = false);
+  m.def("colsum_scratch_floats", &op_colsum_scratch_floats);
   m.def("gelu_fwd", &op_gelu_fwd);
   m.def("gelu_bwd", &op_gelu_bwd);
   m.def("swiglu_fwd", &op_swiglu_fwd);
@@ -231,7 +254,49 @@ void op_gemm(const at::Tensor& A, const at::Tensor& B, const at::Tensor& C, cons
       "gemm");
   count_launch(1);
 }
+// C[M, N] = act(alpha * opA . opB^T + bias) (+ residual) (+ C if accumulate).
+// a_mn: A is given as the stored [K, M] matrix (opA = A^T); b_mn: B is given
+// as [K, N] (opB = B^T). ws: optional fp32 split-K workspace.
+void op_gemm_ex(const at::Tensor& A, const at::Tensor& B, const at::Tensor& C, bool a_mn, bool b_mn,
+                const c10::optional<at::Tensor>& bias, const c10::optional<at::Tensor>& residual,
+                const c10::optional<at::Tensor>& pre, int64_t act, double alpha, bool accumulate, int64_t splits,
+                const c10::optional<at::Tensor>& ws) {
+  TORCH_CHECK(A.is_cuda() && B.is_cuda() && C.is_cuda(), "gemm_ex: CUDA tensors required");
+  TORCH_CHECK(A.scalar_type() == at::kBFloat16 && B.scalar_type() == at::kBFloat16 && C.scalar_type() == at::kBFloat16,
+              "gemm_ex: bf16 operands required");
+  TORCH_CHECK(A.dim() == 2 && B.dim() == 2 && C.dim() == 2, "gemm_ex: 2D operands required");
+  TORCH_CHECK(A.stride(1) == 1 && B.stride(1) == 1 && C.stride(1) == 1, "gemm_ex: inner dimension must be contiguous");
+  const int M = a_mn ? A.size(1) : A.size(0);
+  const int K = a_mn ? A.size(0) : A.size(1);
+  const int N = b_mn ? B.size(1) : B.size(0);
+  const int Kb = b_mn ? B.size(0) : B.size(1);
+  TORCH_CHECK(Kb == K && C.size(0) == M && C.size(1) == N, "gemm_ex: shape mismatch");
+  if (bias) TORCH_CHECK(bias->is_cuda() && bias->numel() == N && bias->scalar_type() == at::kBFloat16, "gemm_ex: bias");
+  if (ws) TORCH_CHECK(ws->is_cuda() && ws->scalar_type() == at::kFloat && ws->is_contiguous(), "gemm_ex: fp32 ws");
+  c10::cuda::CUDAGuard g(A.get_device());
+  int sp = (int)splits;
+  if (sp <= 0) sp = gemm_choose_splits(M, N, K);
+  const size_t wsb = ws ? (size_t)ws->numel() * 4 : 0;
+  if (sp > 1 && wsb < gemm_split_workspace_bytes(M, N, sp)) sp = 1;
+  chk(gemm_bf16_ex(reinterpret_cast<const __nv_bfloat16*>(A.data_ptr()),
+                   reinterpret_cast<const __nv_bfloat16*>(B.data_ptr()), reinterpret_cast<__nv_bfloat16*>(C.data_ptr()),
+                   M, N, K, A.stride(0), B.stride(0), C.stride(0), a_mn, b_mn,
+                   bias ? reinterpret_cast<const __nv_bfloat16*>(bias->data_ptr()) : nullptr,
+                   residual ? reinterpret_cast<const __nv_bfloat16*>(residual->data_ptr()) : nullptr,
+                   residual ? residual->stride(0) : 0, pre ? reinterpret_cast<__nv_bfloat16*>(pre->data_ptr()) : nullptr,
+                   (int)act, (float)alpha, accumulate, sp, ws ? ws->data_ptr<float>() : nullptr, wsb, stream_of(A)),
+      "gemm_ex");
+  count_launch(sp > 1 ? 2 : 1);
+}
+
 void register_gemm_ops(py::module& m) {
+  m.def("gemm_ex", &op_gemm_ex, py::arg("A"), py::arg("B"), py::arg("C"), py::arg("a_t") = false,
+        py::arg("b_t") = false, py::arg("bias") = py::none(), py::arg("residual") = py::none(),
+        py::arg("pre") = py::none(), py::arg("act") = 0, py::arg("alpha") = 1.0, py::arg("accumulate") = false,
+        py::arg("splits") = 1, py::arg("ws") = py::none());
+  m.def("gemm_choose_splits", &gemm_choose_splits);
+  m.def("gemm_split_workspace_bytes",
+        [](int64_t M, int64_t N, int64_t sp) { return (int64_t)gemm_split_workspace_bytes(M, N, sp); });
   m.def("gemm", &op_gemm, py::arg("A"), py::arg("B"), py::arg("C"), py::arg("bias") = py::none(),
         py::arg("residual") = py::none(), py::arg("pre") = py::none(), py::arg("act") = 0, py::arg("alpha") = 1.0);
   m.def("gemm_error_flag", &gemm_error_flag);

@@ -74,6 +74,11 @@ __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void*
   asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];"
                :: "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(smem_src)), "r"(x), "r"(y) : "memory");
 }
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, const void* smem_src, int x, int y, int z) {
+  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];"
+               :: "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(smem_src)), "r"(x), "r"(y), "r"(z)
+               : "memory");
+}
 __device__ __forceinline__ void tma_store_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 // Wait until at most N committed store groups still read shared memory.
 template <int N> __device__ __forceinline__ void tma_store_wait_read() {
@@ -144,9 +149,24 @@ __device__ __forceinline__ uint64_t umma_desc_sw128_kmajor(uint32_t smem_addr) {
   return d;
 }
 
-// kind::f16 instruction descriptor: bf16 x bf16 -> f32, both K-major.
-__host__ __device__ constexpr uint32_t umma_idesc_bf16_f32(int M, int N) {
-  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+// MN-major operand staged by TMA as boxes of 64 contiguous MN elements
+// (128 bytes, swizzled) x 64 K rows: 8-row K groups are 1024 B apart (stride
+// byte offset), 64-wide MN blocks are one 8 KB box apart (leading byte offset).
+__device__ __forceinline__ uint64_t umma_desc_sw128_mnmajor(uint32_t smem_addr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((smem_addr >> 4) & 0x3FFFu);
+  d |= (uint64_t)(8192u >> 4) << 16;         // leading byte offset: next 64-wide MN block
+  d |= (uint64_t)(1024u >> 4) << 32;         // stride byte offset: next 8-row K group
+  d |= (uint64_t)1u << 46;                   // descriptor version (Blackwell)
+  d |= (uint64_t)2u << 61;                   // 128-byte swizzle
+  return d;
+}
+
+// kind::f16 instruction descriptor: bf16 x bf16 -> f32; bit 15 / 16 mark an
+// MN-major (transposed) A / B operand.
+__host__ __device__ constexpr uint32_t umma_idesc_bf16_f32(int M, int N, bool a_mn = false, bool b_mn = false) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((a_mn ? 1u : 0u) << 15) | ((b_mn ? 1u : 0u) << 16) |
+         ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
 
 }  // namespace sm100

@@ -4,11 +4,15 @@ BASELINE config 3: 12 layers, d=768, 12 heads, vocab 50257 (padded to 50304
 for 16-byte aligned rows), context 1024, bf16 compute, N(0, 0.02) init with
 residual projections scaled by 1/sqrt(2*n_layer).
 
-Kernels per layer: fused residual-add + LayerNorm (one launch, also the
-backward), QKV / proj / FC / FC-proj GEMMs (cuBLAS, bias fused), causal
-flash attention (torch SDPA), fused GELU. The head is the tied embedding
-GEMM followed by the fused softmax-cross-entropy kernel that writes its
-gradient in place of the logits.
+Kernels per layer: fused residual-add (+ the residual branch's bias) +
+LayerNorm (its backward also yields that bias's gradient), QKV / proj / FC /
+FC-proj GEMMs on the tcgen05 kernel (forward K-major; backward reads dY^T,
+X^T and W as MN-major operands, split-K for the weight gradients; bias and
+GELU fused into the FC epilogue), causal flash attention (torch SDPA). The
+head is the tied embedding GEMM followed by the fused softmax-cross-entropy
+kernel that writes its gradient in place of the logits. Weight gradients
+are stored straight into the flat gradient buffer (no zero-fill, no
+per-parameter accumulation).
 """
 from __future__ import annotations
 
@@ -100,23 +104,25 @@ class GPT2(torch.nn.Module):
         h = ops.layer_norm(x, p["h0.ln1.w"], p["h0.ln1.b"], cfg.ln_eps)
         for l in range(cfg.n_layer):
             q = f"h{l}."
-            qkv = torch.addmm(p[q + "attn.b"], h, p[q + "attn.w"].t())
+            qkv = ops.linear(h, p[q + "attn.w"], p[q + "attn.b"])
             qkv = qkv.view(B, T, 3, H, hd)
             qh, kh, vh = qkv.unbind(2)
             y = F.scaled_dot_product_attention(qh.transpose(1, 2), kh.transpose(1, 2), vh.transpose(1, 2),
                                                is_causal=True)
             y = y.transpose(1, 2).reshape(B * T, C)
-            a = torch.addmm(p[q + "proj.b"], y, p[q + "proj.w"].t())
-            x, h = ops.residual_layer_norm(x, a, p[q + "ln2.w"], p[q + "ln2.b"], cfg.ln_eps)
-            f = torch.addmm(p[q + "fc.b"], h, p[q + "fc.w"].t())
-            f = ops.gelu(f)
-            m = torch.addmm(p[q + "fcproj.b"], f, p[q + "fcproj.w"].t())
+            # projection bias is folded into the residual add of the next LayerNorm
+            a = ops.linear(y, p[q + "proj.w"])
+            x, h = ops.residual_layer_norm(x, a, p[q + "ln2.w"], p[q + "ln2.b"], cfg.ln_eps, rbias=p[q + "proj.b"])
+            f = ops.linear(h, p[q + "fc.w"], p[q + "fc.b"], act="gelu")
+            m = ops.linear(f, p[q + "fcproj.w"])
             if l + 1 < cfg.n_layer:
                 nq = f"h{l + 1}."
-                x, h = ops.residual_layer_norm(x, m, p[nq + "ln1.w"], p[nq + "ln1.b"], cfg.ln_eps)
+                x, h = ops.residual_layer_norm(x, m, p[nq + "ln1.w"], p[nq + "ln1.b"], cfg.ln_eps,
+                                               rbias=p[q + "fcproj.b"])
             else:
-                x, h = ops.residual_layer_norm(x, m, p["lnf.w"], p["lnf.b"], cfg.ln_eps)
-        logits = torch.mm(h, p["wte"].t())  # [B*T, Vp]
+                x, h = ops.residual_layer_norm(x, m, p["lnf.w"], p["lnf.b"], cfg.ln_eps, rbias=p[q + "fcproj.b"])
+        # tied head: its weight gradient is completed by the embedding backward
+        logits = ops.linear(h, p["wte"], ready=False)  # [B*T, Vp]
         if targets is None:
             return logits.view(B, T, -1)
         return ops.cross_entropy(logits, targets, cfg.vocab_size, unit_grad=unit_grad)

@@ -2,6 +2,16 @@
 
 Each function calls exactly one (or two) native kernels per direction; the
 shapes are flattened to [rows, features] internally.
+
+Gradient sinks: a parameter that carries ``main_grad`` (a view into a flat
+gradient buffer, see ``nexar_b200.utils.flat``) gets its gradient written
+there directly by the backward kernels — the weight-gradient GEMM stores
+into it, LayerNorm / bias reductions write their column sums into it — and
+autograd sees ``None`` for that input, so there is no zero-fill of the
+gradient buffer and no accumulate kernel per parameter. After the write the
+parameter's ``_nexar_on_ready`` callback (if any) runs; the data-parallel
+trainer uses it to launch bucket all-reduces during backward. Parameters
+without ``main_grad`` get ordinary autograd gradients.
 """
 from __future__ import annotations
 
@@ -20,6 +30,135 @@ def _scratch(device, nfloats: int) -> torch.Tensor:
         buf = torch.empty(max(nfloats, 1 << 16), dtype=torch.float32, device=device)
         _SCRATCH[key] = buf
     return buf
+
+
+def _gemm_ws(device, nfloats: int) -> torch.Tensor:
+    """Per-device fp32 split-K workspace (grown on demand, never shrunk)."""
+    key = (device, "gemm_ws")
+    buf = _SCRATCH.get(key)
+    if buf is None or buf.numel() < nfloats:
+        buf = torch.empty(max(nfloats, 1 << 20), dtype=torch.float32, device=device)
+        _SCRATCH[key] = buf
+    return buf
+
+
+def _sink(p):
+    return getattr(p, "main_grad", None)
+
+
+def _ready(p):
+    cb = getattr(p, "_nexar_on_ready", None)
+    if cb is not None:
+        cb()
+
+
+def _grad_out(p, fill):
+    """Write a parameter gradient: into its sink (returns None) or a new tensor."""
+    g = _sink(p)
+    if g is not None:
+        fill(g)
+        _ready(p)
+        return None
+    g = torch.empty_like(p)
+    fill(g)
+    return g
+
+
+def matmul_nt(a, b, out=None, bias=None, act: int = 0, pre=None, a_t: bool = False, b_t: bool = False,
+              accumulate: bool = False, splits: int = 0):
+    """out = act(opA . opB^T + bias) on the tcgen05 GEMM.
+
+    opA = a ([M, K]) or a^T when ``a_t`` (a stored as [K, M]); opB = b ([N, K])
+    or b^T when ``b_t`` (b stored as [K, N]). ``splits=0`` picks split-K by
+    the kernel's cost model (fp32 partials, deterministic reduction).
+    """
+    C = _native.cuda()
+    M = a.shape[1] if a_t else a.shape[0]
+    N = b.shape[1] if b_t else b.shape[0]
+    K = a.shape[0] if a_t else a.shape[1]
+    if out is None:
+        out = torch.empty(M, N, dtype=a.dtype, device=a.device)
+    sp = C.gemm_choose_splits(M, N, K) if splits == 0 else splits
+    ws = _gemm_ws(a.device, C.gemm_split_workspace_bytes(M, N, sp) // 4) if sp > 1 else None
+    C.gemm_ex(a, b, out, a_t, b_t, bias, None, pre, act, 1.0, accumulate, sp, ws)
+    return out
+
+
+def colsum(x, out, accumulate: bool = False):
+    """out[c] (+)= sum over rows of x[:, c] (bf16 in/out, fp32 accumulation)."""
+    C = _native.cuda()
+    x2 = x.reshape(-1, x.shape[-1])
+    scratch = _scratch(x.device, C.colsum_scratch_floats(x2.shape[0], x2.shape[1]))
+    C.colsum(x2, out, scratch, accumulate)
+    return out
+
+
+class _Linear(torch.autograd.Function):
+    """y = act(x . w^T + b) with the tcgen05 GEMM in all three products.
+
+    backward: dx = dz . w (w read MN-major), dw = dz^T . x (both operands
+    MN-major, split-K when the output has few tiles), db = column sums of dz,
+    where dz = dy or gelu'(pre) * dy.
+    """
+
+    @staticmethod
+    def forward(ctx, x, w, b, act, ready):
+        K = x.shape[-1]
+        x2 = x.reshape(-1, K)
+        if not x2.is_contiguous():
+            x2 = x2.contiguous()
+        M, N = x2.shape[0], w.shape[0]
+        y = torch.empty(M, N, dtype=x.dtype, device=x.device)
+        pre = torch.empty_like(y) if act else None
+        matmul_nt(x2, w, out=y, bias=b, act=act, pre=pre, splits=1)
+        ctx.save_for_backward(x2, w, pre)
+        ctx.has_b = b is not None
+        ctx.bias_param = b
+        ctx.act, ctx.ready = act, ready
+        ctx.in_shape = x.shape
+        return y.view(*x.shape[:-1], N)
+
+    @staticmethod
+    def backward(ctx, dy):
+        x2, w, pre = ctx.saved_tensors
+        N = w.shape[0]
+        dz = dy.reshape(-1, N)
+        if not dz.is_contiguous():
+            dz = dz.contiguous()
+        if ctx.act:
+            d = torch.empty_like(pre)
+            _native.cuda().gelu_bwd(pre, dz, d)
+            dz = d
+        dx = matmul_nt(dz, w, b_t=True) if ctx.needs_input_grad[0] else None
+
+        def fill_w(g):
+            matmul_nt(dz, x2, out=g.view(N, -1), a_t=True, b_t=True)
+
+        if ctx.ready:
+            gw = _grad_out(w, fill_w)
+        else:
+            # shared (tied) weight: another op adds to the sink afterwards and signals
+            g = _sink(w)
+            if g is not None:
+                fill_w(g)
+                gw = None
+            else:
+                gw = torch.empty_like(w)
+                fill_w(gw)
+        gb = None
+        if ctx.has_b:
+            gb = _grad_out(ctx.bias_param, lambda g: colsum(dz, g))
+        return (dx.view(ctx.in_shape) if dx is not None else None), gw, gb, None, None
+
+
+def linear(x, w, b=None, act: str = None, ready: bool = True):
+    """x . w^T (+ b), optionally followed by GELU (tanh) fused into the GEMM epilogue.
+
+    ``ready=False`` marks a weight whose gradient sink receives a further
+    contribution later in backward (tied embeddings): it is overwritten here
+    and the later op signals readiness.
+    """
+    return _Linear.apply(x, w, b, 1 if act == "gelu" else 0, ready)
 
 
 def _counter(device, slot: int = 0) -> torch.Tensor:
@@ -42,6 +181,7 @@ class _LayerNorm(torch.autograd.Function):
         rstd = torch.empty(R, dtype=torch.float32, device=x.device)
         _native.cuda().ln_fwd(x2, None, None, w, b, y, mean, rstd, eps)
         ctx.save_for_backward(x2, w, mean, rstd)
+        ctx.b = b
         ctx.shape = x.shape
         return y.view(x.shape)
 
@@ -51,12 +191,20 @@ class _LayerNorm(torch.autograd.Function):
         C = x2.shape[-1]
         dy2 = dy.contiguous().view(-1, C)
         dx = torch.empty_like(x2)
-        dw = torch.empty_like(w)
-        db = torch.empty_like(w)
+        dw, db = _sink(w), _sink(ctx.b)
+        ret_w = ret_b = None
+        if dw is None:
+            dw = ret_w = torch.empty_like(w)
+        if db is None:
+            db = ret_b = torch.empty_like(w)
         C_ = _native.cuda()
         scratch = _scratch(x2.device, C_.ln_bwd_scratch_floats(x2.shape[0], C))
         C_.ln_bwd(dy2, x2, mean, rstd, w, None, dx, dw, db, scratch, _counter(x2.device))
-        return dx.view(ctx.shape), dw, db, None
+        if ret_w is None:
+            _ready(w)
+        if ret_b is None:
+            _ready(ctx.b)
+        return dx.view(ctx.shape), ret_w, ret_b, None
 
 
 def layer_norm(x, w, b, eps: float = 1e-5):
@@ -64,10 +212,15 @@ def layer_norm(x, w, b, eps: float = 1e-5):
 
 
 class _ResidualLayerNorm(torch.autograd.Function):
-    """s = x + r ; y = LayerNorm(s). Returns (s, y)."""
+    """s = x + r (+ rb) ; y = LayerNorm(s). Returns (s, y).
+
+    ``rb`` is the bias of the layer that produced r, folded into the add so
+    that layer's GEMM needs no bias epilogue; its gradient (column sums of
+    ds) comes out of the LayerNorm backward kernel.
+    """
 
     @staticmethod
-    def forward(ctx, x, r, w, b, eps):
+    def forward(ctx, x, r, w, b, rb, eps):
         C = x.shape[-1]
         x2 = x.reshape(-1, C)
         r2 = r.reshape(-1, C)
@@ -76,8 +229,9 @@ class _ResidualLayerNorm(torch.autograd.Function):
         y = torch.empty_like(x2)
         mean = torch.empty(R, dtype=torch.float32, device=x.device)
         rstd = torch.empty(R, dtype=torch.float32, device=x.device)
-        _native.cuda().ln_fwd(x2, r2, s, w, b, y, mean, rstd, eps)
+        _native.cuda().ln_fwd(x2, r2, s, w, b, y, mean, rstd, eps, rb)
         ctx.save_for_backward(s, w, mean, rstd)
+        ctx.b, ctx.rb = b, rb
         ctx.shape = x.shape
         return s.view(x.shape), y.view(x.shape)
 
@@ -86,20 +240,33 @@ class _ResidualLayerNorm(torch.autograd.Function):
         s, w, mean, rstd = ctx.saved_tensors
         C = s.shape[-1]
         dx = torch.empty_like(s)
-        dw = torch.empty_like(w)
-        db = torch.empty_like(w)
+        outs = []
+        for p in (w, ctx.b, ctx.rb):
+            if p is None:
+                outs.append((None, None))
+                continue
+            g = _sink(p)
+            outs.append((g, None) if g is not None else (None, torch.empty_like(p)))
+        dw = outs[0][0] if outs[0][0] is not None else outs[0][1]
+        db = outs[1][0] if outs[1][0] is not None else outs[1][1]
+        drb = None
+        if ctx.rb is not None:
+            drb = outs[2][0] if outs[2][0] is not None else outs[2][1]
         C_ = _native.cuda()
-        scratch = _scratch(s.device, C_.ln_bwd_scratch_floats(s.shape[0], C))
+        scratch = _scratch(s.device, C_.ln_bwd_scratch_floats(s.shape[0], C, drb is not None))
         dres = None if ds is None else ds.contiguous().view(-1, C)
         if dy is None:
             dy = torch.zeros_like(s)
-        C_.ln_bwd(dy.contiguous().view(-1, C), s, mean, rstd, w, dres, dx, dw, db, scratch, _counter(s.device))
+        C_.ln_bwd(dy.contiguous().view(-1, C), s, mean, rstd, w, dres, dx, dw, db, scratch, _counter(s.device), drb)
+        for p, (sink, _) in zip((w, ctx.b, ctx.rb), outs):
+            if p is not None and sink is not None:
+                _ready(p)
         dx = dx.view(ctx.shape)
-        return dx, dx, dw, db, None
+        return dx, dx, outs[0][1], outs[1][1], (outs[2][1] if ctx.rb is not None else None), None
 
 
-def residual_layer_norm(x, r, w, b, eps: float = 1e-5):
-    return _ResidualLayerNorm.apply(x, r, w, b, eps)
+def residual_layer_norm(x, r, w, b, eps: float = 1e-5, rbias=None):
+    return _ResidualLayerNorm.apply(x, r, w, b, rbias, eps)
 
 
 class _Gelu(torch.autograd.Function):
@@ -155,6 +322,7 @@ class _Embedding(torch.autograd.Function):
         _native.cuda().embed_fwd(tok, wte, wpe, out, T)
         ctx.save_for_backward(tok)
         ctx.shapes = (wte.shape, wpe.shape)
+        ctx.params = (wte, wpe)
         return out
 
     @staticmethod
@@ -162,10 +330,20 @@ class _Embedding(torch.autograd.Function):
         (tok,) = ctx.saved_tensors
         B, T = tok.shape
         wte_shape, wpe_shape = ctx.shapes
-        dwte = torch.zeros(wte_shape, dtype=dout.dtype, device=dout.device)
-        dwpe = torch.zeros(wpe_shape, dtype=dout.dtype, device=dout.device)
+        wte, wpe = ctx.params
+        # wte's sink already holds the tied head's gradient (written earlier
+        # in backward): the token scatter adds onto it. wpe is overwritten.
+        swte, swpe = _sink(wte), _sink(wpe)
+        dwte = swte if swte is not None else torch.zeros(wte_shape, dtype=dout.dtype, device=dout.device)
+        dwpe = swpe if swpe is not None else torch.zeros(wpe_shape, dtype=dout.dtype, device=dout.device)
         _native.cuda().embed_bwd(tok, dout.contiguous(), dwte, dwpe, B, T)
-        return None, dwte, dwpe
+        if T < wpe_shape[0]:
+            dwpe[T:].zero_()  # positions past T get no gradient this step
+        if swte is not None:
+            _ready(wte)
+        if swpe is not None:
+            _ready(wpe)
+        return None, (None if swte is not None else dwte), (None if swpe is not None else dwpe)
 
 
 def embedding(tok, wte, wpe):

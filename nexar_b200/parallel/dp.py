@@ -39,6 +39,7 @@ class DataParallelTrainer:
             grad_alloc = lambda n: comm.symmetric_empty([n], torch.bfloat16)  # noqa: E731
         self.model = GPT2(cfg, self.device, grad_alloc=grad_alloc, seed=seed)
         flat = self.model.flat
+        flat.grad.zero_()  # padding between parameters is never written
         if self.world > 1:
             # identical start on every rank (ranks share the seed; this makes it exact)
             comm.broadcast(flat.master, root=0)
@@ -62,9 +63,15 @@ class DataParallelTrainer:
             self._bucket_need.append(len(names))
         self._bucket_left: List[int] = list(self._bucket_need)
         self._launched: List[bool] = [False] * len(self.buckets)
-        if self.world > 1:
-            for name, par in self.model.p.items():
-                par.register_post_accumulate_grad_hook(self._make_hook(name))
+        # Backward kernels write each gradient straight into the flat buffer
+        # and then call the parameter's ready callback (no zero-fill, no
+        # accumulation). A parameter that is ever missed falls back to
+        # zero-fill + autograd accumulation for every later step.
+        self._zero_grads = False
+        self._seen = set()
+        for name, par in self.model.p.items():
+            par._nexar_on_ready = self._make_hook(name)
+            par.register_post_accumulate_grad_hook(self._make_acc_hook(name))
         self.static_idx = torch.zeros(self.B, self.T, dtype=torch.int64, device=self.device)
         self.static_tgt = torch.zeros(self.B, self.T, dtype=torch.int64, device=self.device)
         self.static_loss = torch.zeros((), dtype=torch.float32, device=self.device)
@@ -75,12 +82,22 @@ class DataParallelTrainer:
 
     # ---------------------------------------------------------------- hooks
     def _make_hook(self, name):
-        bi = self._bucket_of[name]
+        bi = self._bucket_of.get(name)
 
-        def hook(_param):
+        def hook():
+            self._seen.add(name)
+            if bi is None:
+                return
             self._bucket_left[bi] -= 1
             if self._bucket_left[bi] == 0:
                 self._launch_bucket(bi)
+        return hook
+
+    def _make_acc_hook(self, name):
+        def hook(_param):
+            # autograd accumulated into the flat view: only valid over a zeroed buffer
+            self._zero_grads = True
+            self._make_hook(name)()
         return hook
 
     def _launch_bucket(self, bi):
@@ -96,9 +113,13 @@ class DataParallelTrainer:
         flat = self.model.flat
         self._bucket_left = list(self._bucket_need)
         self._launched = [False] * len(self.buckets)
-        flat.grad.zero_()
+        self._seen = set()
+        if self._zero_grads:
+            flat.grad.zero_()
         loss = self.model(self.static_idx, self.static_tgt, unit_grad=True)
         loss.backward()
+        if len(self._seen) != len(self.model.p):
+            self._zero_grads = True  # some gradient was not written this step: zero-fill from now on
         if self.world > 1:
             for bi, done in enumerate(self._launched):
                 if not done:  # parameters without gradient (none in GPT-2) still need averaging

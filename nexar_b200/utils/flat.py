@@ -65,6 +65,7 @@ class FlatParams:
         for e in self.entries:
             p = torch.nn.Parameter(self.view(self.param_bf16, e.name), requires_grad=True)
             p.grad = self.view(self.grad, e.name)
+            p.main_grad = p.grad  # gradient sink written directly by the backward kernels
             out[e.name] = p
         return out
 

@@ -50,3 +50,77 @@ def test_gemm_strided_operands(cuda0):
     C.gemm(A, B, out)
     torch.testing.assert_close(out.float(), A.float() @ B.float().t(), atol=0.1, rtol=2e-2)
     assert torch.all(out_big[:, 384:] == 0)
+
+
+@pytest.mark.parametrize("a_t,b_t", [(False, False), (False, True), (True, False), (True, True)])
+@pytest.mark.parametrize("M,N,K,splits", [(256, 512, 128, 1), (328, 200, 520, 1), (768, 768, 8192, 0),
+                                          (136, 264, 1000, 3), (2304, 768, 4096, 2)])
+def test_gemm_operand_majors_and_split_k(cuda0, a_t, b_t, M, N, K, splits):
+    """opA / opB given transposed (MN-major smem operands) and split-K, vs fp32.
+
+    A transposed operand's row length (M or N) must be a multiple of 8 (16-byte
+    TMA rows); tile-ragged sizes are covered."""
+    from nexar_b200 import _native, ops
+    C = _native.cuda()
+    g = torch.Generator(device=cuda0).manual_seed(M * 7 + N * 3 + K + 2 * a_t + b_t)
+    A = torch.randn(M, K, device=cuda0, generator=g).to(torch.bfloat16)
+    B = torch.randn(N, K, device=cuda0, generator=g).to(torch.bfloat16)
+    bias = torch.randn(N, device=cuda0, generator=g).to(torch.bfloat16)
+    a_arg = A.t().contiguous() if a_t else A
+    b_arg = B.t().contiguous() if b_t else B
+    out = ops.matmul_nt(a_arg, b_arg, bias=bias, a_t=a_t, b_t=b_t, splits=splits)
+    torch.cuda.synchronize()
+    assert C.gemm_error_flag() == 0
+    ref = A.float() @ B.float().t() + bias.float()
+    torch.testing.assert_close(out.float(), ref, atol=0.05 * (K ** 0.5) / 8, rtol=2e-2)
+
+
+def test_gemm_accumulate_and_split_gelu(cuda0):
+    from nexar_b200 import ops
+    M, N, K = 384, 512, 2048
+    A = torch.randn(M, K, device=cuda0).to(torch.bfloat16)
+    B = (0.03 * torch.randn(N, K, device=cuda0)).to(torch.bfloat16)
+    base = torch.randn(M, N, device=cuda0).to(torch.bfloat16)
+    for sp in (1, 4):
+        out = base.clone()
+        ops.matmul_nt(A, B, out=out, accumulate=True, splits=sp)
+        torch.testing.assert_close(out.float(), base.float() + A.float() @ B.float().t(), atol=0.1, rtol=2e-2)
+        pre = torch.empty_like(out)
+        ops.matmul_nt(A, B, out=out, act=1, pre=pre, splits=sp)
+        ref_pre = A.float() @ B.float().t()
+        torch.testing.assert_close(pre.float(), ref_pre, atol=0.05, rtol=2e-2)
+        torch.testing.assert_close(out.float(), torch.nn.functional.gelu(ref_pre, approximate="tanh"),
+                                   atol=0.05, rtol=2e-2)
+
+
+def test_linear_op_grads_match_fp32(cuda0):
+    """ops.linear backward (MN-major GEMMs, split-K wgrad, colsum bias grad) vs torch autograd."""
+    from nexar_b200 import ops
+    g = torch.Generator(device=cuda0).manual_seed(11)
+    M, Kin, Nout = 1024, 768, 2304
+    x = torch.randn(M, Kin, device=cuda0, generator=g).to(torch.bfloat16).requires_grad_(True)
+    w = (0.02 * torch.randn(Nout, Kin, device=cuda0, generator=g)).to(torch.bfloat16).requires_grad_(True)
+    b = (0.1 * torch.randn(Nout, device=cuda0, generator=g)).to(torch.bfloat16).requires_grad_(True)
+    dy = torch.randn(M, Nout, device=cuda0, generator=g).to(torch.bfloat16)
+    for act in (None, "gelu"):
+        for t in (x, w, b):
+            t.grad = None
+        y = ops.linear(x, w, b, act=act)
+        y.backward(dy)
+        xf, wf, bf = (t.detach().float().requires_grad_(True) for t in (x, w, b))
+        yf = xf @ wf.t() + bf
+        if act:
+            yf = torch.nn.functional.gelu(yf, approximate="tanh")
+        yf.backward(dy.float())
+        torch.testing.assert_close(y.float(), yf.detach(), atol=3e-2, rtol=2e-2)
+        for ours, ref in ((x.grad, xf.grad), (w.grad, wf.grad), (b.grad, bf.grad)):
+            err = (ours.float() - ref).norm() / ref.norm()
+            assert err < 1e-2, (act, err.item())
+
+
+def test_gemm_rejects_unaligned_transposed_operand(cuda0):
+    from nexar_b200 import ops
+    A = torch.randn(520, 333, device=cuda0).to(torch.bfloat16)  # [K, M] with M*2 bytes not a multiple of 16
+    B = torch.randn(200, 520, device=cuda0).to(torch.bfloat16)
+    with pytest.raises(RuntimeError, match="invalid argument"):
+        ops.matmul_nt(A, B, a_t=True, splits=1)

@@ -45,6 +45,42 @@ def test_layernorm_fwd_bwd(cuda0, R, C):
     torch.testing.assert_close(bs.grad.float(), bf.grad, atol=0.25, rtol=3e-2)
 
 
+@pytest.mark.parametrize("R,C", [(8192, 768), (300, 256)])
+def test_residual_layernorm_with_branch_bias(cuda0, R, C):
+    """s = x + r + rb; the backward returns d(rb) = column sums of ds (fused)."""
+    from nexar_b200 import ops
+    torch.manual_seed(1)
+    x, r = _bf(torch.randn(R, C, device=cuda0)), _bf(torch.randn(R, C, device=cuda0))
+    w = _bf(1 + 0.1 * torch.randn(C, device=cuda0))
+    b, rb = _bf(0.1 * torch.randn(C, device=cuda0)), _bf(0.1 * torch.randn(C, device=cuda0))
+    dy, ds = _bf(torch.randn(R, C, device=cuda0)), _bf(torch.randn(R, C, device=cuda0))
+    xs, rs, ws, bs, rbs = (t.clone().requires_grad_(True) for t in (x, r, w, b, rb))
+    s, y = ops.residual_layer_norm(xs, rs, ws, bs, 1e-5, rbias=rbs)
+    torch.autograd.backward([s, y], [ds, dy])
+    xf, rf, wf, bf, rbf = (t.float().clone().requires_grad_(True) for t in (x, r, w, b, rb))
+    sf = xf + rf + rbf
+    yf = torch.nn.functional.layer_norm(sf.to(torch.bfloat16).float(), (C,), wf, bf, 1e-5)
+    torch.autograd.backward([sf, yf], [ds.float(), dy.float()])
+    torch.testing.assert_close(y.float(), yf, atol=3e-2, rtol=2e-2)
+    torch.testing.assert_close(xs.grad.float(), xf.grad, atol=6e-2, rtol=3e-2)
+    for ours, ref in ((ws.grad, wf.grad), (bs.grad, bf.grad), (rbs.grad, rbf.grad)):
+        assert ((ours.float() - ref).norm() / ref.norm()).item() < 1e-2
+
+
+@pytest.mark.parametrize("R,C", [(8192, 2304), (1000, 768), (5, 64)])
+def test_colsum(cuda0, R, C):
+    from nexar_b200 import ops
+    x = _bf(torch.randn(R, C, device=cuda0))
+    out = torch.empty(C, device=cuda0, dtype=torch.bfloat16)
+    ops.colsum(x, out)
+    ref = x.float().sum(0)
+    torch.testing.assert_close(out.float(), ref, atol=0.05 * math.sqrt(R) / 8 + 1e-2, rtol=1e-2)
+    base = _bf(torch.randn(C, device=cuda0))
+    out2 = base.clone()
+    ops.colsum(x, out2, accumulate=True)
+    torch.testing.assert_close(out2.float(), ref + base.float(), atol=0.05 * math.sqrt(R) / 8 + 1e-2, rtol=1e-2)
+
+
 def test_plain_layernorm(cuda0):
     from nexar_b200 import ops
     x = _bf(torch.randn(128, 768, device=cuda0))
