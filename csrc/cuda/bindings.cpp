@@ -15,6 +15,7 @@
 #include "ops_api.h"
 #include "gemm_api.h"
 #include "moe_api.h"
+#include "nvls_api.h"
 
 namespace nexar {
 
@@ -97,6 +98,19 @@ void all_reduce(const CommPtr& c, const at::Tensor& in, const at::Tensor& out, i
     count_launch(1);
     return;
   }
+  // NVLS (switch-side reduction) for large messages; in place with no staging
+  // when the tensor lives in the NVLS region.
+  const bool nvls_ok = dti == dto && nvls_can_reduce(c->dev(), dti, op, in.data_ptr(), out.data_ptr(), bytes);
+  if (nvls_ok && (algo == kAlgoNvls || (algo == kAlgoAuto && bytes >= c->nvls_min_bytes))) {
+    const long long noff = in.data_ptr() == out.data_ptr() ? c->nvls_offset(in.data_ptr(), bytes) : -1;
+    check_launch(launch_all_reduce_nvls(c->dev(), in.data_ptr(), out.data_ptr(), dti, bytes, (float)scale, noff,
+                                        c->max_blocks, s),
+                 "all_reduce(nvls)");
+    count_launch(1);
+    return;
+  }
+  TORCH_CHECK(algo != kAlgoNvls, "all_reduce: NVLS path unavailable for this message (needs an active NVLS region, "
+              "Sum of f32/bf16/f16, 16-byte aligned sizes and pointers)");
   long long sym = -1;
   if (algo == kAlgoAuto) algo = (long long)bytes <= oneshot_max_bytes ? kAlgoOneShot : kAlgoTwoShot;
   // Zero-copy in place only for two-shot: there rank r alone reads and writes
@@ -131,8 +145,16 @@ void reduce_scatter(const CommPtr& c, const at::Tensor& in, const at::Tensor& ou
   const int dti = dtype_code(in.scalar_type()), dto = dtype_code(out.scalar_type());
   const unsigned long long count = out.numel();
   const int esi = in.element_size(), eso = out.element_size();
-  const unsigned long long per = round_down(c->slot_bytes() / ((unsigned long long)N * std::max(esi, eso)), 256);
   cudaStream_t s = cur_stream(*c);
+  if (dti == dto && N > 1 && count * esi * N >= c->nvls_min_bytes &&
+      nvls_can_reduce(c->dev(), dti, op, in.data_ptr(), out.data_ptr(), count * esi)) {
+    check_launch(launch_reduce_scatter_nvls(c->dev(), in.data_ptr(), out.data_ptr(), dti, count * esi, (float)scale,
+                                            c->max_blocks, s),
+                 "reduce_scatter(nvls)");
+    count_launch(1);
+    return;
+  }
+  const unsigned long long per = round_down(c->slot_bytes() / ((unsigned long long)N * std::max(esi, eso)), 256);
   for (unsigned long long off = 0; off < count; off += per) {
     const unsigned long long m = std::min(per, count - off);
     check_launch(launch_reduce_scatter(c->dev(), (const char*)in.data_ptr() + off * esi,
@@ -153,8 +175,14 @@ void all_gather(const CommPtr& c, const at::Tensor& in, const at::Tensor& out) {
   const int dt = dtype_code(in.scalar_type());
   const unsigned long long count = in.numel();
   const int es = in.element_size();
-  const unsigned long long per = round_down(c->slot_bytes() / es, 256);
   cudaStream_t s = cur_stream(*c);
+  if (N > 1 && count * es * N >= c->nvls_min_bytes && nvls_can_move(c->dev(), in.data_ptr(), out.data_ptr(), count * es)) {
+    check_launch(launch_all_gather_nvls(c->dev(), in.data_ptr(), out.data_ptr(), count * es, c->max_blocks, s),
+                 "all_gather(nvls)");
+    count_launch(1);
+    return;
+  }
+  const unsigned long long per = round_down(c->slot_bytes() / es, 256);
   for (unsigned long long off = 0; off < count; off += per) {
     const unsigned long long m = std::min(per, count - off);
     check_launch(launch_all_gather(c->dev(), (const char*)in.data_ptr() + off * es,
@@ -196,8 +224,14 @@ void broadcast(const CommPtr& c, const at::Tensor& in, const at::Tensor& out, in
   const int dt = dtype_code(in.scalar_type());
   const unsigned long long n = in.numel();
   const int es = in.element_size();
-  const unsigned long long per = round_down(c->slot_bytes() / es, 256);
   cudaStream_t s = cur_stream(*c);
+  if (c->world() > 1 && n * es >= c->nvls_min_bytes && nvls_can_move(c->dev(), in.data_ptr(), out.data_ptr(), n * es)) {
+    check_launch(launch_broadcast_nvls(c->dev(), in.data_ptr(), out.data_ptr(), n * es, root, c->max_blocks, s),
+                 "broadcast(nvls)");
+    count_launch(1);
+    return;
+  }
+  const unsigned long long per = round_down(c->slot_bytes() / es, 256);
   for (unsigned long long off = 0; off < n; off += per) {
     const unsigned long long m = std::min(per, n - off);
     check_launch(launch_broadcast(c->dev(), (const char*)in.data_ptr() + off * es,
@@ -321,6 +355,17 @@ at::Tensor symmetric_tensor(const CommPtr& c, unsigned long long offset, std::ve
   return torch::from_blob(c->local_base() + offset, shape, [keep](void*) {}, opts);
 }
 
+at::Tensor nvls_tensor(const CommPtr& c, unsigned long long offset, std::vector<int64_t> shape, int dtype) {
+  TORCH_CHECK(c->nvls_active(), "nvls_tensor: NVLS region not active");
+  at::ScalarType st = scalar_type_of(dtype);
+  int64_t numel = 1;
+  for (auto d : shape) numel *= d;
+  TORCH_CHECK(offset + numel * c10::elementSize(st) <= c->nvls_bytes(), "nvls_tensor out of region range");
+  CommPtr keep = c;
+  auto opts = at::TensorOptions().dtype(st).device(at::kCUDA, c->device());
+  return torch::from_blob(c->nvls_local() + offset, shape, [keep](void*) {}, opts);
+}
+
 py::dict status_dict(const CommPtr& c) {
   DeviceStatus s = c->status();
   py::dict d;
@@ -410,6 +455,20 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
       .def_property_readonly("connected", &DeviceComm::connected)
       .def_property("timeout_us", &DeviceComm::timeout_us, &DeviceComm::set_timeout_us)
       .def_readwrite("max_blocks", &DeviceComm::max_blocks)
+      .def_readwrite("nvls_min_bytes", &DeviceComm::nvls_min_bytes)
+      .def("nvls_supported", &DeviceComm::nvls_supported)
+      .def("nvls_create", &DeviceComm::nvls_create)
+      .def("nvls_import", &DeviceComm::nvls_import)
+      .def("nvls_add_device", &DeviceComm::nvls_add_device)
+      .def("nvls_bind_map", &DeviceComm::nvls_bind_map)
+      .def("nvls_active", &DeviceComm::nvls_active)
+      .def("nvls_bytes", &DeviceComm::nvls_bytes)
+      .def("nvls_alloc", &DeviceComm::nvls_alloc, py::arg("bytes"), py::arg("align") = 256)
+      .def("nvls_reset", &DeviceComm::nvls_reset)
+      .def("nvls_release", &DeviceComm::nvls_release)
+      .def("nvls_offset", [](const DeviceComm& c, const at::Tensor& t) {
+        return c.nvls_offset(t.data_ptr(), (uint64_t)t.numel() * t.element_size());
+      })
       .def("peer_ptr", [](const DeviceComm& c, int p) { return (uint64_t)c.peer_base(p); })
       .def("local_ptr", [](const DeviceComm& c) { return (uint64_t)c.local_base(); });
   m.def("all_reduce", &all_reduce);
@@ -424,6 +483,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("barrier", &barrier);
   m.def("reduce_inplace", &reduce_inplace);
   m.def("symmetric_tensor", &symmetric_tensor);
+  m.def("nvls_tensor", &nvls_tensor);
+  m.def("nvls_stage_bytes", []() { return (unsigned long long)kNvlsStageBytes; });
   m.def("launch_count", []() { return g_launches.load(); });
   m.def("gemm_reduce_scatter", &gemm_rs);
   m.def("moe_route", &moe_route_op);

@@ -57,6 +57,19 @@ struct CommDev {
   unsigned long long slot_bytes;
   int rank;
   int world;
+  // NVLS (NVSwitch multicast) region; null when unavailable. nvls_uc is this
+  // rank's own mapping of its physical backing, nvls_mc the multicast mapping
+  // through which multimem loads reduce over all ranks and multimem stores
+  // reach every rank. Layout: [0, kNvlsSignalBytes) per-block signal
+  // counters, then per-block staging chunks, then user allocations.
+  char* nvls_uc;
+  char* nvls_mc;
+  unsigned long long nvls_bytes;
+  unsigned int* nvls_seq;       // local per-block round counters
 };
+
+constexpr unsigned long long kNvlsSignalBytes = 1ull << 20;
+constexpr unsigned long long kNvlsChunkBytes = 512ull << 10;  // staging bytes per block per round
+constexpr unsigned long long kNvlsStageBytes = (unsigned long long)kMaxBlocks * kNvlsChunkBytes;
 
 }  // namespace nexar

@@ -60,6 +60,9 @@ DeviceComm::DeviceComm(int rank, int world, int device, uint64_t heap_bytes, uin
   dev_.slot_bytes = slot_bytes_;
   dev_.rank = rank_;
   dev_.world = world_;
+  dev_.nvls_uc = dev_.nvls_mc = nullptr;
+  dev_.nvls_bytes = 0;
+  dev_.nvls_seq = nullptr;
   if (world_ == 1) connected_ = true;
 }
 
@@ -68,6 +71,7 @@ DeviceComm::~DeviceComm() {
   cudaGetDevice(&cur);
   cudaSetDevice(device_);
   cudaDeviceSynchronize();
+  nvls_release();
   for (char* p : opened_) cudaIpcCloseMemHandle(p);
   if (base_) cudaFree(base_);
   if (ctrl_) cudaFree(ctrl_);

@@ -63,8 +63,35 @@ class DeviceComm {
   uint64_t timeout_us() const { return dev_.timeout_ns / 1000ull; }
 
   unsigned int max_blocks = 148;
+  // Messages of at least this many bytes take the NVLS path when it applies.
+  uint64_t nvls_min_bytes = 4ull << 20;
+
+  // ---- NVLS (NVSwitch multicast), multi-process only; see nvls.cpp.
+  // Setup order on every rank: rank 0 nvls_create() and hands the returned
+  // POSIX fd to the others, which nvls_import() it; then every rank
+  // nvls_add_device(); after ALL ranks added their device, every rank
+  // nvls_bind_map(). Ranks must run these steps in lock step.
+  bool nvls_supported() const;
+  int nvls_create(uint64_t bytes);
+  void nvls_import(int fd, uint64_t bytes);
+  void nvls_add_device();
+  void nvls_bind_map();
+  bool nvls_active() const { return dev_.nvls_mc != nullptr; }
+  uint64_t nvls_bytes() const { return dev_.nvls_bytes; }
+  char* nvls_local() const { return dev_.nvls_uc; }
+  uint64_t nvls_alloc(uint64_t bytes, uint64_t align);
+  void nvls_reset();
+  // Offset of [ptr, ptr+bytes) inside the NVLS user region, else -1.
+  long long nvls_offset(const void* ptr, uint64_t bytes) const;
+  // Unmap and release everything NVLS (also used when setup failed on a peer).
+  void nvls_release();
 
  private:
+  uint64_t nvls_size_ = 0, nvls_user_off_ = 0, nvls_user_next_ = 0;
+  unsigned long long nvls_mc_handle_ = 0, nvls_phys_handle_ = 0;
+  bool nvls_bound_ = false;
+  int nvls_fd_ = -1;
+
   int rank_, world_, device_;
   uint64_t heap_bytes_, slot_bytes_;
   uint64_t user_off_ = 0, user_next_ = 0;

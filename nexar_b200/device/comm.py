@@ -90,6 +90,13 @@ class DeviceCommunicator:
         handles = exchange(self._comm.export_handle())
         if world_size > 1:
             self._comm.connect(list(handles))
+        # NVSwitch multicast region: large all-reduce / reduce-scatter /
+        # all-gather / broadcast reduce and replicate inside the switch.
+        self._comm.nvls_min_bytes = _env_int("NEXAR_NVLS_MIN_BYTES", 4 << 20)
+        nvls_user = _env_int("NEXAR_NVLS_USER_BYTES", 1 << 30)
+        from .nvls import setup_nvls
+        self.nvls = setup_nvls(self._comm, rank, world_size, exchange,
+                               (1 << 20) + C.nvls_stage_bytes() + nvls_user)
         self._barrier = barrier
         if barrier is not None:
             barrier()  # every rank has mapped its peers before any kernel runs
@@ -126,20 +133,28 @@ class DeviceCommunicator:
         return cls(client.rank, client.world_size, dev, exchange, barrier=client.barrier, **kw)
 
     # ----------------------------------------------------------- memory
-    def symmetric_empty(self, shape: Sequence[int], dtype=torch.bfloat16, align: int = 256) -> torch.Tensor:
-        """Allocate a tensor inside the symmetric heap (collective: same order on all ranks).
+    def symmetric_empty(self, shape: Sequence[int], dtype=torch.bfloat16, align: int = 256,
+                        nvls: bool = False) -> torch.Tensor:
+        """Allocate a tensor in symmetric memory (collective: same order and sizes on all ranks).
 
-        Collectives on such tensors run in place with no staging copies.
+        Default: the peer-mapped heap. Peers can address the tensor directly
+        (fused kernels store into it) and the two-shot all-reduce runs on it
+        in place. ``nvls=True`` (when the NVLS region is active) places it in
+        the multicast-bound region instead: large all-reduces on it run in
+        place inside the NVSwitch, but peers cannot address it directly.
         """
         numel = 1
         for d in shape:
             numel *= int(d)
         nbytes = numel * torch.empty((), dtype=dtype).element_size()
+        if self.nvls and nvls:
+            off = self._comm.nvls_alloc(nbytes, align)
+            return self._C.nvls_tensor(self._comm, off, list(shape), int(DataType.from_torch(dtype)))
         off = self._comm.alloc_symmetric(nbytes, align)
         return self._C.symmetric_tensor(self._comm, off, list(shape), int(DataType.from_torch(dtype)))
 
     def is_symmetric(self, t: torch.Tensor) -> bool:
-        return self._comm.symmetric_offset(t) >= 0
+        return self._comm.symmetric_offset(t) >= 0 or (self.nvls and self._comm.nvls_offset(t) >= 0)
 
     @property
     def native(self):

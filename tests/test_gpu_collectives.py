@@ -203,3 +203,98 @@ def test_device_wait_timeout_reports_error(cuda0):
     # the context still works
     y = torch.ones(10, device=cuda0) * 2
     assert float(y.sum()) == 20.0
+
+
+def _nvls_worker(rank, world, port, results):
+    """NVLS paths forced for every 16-byte-aligned message (nvls_min_bytes = 0)."""
+    import torch.distributed as dist
+    from nexar_b200.device import DeviceCommunicator
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
+    dev = torch.device("cuda", rank)
+    comm = DeviceCommunicator.from_torch(timeout_us=5_000_000, slot_bytes=8 << 20)
+    errors = []
+    if not comm.nvls:
+        results[rank] = ("no-nvls", [])
+        dist.barrier()
+        dist.destroy_process_group()
+        return
+    comm.native.nvls_min_bytes = 0
+
+    def check(name, got, want, **tol):
+        try:
+            torch.testing.assert_close(got.cpu().double(), want.double(), **tol)
+        except AssertionError as e:
+            errors.append(f"{name}: {str(e)[:300]}")
+
+    # staged all-reduce, several sizes in a row (round counters, slot reuse across calls)
+    for rep in range(2):
+        for dtype in (torch.float32, torch.bfloat16, torch.float16):
+            for n in (8, 4096, 1 << 20, 3 * (1 << 20) + 64, 40 << 20 if dtype != torch.float32 else 24 << 20):
+                xs = [_data(r, n, dtype, seed=rep) for r in range(world)]
+                t = xs[rank].to(dev)
+                out = torch.empty_like(t)
+                comm.all_reduce(t, out=out, scale=1.0 / world)
+                check(f"nvls all_reduce {dtype} n={n}", out, _oracle_reduce(xs, "sum") / world, **_tol(dtype, world))
+    # in place on an NVLS-resident tensor (no staging)
+    n = 5 * (1 << 20) + 8
+    xs = [_data(r, n, torch.bfloat16, seed=7) for r in range(world)]
+    sym = comm.symmetric_empty([n], torch.bfloat16, nvls=True)
+    assert comm.native.nvls_offset(sym) >= 0
+    for _ in range(3):
+        sym.copy_(xs[rank].to(dev))
+        comm.all_reduce(sym, scale=0.5)
+        check("nvls all_reduce in place", sym, _oracle_reduce(xs, "sum") * 0.5, **_tol(torch.bfloat16, world))
+    # CUDA graph replay of an in-place NVLS all-reduce
+    g = torch.cuda.CUDAGraph()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        comm.all_reduce(sym)
+    torch.cuda.current_stream().wait_stream(s)
+    with torch.cuda.graph(g):
+        comm.all_reduce(sym)
+    for _ in range(3):
+        sym.copy_(xs[rank].to(dev))
+        g.replay()
+        torch.cuda.synchronize()
+        check("nvls all_reduce graph replay", sym, _oracle_reduce(xs, "sum"), **_tol(torch.bfloat16, world))
+    del g
+    # reduce-scatter / all-gather / broadcast
+    for dtype in (torch.float32, torch.bfloat16):
+        for count in (8, 1 << 16, (1 << 20) + 8):
+            xs = [_data(r, count * world, dtype, seed=3) for r in range(world)]
+            out = comm.reduce_scatter(xs[rank].to(dev))
+            check(f"nvls reduce_scatter {dtype} {count}", out,
+                  _oracle_reduce(xs, "sum")[rank * count:(rank + 1) * count], **_tol(dtype, world))
+            out = comm.all_gather(xs[rank][:count].to(dev))
+            check(f"nvls all_gather {dtype} {count}", out, torch.cat([xs[r][:count] for r in range(world)]),
+                  atol=0, rtol=0)
+            for root in (0, world - 1):
+                t = xs[rank][:count].clone().to(dev)
+                comm.broadcast(t, root=root)
+                check(f"nvls broadcast {dtype} {count} root{root}", t, xs[root][:count], atol=0, rtol=0)
+    torch.cuda.synchronize()
+    try:
+        comm.check()
+    except Exception as e:  # noqa: BLE001
+        errors.append(f"status: {e}")
+    results[rank] = ("nvls", errors)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.multigpu
+@pytest.mark.skipif(gpu_count() < 2, reason="needs >= 2 GPUs")
+def test_nvls_collectives_multi_gpu():
+    world = gpu_count()
+    port = _free_port()
+    ctx = mp.get_context("spawn")
+    results = ctx.Manager().dict()
+    mp.start_processes(_nvls_worker, args=(world, port, results), nprocs=world, start_method="spawn", join=True)
+    modes = {results[r][0] for r in range(world)}
+    assert len(modes) == 1, modes
+    if modes == {"no-nvls"}:
+        pytest.skip("NVSwitch multicast not available on this box")
+    for r in range(world):
+        assert results[r][1] == [], f"rank {r}: {results[r][1]}"
