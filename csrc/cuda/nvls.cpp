@@ -95,12 +95,28 @@ CUmulticastObjectProp mc_prop(int world, uint64_t bytes) {
   return p;
 }
 
-uint64_t nvls_granule(const DriverApi& a, int world) {
+CUmemAllocationProp phys_prop(int device) {
+  CUmemAllocationProp prop;
+  std::memset(&prop, 0, sizeof(prop));
+  prop.type = CU_MEM_ALLOCATION_TYPE_PINNED;
+  prop.location.type = CU_MEM_LOCATION_TYPE_DEVICE;
+  prop.location.id = device;
+  // Backing bound to a multicast object must be shareable the same way.
+  prop.requestedHandleTypes = CU_MEM_HANDLE_TYPE_POSIX_FILE_DESCRIPTOR;
+  return prop;
+}
+
+// Region size: a multiple of both the multicast and the allocation
+// granularity (powers of two), fixed before the multicast object exists.
+uint64_t nvls_granule(const DriverApi& a, int world, int device) {
   CUmulticastObjectProp p = mc_prop(world, 0);
-  size_t g = 0;
+  size_t g = 0, ag = 0;
   check_cu(a.MulticastGetGranularity(&g, &p, CU_MULTICAST_GRANULARITY_RECOMMENDED), "cuMulticastGetGranularity");
+  CUmemAllocationProp prop = phys_prop(device);
+  check_cu(a.MemGetAllocationGranularity(&ag, &prop, CU_MEM_ALLOC_GRANULARITY_MINIMUM),
+           "cuMemGetAllocationGranularity");
   if (g == 0) g = 2ull << 20;
-  return g;
+  return g > ag ? g : ag;
 }
 }  // namespace
 
@@ -120,7 +136,7 @@ int DeviceComm::nvls_create(uint64_t bytes) {
   const DriverApi& a = api();
   if (!a.ok) throw std::runtime_error("nexar_b200: CUDA driver multicast API unavailable");
   if (nvls_mc_handle_) throw std::runtime_error("nexar_b200: NVLS region already created");
-  nvls_size_ = round_up(bytes, nvls_granule(a, world_));
+  nvls_size_ = round_up(bytes, nvls_granule(a, world_, device_));
   CUmulticastObjectProp p = mc_prop(world_, nvls_size_);
   CUmemGenericAllocationHandle h;
   check_cu(a.MulticastCreate(&h, &p), "cuMulticastCreate");
@@ -136,7 +152,7 @@ void DeviceComm::nvls_import(int fd, uint64_t bytes) {
   const DriverApi& a = api();
   if (!a.ok) throw std::runtime_error("nexar_b200: CUDA driver multicast API unavailable");
   if (nvls_mc_handle_) throw std::runtime_error("nexar_b200: NVLS region already created");
-  nvls_size_ = round_up(bytes, nvls_granule(a, world_));
+  nvls_size_ = round_up(bytes, nvls_granule(a, world_, device_));
   CUmemGenericAllocationHandle h;
   check_cu(a.MemImportFromShareableHandle(&h, reinterpret_cast<void*>(static_cast<uintptr_t>(fd)),
                                           CU_MEM_HANDLE_TYPE_POSIX_FILE_DESCRIPTOR),
@@ -159,15 +175,10 @@ void DeviceComm::nvls_bind_map() {
   int cur = -1;
   cudaGetDevice(&cur);
   check_cuda(cudaSetDevice(device_), "cudaSetDevice");
-  CUmemAllocationProp prop;
-  std::memset(&prop, 0, sizeof(prop));
-  prop.type = CU_MEM_ALLOCATION_TYPE_PINNED;
-  prop.location.type = CU_MEM_LOCATION_TYPE_DEVICE;
-  prop.location.id = device_;
+  CUmemAllocationProp prop = phys_prop(device_);
   size_t ag = 0;
   check_cu(a.MemGetAllocationGranularity(&ag, &prop, CU_MEM_ALLOC_GRANULARITY_MINIMUM),
            "cuMemGetAllocationGranularity");
-  nvls_size_ = round_up(nvls_size_, ag);
   CUmemGenericAllocationHandle phys;
   check_cu(a.MemCreate(&phys, nvls_size_, &prop, 0), "cuMemCreate(NVLS backing)");
   nvls_phys_handle_ = phys;

@@ -94,9 +94,10 @@ class DeviceCommunicator:
         # all-gather / broadcast reduce and replicate inside the switch.
         self._comm.nvls_min_bytes = _env_int("NEXAR_NVLS_MIN_BYTES", 4 << 20)
         nvls_user = _env_int("NEXAR_NVLS_USER_BYTES", 1 << 30)
-        from .nvls import setup_nvls
-        self.nvls = setup_nvls(self._comm, rank, world_size, exchange,
-                               (1 << 20) + C.nvls_stage_bytes() + nvls_user)
+        from . import nvls as _nvls
+        self.nvls = _nvls.setup_nvls(self._comm, rank, world_size, exchange,
+                                     (1 << 20) + C.nvls_stage_bytes() + nvls_user)
+        self.nvls_reason = _nvls.LAST_REASON
         self._barrier = barrier
         if barrier is not None:
             barrier()  # every rank has mapped its peers before any kernel runs

@@ -24,22 +24,45 @@ def _all_ok(exchange: Callable[[bytes], List[bytes]], ok: bool) -> bool:
     return all(s == b"1" for s in exchange(b"1" if ok else b"0"))
 
 
+LAST_REASON = ""
+
+
+def _fail(native, why: str, release: bool = True) -> bool:
+    global LAST_REASON
+    LAST_REASON = why
+    if release:
+        native.nvls_release()
+    if os.environ.get("NEXAR_NVLS_DEBUG"):
+        print(f"nexar_b200: NVLS disabled: {why}", flush=True)
+    return False
+
+
 def setup_nvls(native, rank: int, world: int, exchange: Callable[[bytes], List[bytes]], nbytes: int,
                timeout_s: float = 120.0) -> bool:
-    """Create, share, bind and map the multicast region. Collective over all ranks."""
+    """Create, share, bind and map the multicast region. Collective over all ranks.
+
+    Returns True when active on every rank; otherwise False on every rank and
+    ``LAST_REASON`` says why.
+    """
+    global LAST_REASON
     want = os.environ.get("NEXAR_NVLS", "1") != "0" and world > 1
     supported = False
+    why = "disabled (NEXAR_NVLS=0 or a single rank)" if not want else ""
     if want:
         try:
             supported = bool(native.nvls_supported())
-        except Exception:  # noqa: BLE001 - any driver error means "not available"
-            supported = False
+            if not supported:
+                why = "device reports no multicast / POSIX-fd handle support"
+        except Exception as e:  # noqa: BLE001 - any driver error means "not available"
+            supported, why = False, f"capability query failed: {e}"
     # One rank per process: a descriptor handoff to oneself (a single process
     # posing as several ranks) has nobody on the other end.
     votes = exchange(f"{int(supported)}:{os.getpid()}".encode())
     pids = {v.split(b":")[1] for v in votes}
-    if not all(v.startswith(b"1:") for v in votes) or len(pids) != world:
-        return False
+    if not all(v.startswith(b"1:") for v in votes):
+        return _fail(native, why or "unsupported on a peer rank", release=False)
+    if len(pids) != world:
+        return _fail(native, "ranks share a process", release=False)
     err = None
     if rank == 0:
         srv = None
@@ -80,20 +103,18 @@ def setup_nvls(native, rank: int, world: int, exchange: Callable[[bytes], List[b
             except Exception as e:  # noqa: BLE001
                 err = e
     if not _all_ok(exchange, err is None):
-        native.nvls_release()
-        return False
+        return _fail(native, f"multicast object create/share failed: {err}")
     try:
         native.nvls_add_device()
     except Exception as e:  # noqa: BLE001
         err = e
     if not _all_ok(exchange, err is None):  # every device added before anyone binds
-        native.nvls_release()
-        return False
+        return _fail(native, f"cuMulticastAddDevice failed: {err}")
     try:
         native.nvls_bind_map()
     except Exception as e:  # noqa: BLE001
         err = e
     if not _all_ok(exchange, err is None):
-        native.nvls_release()
-        return False
+        return _fail(native, f"bind/map failed: {err}")
+    LAST_REASON = "active"
     return True

@@ -215,7 +215,7 @@ def _nvls_worker(rank, world, port, results):
     comm = DeviceCommunicator.from_torch(timeout_us=5_000_000, slot_bytes=8 << 20)
     errors = []
     if not comm.nvls:
-        results[rank] = ("no-nvls", [])
+        results[rank] = ("no-nvls", [comm.nvls_reason])
         dist.barrier()
         dist.destroy_process_group()
         return
@@ -295,6 +295,6 @@ def test_nvls_collectives_multi_gpu():
     modes = {results[r][0] for r in range(world)}
     assert len(modes) == 1, modes
     if modes == {"no-nvls"}:
-        pytest.skip("NVSwitch multicast not available on this box")
+        pytest.skip(f"NVSwitch multicast not available on this box: {results[0][1]}")
     for r in range(world):
         assert results[r][1] == [], f"rank {r}: {results[r][1]}"
