@@ -101,8 +101,9 @@ void all_reduce(const CommPtr& c, const at::Tensor& in, const at::Tensor& out, i
   // NVLS (switch-side reduction) for large messages; in place with no staging
   // when the tensor lives in the NVLS region.
   const bool nvls_ok = dti == dto && nvls_can_reduce(c->dev(), dti, op, in.data_ptr(), out.data_ptr(), bytes);
-  if (nvls_ok && (algo == kAlgoNvls || (algo == kAlgoAuto && bytes >= c->nvls_min_bytes))) {
-    const long long noff = in.data_ptr() == out.data_ptr() ? c->nvls_offset(in.data_ptr(), bytes) : -1;
+  const long long noff = in.data_ptr() == out.data_ptr() ? c->nvls_offset(in.data_ptr(), bytes) : -1;
+  const uint64_t nvls_from = noff >= 0 ? (256ull << 10) : c->nvls_min_bytes;  // in place: no copies to amortise
+  if (nvls_ok && (algo == kAlgoNvls || (algo == kAlgoAuto && bytes >= nvls_from))) {
     check_launch(launch_all_reduce_nvls(c->dev(), in.data_ptr(), out.data_ptr(), dti, bytes, (float)scale, noff,
                                         c->max_blocks, s),
                  "all_reduce(nvls)");
@@ -146,10 +147,11 @@ void reduce_scatter(const CommPtr& c, const at::Tensor& in, const at::Tensor& ou
   const unsigned long long count = out.numel();
   const int esi = in.element_size(), eso = out.element_size();
   cudaStream_t s = cur_stream(*c);
-  if (dti == dto && N > 1 && count * esi * N >= c->nvls_min_bytes &&
+  const long long in_sym = c->nvls_offset(in.data_ptr(), count * esi * N);
+  if (dti == dto && N > 1 && (in_sym >= 0 || count * esi * N >= c->nvls_min_rs_bytes) &&
       nvls_can_reduce(c->dev(), dti, op, in.data_ptr(), out.data_ptr(), count * esi)) {
     check_launch(launch_reduce_scatter_nvls(c->dev(), in.data_ptr(), out.data_ptr(), dti, count * esi, (float)scale,
-                                            c->max_blocks, s),
+                                            in_sym, c->max_blocks, s),
                  "reduce_scatter(nvls)");
     count_launch(1);
     return;
@@ -176,8 +178,10 @@ void all_gather(const CommPtr& c, const at::Tensor& in, const at::Tensor& out) {
   const unsigned long long count = in.numel();
   const int es = in.element_size();
   cudaStream_t s = cur_stream(*c);
-  if (N > 1 && count * es * N >= c->nvls_min_bytes && nvls_can_move(c->dev(), in.data_ptr(), out.data_ptr(), count * es)) {
-    check_launch(launch_all_gather_nvls(c->dev(), in.data_ptr(), out.data_ptr(), count * es, c->max_blocks, s),
+  const long long out_sym = c->nvls_offset(out.data_ptr(), count * es * N);
+  if (N > 1 && (out_sym >= 0 || count * es * N >= c->nvls_min_ag_bytes) &&
+      nvls_can_move(c->dev(), in.data_ptr(), out.data_ptr(), count * es)) {
+    check_launch(launch_all_gather_nvls(c->dev(), in.data_ptr(), out.data_ptr(), count * es, out_sym, c->max_blocks, s),
                  "all_gather(nvls)");
     count_launch(1);
     return;
@@ -225,8 +229,11 @@ void broadcast(const CommPtr& c, const at::Tensor& in, const at::Tensor& out, in
   const unsigned long long n = in.numel();
   const int es = in.element_size();
   cudaStream_t s = cur_stream(*c);
-  if (c->world() > 1 && n * es >= c->nvls_min_bytes && nvls_can_move(c->dev(), in.data_ptr(), out.data_ptr(), n * es)) {
-    check_launch(launch_broadcast_nvls(c->dev(), in.data_ptr(), out.data_ptr(), n * es, root, c->max_blocks, s),
+  // Every rank must pass an NVLS-resident output, or none (same path on all ranks).
+  const long long out_sym = c->nvls_offset(out.data_ptr(), n * es);
+  if (c->world() > 1 && (out_sym >= 0 || n * es >= c->nvls_min_bcast_bytes) &&
+      nvls_can_move(c->dev(), in.data_ptr(), out.data_ptr(), n * es)) {
+    check_launch(launch_broadcast_nvls(c->dev(), in.data_ptr(), out.data_ptr(), n * es, root, out_sym, c->max_blocks, s),
                  "broadcast(nvls)");
     count_launch(1);
     return;
@@ -456,6 +463,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
       .def_property("timeout_us", &DeviceComm::timeout_us, &DeviceComm::set_timeout_us)
       .def_readwrite("max_blocks", &DeviceComm::max_blocks)
       .def_readwrite("nvls_min_bytes", &DeviceComm::nvls_min_bytes)
+      .def_readwrite("nvls_min_rs_bytes", &DeviceComm::nvls_min_rs_bytes)
+      .def_readwrite("nvls_min_ag_bytes", &DeviceComm::nvls_min_ag_bytes)
+      .def_readwrite("nvls_min_bcast_bytes", &DeviceComm::nvls_min_bcast_bytes)
       .def("nvls_supported", &DeviceComm::nvls_supported)
       .def("nvls_create", &DeviceComm::nvls_create)
       .def("nvls_import", &DeviceComm::nvls_import)

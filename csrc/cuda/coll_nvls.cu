@@ -145,24 +145,25 @@ NEXAR_D void copy_vec(uint4* __restrict__ dst, const uint4* __restrict__ src, un
   for (; i < nv; i += kNvlsThreads) dst[i] = src[i];
 }
 
+// Switch round trips are long: every loop keeps kUnroll multimem
+// operations per thread in flight.
+constexpr int kUnroll = 8;
+
 // mc[v] = scale * sum over ranks of mc[v] for v in [lo, hi) (vectors).
 template <typename T>
 NEXAR_D void reduce_bcast_vec(char* mc, unsigned long long lo, unsigned long long hi, float scale) {
   uint4* p = reinterpret_cast<uint4*>(mc);
   unsigned long long i = lo + threadIdx.x;
-  for (; i + 3 * kNvlsThreads < hi; i += 4 * kNvlsThreads) {
-    uint4 a = MM<T>::ld_reduce(p + i), b = MM<T>::ld_reduce(p + i + kNvlsThreads);
-    uint4 d = MM<T>::ld_reduce(p + i + 2 * kNvlsThreads), e = MM<T>::ld_reduce(p + i + 3 * kNvlsThreads);
+  for (; i + (kUnroll - 1) * kNvlsThreads < hi; i += kUnroll * kNvlsThreads) {
+    uint4 v[kUnroll];
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) v[u] = MM<T>::ld_reduce(p + i + u * kNvlsThreads);
     if (scale != 1.f) {
-      a = MM<T>::scale(a, scale);
-      b = MM<T>::scale(b, scale);
-      d = MM<T>::scale(d, scale);
-      e = MM<T>::scale(e, scale);
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) v[u] = MM<T>::scale(v[u], scale);
     }
-    MM<T>::st(p + i, a);
-    MM<T>::st(p + i + kNvlsThreads, b);
-    MM<T>::st(p + i + 2 * kNvlsThreads, d);
-    MM<T>::st(p + i + 3 * kNvlsThreads, e);
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) MM<T>::st(p + i + u * kNvlsThreads, v[u]);
   }
   for (; i < hi; i += kNvlsThreads) {
     uint4 a = MM<T>::ld_reduce(p + i);
@@ -175,7 +176,15 @@ NEXAR_D void reduce_bcast_vec(char* mc, unsigned long long lo, unsigned long lon
 template <typename T>
 NEXAR_D void reduce_to_local(uint4* __restrict__ out, const char* mc, unsigned long long nv, float scale) {
   const uint4* p = reinterpret_cast<const uint4*>(mc);
-  for (unsigned long long i = threadIdx.x; i < nv; i += kNvlsThreads) {
+  unsigned long long i = threadIdx.x;
+  for (; i + (kUnroll - 1) * kNvlsThreads < nv; i += kUnroll * kNvlsThreads) {
+    uint4 v[kUnroll];
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) v[u] = MM<T>::ld_reduce(p + i + u * kNvlsThreads);
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) out[i + u * kNvlsThreads] = scale != 1.f ? MM<T>::scale(v[u], scale) : v[u];
+  }
+  for (; i < nv; i += kNvlsThreads) {
     uint4 a = MM<T>::ld_reduce(p + i);
     if (scale != 1.f) a = MM<T>::scale(a, scale);
     out[i] = a;
@@ -185,7 +194,15 @@ NEXAR_D void reduce_to_local(uint4* __restrict__ out, const char* mc, unsigned l
 // multimem.st of local data to every rank (any 16-byte type).
 NEXAR_D void bcast_from_local(char* mc, const uint4* __restrict__ src, unsigned long long nv) {
   uint4* p = reinterpret_cast<uint4*>(mc);
-  for (unsigned long long i = threadIdx.x; i < nv; i += kNvlsThreads) MM<float>::st(p + i, src[i]);
+  unsigned long long i = threadIdx.x;
+  for (; i + (kUnroll - 1) * kNvlsThreads < nv; i += kUnroll * kNvlsThreads) {
+    uint4 v[kUnroll];
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) v[u] = src[i + u * kNvlsThreads];
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) MM<float>::st(p + i + u * kNvlsThreads, v[u]);
+  }
+  for (; i < nv; i += kNvlsThreads) MM<float>::st(p + i, src[i]);
 }
 
 // ---------------------------------------------------------------- all-reduce
@@ -233,16 +250,29 @@ __global__ void __launch_bounds__(kNvlsThreads) k_allreduce_nvls(CommDev c, cons
 
 // ---------------------------------------------------------------- reduce-scatter
 // in: [W][count] local, out: [count] = scale * sum over ranks of in[rank].
+// in_sym >= 0: the input lives in the NVLS user region at that offset: no
+// staging, one round per block over a contiguous range of the segment.
 template <typename T>
 __global__ void __launch_bounds__(kNvlsThreads) k_reduce_scatter_nvls(CommDev c, const T* in, T* out,
                                                                       unsigned long long count_bytes,
-                                                                      float scale) {
+                                                                      float scale, long long in_sym) {
   __shared__ unsigned int s_seq;
   if (threadIdx.x == 0) s_seq = c.nvls_seq[blockIdx.x];
   __syncthreads();
   unsigned int seq = s_seq;
   const unsigned int W = (unsigned)c.world;
   const unsigned long long nvec = count_bytes / 16;
+  if (in_sym >= 0) {
+    unsigned long long lo, hi;
+    block_range(nvec, gridDim.x, blockIdx.x, 1, &lo, &hi);
+    if (nvls_sync(c, 0, W * (seq + 1), kOpReduceScatter)) {
+      reduce_to_local<T>(reinterpret_cast<uint4*>(out) + lo, c.nvls_mc + in_sym + ((size_t)c.rank * nvec + lo) * 16,
+                         hi - lo, scale);
+      nvls_sync(c, 1, W * (seq + 1), kOpReduceScatter);
+    }
+    if (threadIdx.x == 0) c.nvls_seq[blockIdx.x] = seq + 1;
+    return;
+  }
   const unsigned long long per = (kNvlsChunkBytes / 16) / W;  // vectors of each rank's segment per round
   const unsigned long long chunks = (nvec + per - 1) / per;
   char* slot_uc = c.nvls_uc + kNvlsSignalBytes + (size_t)blockIdx.x * kNvlsChunkBytes;
@@ -264,8 +294,12 @@ __global__ void __launch_bounds__(kNvlsThreads) k_reduce_scatter_nvls(CommDev c,
 // ---------------------------------------------------------------- all-gather / broadcast
 // all-gather (root < 0): out[q][...] = in of rank q. broadcast (root >= 0):
 // out = in of root (W segments of one = the whole message on every rank).
+// out_sym >= 0: the output lives in the NVLS user region at that offset:
+// the multimem stores land in every rank's output directly (entry sync:
+// every rank is ready to receive; exit sync: every store has landed).
 __global__ void __launch_bounds__(kNvlsThreads) k_gather_bcast_nvls(CommDev c, const void* in, void* out,
-                                                                    unsigned long long count_bytes, int root) {
+                                                                    unsigned long long count_bytes, int root,
+                                                                    long long out_sym) {
   __shared__ unsigned int s_seq;
   if (threadIdx.x == 0) s_seq = c.nvls_seq[blockIdx.x];
   __syncthreads();
@@ -273,6 +307,22 @@ __global__ void __launch_bounds__(kNvlsThreads) k_gather_bcast_nvls(CommDev c, c
   const unsigned int W = (unsigned)c.world;
   const unsigned long long nvec = count_bytes / 16;
   const bool ag = root < 0;
+  if (out_sym >= 0) {
+    const int op = ag ? kOpAllGather : kOpBroadcast;
+    unsigned long long lo, hi;
+    block_range(nvec, gridDim.x, blockIdx.x, 1, &lo, &hi);
+    if (nvls_sync(c, 0, W * (seq + 1), op)) {
+      if (ag) {
+        bcast_from_local(c.nvls_mc + out_sym + ((size_t)c.rank * nvec + lo) * 16,
+                         reinterpret_cast<const uint4*>(in) + lo, hi - lo);
+      } else if (c.rank == root) {
+        bcast_from_local(c.nvls_mc + out_sym + lo * 16, reinterpret_cast<const uint4*>(in) + lo, hi - lo);
+      }
+      nvls_sync(c, 1, W * (seq + 1), op);
+    }
+    if (threadIdx.x == 0) c.nvls_seq[blockIdx.x] = seq + 1;
+    return;
+  }
   const unsigned long long per = ag ? (kNvlsChunkBytes / 16) / W : kNvlsChunkBytes / 16;
   const unsigned long long chunks = (nvec + per - 1) / per;
   char* slot_uc = c.nvls_uc + kNvlsSignalBytes + (size_t)blockIdx.x * kNvlsChunkBytes;
@@ -298,9 +348,10 @@ __global__ void __launch_bounds__(kNvlsThreads) k_gather_bcast_nvls(CommDev c, c
   if (threadIdx.x == 0) c.nvls_seq[blockIdx.x] = seq;
 }
 
-int nvls_grid(unsigned long long units, unsigned int max_blocks) {
+// Up to kMaxBlocks CTAs (two per SM): while one CTA of an SM waits on a
+// signal, the other copies, so HBM staging overlaps the NVLink phase.
+int nvls_grid(unsigned long long units, unsigned int /*max_blocks*/) {
   unsigned long long g = units < 1 ? 1 : units;
-  if (g > max_blocks) g = max_blocks;
   if (g > (unsigned long long)kMaxBlocks) g = kMaxBlocks;
   return (int)g;
 }
@@ -324,7 +375,7 @@ cudaError_t launch_all_reduce_nvls(const CommDev& c, const void* in, void* out, 
                                    float scale, long long sym_off, unsigned int max_blocks, cudaStream_t s) {
   const unsigned long long nvec = bytes / 16;
   int grid;
-  if (sym_off >= 0) grid = nvls_grid((nvec + 4095) / 4096, max_blocks);  // >= 64 KB per block
+  if (sym_off >= 0) grid = nvls_grid((nvec + 4095) / 4096, max_blocks);  // >= 64 KB per CTA
   else grid = nvls_grid((bytes + kNvlsChunkBytes - 1) / kNvlsChunkBytes, max_blocks);
   switch (dt) {
     case kF32:
@@ -345,21 +396,23 @@ cudaError_t launch_all_reduce_nvls(const CommDev& c, const void* in, void* out, 
 }
 
 cudaError_t launch_reduce_scatter_nvls(const CommDev& c, const void* in, void* out, int dt,
-                                       unsigned long long count_bytes, float scale, unsigned int max_blocks,
-                                       cudaStream_t s) {
+                                       unsigned long long count_bytes, float scale, long long in_sym,
+                                       unsigned int max_blocks, cudaStream_t s) {
   const unsigned long long per = kNvlsChunkBytes / c.world;
-  const int grid = nvls_grid((count_bytes + per - 1) / per, max_blocks);
+  const int grid = in_sym >= 0 ? nvls_grid((count_bytes + 65535) / 65536, max_blocks)
+                               : nvls_grid((count_bytes + per - 1) / per, max_blocks);
   switch (dt) {
     case kF32:
-      k_reduce_scatter_nvls<float><<<grid, kNvlsThreads, 0, s>>>(c, (const float*)in, (float*)out, count_bytes, scale);
+      k_reduce_scatter_nvls<float><<<grid, kNvlsThreads, 0, s>>>(c, (const float*)in, (float*)out, count_bytes, scale,
+                                                                 in_sym);
       break;
     case kBF16:
       k_reduce_scatter_nvls<__nv_bfloat16><<<grid, kNvlsThreads, 0, s>>>(c, (const __nv_bfloat16*)in,
-                                                                        (__nv_bfloat16*)out, count_bytes, scale);
+                                                                        (__nv_bfloat16*)out, count_bytes, scale, in_sym);
       break;
     case kF16:
       k_reduce_scatter_nvls<__half><<<grid, kNvlsThreads, 0, s>>>(c, (const __half*)in, (__half*)out, count_bytes,
-                                                                 scale);
+                                                                 scale, in_sym);
       break;
     default:
       return cudaErrorInvalidValue;
@@ -368,17 +421,19 @@ cudaError_t launch_reduce_scatter_nvls(const CommDev& c, const void* in, void* o
 }
 
 cudaError_t launch_all_gather_nvls(const CommDev& c, const void* in, void* out, unsigned long long count_bytes,
-                                   unsigned int max_blocks, cudaStream_t s) {
+                                   long long out_sym, unsigned int max_blocks, cudaStream_t s) {
   const unsigned long long per = kNvlsChunkBytes / c.world;
-  const int grid = nvls_grid((count_bytes + per - 1) / per, max_blocks);
-  k_gather_bcast_nvls<<<grid, kNvlsThreads, 0, s>>>(c, in, out, count_bytes, -1);
+  const int grid = out_sym >= 0 ? nvls_grid((count_bytes + 65535) / 65536, max_blocks)
+                                : nvls_grid((count_bytes + per - 1) / per, max_blocks);
+  k_gather_bcast_nvls<<<grid, kNvlsThreads, 0, s>>>(c, in, out, count_bytes, -1, out_sym);
   return cudaGetLastError();
 }
 
 cudaError_t launch_broadcast_nvls(const CommDev& c, const void* in, void* out, unsigned long long bytes, int root,
-                                  unsigned int max_blocks, cudaStream_t s) {
-  const int grid = nvls_grid((bytes + kNvlsChunkBytes - 1) / kNvlsChunkBytes, max_blocks);
-  k_gather_bcast_nvls<<<grid, kNvlsThreads, 0, s>>>(c, in, out, bytes, root);
+                                  long long out_sym, unsigned int max_blocks, cudaStream_t s) {
+  const int grid = out_sym >= 0 ? nvls_grid((bytes + 65535) / 65536, max_blocks)
+                                : nvls_grid((bytes + kNvlsChunkBytes - 1) / kNvlsChunkBytes, max_blocks);
+  k_gather_bcast_nvls<<<grid, kNvlsThreads, 0, s>>>(c, in, out, bytes, root, out_sym);
   return cudaGetLastError();
 }
 

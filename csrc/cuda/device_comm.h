@@ -63,8 +63,14 @@ class DeviceComm {
   uint64_t timeout_us() const { return dev_.timeout_ns / 1000ull; }
 
   unsigned int max_blocks = 148;
-  // Messages of at least this many bytes take the NVLS path when it applies.
-  uint64_t nvls_min_bytes = 4ull << 20;
+  // Messages of at least this many bytes take the staged NVLS path when it
+  // applies (all-reduce, reduce-scatter input, all-gather output, broadcast).
+  // Buffers that live in the NVLS region take the zero-copy NVLS path at any
+  // size. Staged all-gather loses to the peer-to-peer kernel: off by default.
+  uint64_t nvls_min_bytes = 16ull << 20;
+  uint64_t nvls_min_rs_bytes = 16ull << 20;
+  uint64_t nvls_min_ag_bytes = ~0ull;
+  uint64_t nvls_min_bcast_bytes = 1ull << 20;
 
   // ---- NVLS (NVSwitch multicast), multi-process only; see nvls.cpp.
   // Setup order on every rank: rank 0 nvls_create() and hands the returned

@@ -16,12 +16,14 @@ bool nvls_can_move(const CommDev& c, const void* in, const void* out, unsigned l
 cudaError_t launch_all_reduce_nvls(const CommDev& c, const void* in, void* out, int dt, unsigned long long bytes,
                                    float scale, long long sym_off, unsigned int max_blocks, cudaStream_t s);
 // in: [world][count] (count_bytes per rank), out: this rank's reduced segment.
+// in_sym >= 0: the input lives in the NVLS user region (no staging).
 cudaError_t launch_reduce_scatter_nvls(const CommDev& c, const void* in, void* out, int dt,
-                                       unsigned long long count_bytes, float scale, unsigned int max_blocks,
-                                       cudaStream_t s);
+                                       unsigned long long count_bytes, float scale, long long in_sym,
+                                       unsigned int max_blocks, cudaStream_t s);
+// out_sym >= 0: the output lives in the NVLS user region (stores land there directly).
 cudaError_t launch_all_gather_nvls(const CommDev& c, const void* in, void* out, unsigned long long count_bytes,
-                                   unsigned int max_blocks, cudaStream_t s);
+                                   long long out_sym, unsigned int max_blocks, cudaStream_t s);
 cudaError_t launch_broadcast_nvls(const CommDev& c, const void* in, void* out, unsigned long long bytes, int root,
-                                  unsigned int max_blocks, cudaStream_t s);
+                                  long long out_sym, unsigned int max_blocks, cudaStream_t s);
 
 }  // namespace nexar

@@ -7,7 +7,10 @@
 The NCCL arm issues the same call sequence as the reference's nexar-nccl
 single-node path (ncclAllReduce / ncclReduceScatter / ncclAllGather /
 ncclBroadcast in place on one stream; all_to_all as grouped send/recv),
-through torch.distributed's NCCL backend. Both arms are timed the same way:
+through torch.distributed's NCCL backend. The ``nexar_sym`` arm runs the same
+calls on buffers allocated in symmetric memory (the NVSwitch multicast region
+when NVLS is the preferred path, else the peer-mapped heap), the equivalent of NCCL's
+registered buffers: no staging copies. Both arms are timed the same way:
 warm-up iterations, then `iters` back-to-back launches between CUDA events,
 max over ranks. Bus bandwidth follows the nccl-tests convention.
 """
@@ -36,7 +39,7 @@ def main(argv=None):
     ap.add_argument("--step", type=int, default=2, help="size multiplier between points")
     ap.add_argument("--iters", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=20)
-    ap.add_argument("--impls", default="nexar,nccl")
+    ap.add_argument("--impls", default="nexar,nexar_sym,nccl")
     ap.add_argument("--algo", default="auto")
     ap.add_argument("--out", default=None)
     args = ap.parse_args(argv)
@@ -76,6 +79,15 @@ def main(argv=None):
 
     ops = args.ops.split(",")
     impls = args.impls.split(",")
+
+    def sym_buf(numel):
+        return comm.symmetric_empty([numel], dtype, nvls=comm.nvls_preferred)
+
+    def sym_reset():
+        if comm.nvls_preferred:
+            comm.native.nvls_reset()
+        else:
+            comm.native.reset_symmetric()
     size = args.min_bytes
     while size <= args.max_bytes:
         n = max(world, size // es)
@@ -83,7 +95,28 @@ def main(argv=None):
         big = torch.randn(n, device=dev, generator=g).to(dtype)
         for op in ops:
             for impl in impls:
-                if op == "all_reduce":
+                if impl == "nexar_sym":
+                    if op == "all_to_all":
+                        continue
+                    if op == "all_reduce":
+                        t = sym_buf(n)
+                        t.copy_(big)
+                        fn = lambda: comm.all_reduce(t)  # noqa: E731
+                    elif op == "reduce_scatter":
+                        inp = sym_buf(n)
+                        inp.copy_(big)
+                        out = torch.empty(n // world, dtype=dtype, device=dev)
+                        fn = lambda: comm.reduce_scatter(inp, out)  # noqa: E731
+                    elif op == "all_gather":
+                        inp = big[: n // world].clone()
+                        out = sym_buf(n)
+                        fn = lambda: comm.all_gather(inp, out)  # noqa: E731
+                    else:
+                        t = sym_buf(n)
+                        t.copy_(big)
+                        fn = lambda: comm.broadcast(t, 0)  # noqa: E731
+                    nbytes = n * es
+                elif op == "all_reduce":
                     t = big.clone()
                     fn = (lambda: comm.all_reduce(t, algo=args.algo)) if impl == "nexar" else (lambda: dist.all_reduce(t))
                     nbytes = n * es
@@ -107,6 +140,9 @@ def main(argv=None):
                 else:
                     raise SystemExit(f"unknown op {op}")
                 ms = time_it(fn)
+                if impl == "nexar_sym":
+                    torch.cuda.synchronize()
+                    sym_reset()
                 algbw = nbytes / (ms / 1e3) / 1e9
                 rec = {"op": op, "impl": impl, "dtype": args.dtype, "bytes": nbytes, "n_gpus": world,
                        "us": round(ms * 1e3, 2), "algbw_gbs": round(algbw, 2),

@@ -92,12 +92,21 @@ class DeviceCommunicator:
             self._comm.connect(list(handles))
         # NVSwitch multicast region: large all-reduce / reduce-scatter /
         # all-gather / broadcast reduce and replicate inside the switch.
-        self._comm.nvls_min_bytes = _env_int("NEXAR_NVLS_MIN_BYTES", 4 << 20)
+        self._comm.nvls_min_bytes = _env_int("NEXAR_NVLS_MIN_BYTES", 16 << 20)
         nvls_user = _env_int("NEXAR_NVLS_USER_BYTES", 1 << 30)
         from . import nvls as _nvls
         self.nvls = _nvls.setup_nvls(self._comm, rank, world_size, exchange,
                                      (1 << 20) + C.nvls_stage_bytes() + nvls_user)
         self.nvls_reason = _nvls.LAST_REASON
+        # NVLS moves about S bytes per GPU and direction for an all-reduce of S
+        # bytes, the peer-to-peer two-shot 2 S (W-1)/W, but multimem runs
+        # well below link rate: it only wins from 4 ranks up. Below that the
+        # region stays available for explicit use (algo="nvls", nvls=True).
+        self.nvls_preferred = self.nvls and world_size >= _env_int("NEXAR_NVLS_MIN_RANKS", 4)
+        if self.nvls and not self.nvls_preferred:
+            never = (1 << 64) - 1
+            for k in ("nvls_min_bytes", "nvls_min_rs_bytes", "nvls_min_ag_bytes", "nvls_min_bcast_bytes"):
+                setattr(self._comm, k, never)
         self._barrier = barrier
         if barrier is not None:
             barrier()  # every rank has mapped its peers before any kernel runs

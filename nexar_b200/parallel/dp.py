@@ -36,7 +36,10 @@ class DataParallelTrainer:
         self.device = torch.device("cuda", torch.cuda.current_device() if device is None else device)
         grad_alloc = None
         if self.world > 1:
-            grad_alloc = lambda n: comm.symmetric_empty([n], torch.bfloat16, nvls=True)  # noqa: E731
+            # NVLS region when NVLS is the better all-reduce at this size of job,
+            # else the peer-mapped heap (zero-copy two-shot)
+            grad_alloc = lambda n: comm.symmetric_empty(  # noqa: E731
+                [n], torch.bfloat16, nvls=getattr(comm, "nvls_preferred", False))
         self.model = GPT2(cfg, self.device, grad_alloc=grad_alloc, seed=seed)
         flat = self.model.flat
         flat.grad.zero_()  # padding between parameters is never written

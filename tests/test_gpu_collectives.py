@@ -219,7 +219,8 @@ def _nvls_worker(rank, world, port, results):
         dist.barrier()
         dist.destroy_process_group()
         return
-    comm.native.nvls_min_bytes = 0
+    for k in ("nvls_min_bytes", "nvls_min_rs_bytes", "nvls_min_ag_bytes", "nvls_min_bcast_bytes"):
+        setattr(comm.native, k, 0)
 
     def check(name, got, want, **tol):
         try:
@@ -274,6 +275,23 @@ def _nvls_worker(rank, world, port, results):
                 t = xs[rank][:count].clone().to(dev)
                 comm.broadcast(t, root=root)
                 check(f"nvls broadcast {dtype} {count} root{root}", t, xs[root][:count], atol=0, rtol=0)
+    # zero-copy variants: NVLS-resident RS input, AG output, broadcast buffer
+    count = (1 << 19) + 8
+    xs = [_data(r, count * world, torch.bfloat16, seed=5) for r in range(world)]
+    rin = comm.symmetric_empty([count * world], torch.bfloat16, nvls=True)
+    agout = comm.symmetric_empty([count * world], torch.bfloat16, nvls=True)
+    bbuf = comm.symmetric_empty([count], torch.bfloat16, nvls=True)
+    for _ in range(2):
+        rin.copy_(xs[rank].to(dev))
+        out = comm.reduce_scatter(rin)
+        check("nvls reduce_scatter resident", out, _oracle_reduce(xs, "sum")[rank * count:(rank + 1) * count],
+              **_tol(torch.bfloat16, world))
+        comm.all_gather(xs[rank][:count].to(dev), agout)
+        check("nvls all_gather resident", agout, torch.cat([xs[r][:count] for r in range(world)]), atol=0, rtol=0)
+        for root in (0, world - 1):
+            bbuf.copy_(xs[rank][:count].to(dev))
+            comm.broadcast(bbuf, root=root)
+            check(f"nvls broadcast resident root{root}", bbuf, xs[root][:count], atol=0, rtol=0)
     torch.cuda.synchronize()
     try:
         comm.check()
