@@ -28,7 +28,7 @@ SEQ_LEN = 1024
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="nexar", choices=["nexar", "reference", "torch"])
     ap.add_argument("--micro-batch", type=int, default=MICRO_BATCH)
@@ -101,7 +101,7 @@ def main():
     barrier()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     launches0 = _native.launch_count()
-    with ClockSampler(device_uuids([local_rank])) as clk:
+    with ClockSampler(device_uuids([local_rank]), period_ms=100) as clk:
         start.record()
         for _ in range(args.steps):
             trainer.run_step()
