@@ -61,6 +61,22 @@ cudaError_t make_tmap_bf16(CUtensorMap* map, const void* base, long long rows, l
   return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
+// Generic 2-D tensor map over a row-major [rows, cols] matrix of `esize`-byte
+// elements (leading dimension ld elements), 128-byte swizzle.
+cudaError_t make_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, int esize, const void* base, long long rows,
+                         long long cols, long long ld, int box_rows, int box_cols) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return cudaErrorNotSupported;
+  if ((reinterpret_cast<uintptr_t>(base) & 15u) || (ld * esize) % 16) return cudaErrorInvalidValue;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)ld * esize};
+  cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, dtype, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
 // 3-D fp32 tensor map over [splits, rows, cols] (contiguous), box 1 x 32 x 32,
 // 128-byte swizzle: the split-K partial sink.
 cudaError_t make_tmap_f32_3d(CUtensorMap* map, void* base, long long splits, long long rows, long long cols) {

@@ -31,6 +31,23 @@ unsigned int gemm_error_flag();
 
 cudaError_t make_tmap_bf16(CUtensorMap* map, const void* base, long long rows, long long cols, long long ld,
                            int box_rows, int box_cols);
+cudaError_t make_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, int esize, const void* base, long long rows,
+                         long long cols, long long ld, int box_rows, int box_cols);
+
+// ---- fp8 (e4m3) block-scaled GEMM: C[M,N] = epi( sum_kb sa[m,kb] sb[n/128,kb] (A_kb . B_kb^T) )
+// A [M, K] e4m3 with 1x128 scales sa [M, ceil(K/128)] (fp32, row-major);
+// B [N, K] e4m3 with 128x128 block scales sb [ceil(N/128), ceil(K/128)].
+// K-major operands; lda / ldb in elements (bytes), multiples of 16. `pre`
+// must be null (the fp8 kernel keeps no pre-activation copy).
+cudaError_t gemm_fp8_blockscaled(const uint8_t* A, const float* sa, const uint8_t* B, const float* sb,
+                                 __nv_bfloat16* C, int M, int N, int K, long long lda, long long ldb, long long ldc,
+                                 const __nv_bfloat16* bias, int act, __nv_bfloat16* pre, float alpha, cudaStream_t s);
+// x [R, K] bf16 -> q e4m3 [R, K] and s [R, ceil(K/128)] with s = amax(block)/448 (1x128 blocks).
+cudaError_t quant_fp8_1x128(const __nv_bfloat16* x, long long ldx, uint8_t* q, long long ldq, float* s, int R, int K,
+                            cudaStream_t st);
+// w [N, K] bf16 -> q e4m3 [N, K] and s [ceil(N/128), ceil(K/128)] (128x128 blocks).
+cudaError_t quant_fp8_128x128(const __nv_bfloat16* w, long long ldw, uint8_t* q, long long ldq, float* s, int N, int K,
+                              cudaStream_t st);
 
 }  // namespace nexar
 

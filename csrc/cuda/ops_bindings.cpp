@@ -289,7 +289,67 @@ void op_gemm_ex(const at::Tensor& A, const at::Tensor& B, const at::Tensor& C, b
   count_launch(sp > 1 ? 2 : 1);
 }
 
+// fp8 e4m3 tensors travel as torch.float8_e4m3fn (or uint8) tensors.
+static bool is_fp8_bytes(const at::Tensor& t) {
+  return t.scalar_type() == at::kFloat8_e4m3fn || t.scalar_type() == at::kByte;
+}
+
+void op_quant_fp8_1x128(const at::Tensor& x, const at::Tensor& q, const at::Tensor& s) {
+  TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.dim() == 2 && x.stride(1) == 1, "x: 2-D bf16");
+  TORCH_CHECK(q.is_cuda() && is_fp8_bytes(q) && q.dim() == 2 && q.stride(1) == 1 && q.sizes() == x.sizes(), "q: e4m3 like x");
+  const int R = x.size(0), K = x.size(1);
+  TORCH_CHECK(s.is_cuda() && s.scalar_type() == at::kFloat && s.is_contiguous() && s.numel() == (int64_t)R * ((K + 127) / 128),
+              "s: fp32 [R, ceil(K/128)]");
+  c10::cuda::CUDAGuard g(x.get_device());
+  chk(quant_fp8_1x128(reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), x.stride(0),
+                      reinterpret_cast<uint8_t*>(q.data_ptr()), q.stride(0), s.data_ptr<float>(), R, K, stream_of(x)),
+      "quant_fp8_1x128");
+  count_launch(1);
+}
+
+void op_quant_fp8_128x128(const at::Tensor& w, const at::Tensor& q, const at::Tensor& s) {
+  TORCH_CHECK(w.is_cuda() && w.scalar_type() == at::kBFloat16 && w.dim() == 2 && w.stride(1) == 1, "w: 2-D bf16");
+  TORCH_CHECK(q.is_cuda() && is_fp8_bytes(q) && q.dim() == 2 && q.stride(1) == 1 && q.sizes() == w.sizes(), "q: e4m3 like w");
+  const int N = w.size(0), K = w.size(1);
+  TORCH_CHECK(s.is_cuda() && s.scalar_type() == at::kFloat && s.is_contiguous() &&
+                  s.numel() == (int64_t)((N + 127) / 128) * ((K + 127) / 128),
+              "s: fp32 [ceil(N/128), ceil(K/128)]");
+  c10::cuda::CUDAGuard g(w.get_device());
+  chk(quant_fp8_128x128(reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()), w.stride(0),
+                        reinterpret_cast<uint8_t*>(q.data_ptr()), q.stride(0), s.data_ptr<float>(), N, K, stream_of(w)),
+      "quant_fp8_128x128");
+  count_launch(1);
+}
+
+// C[M, N] = act(alpha * blockscaled(A, sa) . blockscaled(B, sb)^T + bias)
+void op_gemm_fp8(const at::Tensor& A, const at::Tensor& sa, const at::Tensor& B, const at::Tensor& sb,
+                 const at::Tensor& C, const c10::optional<at::Tensor>& bias, const c10::optional<at::Tensor>& pre,
+                 int64_t act, double alpha) {
+  TORCH_CHECK(A.is_cuda() && B.is_cuda() && C.is_cuda(), "gemm_fp8: CUDA tensors required");
+  TORCH_CHECK(is_fp8_bytes(A) && is_fp8_bytes(B) && C.scalar_type() == at::kBFloat16, "gemm_fp8: e4m3 A/B, bf16 C");
+  TORCH_CHECK(A.dim() == 2 && B.dim() == 2 && C.dim() == 2 && A.stride(1) == 1 && B.stride(1) == 1 && C.stride(1) == 1,
+              "gemm_fp8: 2-D operands with contiguous rows");
+  const int M = A.size(0), K = A.size(1), N = B.size(0);
+  TORCH_CHECK(B.size(1) == K && C.size(0) == M && C.size(1) == N, "gemm_fp8: shape mismatch");
+  const int kb = (K + 127) / 128;
+  TORCH_CHECK(sa.scalar_type() == at::kFloat && sa.is_contiguous() && sa.numel() == (int64_t)M * kb, "gemm_fp8: sa [M, ceil(K/128)]");
+  TORCH_CHECK(sb.scalar_type() == at::kFloat && sb.is_contiguous() && sb.numel() == (int64_t)((N + 127) / 128) * kb,
+              "gemm_fp8: sb [ceil(N/128), ceil(K/128)]");
+  c10::cuda::CUDAGuard g(A.get_device());
+  chk(gemm_fp8_blockscaled(reinterpret_cast<const uint8_t*>(A.data_ptr()), sa.data_ptr<float>(),
+                           reinterpret_cast<const uint8_t*>(B.data_ptr()), sb.data_ptr<float>(),
+                           reinterpret_cast<__nv_bfloat16*>(C.data_ptr()), M, N, K, A.stride(0), B.stride(0), C.stride(0),
+                           bias ? reinterpret_cast<const __nv_bfloat16*>(bias->data_ptr()) : nullptr, (int)act,
+                           pre ? reinterpret_cast<__nv_bfloat16*>(pre->data_ptr()) : nullptr, (float)alpha, stream_of(A)),
+      "gemm_fp8");
+  count_launch(1);
+}
+
 void register_gemm_ops(py::module& m) {
+  m.def("quant_fp8_1x128", &op_quant_fp8_1x128);
+  m.def("quant_fp8_128x128", &op_quant_fp8_128x128);
+  m.def("gemm_fp8", &op_gemm_fp8, py::arg("A"), py::arg("sa"), py::arg("B"), py::arg("sb"), py::arg("C"),
+        py::arg("bias") = py::none(), py::arg("pre") = py::none(), py::arg("act") = 0, py::arg("alpha") = 1.0);
   m.def("gemm_ex", &op_gemm_ex, py::arg("A"), py::arg("B"), py::arg("C"), py::arg("a_t") = false,
         py::arg("b_t") = false, py::arg("bias") = py::none(), py::arg("residual") = py::none(),
         py::arg("pre") = py::none(), py::arg("act") = 0, py::arg("alpha") = 1.0, py::arg("accumulate") = false,

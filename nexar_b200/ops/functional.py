@@ -391,3 +391,31 @@ def cross_entropy_loss_only(logits, targets, vocab_size: int):
     losses = torch.empty(l2.shape[0], dtype=torch.float32, device=logits.device)
     _native.cuda().xent(l2, targets.reshape(-1).contiguous(), losses, None, vocab_size, 1.0)
     return losses
+
+
+def quant_fp8_1x128(x):
+    """bf16 [R, K] -> (e4m3 [R, K], fp32 scales [R, ceil(K/128)]), scale = amax/448 per 1x128 block."""
+    x2 = x.reshape(-1, x.shape[-1])
+    R, K = x2.shape
+    q = torch.empty(R, K, dtype=torch.float8_e4m3fn, device=x.device)
+    s = torch.empty(R, (K + 127) // 128, dtype=torch.float32, device=x.device)
+    _native.cuda().quant_fp8_1x128(x2, q, s)
+    return q, s
+
+
+def quant_fp8_128x128(w):
+    """bf16 [N, K] -> (e4m3 [N, K], fp32 scales [ceil(N/128), ceil(K/128)]) per 128x128 block."""
+    N, K = w.shape
+    q = torch.empty(N, K, dtype=torch.float8_e4m3fn, device=w.device)
+    s = torch.empty((N + 127) // 128, (K + 127) // 128, dtype=torch.float32, device=w.device)
+    _native.cuda().quant_fp8_128x128(w, q, s)
+    return q, s
+
+
+def matmul_fp8(a_q, a_s, b_q, b_s, out=None, bias=None, act: int = 0, pre=None, alpha: float = 1.0):
+    """out[M, N] = act(alpha * (a_q * a_s) . (b_q * b_s)^T + bias) on the block-scaled fp8 tcgen05 GEMM."""
+    M, N = a_q.shape[0], b_q.shape[0]
+    if out is None:
+        out = torch.empty(M, N, dtype=torch.bfloat16, device=a_q.device)
+    _native.cuda().gemm_fp8(a_q, a_s, b_q, b_s, out, bias, pre, act, alpha)
+    return out
