@@ -406,6 +406,27 @@ void gemm_rs(const CommPtr& c, const at::Tensor& A, const at::Tensor& B, const a
   count_launch(1);
 }
 
+void gemm_fp8_rs(const CommPtr& c, const at::Tensor& A, const at::Tensor& sa, const at::Tensor& B, const at::Tensor& sb,
+                 const at::Tensor& out, const c10::optional<at::Tensor>& bias, double alpha) {
+  auto fp8 = [](const at::Tensor& t) { return t.scalar_type() == at::kFloat8_e4m3fn || t.scalar_type() == at::kByte; };
+  TORCH_CHECK(A.is_cuda() && B.is_cuda() && fp8(A) && fp8(B) && A.dim() == 2 && B.dim() == 2 && A.stride(1) == 1 &&
+                  B.stride(1) == 1, "gemm_fp8_reduce_scatter: 2-D e4m3 A and B");
+  need_bf16_2d(out, "out");
+  const int M = A.size(0), K = A.size(1), N = B.size(0);
+  TORCH_CHECK(B.size(1) == K && out.size(0) * c->world() == M && out.size(1) == N, "gemm_fp8_reduce_scatter: shape mismatch");
+  const int kb = (K + 127) / 128;
+  TORCH_CHECK(sa.scalar_type() == at::kFloat && sa.is_contiguous() && sa.numel() == (int64_t)M * kb, "sa [M, ceil(K/128)]");
+  TORCH_CHECK(sb.scalar_type() == at::kFloat && sb.is_contiguous() && sb.numel() == (int64_t)((N + 127) / 128) * kb,
+              "sb [ceil(N/128), ceil(K/128)]");
+  c10::cuda::CUDAGuard g(c->device());
+  check_launch(gemm_fp8_reduce_scatter(c->dev(), reinterpret_cast<const uint8_t*>(A.data_ptr()), sa.data_ptr<float>(),
+                                       reinterpret_cast<const uint8_t*>(B.data_ptr()), sb.data_ptr<float>(), mbf(out), M,
+                                       N, K, A.stride(0), B.stride(0), out.stride(0), bias ? cbf(*bias) : nullptr,
+                                       (float)alpha, cur_stream(*c)),
+               "gemm_fp8_reduce_scatter");
+  count_launch(1);
+}
+
 void ag_gemm(const CommPtr& c, const at::Tensor& x, const at::Tensor& B, const at::Tensor& out, const at::Tensor& afull,
              const at::Tensor& cnt, const c10::optional<at::Tensor>& bias, int act, const c10::optional<at::Tensor>& pre,
              double alpha) {
@@ -501,5 +522,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_dispatch", &moe_dispatch_op);
   m.def("moe_combine", &moe_combine_op);
   m.def("all_gather_gemm", &ag_gemm);
+  m.def("gemm_fp8_reduce_scatter", &gemm_fp8_rs);
   register_ops(m);
 }

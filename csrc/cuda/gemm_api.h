@@ -42,6 +42,8 @@ cudaError_t make_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, int esize,
 cudaError_t gemm_fp8_blockscaled(const uint8_t* A, const float* sa, const uint8_t* B, const float* sb,
                                  __nv_bfloat16* C, int M, int N, int K, long long lda, long long ldb, long long ldc,
                                  const __nv_bfloat16* bias, int act, __nv_bfloat16* pre, float alpha, cudaStream_t s);
+// gu [R, 2F] bf16 (gate | up) -> h = silu(gate) * up quantised: q e4m3 [R, F], s [R, ceil(F/128)].
+cudaError_t swiglu_quant_fp8_1x128(const __nv_bfloat16* gu, uint8_t* q, float* s, int R, int F, cudaStream_t st);
 // x [R, K] bf16 -> q e4m3 [R, K] and s [R, ceil(K/128)] with s = amax(block)/448 (1x128 blocks).
 cudaError_t quant_fp8_1x128(const __nv_bfloat16* x, long long ldx, uint8_t* q, long long ldq, float* s, int R, int K,
                             cudaStream_t st);
@@ -61,6 +63,12 @@ cudaError_t gemm_reduce_scatter(const CommDev& c, const __nv_bfloat16* A, const 
 // Column-parallel linear fused with all-gather: out[M, N] = act(AG(x) . B^T + bias)
 // with x the local [M/W, K] shard; afull [M, K] is a local gather workspace and
 // cnt a zeroed uint32 array of M/128 + 2 entries (left zeroed on exit).
+// fp8 block-scaled variant of gemm_reduce_scatter (A / B e4m3 with 1x128 /
+// 128x128 scales as gemm_fp8_blockscaled).
+cudaError_t gemm_fp8_reduce_scatter(const CommDev& c, const uint8_t* A, const float* sa, const uint8_t* B,
+                                    const float* sb, __nv_bfloat16* out, int M, int N, int K, long long lda,
+                                    long long ldb, long long ldo, const __nv_bfloat16* bias, float alpha,
+                                    cudaStream_t s);
 cudaError_t all_gather_gemm(const CommDev& c, const __nv_bfloat16* x, long long ldx, const __nv_bfloat16* B,
                             __nv_bfloat16* out, __nv_bfloat16* afull, unsigned int* cnt, int M, int N, int K,
                             long long ldb, long long ldo, const __nv_bfloat16* bias, int act, __nv_bfloat16* pre,

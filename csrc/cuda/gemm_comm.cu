@@ -30,6 +30,7 @@
 #include "coll.cuh"
 #include "coll_api.h"
 #include "gemm_launch.cuh"
+#include "gemm_fp8.cuh"
 
 namespace nexar {
 namespace gemm {
@@ -76,6 +77,7 @@ struct EpiPeerRS {
   __nv_bfloat16* out;         // [rpr, ldo] this rank's reduced rows
   long long ldo;
   int op_id;
+  int arrivals;   // epilogue warps that store each tile (4 bf16 kernel, 8 fp8 kernel)
   static constexpr int has_pre = 0;
 
   __device__ __forceinline__ unsigned long long epoch() const { return epoch_of(s_call(), 0); }
@@ -119,7 +121,7 @@ struct EpiPeerRS {
       if (col0 + ch * 8 < N) *reinterpret_cast<uint4*>(dst + (long long)r * N + ch * 8) = v;
     }
   }
-  // Publish the tile once all 4 epilogue warps have stored their rows. A
+  // Publish the tile once all epilogue warps have stored their rows. A
   // shared counter (not a named barrier) joins the warps so that a warp that
   // gave up on an earlier wait can never leave the others blocked forever.
   __device__ void end_tile(int tm, int tn, int lane) const {
@@ -131,7 +133,7 @@ struct EpiPeerRS {
       atomicAdd(&s_tile_arrivals(), 1u);
     }
     if (threadIdx.x == 64) {
-      const unsigned int target = (s_tile_seq() += 4u);
+      const unsigned int target = (s_tile_seq() += (unsigned)arrivals);
       const unsigned long long t0 = globaltimer_ns();
       while (*reinterpret_cast<volatile unsigned int*>(&s_tile_arrivals()) < target) {
         if (globaltimer_ns() - t0 > c.timeout_ns) return;
@@ -342,10 +344,44 @@ cudaError_t gemm_reduce_scatter(const CommDev& c, const __nv_bfloat16* A, const 
   CUtensorMap dummy;
   cudaError_t e = make_tmap_bf16(&dummy, A, M, K, lda, 32, 64);
   if (e != cudaSuccess) return e;
-  EpiPeerRS epi{c, rpr, N, tiles_n, alpha, bias, out, ldo, kOpGemmRs};
+  EpiPeerRS epi{c, rpr, N, tiles_n, alpha, bias, out, ldo, kOpGemmRs, EPI_WARPS};
   const int m_rotate = ((c.rank + 1) % W) * (rpr / BM);
   return launch_gemm_generic<EpiPeerRS, NoGate, 0>(A, B, M, N, K, lda, ldb, dummy, dummy, m_rotate, epi, NoGate{},
                                                    gemm_sm_count(), s);
+}
+
+// fp8 (block-scaled) row-parallel linear fused with reduce-scatter: the fp8
+// promotion kernel with the same peer-store epilogue (BM = 128, BN = 256 as
+// the bf16 kernel, eight storing warps per tile).
+cudaError_t gemm_fp8_reduce_scatter(const CommDev& c, const uint8_t* A, const float* sa, const uint8_t* B,
+                                    const float* sb, __nv_bfloat16* out, int M, int N, int K, long long lda,
+                                    long long ldb, long long ldo, const __nv_bfloat16* bias, float alpha,
+                                    cudaStream_t s) {
+  using namespace gemm;
+  static_assert(gemm8::BM == BM && gemm8::BN == BN, "tile geometry shared with EpiPeerRS");
+  const int W = c.world;
+  if (M % (W * BM) != 0 || N % 8 != 0 || K % 16 != 0) return cudaErrorInvalidValue;
+  const int rpr = M / W;
+  const int tiles_n = (N + BN - 1) / BN;
+  if ((rpr / BM) * tiles_n > kMaxFusedTiles) return cudaErrorInvalidValue;
+  if ((unsigned long long)M * N * 2 > c.slot_bytes) return cudaErrorInvalidValue;
+  CUtensorMap ta, tb, dummy;
+  cudaError_t e = make_tmap_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, A, M, K, lda, gemm8::BM, gemm8::BK);
+  if (e != cudaSuccess) return e;
+  e = make_tmap_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, B, N, K, ldb, gemm8::BN, gemm8::BK);
+  if (e != cudaSuccess) return e;
+  dummy = ta;
+  EpiPeerRS epi{c, rpr, N, tiles_n, alpha, bias, out, ldo, kOpGemmRs, gemm8::PROMO_WARPS};
+  const int m_rotate = ((c.rank + 1) % W) * (rpr / BM);
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaFuncSetAttribute(gemm8::k_gemm_fp8<EpiPeerRS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         gemm8::SMEM_BYTES);
+    attr_set = true;
+  }
+  gemm8::k_gemm_fp8<EpiPeerRS><<<gemm_sm_count(), gemm8::THREADS, gemm8::SMEM_BYTES, s>>>(
+      ta, tb, dummy, dummy, sa, sb, M, N, K, m_rotate, epi, NoGate{}, gemm_err_word());
+  return cudaGetLastError();
 }
 
 cudaError_t all_gather_gemm(const CommDev& c, const __nv_bfloat16* x, long long ldx, const __nv_bfloat16* B,

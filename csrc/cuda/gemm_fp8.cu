@@ -57,6 +57,38 @@ __global__ void __launch_bounds__(256) k_quant_1x128(const __nv_bfloat16* __rest
   if (lane == 0) s[(long long)r * kb_count + kb] = scale;
 }
 
+// SwiGLU fused with the 1x128 quantiser: one warp per (row, 128-column block).
+__global__ void __launch_bounds__(256) k_swiglu_quant_1x128(const __nv_bfloat16* __restrict__ gu,
+                                                            uint8_t* __restrict__ q, float* __restrict__ s, int R,
+                                                            int F) {
+  const int kb_count = (F + 127) / 128;
+  const long long w = (long long)blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (w >= (long long)R * kb_count) return;
+  const int lane = threadIdx.x & 31;
+  const int r = (int)(w / kb_count), kb = (int)(w % kb_count);
+  const int c = kb * 128 + lane * 4;
+  const __nv_bfloat16* g = gu + (long long)r * 2 * F;
+  float h[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    if (c + e < F) {
+      const float a = __bfloat162float(g[c + e]), u = __bfloat162float(g[F + c + e]);
+      // the bf16 path rounds h to bf16 before the down projection: do the same
+      h[e] = __bfloat162float(__float2bfloat16_rn(a / (1.f + __expf(-a)) * u));
+    }
+  }
+  float m = fmaxf(fmaxf(fabsf(h[0]), fabsf(h[1])), fmaxf(fabsf(h[2]), fabsf(h[3])));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  const float scale = m > 0.f ? m / kE4M3Max : 1.f;
+  const float inv = 1.f / scale;
+  uint8_t* qr = q + (long long)r * F;
+#pragma unroll
+  for (int e = 0; e < 4; ++e)
+    if (c + e < F) qr[c + e] = to_e4m3(h[e] * inv);
+  if (lane == 0) s[(long long)r * kb_count + kb] = scale;
+}
+
 // One CTA per 128x128 block: 256 threads, amax over the block, then quantise.
 __global__ void __launch_bounds__(256) k_quant_128x128(const __nv_bfloat16* __restrict__ w, long long ldw,
                                                        uint8_t* __restrict__ q, long long ldq, float* __restrict__ s,
@@ -94,6 +126,13 @@ cudaError_t quant_fp8_1x128(const __nv_bfloat16* x, long long ldx, uint8_t* q, l
     return cudaErrorInvalidValue;
   const long long warps = (long long)R * ((K + 127) / 128);
   k_quant_1x128<<<(unsigned)((warps + 7) / 8), 256, 0, st>>>(x, ldx, q, ldq, s, R, K);
+  return cudaGetLastError();
+}
+
+cudaError_t swiglu_quant_fp8_1x128(const __nv_bfloat16* gu, uint8_t* q, float* s, int R, int F, cudaStream_t st) {
+  if (R <= 0 || F <= 0) return cudaSuccess;
+  const long long warps = (long long)R * ((F + 127) / 128);
+  k_swiglu_quant_1x128<<<(unsigned)((warps + 7) / 8), 256, 0, st>>>(gu, q, s, R, F);
   return cudaGetLastError();
 }
 

@@ -345,7 +345,21 @@ void op_gemm_fp8(const at::Tensor& A, const at::Tensor& sa, const at::Tensor& B,
   count_launch(1);
 }
 
+void op_swiglu_quant_fp8(const at::Tensor& gu, const at::Tensor& q, const at::Tensor& s) {
+  TORCH_CHECK(gu.is_cuda() && gu.scalar_type() == at::kBFloat16 && gu.dim() == 2 && gu.is_contiguous(), "gu: [R, 2F] bf16");
+  const int R = gu.size(0), F = gu.size(1) / 2;
+  TORCH_CHECK(q.is_cuda() && is_fp8_bytes(q) && q.is_contiguous() && q.numel() == (int64_t)R * F, "q: e4m3 [R, F]");
+  TORCH_CHECK(s.is_cuda() && s.scalar_type() == at::kFloat && s.is_contiguous() && s.numel() == (int64_t)R * ((F + 127) / 128),
+              "s: fp32 [R, ceil(F/128)]");
+  c10::cuda::CUDAGuard g(gu.get_device());
+  chk(swiglu_quant_fp8_1x128(reinterpret_cast<const __nv_bfloat16*>(gu.data_ptr()), reinterpret_cast<uint8_t*>(q.data_ptr()),
+                             s.data_ptr<float>(), R, F, stream_of(gu)),
+      "swiglu_quant_fp8");
+  count_launch(1);
+}
+
 void register_gemm_ops(py::module& m) {
+  m.def("swiglu_quant_fp8", &op_swiglu_quant_fp8);
   m.def("quant_fp8_1x128", &op_quant_fp8_1x128);
   m.def("quant_fp8_128x128", &op_quant_fp8_128x128);
   m.def("gemm_fp8", &op_gemm_fp8, py::arg("A"), py::arg("sa"), py::arg("B"), py::arg("sb"), py::arg("C"),

@@ -61,6 +61,7 @@ def main():
     T, d, F, W = cfg.tokens, cfg.d_model, cfg.ffn, world
     ms_fused = timeit(lambda: mlp.forward(x))
     ms_base = timeit(lambda: mlp.forward_baseline(x))
+    ms_fp8 = timeit(lambda: mlp.forward_fp8(x))
     # per-kernel rooflines
     xf_shard = x
     gu = comm.all_gather_gemm(xf_shard, mlp.w_up)
@@ -84,6 +85,14 @@ def main():
             "tflops_fused": round(mlp.flops() / (ms_fused / 1e3) / 1e12, 1),
             "ag_gemm": {"ms": round(ms_ag, 4), "roofline_ms": round(roof_ag, 4), "frac": round(roof_ag / ms_ag, 3)},
             "gemm_rs": {"ms": round(ms_rs, 4), "roofline_ms": round(roof_rs, 4), "frac": round(roof_rs / ms_rs, 3)},
+        }), flush=True)
+        print(json.dumps({
+            "bench": "tp_llama_mlp_fwd", "n_gpus": W, "tokens": T, "d": d, "ffn": F,
+            "dtype": "fp8 e4m3 block-scaled (1x128 activations, 128x128 weights)",
+            "ms_fp8": round(ms_fp8, 4), "ms_bf16_fused": round(ms_fused, 4), "ms_bf16_nccl_cublas": round(ms_base, 4),
+            "speedup_vs_bf16_nccl_cublas": round(ms_base / ms_fp8, 3),
+            "tokens_per_s_fp8": round(T / (ms_fp8 / 1e3), 1),
+            "tflops_fp8": round(mlp.flops() / (ms_fp8 / 1e3) / 1e12, 1),
         }), flush=True)
     dist.barrier()
     dist.destroy_process_group()

@@ -308,6 +308,20 @@ class DeviceCommunicator:
         self._C.gemm_reduce_scatter(self._comm, A, B, out, bias, float(alpha))
         return out
 
+    def gemm_fp8_reduce_scatter(self, A_q: torch.Tensor, A_s: torch.Tensor, B_q: torch.Tensor, B_s: torch.Tensor,
+                                out: Optional[torch.Tensor] = None, bias: Optional[torch.Tensor] = None,
+                                alpha: float = 1.0) -> torch.Tensor:
+        """Block-scaled fp8 row-parallel linear fused with reduce-scatter (bf16 output).
+
+        A_q: [M, K] e4m3 with 1x128 scales A_s [M, K/128]; B_q: [N, K] e4m3 with
+        128x128 block scales B_s [N/128, K/128]; out: [M/world, N] bf16.
+        """
+        M, N = A_q.shape[0], B_q.shape[0]
+        if out is None:
+            out = torch.empty(M // self.world_size, N, dtype=torch.bfloat16, device=A_q.device)
+        self._C.gemm_fp8_reduce_scatter(self._comm, A_q, A_s, B_q, B_s, out, bias, float(alpha))
+        return out
+
     def all_gather_gemm(self, x: torch.Tensor, B: torch.Tensor, out: Optional[torch.Tensor] = None,
                         bias: Optional[torch.Tensor] = None, act: Optional[str] = None,
                         pre: Optional[torch.Tensor] = None, alpha: float = 1.0) -> torch.Tensor:

@@ -7,6 +7,13 @@ one fused all-gather->GEMM kernel; SwiGLU is one elementwise kernel; the
 row-parallel down projection ([d, F/W] per rank) runs as one fused
 GEMM->reduce-scatter kernel. `forward_baseline` is the same block with NCCL
 collectives and cuBLAS GEMMs (the comparator).
+
+`forward_fp8` is the block-scaled fp8 variant of config 4: weights are kept
+as e4m3 with 128x128 block scales; the input shard is quantised per 1x128
+block, all-gathered as fp8 bytes + fp32 scales (half the NVLink bytes of
+bf16), multiplied on the fp8 promotion GEMM, SwiGLU is fused with the
+re-quantisation, and the down projection runs as one fused fp8
+GEMM->reduce-scatter kernel (bf16 output).
 """
 from __future__ import annotations
 
@@ -43,6 +50,13 @@ class TPLlamaMLP:
         self.w_up = (0.02 * torch.randn(2 * F, cfg.d_model, device=dev, generator=g)).to(torch.bfloat16)
         self.w_down = (0.02 * torch.randn(cfg.d_model, F, device=dev, generator=g)).to(torch.bfloat16)
         self.F = F
+        self._fp8 = None
+
+    def fp8_weights(self):
+        """e4m3 weights with 128x128 block scales (quantised once, cached)."""
+        if self._fp8 is None:
+            self._fp8 = (ops.quant_fp8_128x128(self.w_up), ops.quant_fp8_128x128(self.w_down))
+        return self._fp8
 
     def flops(self) -> float:
         """Forward FLOPs of the whole block (all ranks)."""
@@ -54,6 +68,17 @@ class TPLlamaMLP:
         gu = self.comm.all_gather_gemm(x_shard, self.w_up)          # [T, 2F/W]
         h = ops.swiglu(gu)                                          # [T, F/W]
         return self.comm.gemm_reduce_scatter(h, self.w_down)        # [T/W, d]
+
+    def forward_fp8(self, x_shard: torch.Tensor) -> torch.Tensor:
+        """x_shard: [T/W, d] bf16 -> y_shard: [T/W, d] bf16 through the block-scaled fp8 kernels."""
+        T, d = self.cfg.tokens, self.cfg.d_model
+        (wuq, wus), (wdq, wds) = self.fp8_weights()
+        xq, xs = ops.quant_fp8_1x128(x_shard)
+        xq_full = self.comm.all_gather(xq.view(torch.uint8).reshape(-1)).view(torch.float8_e4m3fn).view(T, d)
+        xs_full = self.comm.all_gather(xs.reshape(-1)).view(T, -1)
+        gu = ops.matmul_fp8(xq_full, xs_full, wuq, wus)             # [T, 2F/W]
+        hq, hs = ops.swiglu_quant_fp8(gu)                          # [T, F/W] e4m3
+        return self.comm.gemm_fp8_reduce_scatter(hq, hs, wdq, wds)  # [T/W, d]
 
     def forward_baseline(self, x_shard: torch.Tensor, group=None) -> torch.Tensor:
         """Same block with NCCL all_gather / reduce_scatter and cuBLAS GEMMs."""

@@ -2,5 +2,5 @@
 from .functional import (  # noqa: F401
     colsum, cross_entropy, cross_entropy_loss_only, embedding, gelu, layer_norm, linear, matmul_fp8, matmul_nt,
     quant_fp8_128x128, quant_fp8_1x128,
-    residual_layer_norm, swiglu,
+    residual_layer_norm, swiglu, swiglu_quant_fp8,
 )

@@ -419,3 +419,13 @@ def matmul_fp8(a_q, a_s, b_q, b_s, out=None, bias=None, act: int = 0, pre=None, 
         out = torch.empty(M, N, dtype=torch.bfloat16, device=a_q.device)
     _native.cuda().gemm_fp8(a_q, a_s, b_q, b_s, out, bias, pre, act, alpha)
     return out
+
+
+def swiglu_quant_fp8(gu):
+    """gu [R, 2F] bf16 (gate | up) -> (e4m3 [R, F], fp32 scales [R, ceil(F/128)]) of silu(gate) * up."""
+    R, F2 = gu.shape
+    F = F2 // 2
+    q = torch.empty(R, F, dtype=torch.float8_e4m3fn, device=gu.device)
+    s = torch.empty(R, (F + 127) // 128, dtype=torch.float32, device=gu.device)
+    _native.cuda().swiglu_quant_fp8(gu.contiguous(), q, s)
+    return q, s

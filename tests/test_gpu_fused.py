@@ -73,6 +73,36 @@ def _worker(rank, world, port, results):
     yb = mlp.forward_baseline(x)
     torch.cuda.synchronize()
     check("tp_mlp fused vs baseline", y, yb, atol=2e-2, rtol=5e-2)
+    # fp8 block-scaled block: against an fp32 evaluation of the same quantised math
+    from nexar_b200 import ops
+    import torch.distributed as dist
+    yf8 = mlp.forward_fp8(x)
+    torch.cuda.synchronize()
+    (wuq, wus), (wdq, wds) = mlp.fp8_weights()
+
+    def deq(q, s, bm):
+        R, K = q.shape
+        f = q.float()
+        sr = s.repeat_interleave(bm, 0)[:R] if bm > 1 else s
+        return f * sr.repeat_interleave(128, 1)[:, :K]
+
+    xs_all = [torch.empty_like(x) for _ in range(world)]
+    dist.all_gather(xs_all, x)
+    xfull = torch.cat(xs_all)
+    xq, xsc = ops.quant_fp8_1x128(xfull)
+    gu = deq(xq, xsc, 1) @ deq(wuq, wus, 128).t()
+    F = mlp.F
+    h = torch.nn.functional.silu(gu[:, :F]) * gu[:, F:]
+    hq, hs = ops.quant_fp8_1x128(h.to(torch.bfloat16))
+    yp = deq(hq, hs, 1) @ deq(wdq, wds, 128).t()
+    yp_all = [torch.empty_like(yp) for _ in range(world)]
+    dist.all_gather(yp_all, yp.contiguous())
+    rpr = cfg.tokens // world
+    yref = sum(yp_all)[rank * rpr:(rank + 1) * rpr]
+    check("tp_mlp fp8 vs fp32 of the quantised math", yf8, yref, atol=3e-2, rtol=5e-2)
+    rel = ((yf8.float() - yb.float()).norm() / yb.float().norm()).item()
+    if rel > 0.08:
+        errs.append(f"tp_mlp fp8 vs bf16 baseline: relative error {rel:.3f}")
     try:
         comm.check()
     except Exception as e:  # noqa: BLE001
