@@ -10,7 +10,19 @@ using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t
                                    const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                                    CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
+// Driver-API calls need the context current on the calling thread; the
+// runtime makes it current only on its own calls. A thread whose first CUDA
+// work is a tensor-map encode (PyTorch's autograd worker runs backward
+// kernels on one) would otherwise fail with an invalid-context error.
+void ensure_context() {
+  thread_local bool done = false;
+  if (done) return;
+  int dev = 0;
+  if (cudaGetDevice(&dev) == cudaSuccess && cudaSetDevice(dev) == cudaSuccess) done = true;
+}
+
 EncodeTiledFn encode_fn() {
+  ensure_context();
   static EncodeTiledFn fn = nullptr;
   static std::once_flag once;
   std::call_once(once, [] {
@@ -134,49 +146,95 @@ __global__ void __launch_bounds__(256) k_splitk_reduce(const float* __restrict__
 
 template <class Epi, int AMN, int BMN>
 cudaError_t launch_major(const void* A, const void* B, int M, int N, int K, long long lda, long long ldb,
-                         const CUtensorMap& tout, const CUtensorMap& tpre, const Epi& epi, int splits,
+                         const CUtensorMap& tout, const CUtensorMap& tpre, const Epi& epi, int splits, int tbn,
                          cudaStream_t s) {
-  return launch_gemm_generic<Epi, gemm::NoGate, 0, AMN, BMN>(A, B, M, N, K, lda, ldb, tout, tpre, 0, epi,
-                                                              gemm::NoGate{}, 0, s, splits);
+  (void)tbn;  // only 256-wide tiles are planned (see choose_plan)
+  return launch_gemm_generic<Epi, gemm::NoGate, 0, AMN, BMN, 256>(A, B, M, N, K, lda, ldb, tout, tpre, 0, epi,
+                                                                   gemm::NoGate{}, 0, s, splits);
 }
 
 template <class Epi>
 cudaError_t launch_any_major(bool a_mn, bool b_mn, const void* A, const void* B, int M, int N, int K, long long lda,
                              long long ldb, const CUtensorMap& tout, const CUtensorMap& tpre, const Epi& epi,
-                             int splits, cudaStream_t s) {
-  if (!a_mn && !b_mn) return launch_major<Epi, 0, 0>(A, B, M, N, K, lda, ldb, tout, tpre, epi, splits, s);
-  if (!a_mn && b_mn) return launch_major<Epi, 0, 1>(A, B, M, N, K, lda, ldb, tout, tpre, epi, splits, s);
-  if (a_mn && !b_mn) return launch_major<Epi, 1, 0>(A, B, M, N, K, lda, ldb, tout, tpre, epi, splits, s);
-  return launch_major<Epi, 1, 1>(A, B, M, N, K, lda, ldb, tout, tpre, epi, splits, s);
+                             int splits, int tbn, cudaStream_t s) {
+  if (!a_mn && !b_mn) return launch_major<Epi, 0, 0>(A, B, M, N, K, lda, ldb, tout, tpre, epi, splits, tbn, s);
+  if (!a_mn && b_mn) return launch_major<Epi, 0, 1>(A, B, M, N, K, lda, ldb, tout, tpre, epi, splits, tbn, s);
+  if (a_mn && !b_mn) return launch_major<Epi, 1, 0>(A, B, M, N, K, lda, ldb, tout, tpre, epi, splits, tbn, s);
+  return launch_major<Epi, 1, 1>(A, B, M, N, K, lda, ldb, tout, tpre, epi, splits, tbn, s);
+}
+
+// Cost model over (tile width, K splits): k-blocks per split x waves x (one
+// 128 x tbn x 64 block at the per-SM tensor rate, ~0.43 us for tbn = 256) +
+// the fp32 partial round trip through HBM.
+void choose_plan(int M, int N, int K, int* tbn_out, int* splits_out, bool allow_split) {
+  const int sm = gemm_sm_count();
+  const int kb = (K + gemm::BK - 1) / gemm::BK;
+  int best_sp = 1, best_bn = 256;
+  double best_t = 1e30;
+  // 192-wide tiles fix the wave count for N = 768 but were measured no faster:
+  // these GEMMs are bound by L2 operand traffic, which a narrower tile raises
+  // per FLOP. The width stays a kernel parameter; the plan uses 256.
+  const int widths[1] = {256};
+  for (int wi = 0; wi < 1; ++wi) {
+    const int bn = widths[wi];
+    const long long tiles = (long long)((M + gemm::BM - 1) / gemm::BM) * ((N + bn - 1) / bn);
+    for (int sp = 1; sp <= (allow_split ? 16 : 1); ++sp) {
+      if (sp > 1 && kb / sp < 4) break;
+      const int kps = (kb + sp - 1) / sp;
+      const int eff = (kb + kps - 1) / kps;
+      const long long waves = (tiles * eff + sm - 1) / sm;
+      double t = (double)kps * (double)waves * 0.43 * bn / 256.0;
+      if (eff > 1) t += ((double)eff * M * N * 8.0 + (double)M * N * 2.0) / 6.0e6;
+      if (t < best_t * 0.97) {
+        best_t = t;
+        best_sp = eff;
+        best_bn = bn;
+      }
+    }
+  }
+  *tbn_out = best_bn;
+  *splits_out = best_sp;
+}
+// Tile width for a given split count: fewer waves of (narrower) tiles.
+int width_for(int M, int N, int splits) {
+  const int sm = gemm_sm_count();
+  double best = 1e30;
+  int best_bn = 256;
+  const int widths[1] = {256};
+  for (int wi = 0; wi < 1; ++wi) {
+    const int bn = widths[wi];
+    const long long tiles = (long long)((M + gemm::BM - 1) / gemm::BM) * ((N + bn - 1) / bn) * splits;
+    const double t = (double)((tiles + sm - 1) / sm) * bn;
+    if (t < best * 0.97) {
+      best = t;
+      best_bn = bn;
+    }
+  }
+  return best_bn;
 }
 }  // namespace
 
 int gemm_choose_splits(int M, int N, int K) {
-  // Model: time = k-blocks per split x waves x (one 128x256x64 block at the
-  // per-SM tensor rate, ~0.43 us) + the fp32 partial round trip through HBM.
-  const int sm = gemm_sm_count();
-  const long long tiles = (long long)((M + gemm::BM - 1) / gemm::BM) * ((N + gemm::BN - 1) / gemm::BN);
-  const int kb = (K + gemm::BK - 1) / gemm::BK;
-  int best = 1;
-  double best_t = 1e30;
-  for (int sp = 1; sp <= 16; ++sp) {
-    if (sp > 1 && kb / sp < 4) break;
-    const int kps = (kb + sp - 1) / sp;
-    const int eff = (kb + kps - 1) / kps;
-    const long long waves = (tiles * eff + sm - 1) / sm;
-    double t = (double)kps * (double)waves * 0.43;
-    if (eff > 1) t += ((double)eff * M * N * 8.0 + (double)M * N * 2.0) / 6.0e6;
-    if (t < best_t * 0.97) {
-      best_t = t;
-      best = eff;
-    }
-  }
-  return best;
+  int bn, sp;
+  choose_plan(M, N, K, &bn, &sp, true);
+  return sp;
 }
 
 size_t gemm_split_workspace_bytes(int M, int N, int splits) {
   return splits > 1 ? (size_t)splits * M * N * sizeof(float) : 0;
 }
+
+namespace {
+thread_local const char* g_gemm_fail = "";
+thread_local const char* g_gemm_stale = "";
+inline cudaError_t fail_at(cudaError_t e, const char* where) {
+  if (e != cudaSuccess) g_gemm_fail = where;
+  return e;
+}
+}  // namespace
+
+const char* gemm_last_failure() { return g_gemm_fail; }
+const char* gemm_stale_error() { return g_gemm_stale; }
 
 cudaError_t gemm_bf16_ex(const __nv_bfloat16* A, const __nv_bfloat16* B, __nv_bfloat16* C, int M, int N, int K,
                          long long lda, long long ldb, long long ldc, bool a_mn, bool b_mn,
@@ -184,7 +242,20 @@ cudaError_t gemm_bf16_ex(const __nv_bfloat16* A, const __nv_bfloat16* B, __nv_bf
                          __nv_bfloat16* pre_act, int act, float alpha, bool accumulate, int splits, float* ws,
                          size_t ws_bytes, cudaStream_t s) {
   if (M <= 0 || N <= 0 || K <= 0) return cudaSuccess;
-  if (splits <= 0) splits = gemm_choose_splits(M, N, K);
+  g_gemm_fail = "";
+  {
+    // A launch error is reported by the next cudaGetLastError() of the same
+    // host thread. Take over an error left by an unrelated earlier call on
+    // this thread so it is not blamed on this launch.
+    const cudaError_t stale = cudaPeekAtLastError();
+    if (stale != cudaSuccess) {
+      cudaGetLastError();
+      g_gemm_stale = cudaGetErrorName(stale);
+    }
+  }
+  int tbn = 256;
+  if (splits <= 0) choose_plan(M, N, K, &tbn, &splits, true);
+  else tbn = width_for(M, N, splits);
   const int kb = (K + gemm::BK - 1) / gemm::BK;
   if (splits > kb) splits = kb;
   if (splits > 1) {
@@ -195,24 +266,25 @@ cudaError_t gemm_bf16_ex(const __nv_bfloat16* A, const __nv_bfloat16* B, __nv_bf
     splits = 1;
   if (splits > 1) {
     CUtensorMap tpart;
-    cudaError_t e = make_tmap_f32_3d(&tpart, ws, splits, M, N);
+    cudaError_t e = fail_at(make_tmap_f32_3d(&tpart, ws, splits, M, N), "split-K partial tensor map");
     if (e != cudaSuccess) return e;
     gemm::EpiSplitF32 epi{alpha};
-    e = launch_any_major(a_mn, b_mn, A, B, M, N, K, lda, ldb, tpart, tpart, epi, splits, s);
+    e = fail_at(launch_any_major(a_mn, b_mn, A, B, M, N, K, lda, ldb, tpart, tpart, epi, splits, tbn, s),
+                "split-K GEMM (operand maps or launch)");
     if (e != cudaSuccess) return e;
     const long long n4 = (long long)M * (N / 4);
     long long g = (n4 + 255) / 256;
     if (g > gemm_sm_count() * 8) g = gemm_sm_count() * 8;
     k_splitk_reduce<<<(int)g, 256, 0, s>>>(ws, splits, M, N, bias, residual, ldr, C, ldc, pre_act, act,
                                            accumulate ? 1 : 0);
-    return cudaGetLastError();
+    return fail_at(cudaGetLastError(), "split-K reduction launch");
   }
   CUtensorMap tout, tpre;
-  cudaError_t e = make_tmap_bf16(&tout, C, M, N, ldc, 32, 64);
+  cudaError_t e = fail_at(make_tmap_bf16(&tout, C, M, N, ldc, 32, 64), "output tensor map");
   if (e != cudaSuccess) return e;
   tpre = tout;
   if (pre_act) {
-    e = make_tmap_bf16(&tpre, pre_act, M, N, ldc, 32, 64);
+    e = fail_at(make_tmap_bf16(&tpre, pre_act, M, N, ldc, 32, 64), "pre-activation tensor map");
     if (e != cudaSuccess) return e;
   }
   if (accumulate) {
@@ -221,7 +293,8 @@ cudaError_t gemm_bf16_ex(const __nv_bfloat16* A, const __nv_bfloat16* B, __nv_bf
     ldr = ldc;
   }
   gemm::EpiStore epi{bias, residual, ldr, alpha, act, pre_act != nullptr};
-  return launch_any_major(a_mn, b_mn, A, B, M, N, K, lda, ldb, tout, tpre, epi, 1, s);
+  return fail_at(launch_any_major(a_mn, b_mn, A, B, M, N, K, lda, ldb, tout, tpre, epi, 1, tbn, s),
+                 "GEMM (operand maps or launch)");
 }
 
 cudaError_t gemm_bf16(const __nv_bfloat16* A, const __nv_bfloat16* B, __nv_bfloat16* C, int M, int N, int K,

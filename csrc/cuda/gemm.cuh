@@ -37,9 +37,16 @@ namespace gemm {
 
 constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4, THREADS = 192;
 constexpr int A_BYTES = BM * BK * 2, B_BYTES = BN * BK * 2, STAGE_BYTES = A_BYTES + B_BYTES;
+// The tile width is a kernel parameter (any multiple of 64 up to 256). A
+// 128x192 tile fixes the wave count of N = 768 GEMMs on 148 SMs but measured
+// no faster there (L2 operand traffic per FLOP rises), so launches use 256.
+__host__ __device__ constexpr int stages_for(int) { return 4; }
 constexpr int EPI_WARPS = 4, EPI_BUF_BYTES = 32 * 64 * 2;  // one 32x64 bf16 block
 constexpr int EPI_BYTES = EPI_WARPS * 2 * EPI_BUF_BYTES;   // double-buffered per warp
 constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + EPI_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+__host__ __device__ constexpr int smem_bytes_for(int tbn) {
+  return stages_for(tbn) * (A_BYTES + tbn * BK * 2) + EPI_BYTES + 1024 + 256;
+}
 constexpr uint64_t kWaitLimit = 2000000000ull;  // ns: 2 s per wait, far above any legitimate wait
 
 struct TileSched {
@@ -197,12 +204,19 @@ struct EpiSplitF32 {
 template <class Epi> struct EpiTraits { static constexpr bool f32_split = false; };
 template <> struct EpiTraits<EpiSplitF32> { static constexpr bool f32_split = true; };
 
-template <class Epi, class Gate = NoGate, int EXTRA = 0, int AMN = 0, int BMN = 0>
+template <class Epi, class Gate = NoGate, int EXTRA = 0, int AMN = 0, int BMN = 0, int TBN = 256>
 __global__ void __launch_bounds__(THREADS + 32 * EXTRA, 1)
 k_gemm_bf16(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
             const __grid_constant__ CUtensorMap tmOut, const __grid_constant__ CUtensorMap tmPre, int M, int N,
             int K, int m_rotate, int splits, Epi epi, Gate gate, unsigned int* err) {
   using namespace sm100;
+  static_assert(TBN % 64 == 0 && TBN >= 64 && TBN <= 256, "tile width");
+  // Tile-width-dependent geometry (shadows the 256-wide defaults).
+  constexpr int BN = TBN;
+  constexpr int B_BYTES = BN * BK * 2;
+  constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  constexpr int STAGES = stages_for(TBN);
+  (void)B_BYTES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* epi_smem = smem + STAGES * STAGE_BYTES;

@@ -24,6 +24,11 @@ cudaError_t gemm_bf16_ex(const __nv_bfloat16* A, const __nv_bfloat16* B, __nv_bf
                          __nv_bfloat16* pre_act, int act, float alpha, bool accumulate, int splits, float* ws,
                          size_t ws_bytes, cudaStream_t s);
 int gemm_choose_splits(int M, int N, int K);
+// Which step of the last failing gemm_bf16_ex call on this thread failed.
+const char* gemm_last_failure();
+// Name of a CUDA error that an unrelated earlier call left on this host thread
+// and that the last gemm_bf16_ex call cleared before launching ("" if none).
+const char* gemm_stale_error();
 size_t gemm_split_workspace_bytes(int M, int N, int splits);
 
 // Nonzero if any GEMM launch on this device gave up on a bounded wait.

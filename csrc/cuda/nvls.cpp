@@ -134,6 +134,7 @@ bool DeviceComm::nvls_supported() const {
 
 int DeviceComm::nvls_create(uint64_t bytes) {
   const DriverApi& a = api();
+  check_cuda(cudaSetDevice(device_), "cudaSetDevice");  // driver calls need the context current
   if (!a.ok) throw std::runtime_error("nexar_b200: CUDA driver multicast API unavailable");
   if (nvls_mc_handle_) throw std::runtime_error("nexar_b200: NVLS region already created");
   nvls_size_ = round_up(bytes, nvls_granule(a, world_, device_));
@@ -150,6 +151,7 @@ int DeviceComm::nvls_create(uint64_t bytes) {
 
 void DeviceComm::nvls_import(int fd, uint64_t bytes) {
   const DriverApi& a = api();
+  check_cuda(cudaSetDevice(device_), "cudaSetDevice");  // driver calls need the context current
   if (!a.ok) throw std::runtime_error("nexar_b200: CUDA driver multicast API unavailable");
   if (nvls_mc_handle_) throw std::runtime_error("nexar_b200: NVLS region already created");
   nvls_size_ = round_up(bytes, nvls_granule(a, world_, device_));
@@ -163,6 +165,7 @@ void DeviceComm::nvls_import(int fd, uint64_t bytes) {
 
 void DeviceComm::nvls_add_device() {
   const DriverApi& a = api();
+  check_cuda(cudaSetDevice(device_), "cudaSetDevice");  // driver calls need the context current
   if (!nvls_mc_handle_) throw std::runtime_error("nexar_b200: NVLS region not created");
   CUdevice d;
   check_cu(a.DeviceGet(&d, device_), "cuDeviceGet");

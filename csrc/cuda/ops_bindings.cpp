@@ -278,14 +278,18 @@ void op_gemm_ex(const at::Tensor& A, const at::Tensor& B, const at::Tensor& C, b
   if (sp <= 0) sp = gemm_choose_splits(M, N, K);
   const size_t wsb = ws ? (size_t)ws->numel() * 4 : 0;
   if (sp > 1 && wsb < gemm_split_workspace_bytes(M, N, sp)) sp = 1;
-  chk(gemm_bf16_ex(reinterpret_cast<const __nv_bfloat16*>(A.data_ptr()),
-                   reinterpret_cast<const __nv_bfloat16*>(B.data_ptr()), reinterpret_cast<__nv_bfloat16*>(C.data_ptr()),
-                   M, N, K, A.stride(0), B.stride(0), C.stride(0), a_mn, b_mn,
-                   bias ? reinterpret_cast<const __nv_bfloat16*>(bias->data_ptr()) : nullptr,
-                   residual ? reinterpret_cast<const __nv_bfloat16*>(residual->data_ptr()) : nullptr,
-                   residual ? residual->stride(0) : 0, pre ? reinterpret_cast<__nv_bfloat16*>(pre->data_ptr()) : nullptr,
-                   (int)act, (float)alpha, accumulate, sp, ws ? ws->data_ptr<float>() : nullptr, wsb, stream_of(A)),
-      "gemm_ex");
+  const cudaError_t err = gemm_bf16_ex(
+      reinterpret_cast<const __nv_bfloat16*>(A.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(B.data_ptr()),
+      reinterpret_cast<__nv_bfloat16*>(C.data_ptr()), M, N, K, A.stride(0), B.stride(0), C.stride(0), a_mn, b_mn,
+      bias ? reinterpret_cast<const __nv_bfloat16*>(bias->data_ptr()) : nullptr,
+      residual ? reinterpret_cast<const __nv_bfloat16*>(residual->data_ptr()) : nullptr,
+      residual ? residual->stride(0) : 0, pre ? reinterpret_cast<__nv_bfloat16*>(pre->data_ptr()) : nullptr, (int)act,
+      (float)alpha, accumulate, sp, ws ? ws->data_ptr<float>() : nullptr, wsb, stream_of(A));
+  const std::string what = std::string("gemm_ex [") + gemm_last_failure() + "; earlier error on this thread: " +
+                           gemm_stale_error() + "] M=" + std::to_string(M) + " N=" + std::to_string(N) +
+                           " K=" + std::to_string(K) + " a_t=" + std::to_string(a_mn) + " b_t=" + std::to_string(b_mn) +
+                           " splits=" + std::to_string(sp);
+  chk(err, what.c_str());
   count_launch(sp > 1 ? 2 : 1);
 }
 
