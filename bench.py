@@ -1,4 +1,4 @@
-"""Flagship benchmark: data-parallel GPT-2-small training step.
+"""Flagship benchmark: data-parallel GPT-2-small training step (GPT-2-small, micro-batch 8 x 1024 tokens per GPU, bf16).
 
     python bench.py --gpus N --steps K --warmup W            # nexar_b200 (this repo)
     python bench.py --impl reference ...                     # the reference (unavailable here)

@@ -1,4 +1,4 @@
-"""Device collective sweep: nexar_b200 peer-memory kernels vs NCCL.
+"""Device collective sweep: nexar_b200 peer-memory kernels vs NCCL (1 KB - 1 GB, 2/4/8 GPUs).
 
     torchrun --nproc-per-node N --master-addr 127.0.0.1 -m nexar_b200.bench.collectives \
         [--ops all_reduce,reduce_scatter,all_gather,all_to_all,broadcast] [--dtype bf16]

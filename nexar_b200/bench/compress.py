@@ -1,4 +1,4 @@
-"""Top-k + fp8 compressed all-reduce vs uncompressed all-reduce (second part).
+"""Top-k + fp8 compressed all-reduce vs uncompressed all-reduce (1 GiB bf16 gradient, top-1 %).
 
     torchrun --nproc-per-node N --master-addr 127.0.0.1 -m nexar_b200.bench.compress \
         [--numel 536870912] [--ratio 0.01] [--iters 10] [--warmup 3]

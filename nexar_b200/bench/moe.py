@@ -1,5 +1,5 @@
 """Expert-parallel MoE layer forward: fused dispatch/combine kernels vs
-NCCL all_to_all_single + torch permutation + cuBLAS.
+NCCL all_to_all_single + torch permutation + cuBLAS (the MoE benchmark configuration).
 
     torchrun --nproc-per-node N --master-addr 127.0.0.1 -m nexar_b200.bench.moe [--tokens 16384]
 """

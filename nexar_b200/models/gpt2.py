@@ -1,6 +1,6 @@
 """GPT-2 decoder built on the nexar_b200 sm_100a kernels.
 
-12 layers, d=768, 12 heads, vocab 50257 (padded to 50304
+Benchmark configuration: 12 layers, d=768, 12 heads, vocab 50257 (padded to 50304
 for 16-byte aligned rows), context 1024, bf16 compute, N(0, 0.02) init with
 residual projections scaled by 1/sqrt(2*n_layer).
 

@@ -1,5 +1,5 @@
 """Llama-style SwiGLU MLP block, tensor parallel over the GPUs of one box
-(d=4096, ffn=14336, TP=8, 8192 tokens, bf16).
+(benchmark configuration: d=4096, ffn=14336, TP=8, 8192 tokens, bf16).
 
 Sequence-parallel layout: each rank holds T/W tokens of the input and of the
 output. Column-parallel up projection (gate|up, [2F/W, d] per rank) runs as

@@ -1,4 +1,4 @@
-"""Expert-parallel MoE layer: one SwiGLU expert per GPU,
+"""Expert-parallel MoE layer (8 experts on 8 GPUs, top-2 router): one SwiGLU expert per GPU,
 top-2 softmax routing, d=4096, expert ffn=14336, 16384 tokens per GPU, bf16.
 
 forward():          route kernel -> device all-gather of the per-expert counts

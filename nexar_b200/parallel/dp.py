@@ -1,4 +1,4 @@
-"""Data-parallel training entry point.
+"""Data-parallel training entry point (the GPT-2-small benchmark configuration).
 
 One process per GPU. Gradients live in one flat bf16 buffer inside the
 symmetric heap, split into ~25 MB buckets (contiguous ranges). A
