@@ -123,12 +123,16 @@ std::vector<Rank> RecoveryOrchestrator::agree(const std::shared_ptr<NexarClient>
     std::set<Rank> uni(my_dead.begin(), my_dead.end());
     for (Rank src : alive) {
       if (src == leader) continue;
-      Message m;
-      if (!wait_control(c, src, MsgKind::RecoveryVote, timeout, &m, interrupt)) {
-        *interrupted = true;
-        return {};
+      auto it = votes_.find(src);
+      if (it == votes_.end()) {
+        Message m;
+        if (!wait_control(c, src, MsgKind::RecoveryVote, timeout, &m, interrupt)) {
+          *interrupted = true;
+          return {};
+        }
+        it = votes_.emplace(src, m.dead_ranks).first;
       }
-      uni.insert(m.dead_ranks.begin(), m.dead_ranks.end());
+      uni.insert(it->second.begin(), it->second.end());
     }
     std::vector<Rank> agreed(uni.begin(), uni.end());
     for (Rank dst : alive)
@@ -168,6 +172,7 @@ void RecoveryOrchestrator::recover(std::vector<Rank> dead_in) {
       }
     }
     if (interrupted) continue;
+    votes_.clear();
     auto nc = c->rebuild_excluding(agreed);
     const Rank old = c->rank();
     {

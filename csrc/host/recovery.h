@@ -17,6 +17,7 @@
 #pragma once
 
 #include <deque>
+#include <map>
 
 #include "client.h"
 
@@ -57,6 +58,11 @@ class RecoveryOrchestrator {
   RecoveryPolicy policy_;
   std::deque<RecoveryEvent> events_;
   std::string error_;
+  // Leader side: the latest vote of each survivor, kept across agreement
+  // attempts (a vote consumed by an attempt that a later failure interrupted
+  // is not sent again by a voter that already knew every failure). Cleared
+  // after a rebuild, which renumbers the ranks. Orchestrator thread only.
+  std::map<Rank, std::vector<Rank>> votes_;
   std::thread thr_;
   std::atomic<bool> stop_{false};
 };
