@@ -1,7 +1,9 @@
 // Host side of the tcgen05 GEMM: tensor-map creation and launch.
+#include <cstdlib>
 #include <mutex>
 
 #include "gemm_launch.cuh"
+#include "gemm2sm.cuh"
 
 namespace nexar {
 
@@ -163,6 +165,106 @@ cudaError_t launch_any_major(bool a_mn, bool b_mn, const void* A, const void* B,
   return launch_major<Epi, 1, 1>(A, B, M, N, K, lda, ldb, tout, tpre, epi, splits, tbn, s);
 }
 
+bool use_2sm();
+
+// ---- 2-SM (CTA pair) launch
+template <class Epi, int AMN, int BMN, int TN>
+cudaError_t launch_2sm_major(const void* A, const void* B, int M, int N, int K, long long lda, long long ldb,
+                             const CUtensorMap& tout, const CUtensorMap& tpre, const Epi& epi, int splits,
+                             cudaStream_t s) {
+  using namespace gemm2;
+  constexpr int SMEM_BYTES = smem_bytes_2sm(TN);
+  CUtensorMap ta, tb;
+  cudaError_t e = AMN ? make_tmap_bf16(&ta, A, K, M, lda, 64, 64) : make_tmap_bf16(&ta, A, M, K, lda, HM, BK);
+  if (e != cudaSuccess) return e;
+  e = BMN ? make_tmap_bf16(&tb, B, K, N, ldb, 64, 64) : make_tmap_bf16(&tb, B, N, K, ldb, TN / 2, BK);
+  if (e != cudaSuccess) return e;
+  static int max_pairs = -1;
+  if (max_pairs < 0) {
+    cudaFuncSetAttribute(k_gemm_bf16_2sm<Epi, AMN, BMN, TN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         SMEM_BYTES);
+    cudaLaunchConfig_t q = {};
+    q.gridDim = dim3(2 * 74);
+    q.blockDim = dim3(THREADS);
+    q.dynamicSmemBytes = SMEM_BYTES;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = 2;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    q.attrs = at;
+    q.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, k_gemm_bf16_2sm<Epi, AMN, BMN, TN>, &q) != cudaSuccess || n <= 0) {
+      cudaGetLastError();
+      n = gemm_sm_count() / 2;
+    }
+    max_pairs = n;
+  }
+  const long long tiles = (long long)((M + TM - 1) / TM) * ((N + TN - 1) / TN) * splits;
+  const int pairs = (int)(tiles < max_pairs ? tiles : max_pairs);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * pairs);
+  cfg.blockDim = dim3(THREADS);
+  cfg.dynamicSmemBytes = SMEM_BYTES;
+  cfg.stream = s;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = 2;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, k_gemm_bf16_2sm<Epi, AMN, BMN, TN>, ta, tb, tout, tpre, M, N, K, splits, epi,
+                            gemm_err_word());
+}
+
+template <class Epi, int TN>
+cudaError_t launch_2sm_tn(bool a_mn, bool b_mn, const void* A, const void* B, int M, int N, int K, long long lda,
+                          long long ldb, const CUtensorMap& tout, const CUtensorMap& tpre, const Epi& epi, int splits,
+                          cudaStream_t s) {
+  if (!a_mn && !b_mn) return launch_2sm_major<Epi, 0, 0, TN>(A, B, M, N, K, lda, ldb, tout, tpre, epi, splits, s);
+  if (!a_mn && b_mn) return launch_2sm_major<Epi, 0, 1, TN>(A, B, M, N, K, lda, ldb, tout, tpre, epi, splits, s);
+  if (a_mn && !b_mn) return launch_2sm_major<Epi, 1, 0, TN>(A, B, M, N, K, lda, ldb, tout, tpre, epi, splits, s);
+  return launch_2sm_major<Epi, 1, 1, TN>(A, B, M, N, K, lda, ldb, tout, tpre, epi, splits, s);
+}
+
+template <class Epi>
+cudaError_t launch_2sm_any(bool a_mn, bool b_mn, const void* A, const void* B, int M, int N, int K, long long lda,
+                           long long ldb, const CUtensorMap& tout, const CUtensorMap& tpre, const Epi& epi,
+                           int splits, int tn, cudaStream_t s) {
+  (void)tn;  // 256-wide pair tiles only (128-wide measured slower at N = 768)
+  return launch_2sm_tn<Epi, 256>(a_mn, b_mn, A, B, M, N, K, lda, ldb, tout, tpre, epi, splits, s);
+}
+
+// Kernel choice for one GEMM: 1-SM 128x256 tiles or CTA-pair 256x256 tiles.
+// Wave model: waves x per-SM work per tile, the pair tile counted 0.93x
+// (measured on 8192^3: it streams a third less operand data from L2; GPT-2
+// step 10.16 vs 10.47 ms). A 256x128 pair tile fixes the wave count of
+// N = 768 GEMMs but measured 20-30 % slower, so it is not offered.
+// Returns 0 (1-SM) or 256 (pair tile width).
+int choose_kernel(int M, int N, int splits) {
+  if (!use_2sm()) return 0;
+  const int sm = gemm_sm_count();
+  const int pairs = sm / 2;
+  const double one = (double)((((long long)((M + 127) / 128) * ((N + 255) / 256) * splits) + sm - 1) / sm) * 256.0;
+  double best = one;
+  int pick = 0;
+  const int tns[1] = {256};
+  for (int i = 0; i < 1; ++i) {
+    const int tn = tns[i];
+    const long long tiles = (long long)((M + 255) / 256) * ((N + tn - 1) / tn) * splits;
+    // per-SM work per wave ~ tn; the 256-wide pair tile streams a third less
+    // operand data per FLOP than the 1-SM tile, the 128-wide one the same.
+    const double t = (double)((tiles + pairs - 1) / pairs) * tn * (tn == 256 ? 0.93 : 1.0);
+    if (t < best * 0.97) {
+      best = t;
+      pick = tn;
+    }
+  }
+  return pick;
+}
+
 // Cost model over (tile width, K splits): k-blocks per split x waves x (one
 // 128 x tbn x 64 block at the per-SM tensor rate, ~0.43 us for tbn = 256) +
 // the fp32 partial round trip through HBM.
@@ -226,6 +328,14 @@ size_t gemm_split_workspace_bytes(int M, int N, int splits) {
 
 namespace {
 thread_local const char* g_gemm_fail = "";
+int g_gemm_2sm = -1;  // -1: read NEXAR_GEMM_2SM once (default on), 0 off, 1 on
+bool use_2sm() {
+  if (g_gemm_2sm < 0) {
+    const char* v = std::getenv("NEXAR_GEMM_2SM");
+    g_gemm_2sm = (v && v[0] == '0') ? 0 : 1;
+  }
+  return g_gemm_2sm == 1;
+}
 thread_local const char* g_gemm_stale = "";
 inline cudaError_t fail_at(cudaError_t e, const char* where) {
   if (e != cudaSuccess) g_gemm_fail = where;
@@ -234,6 +344,8 @@ inline cudaError_t fail_at(cudaError_t e, const char* where) {
 }  // namespace
 
 const char* gemm_last_failure() { return g_gemm_fail; }
+void gemm_set_2sm(int on) { g_gemm_2sm = on ? 1 : 0; }
+int gemm_get_2sm() { return use_2sm() ? 1 : 0; }
 const char* gemm_stale_error() { return g_gemm_stale; }
 
 cudaError_t gemm_bf16_ex(const __nv_bfloat16* A, const __nv_bfloat16* B, __nv_bfloat16* C, int M, int N, int K,
@@ -269,8 +381,13 @@ cudaError_t gemm_bf16_ex(const __nv_bfloat16* A, const __nv_bfloat16* B, __nv_bf
     cudaError_t e = fail_at(make_tmap_f32_3d(&tpart, ws, splits, M, N), "split-K partial tensor map");
     if (e != cudaSuccess) return e;
     gemm::EpiSplitF32 epi{alpha};
-    e = fail_at(launch_any_major(a_mn, b_mn, A, B, M, N, K, lda, ldb, tpart, tpart, epi, splits, tbn, s),
-                "split-K GEMM (operand maps or launch)");
+    const int pk = choose_kernel(M, N, splits);
+    if (pk)
+      e = fail_at(launch_2sm_any(a_mn, b_mn, A, B, M, N, K, lda, ldb, tpart, tpart, epi, splits, pk, s),
+                  "2-SM split-K GEMM (operand maps or launch)");
+    else
+      e = fail_at(launch_any_major(a_mn, b_mn, A, B, M, N, K, lda, ldb, tpart, tpart, epi, splits, tbn, s),
+                  "split-K GEMM (operand maps or launch)");
     if (e != cudaSuccess) return e;
     const long long n4 = (long long)M * (N / 4);
     long long g = (n4 + 255) / 256;
@@ -293,6 +410,9 @@ cudaError_t gemm_bf16_ex(const __nv_bfloat16* A, const __nv_bfloat16* B, __nv_bf
     ldr = ldc;
   }
   gemm::EpiStore epi{bias, residual, ldr, alpha, act, pre_act != nullptr};
+  if (const int pk = choose_kernel(M, N, 1))
+    return fail_at(launch_2sm_any(a_mn, b_mn, A, B, M, N, K, lda, ldb, tout, tpre, epi, 1, pk, s),
+                   "2-SM GEMM (operand maps or launch)");
   return fail_at(launch_any_major(a_mn, b_mn, A, B, M, N, K, lda, ldb, tout, tpre, epi, 1, tbn, s),
                  "GEMM (operand maps or launch)");
 }

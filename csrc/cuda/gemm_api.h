@@ -24,6 +24,10 @@ cudaError_t gemm_bf16_ex(const __nv_bfloat16* A, const __nv_bfloat16* B, __nv_bf
                          __nv_bfloat16* pre_act, int act, float alpha, bool accumulate, int splits, float* ws,
                          size_t ws_bytes, cudaStream_t s);
 int gemm_choose_splits(int M, int N, int K);
+// Plain GEMMs may run on the 2-SM (CTA pair, 256x256 tile) kernel (default
+// on; NEXAR_GEMM_2SM=0 or gemm_set_2sm(0) keeps every GEMM on the 1-SM kernel).
+void gemm_set_2sm(int on);
+int gemm_get_2sm();
 // Which step of the last failing gemm_bf16_ex call on this thread failed.
 const char* gemm_last_failure();
 // Name of a CUDA error that an unrelated earlier call left on this host thread

@@ -373,6 +373,8 @@ void register_gemm_ops(py::module& m) {
         py::arg("pre") = py::none(), py::arg("act") = 0, py::arg("alpha") = 1.0, py::arg("accumulate") = false,
         py::arg("splits") = 1, py::arg("ws") = py::none());
   m.def("gemm_choose_splits", &gemm_choose_splits);
+  m.def("gemm_set_2sm", &gemm_set_2sm);
+  m.def("gemm_get_2sm", &gemm_get_2sm);
   m.def("gemm_split_workspace_bytes",
         [](int64_t M, int64_t N, int64_t sp) { return (int64_t)gemm_split_workspace_bytes(M, N, sp); });
   m.def("gemm", &op_gemm, py::arg("A"), py::arg("B"), py::arg("C"), py::arg("bias") = py::none(),

@@ -21,6 +21,7 @@ def main():
                                         "8192x50304x768,8192x3584x4096,8192x4096x1792")
     ap.add_argument("--majors", default="nn")
     ap.add_argument("--iters", type=int, default=30)
+    ap.add_argument("--pair", action="store_true", help="also time the 2-SM (CTA pair) kernel")
     ap.add_argument("--fp8", action="store_true",
                     help="block-scaled e4m3 GEMM (1x128 / 128x128 scales) vs torch._scaled_mm and bf16 cuBLAS")
     args = ap.parse_args()
@@ -40,8 +41,17 @@ def main():
             opBt = B if b_t else B.t()
             splits = C.gemm_choose_splits(M, N, K)
             res = {}
-            for name, fn in (("nexar", lambda: ops.matmul_nt(A, B, out=out, a_t=a_t, b_t=b_t)),
-                             ("cublas", lambda: torch.matmul(opA, opBt, out=out))):
+            arms = [("nexar", lambda: ops.matmul_nt(A, B, out=out, a_t=a_t, b_t=b_t)),
+                    ("cublas", lambda: torch.matmul(opA, opBt, out=out))]
+            if args.pair:
+                def pair_fn():
+                    C.gemm_set_2sm(1)
+                    try:
+                        ops.matmul_nt(A, B, out=out, a_t=a_t, b_t=b_t)
+                    finally:
+                        C.gemm_set_2sm(0)
+                arms.insert(1, ("nexar_2sm", pair_fn))
+            for name, fn in arms:
                 for _ in range(5):
                     fn()
                 torch.cuda.synchronize()

@@ -124,3 +124,32 @@ def test_gemm_rejects_unaligned_transposed_operand(cuda0):
     B = torch.randn(200, 520, device=cuda0).to(torch.bfloat16)
     with pytest.raises(RuntimeError, match="invalid argument"):
         ops.matmul_nt(A, B, a_t=True, splits=1)
+
+
+@pytest.mark.parametrize("a_t,b_t", [(False, False), (False, True), (True, True)])
+@pytest.mark.parametrize("M,N,K,splits", [(256, 256, 64, 1), (8192, 768, 768, 1), (520, 392, 1000, 1),
+                                          (768, 768, 8192, 6), (2304, 768, 4096, 2), (8192, 3072, 256, 1),
+                                          (4096, 2304, 768, 1)])
+def test_gemm_2sm_pair_kernel_matches_fp32(cuda0, a_t, b_t, M, N, K, splits):
+    """The CTA-pair (cta_group::2, 256x256 tile) kernel: operand majors, ragged tiles, split-K."""
+    from nexar_b200 import _native, ops
+    C = _native.cuda()
+    g = torch.Generator(device=cuda0).manual_seed(M + 3 * N + 7 * K + a_t + 2 * b_t)
+    A = torch.randn(M, K, device=cuda0, generator=g).to(torch.bfloat16)
+    B = torch.randn(N, K, device=cuda0, generator=g).to(torch.bfloat16)
+    bias = torch.randn(N, device=cuda0, generator=g).to(torch.bfloat16)
+    a_arg = A.t().contiguous() if a_t else A
+    b_arg = B.t().contiguous() if b_t else B
+    prev = C.gemm_get_2sm()
+    C.gemm_set_2sm(1)
+    try:
+        out = ops.matmul_nt(a_arg, b_arg, bias=bias, a_t=a_t, b_t=b_t, splits=splits)
+        C.gemm_set_2sm(0)
+        out1 = ops.matmul_nt(a_arg, b_arg, bias=bias, a_t=a_t, b_t=b_t, splits=splits)
+        torch.cuda.synchronize()
+    finally:
+        C.gemm_set_2sm(prev)
+    torch.testing.assert_close(out.float(), out1.float(), atol=0.05 * (K ** 0.5) / 8, rtol=2e-2)
+    assert C.gemm_error_flag() == 0
+    ref = A.float() @ B.float().t() + bias.float()
+    torch.testing.assert_close(out.float(), ref, atol=0.05 * (K ** 0.5) / 8, rtol=2e-2)
