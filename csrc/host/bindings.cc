@@ -4,12 +4,16 @@
 // reference's pointer API (nexar/src/client/collectives.rs). Blocking calls
 // release the GIL. NexarError is raised as the matching nexar_b200.core
 // exception class.
+#include <sys/socket.h>
+
+#include <cstring>
 #include <pybind11/functional.h>
 #include <pybind11/pybind11.h>
 #include <pybind11/stl.h>
 
 #include "buffer_pool.h"
 #include "client.h"
+#include "tls.h"
 #include "recovery.h"
 
 namespace py = pybind11;
@@ -42,7 +46,41 @@ py::dict msg_to_dict(const Message& m) {
 }
 }  // namespace
 
+// TLS check over a local socket pair: a server with an identity from CA
+// `a` and a client with one from CA `a` (same_ca) or from an unrelated CA;
+// both verify the peer. Returns true if the handshake and an echo succeed.
+static bool tls_pair_check(bool same_ca) {
+  int sv[2];
+  if (socketpair(AF_UNIX, SOCK_STREAM, 0, sv) != 0) fail(Err::ConnectionFailed, "socketpair failed");
+  auto ca_a = ClusterCA::generate("ca-a");
+  auto ca_b = same_ca ? ca_a : ClusterCA::generate("ca-b");
+  TlsIdentity sid = ca_a->issue("server"), cid = ca_b->issue("client");
+  bool server_ok = false;
+  std::thread srv([&] {
+    try {
+      auto s = tls_server(sv[0], sid, true, 5.0);
+      char b[4];
+      server_ok = s->read_exact(b, 4) && std::memcmp(b, "ping", 4) == 0;
+      if (server_ok) s->write_all("pong", 4);
+    } catch (const std::exception&) {
+      server_ok = false;
+    }
+  });
+  bool client_ok = false;
+  try {
+    auto c = tls_client(sv[1], cid, true, 5.0);
+    c->write_all("ping", 4);
+    char b[4];
+    client_ok = c->read_exact(b, 4) && std::memcmp(b, "pong", 4) == 0;
+  } catch (const std::exception&) {
+    client_ok = false;
+  }
+  srv.join();
+  return server_ok && client_ok;
+}
+
 PYBIND11_MODULE(_host, m) {
+  m.def("tls_pair_check", &tls_pair_check, py::arg("same_ca"), py::call_guard<py::gil_scoped_release>());
   m.doc() = "nexar_b200 host runtime (C++): TCP control plane, CPU collectives, cluster management";
 
   py::register_exception_translator([](std::exception_ptr p) {
@@ -79,6 +117,7 @@ PYBIND11_MODULE(_host, m) {
       .def_readwrite("ring_max_world", &Config::ring_max_world)
       .def_readwrite("enable_tcp_bulk_sidecar", &Config::enable_tcp_bulk_sidecar)
       .def_readwrite("encrypt_bulk_transport", &Config::encrypt_bulk_transport)
+      .def_readwrite("tls", &Config::tls)
       .def_readwrite("compressed_allreduce_max_bytes", &Config::compressed_allreduce_max_bytes)
       .def_readwrite("heartbeat_interval_s", &Config::heartbeat_interval_s)
       .def_readwrite("heartbeat_timeout_s", &Config::heartbeat_timeout_s)
@@ -240,11 +279,12 @@ PYBIND11_MODULE(_host, m) {
 
   // ------------------------------------------------------------ seed / worker
   py::class_<SeedNode, std::shared_ptr<SeedNode>>(m, "SeedNode")
-      .def_static("bind", [](const std::string& addr, const py::object& token) {
+      .def_static("bind", [](const std::string& addr, const py::object& token, bool tls) {
         Bytes t = token.is_none() ? token_from_env() : to_bytes(token.cast<py::bytes>());
-        return SeedNode::bind(addr, t);
-      }, py::arg("addr"), py::arg("token") = py::none())
-      .def_static("bind_local", &SeedNode::bind_local)
+        return SeedNode::bind(addr, t, tls);
+      }, py::arg("addr"), py::arg("token") = py::none(), py::arg("tls") = false)
+      .def_static("bind_local", &SeedNode::bind_local, py::arg("tls") = false)
+      .def("tls", &SeedNode::tls)
       .def("local_addr", &SeedNode::local_addr)
       .def("token", [](const SeedNode& s) { return from_bytes(s.token()); })
       .def("with_formation_timeout", [](std::shared_ptr<SeedNode> s, double t) { s->set_formation_timeout(t); return s; })
@@ -269,6 +309,7 @@ PYBIND11_MODULE(_host, m) {
       .def_property_readonly("mesh_rank_of_self", [](const NexarClient& c) { return c.mesh()->rank(); })
       .def_property_readonly("adapter_name", [](const NexarClient& c) { return c.adapter()->name(); })
       .def("has_direct_peer", &NexarClient::has_direct_peer)
+      .def("transport_encrypted", [](const NexarClient& c) { return c.mesh()->all_encrypted(); })
       .def("is_sparse", &NexarClient::is_sparse)
       .def("config", &NexarClient::config)
       // p2p

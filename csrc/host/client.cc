@@ -12,17 +12,17 @@ enum RelayLane : uint8_t { kRelayTagged = 0, kRelayControl = 1, kRelayRaw = 2 };
 
 uint64_t token_hash(const Bytes& t) { return t.empty() ? 0 : fnv1a_comm_id({t}); }
 
-void send_handshake(int fd, Rank rank, uint32_t world, const Bytes& token) {
+void send_handshake(Stream& io, Rank rank, uint32_t world, const Bytes& token) {
   Bytes b;
   put_u32(b, kMeshMagic);
   put_u32(b, rank);
   put_u32(b, world);
   put_u64(b, token_hash(token));
-  write_all(fd, b.data(), b.size());
+  io.write_all(b.data(), b.size());
 }
-Rank read_handshake(int fd, const Bytes& token) {
+Rank read_handshake(Stream& io, const Bytes& token) {
   uint8_t b[20];
-  if (!read_exact(fd, b, sizeof(b))) fail(Err::ConnectionFailed, "mesh handshake: connection closed");
+  if (!io.read_exact(b, sizeof(b))) fail(Err::ConnectionFailed, "mesh handshake: connection closed");
   if ((uint32_t)get_le(b, 4) != kMeshMagic) fail(Err::ConnectionFailed, "mesh handshake: bad magic");
   if (get_le(b + 12, 8) != token_hash(token)) fail(Err::ClusterTokenMismatch, "cluster token mismatch: bootstrap authentication failed");
   return (Rank)get_le(b + 4, 4);
@@ -55,8 +55,16 @@ void Mesh::grow(uint32_t new_world) {
   if (new_world > world_) world_ = new_world;
 }
 
-void Mesh::add_connection(Rank r, int fd) {
-  auto conn = std::make_shared<PeerConnection>(r, fd);
+std::shared_ptr<Stream> Mesh::dial(int fd) const {
+  return tls() ? tls_client(fd, tls_id_, true, cfg_.collective_timeout_s) : plain_stream(fd);
+}
+
+std::shared_ptr<Stream> Mesh::answer(int fd) const {
+  return tls() ? tls_server(fd, tls_id_, true, cfg_.collective_timeout_s) : plain_stream(fd);
+}
+
+void Mesh::add_connection(Rank r, std::shared_ptr<Stream> io) {
+  auto conn = std::make_shared<PeerConnection>(r, std::move(io));
   std::shared_ptr<Mailbox> b;
   {
     std::lock_guard<std::mutex> g(mu_);
@@ -75,6 +83,14 @@ void Mesh::add_connection(Rank r, int fd) {
       });
   std::lock_guard<std::mutex> g(mu_);
   routers_[r] = std::move(router);
+}
+
+bool Mesh::all_encrypted() const {
+  std::lock_guard<std::mutex> g(mu_);
+  if (conns_.empty()) return false;
+  for (auto& kv : conns_)
+    if (!kv.second->encrypted()) return false;
+  return true;
 }
 
 bool Mesh::has_direct(Rank r) const {
@@ -313,6 +329,10 @@ std::shared_ptr<NexarClient> NexarClient::from_worker_info(WorkerInfo info, cons
   auto mesh = std::make_shared<Mesh>(info.rank, info.world_size, cfg, info.token);
   mesh->listen_fd = info.listen_fd;
   mesh->listen_addr = info.listen_addr;
+  if (cfg.tls) {
+    if (!info.tls.valid()) fail(Err::ConnectionFailed, "TLS is on but the seed issued no certificate (seed without TLS?)");
+    mesh->set_tls(info.tls);
+  }
   std::map<Rank, std::string> addr;
   for (auto& p : info.peers) addr[p.first] = p.second;
   const auto nbrs = build_neighbors(cfg.topology, info.rank, info.world_size);
@@ -320,9 +340,9 @@ std::shared_ptr<NexarClient> NexarClient::from_worker_info(WorkerInfo info, cons
   for (Rank p : nbrs) {
     if (p < info.rank) {
       auto hp = split_host_port(addr.at(p));
-      int fd = tcp_connect(hp.first, hp.second, 30.0);
-      send_handshake(fd, info.rank, info.world_size, info.token);
-      mesh->add_connection(p, fd);
+      auto io = mesh->dial(tcp_connect(hp.first, hp.second, 30.0));
+      send_handshake(*io, info.rank, info.world_size, info.token);
+      mesh->add_connection(p, io);
     } else {
       ++expect_accept;
     }
@@ -333,18 +353,16 @@ std::shared_ptr<NexarClient> NexarClient::from_worker_info(WorkerInfo info, cons
     int fd = tcp_accept(info.listen_fd, 0.5);
     if (fd < 0) continue;
     Rank p;
+    std::shared_ptr<Stream> io;
     try {
-      p = read_handshake(fd, info.token);
+      io = mesh->answer(fd);  // owns fd from here on, also when it throws
+      p = read_handshake(*io, info.token);
     } catch (const NexarError& e) {
-      close_fd(fd);
       NEXAR_LOG(LogLevel::Warn, std::string("rejected mesh connection: ") + e.what());
       continue;
     }
-    if (!nbrs.count(p) || p <= info.rank || mesh->has_direct(p)) {
-      close_fd(fd);
-      continue;
-    }
-    mesh->add_connection(p, fd);
+    if (!nbrs.count(p) || p <= info.rank || mesh->has_direct(p)) continue;
+    mesh->add_connection(p, io);
     --expect_accept;
   }
   mesh->set_routing(cfg.topology);
@@ -356,7 +374,7 @@ std::shared_ptr<NexarClient> NexarClient::from_worker_info(WorkerInfo info, cons
 
 std::vector<std::shared_ptr<NexarClient>> NexarClient::bootstrap_local(uint32_t world, const Config& cfg) {
   if (world == 0) fail(Err::InvalidRank, "world size must be >= 1");
-  auto seed = SeedNode::bind_local();
+  auto seed = SeedNode::bind_local(cfg.tls);
   std::vector<WorkerInfo> infos(world);
   std::vector<std::exception_ptr> errs(world + 1);
   std::thread seed_thr([&] {
@@ -370,7 +388,7 @@ std::vector<std::shared_ptr<NexarClient>> NexarClient::bootstrap_local(uint32_t 
   for (uint32_t i = 0; i < world; ++i) {
     ts.emplace_back([&, i] {
       try {
-        infos[i] = WorkerNode::connect(seed->local_addr(), {}, "127.0.0.1");
+        infos[i] = WorkerNode::connect(seed->local_addr(), {}, "127.0.0.1", cfg.tls);
       } catch (...) {
         errs[i] = std::current_exception();
       }
@@ -400,7 +418,7 @@ std::vector<std::shared_ptr<NexarClient>> NexarClient::bootstrap_local(uint32_t 
 
 std::shared_ptr<NexarClient> NexarClient::bootstrap_worker(const std::string& seed_addr, const Bytes& token,
                                                           const Config& cfg, const std::string& bind_host) {
-  WorkerInfo info = WorkerNode::connect(seed_addr, token, bind_host);
+  WorkerInfo info = WorkerNode::connect(seed_addr, token, bind_host, cfg.tls);
   return from_worker_info(std::move(info), cfg);
 }
 

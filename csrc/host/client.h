@@ -62,9 +62,18 @@ class Mesh : public std::enable_shared_from_this<Mesh> {
   const Config& config() const { return cfg_; }
 
   // Adopt an established connection to mesh rank r (handshake done).
-  void add_connection(Rank r, int fd);
+  void add_connection(Rank r, std::shared_ptr<Stream> io);
+  // TLS for mesh links: with an identity set, dial() / answer() run a mutually
+  // authenticated TLS handshake on a freshly connected / accepted socket (and
+  // take ownership of it); without one they wrap it as plain TCP.
+  void set_tls(const TlsIdentity& id) { tls_id_ = id; }
+  bool tls() const { return tls_id_.valid(); }
+  std::shared_ptr<Stream> dial(int fd) const;
+  std::shared_ptr<Stream> answer(int fd) const;
   void grow(uint32_t new_world);
   bool has_direct(Rank r) const;
+  // True if this mesh has links and every one of them runs TLS.
+  bool all_encrypted() const;
   std::shared_ptr<Mailbox> box(Rank r) const;
   std::shared_ptr<PeerConnection> conn(Rank r) const;
   void set_routing(const TopologyStrategy& t);
@@ -102,6 +111,7 @@ class Mesh : public std::enable_shared_from_this<Mesh> {
   uint32_t world_;
   Config cfg_;
   Bytes token_;
+  TlsIdentity tls_id_;
   mutable std::mutex mu_;
   std::map<Rank, std::shared_ptr<PeerConnection>> conns_;
   std::map<Rank, std::unique_ptr<PeerRouter>> routers_;

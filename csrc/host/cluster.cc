@@ -193,9 +193,25 @@ static std::string hex(const Bytes& b) {
 }
 
 // ------------------------------------------------------------------ seed
-std::shared_ptr<SeedNode> SeedNode::bind(const std::string& addr, const Bytes& token) {
+namespace {
+constexpr double kTlsHandshakeTimeoutS = 10.0;
+}
+
+std::shared_ptr<Stream> SeedNode::accept_bootstrap(int fd) {
+  if (!ca_) return plain_stream(fd);
+  // Workers do not verify the seed (they hold no CA yet): the cluster token
+  // in their Hello authenticates them, TLS keeps the token and the issued
+  // key private (nexar/src/transport/tls.rs:179-298).
+  return tls_server(fd, seed_id_, false, kTlsHandshakeTimeoutS);
+}
+
+std::shared_ptr<SeedNode> SeedNode::bind(const std::string& addr, const Bytes& token, bool tls) {
   auto hp = split_host_port(addr);
   std::shared_ptr<SeedNode> s(new SeedNode());
+  if (tls) {
+    s->ca_ = ClusterCA::generate();
+    s->seed_id_ = s->ca_->issue("nexar-seed");
+  }
   int port = 0;
   s->listen_fd_ = tcp_listen(hp.first, hp.second, &port);
   s->addr_ = hp.first + ":" + std::to_string(port);
@@ -208,8 +224,12 @@ std::shared_ptr<SeedNode> SeedNode::bind(const std::string& addr, const Bytes& t
   return s;
 }
 
-std::shared_ptr<SeedNode> SeedNode::bind_local() {
+std::shared_ptr<SeedNode> SeedNode::bind_local(bool tls) {
   std::shared_ptr<SeedNode> s(new SeedNode());
+  if (tls) {
+    s->ca_ = ClusterCA::generate();
+    s->seed_id_ = s->ca_->issue("nexar-seed");
+  }
   int port = 0;
   s->listen_fd_ = tcp_listen("127.0.0.1", 0, &port);
   s->addr_ = "127.0.0.1:" + std::to_string(port);
@@ -226,47 +246,44 @@ void SeedNode::close() {
   }
   if (elastic_thr_.joinable()) elastic_thr_.join();
   std::lock_guard<std::mutex> g(mu_);
-  for (auto& p : pending_) close_fd(p.fd);
-  pending_.clear();
+  pending_.clear();  // drops (closes) the bootstrap streams
 }
 
 PeerList SeedNode::form_cluster(uint32_t world) {
   const auto t0 = Clock::now();
-  std::vector<int> fds;
+  std::vector<std::shared_ptr<Stream>> ios;
   PeerList table;
   while (table.size() < world) {
     const double left = formation_timeout_s_ - seconds_since(t0);
     if (left <= 0) {
-      for (int fd : fds) close_fd(fd);
       fail(Err::ClusterFormationTimeout, "cluster formation timed out: " + std::to_string(table.size()) + "/" +
                                              std::to_string(world) + " nodes joined");
     }
     int fd = tcp_accept(listen_fd_, std::min(left, 0.5));
     if (fd < 0) continue;
     try {
-      Message h = read_framed(fd);
+      auto io = accept_bootstrap(fd);
+      Message h = read_framed(*io);
       if (h.kind != MsgKind::Hello) fail(Err::DecodeFailed, "expected Hello");
       if (h.protocol_version != kProtocolVersion) {
-        close_fd(fd);
         NEXAR_LOG(LogLevel::Warn, "rejecting worker with protocol version " + std::to_string(h.protocol_version));
         continue;
       }
       if (!token_.empty() && h.cluster_token != token_) {
-        close_fd(fd);
         NEXAR_LOG(LogLevel::Warn, "rejecting worker: cluster token mismatch");
         continue;
       }
       table.emplace_back((Rank)table.size(), h.listen_addr);
-      fds.push_back(fd);
+      ios.push_back(io);
     } catch (const NexarError& e) {
-      close_fd(fd);
       NEXAR_LOG(LogLevel::Warn, std::string("bad bootstrap connection: ") + e.what());
     }
   }
   for (uint32_t r = 0; r < world; ++r) {
-    write_framed(fds[r], Message::welcome(r, world, table));
-    close_fd(fds[r]);
+    write_framed(*ios[r], Message::welcome(r, world, table));
+    if (ca_) send_identity(*ios[r], ca_->issue("nexar-rank-" + std::to_string(r)));
   }
+  ios.clear();
   table_ = table;
   next_rank_ = world;
   return table;
@@ -279,25 +296,22 @@ void SeedNode::accept_elastic(uint32_t max_world) {
       int fd = tcp_accept(listen_fd_, 0.2);
       if (fd < 0) continue;
       try {
-        Message h = read_framed(fd);
+        auto io = accept_bootstrap(fd);
+        Message h = read_framed(*io);
         if (h.kind != MsgKind::Hello || h.protocol_version != kProtocolVersion ||
             (!token_.empty() && h.cluster_token != token_)) {
-          close_fd(fd);
           continue;
         }
         std::lock_guard<std::mutex> g(mu_);
-        if (max_world && next_rank_ >= max_world) {
-          close_fd(fd);
-          continue;
-        }
+        if (max_world && next_rank_ >= max_world) continue;
         const Rank r = next_rank_++;
         PeerList table = table_;
         table.emplace_back(r, h.listen_addr);
         table_ = table;
-        write_framed(fd, Message::welcome(r, (uint32_t)table.size(), table));
-        pending_.push_back(PendingJoin{r, h.listen_addr, fd});
+        write_framed(*io, Message::welcome(r, (uint32_t)table.size(), table));
+        if (ca_) send_identity(*io, ca_->issue("nexar-rank-" + std::to_string(r)));
+        pending_.push_back(PendingJoin{r, h.listen_addr, io});
       } catch (const NexarError&) {
-        close_fd(fd);
       }
     }
   });
@@ -311,7 +325,8 @@ std::vector<PendingJoin> SeedNode::take_pending_joins() {
 }
 
 // ------------------------------------------------------------------ worker
-WorkerInfo WorkerNode::connect(const std::string& seed_addr, const Bytes& token, const std::string& bind_host) {
+WorkerInfo WorkerNode::connect(const std::string& seed_addr, const Bytes& token, const std::string& bind_host,
+                               bool tls) {
   WorkerInfo w;
   int port = 0;
   w.listen_fd = tcp_listen(bind_host, 0, &port);
@@ -332,18 +347,21 @@ WorkerInfo WorkerNode::connect(const std::string& seed_addr, const Bytes& token,
     }
   }
   try {
-    write_framed(fd, Message::hello(token, w.listen_addr));
-    Message m = read_framed(fd);
+    const int raw = fd;
+    fd = -1;  // the stream owns (and on failure closes) the socket
+    auto io = tls ? tls_client(raw, TlsIdentity{}, false, kTlsHandshakeTimeoutS) : plain_stream(raw);
+    write_framed(*io, Message::hello(token, w.listen_addr));
+    Message m = read_framed(*io);
     if (m.kind != MsgKind::Welcome) fail(Err::DecodeFailed, "expected Welcome from seed");
     w.rank = m.rank;
     w.world_size = m.world_size;
     w.peers = m.peers;
+    if (tls) w.tls = recv_identity(*io);
   } catch (...) {
-    close_fd(fd);
+    if (fd >= 0) close_fd(fd);
     close_fd(w.listen_fd);
     throw;
   }
-  close_fd(fd);
   return w;
 }
 

@@ -19,6 +19,7 @@
 #include <set>
 #include <thread>
 
+#include "tls.h"
 #include "transport.h"
 
 namespace nexar {
@@ -75,14 +76,17 @@ class ClusterMap {
 struct PendingJoin {
   Rank rank;
   std::string listen_addr;
-  int fd;  // bootstrap connection, Welcome already sent
+  std::shared_ptr<Stream> io;  // bootstrap connection, Welcome already sent
 };
 
 class SeedNode {
  public:
-  // `token` empty = no authentication (bind_local in the reference).
-  static std::shared_ptr<SeedNode> bind(const std::string& addr, const Bytes& token);
-  static std::shared_ptr<SeedNode> bind_local();
+  // `token` empty = no authentication (bind_local in the reference). With
+  // `tls` the seed creates the cluster CA, serves bootstrap over TLS and
+  // hands every worker its certificate (see tls.h).
+  static std::shared_ptr<SeedNode> bind(const std::string& addr, const Bytes& token, bool tls = false);
+  static std::shared_ptr<SeedNode> bind_local(bool tls = false);
+  bool tls() const { return ca_ != nullptr; }
   ~SeedNode();
   std::string local_addr() const { return addr_; }
   const Bytes& token() const { return token_; }
@@ -99,6 +103,9 @@ class SeedNode {
 
  private:
   SeedNode() = default;
+  std::shared_ptr<Stream> accept_bootstrap(int fd);
+  std::shared_ptr<ClusterCA> ca_;
+  TlsIdentity seed_id_;
   int listen_fd_ = -1;
   std::string addr_;
   Bytes token_;
@@ -118,6 +125,7 @@ struct WorkerInfo {
   int listen_fd = -1;         // mesh listener (already bound)
   std::string listen_addr;
   Bytes token;
+  TlsIdentity tls;            // issued by the seed when the cluster runs TLS
 };
 
 class WorkerNode {
@@ -126,7 +134,7 @@ class WorkerNode {
   // doubling backoff from 500 ms, like nexar/src/cluster/worker.rs:113),
   // send Hello, wait for Welcome.
   static WorkerInfo connect(const std::string& seed_addr, const Bytes& token,
-                            const std::string& bind_host = "127.0.0.1");
+                            const std::string& bind_host = "127.0.0.1", bool tls = false);
 };
 
 Bytes token_from_env();

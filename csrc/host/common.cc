@@ -97,6 +97,7 @@ Config Config::from_env() {
   c.pipeline_segment_bytes = env_u("NEXAR_PIPELINE_SEGMENT_BYTES", c.pipeline_segment_bytes);
   c.ring_max_world = (uint32_t)env_u("NEXAR_RING_MAX_WORLD", c.ring_max_world);
   c.enable_tcp_bulk_sidecar = env_b("NEXAR_ENABLE_TCP_BULK_SIDECAR", c.enable_tcp_bulk_sidecar);
+  c.tls = env_b("NEXAR_TLS", c.tls);
   c.encrypt_bulk_transport = env_b("NEXAR_ENCRYPT_BULK_TRANSPORT", c.encrypt_bulk_transport);
   c.compressed_allreduce_max_bytes = env_u("NEXAR_COMPRESSED_ALLREDUCE_MAX_BYTES", c.compressed_allreduce_max_bytes);
   c.heartbeat_interval_s = env_f("NEXAR_HEARTBEAT_INTERVAL_SECS", c.heartbeat_interval_s);

@@ -86,6 +86,9 @@ struct Config {
   uint32_t ring_max_world = 8;
   bool enable_tcp_bulk_sidecar = true;
   bool encrypt_bulk_transport = true;
+  // TLS 1.3 with a per-cluster CA on every host link (bootstrap and mesh).
+  // Off by default: the default deployment is one box over loopback.
+  bool tls = false;
   uint64_t compressed_allreduce_max_bytes = 4ull << 30;
   double heartbeat_interval_s = 1.0;
   double heartbeat_timeout_s = 5.0;

@@ -230,8 +230,7 @@ bool ElasticManager::elastic_checkpoint() {
     PeerList joining;
     if (seed_) {
       for (auto& pj : seed_->take_pending_joins()) {
-        joining.emplace_back(pj.rank, pj.listen_addr);
-        close_fd(pj.fd);
+        joining.emplace_back(pj.rank, pj.listen_addr);  // dropping pj closes its bootstrap stream
       }
     }
     std::vector<Rank> leaving = pending_leave_;
@@ -257,14 +256,14 @@ bool ElasticManager::elastic_checkpoint() {
     mesh->grow(maxr + 1);
     for (auto& j : ack.joining) {
       auto hp = split_host_port(j.second);
-      int fd = tcp_connect(hp.first, hp.second, timeout);
+      auto io = mesh->dial(tcp_connect(hp.first, hp.second, timeout));
       Bytes h;
       put_u32(h, 0x4e584d31);
       put_u32(h, mesh->rank());
       put_u32(h, ack.new_world_size);
       put_u64(h, mesh->token().empty() ? 0 : fnv1a_comm_id({mesh->token()}));
-      write_all(fd, h.data(), h.size());
-      mesh->add_connection(j.first, fd);
+      io->write_all(h.data(), h.size());
+      mesh->add_connection(j.first, io);
       joined.push_back(j.first);
     }
     if (c->rank() == 0)
@@ -287,11 +286,12 @@ bool ElasticManager::elastic_checkpoint() {
 
 std::shared_ptr<NexarClient> ElasticManager::join(const std::string& seed_addr, const Bytes& token, const Config& cfg,
                                                   double timeout_s) {
-  WorkerInfo info = WorkerNode::connect(seed_addr, token, "127.0.0.1");
+  WorkerInfo info = WorkerNode::connect(seed_addr, token, "127.0.0.1", cfg.tls);
   const Rank me = info.rank;
   auto mesh = std::make_shared<Mesh>(me, me + 1, cfg, token);
   mesh->listen_fd = info.listen_fd;
   mesh->listen_addr = info.listen_addr;
+  if (cfg.tls) mesh->set_tls(info.tls);
   std::set<Rank> connected;
   bool have_ack = false;
   Message ack;
@@ -301,14 +301,17 @@ std::shared_ptr<NexarClient> ElasticManager::join(const std::string& seed_addr, 
     if (seconds_since(t0) > timeout_s) fail(Err::ElasticTimeout, "elastic join timed out");
     int fd = tcp_accept(info.listen_fd, 0.05);
     if (fd >= 0) {
-      uint8_t b[20];
-      if (read_exact(fd, b, sizeof(b)) && (uint32_t)get_le(b, 4) == 0x4e584d31) {
-        const Rank p = (Rank)get_le(b + 4, 4);
-        mesh->grow(std::max<uint32_t>(mesh->world(), p + 1));
-        mesh->add_connection(p, fd);
-        connected.insert(p);
-      } else {
-        close_fd(fd);
+      try {
+        auto io = mesh->answer(fd);
+        uint8_t b[20];
+        if (io->read_exact(b, sizeof(b)) && (uint32_t)get_le(b, 4) == 0x4e584d31) {
+          const Rank p = (Rank)get_le(b + 4, 4);
+          mesh->grow(std::max<uint32_t>(mesh->world(), p + 1));
+          mesh->add_connection(p, io);
+          connected.insert(p);
+        }
+      } catch (const NexarError& e) {
+        NEXAR_LOG(LogLevel::Warn, std::string("rejected join connection: ") + e.what());
       }
     }
     if (!have_ack && connected.count(0)) {
@@ -328,14 +331,14 @@ std::shared_ptr<NexarClient> ElasticManager::join(const std::string& seed_addr, 
           for (auto& j : ack.joining) {
             if (j.first <= me) continue;
             auto hp = split_host_port(j.second);
-            int cfd = tcp_connect(hp.first, hp.second, timeout_s);
+            auto cio = mesh->dial(tcp_connect(hp.first, hp.second, timeout_s));
             Bytes h;
             put_u32(h, 0x4e584d31);
             put_u32(h, me);
             put_u32(h, ack.new_world_size);
             put_u64(h, token.empty() ? 0 : fnv1a_comm_id({token}));
-            write_all(cfd, h.data(), h.size());
-            mesh->add_connection(j.first, cfd);
+            cio->write_all(h.data(), h.size());
+            mesh->add_connection(j.first, cio);
           }
         }
       } catch (const NexarError&) {

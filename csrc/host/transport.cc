@@ -137,6 +137,29 @@ void write_framed(int fd, const Message& m, Priority prio) {
   write_all(fd, frame.data(), frame.size());
 }
 
+void write_framed(Stream& st, const Message& m, Priority prio) {
+  Bytes enc = encode_message(m, prio);
+  Bytes frame;
+  frame.reserve(9 + enc.size());
+  frame.push_back(kFrameMessage);
+  put_u64(frame, enc.size());
+  frame.insert(frame.end(), enc.begin(), enc.end());
+  st.write_all(frame.data(), frame.size());
+}
+
+Message read_framed(Stream& st) {
+  uint8_t kind = 0;
+  if (!st.read_exact(&kind, 1)) fail(Err::PeerDisconnected, "connection closed");
+  if (kind != kFrameMessage) fail(Err::DecodeFailed, "expected a framed message");
+  uint8_t lb[8];
+  if (!st.read_exact(lb, 8)) fail(Err::PeerDisconnected, "connection closed");
+  const uint64_t len = get_le(lb, 8);
+  if (len > kMaxMessageBytes) fail(Err::DecodeFailed, "message too large");
+  Bytes b(len);
+  if (len && !st.read_exact(b.data(), len)) fail(Err::PeerDisconnected, "connection closed");
+  return decode_message(b.data(), b.size());
+}
+
 Message read_framed(int fd) {
   uint8_t kind = 0;
   if (!read_exact(fd, &kind, 1)) fail(Err::PeerDisconnected, "connection closed");
@@ -245,8 +268,8 @@ void PeerConnection::send_frame(uint8_t kind, const uint64_t* prefix, int nprefi
   }
   std::lock_guard<std::mutex> g(write_mu_);
   try {
-    write_all(fd_, hdr, h);
-    if (n) write_all(fd_, p, n);
+    io_->write_all(hdr, h);
+    if (n) io_->write_all(p, n);
   } catch (const NexarError&) {
     alive_ = false;
     throw NexarError(Err::PeerDisconnected, "peer " + std::to_string(peer_) + " disconnected unexpectedly");
@@ -277,7 +300,7 @@ void PeerConnection::send_raw_tagged(uint64_t comm_id, uint64_t tag, const void*
 }
 
 void PeerConnection::close() {
-  if (alive_.exchange(false)) ::shutdown(fd_, SHUT_RDWR);
+  if (alive_.exchange(false)) io_->shutdown();
 }
 
 // ------------------------------------------------------------------ router
@@ -335,12 +358,11 @@ void PeerRouter::dispatch(Message&& m) {
 }
 
 void PeerRouter::run() {
-  const int fd = conn_->fd();
   const Rank peer = conn_->peer();
   try {
     while (true) {
       uint8_t kind;
-      if (!read_exact(fd, &kind, 1)) break;
+      if (!conn_->read_exact(&kind, 1)) break;
       uint64_t pre[3] = {0, 0, 0};
       int np = 0;
       switch (kind) {
@@ -352,7 +374,7 @@ void PeerRouter::run() {
           goto done;
       }
       uint8_t buf[24];
-      if (!read_exact(fd, buf, 8 * np)) break;
+      if (!conn_->read_exact(buf, 8 * np)) break;
       for (int i = 0; i < np; ++i) pre[i] = get_le(buf + 8 * i, 8);
       const uint64_t len = pre[np - 1];
       if (len > kMaxMessageBytes) {
@@ -360,7 +382,7 @@ void PeerRouter::run() {
         break;
       }
       Bytes payload(len);
-      if (len && !read_exact(fd, payload.data(), len)) break;
+      if (len && !conn_->read_exact(payload.data(), len)) break;
       last_seen_ns_ = now_ns();
       switch (kind) {
         case kFrameMessage: {

@@ -35,6 +35,7 @@
 #include <typeindex>
 #include <unordered_map>
 
+#include "tls.h"
 #include "wire.h"
 
 namespace nexar {
@@ -55,6 +56,8 @@ void close_fd(int fd);
 
 // Read/write one framed message (kind 0x01) on a bootstrap socket.
 void write_framed(int fd, const Message& m, Priority prio = Priority::Critical);
+void write_framed(Stream& s, const Message& m, Priority prio = Priority::Critical);
+Message read_framed(Stream& s);
 Message read_framed(int fd);
 
 // ------------------------------------------------------------------ mailbox
@@ -107,10 +110,14 @@ class Mailbox {
 // ------------------------------------------------------------------ connection
 class PeerConnection {
  public:
-  PeerConnection(Rank peer, int fd) : peer_(peer), fd_(fd) {}
+  // Takes ownership of the stream (and its socket).
+  PeerConnection(Rank peer, std::shared_ptr<Stream> io) : peer_(peer), io_(std::move(io)) {}
   ~PeerConnection();
   Rank peer() const { return peer_; }
-  int fd() const { return fd_; }
+  int fd() const { return io_->fd(); }
+  bool encrypted() const { return io_->encrypted(); }
+  // Reader side (the router thread): false on EOF or error.
+  bool read_exact(void* p, size_t n) { return io_->read_exact(p, n); }
 
   void send_message(const Message& m, Priority prio);
   void send_raw(const void* p, size_t n);
@@ -135,7 +142,7 @@ class PeerConnection {
  private:
   void send_frame(uint8_t kind, const uint64_t* prefix, int nprefix, const void* p, size_t n);
   Rank peer_;
-  int fd_;
+  std::shared_ptr<Stream> io_;
   std::mutex write_mu_;
   std::atomic<bool> alive_{true};
   mutable std::mutex ext_mu_;

@@ -45,6 +45,7 @@ if host_sources:
         include_dirs=[os.path.join(ROOT, "csrc", "host")],
         extra_compile_args={"cxx": CXX_FLAGS + ["-pthread"]},
         extra_link_args=["-pthread"],
+        libraries=["ssl", "crypto"],  # TLS 1.3 for host links (csrc/host/tls.cc)
     ))
 ext_modules.append(CUDAExtension(
     "nexar_b200._cuda",

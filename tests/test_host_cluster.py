@@ -201,10 +201,11 @@ def test_rebuild_excluding_direct():
 
 
 # ------------------------------------------------------------ elastic
-def test_elastic_noop_checkpoint_and_grow_and_shrink():
+@pytest.mark.parametrize("tls", [False, True])
+def test_elastic_noop_checkpoint_and_grow_and_shrink(tls):
     H = _h()
-    seed = H.SeedNode.bind_local()
-    cfg = Config(**FAST)
+    seed = H.SeedNode.bind_local(tls)
+    cfg = Config(tls=tls, **FAST)
     clients = [None, None]
 
     def boot(i):
@@ -235,6 +236,7 @@ def test_elastic_noop_checkpoint_and_grow_and_shrink():
     bufs = [np.full(5, float(c.rank + 1), np.float32) for c in grown]
     run_collective(grown, lambda c: c.all_reduce_host(bufs[c.rank]))
     assert all((b == 6).all() for b in bufs)
+    assert all(c.native.transport_encrypted() == tls for c in grown)
     # shrink: rank 1 leaves at the next checkpoint
     m3 = [H.ElasticManager(c.native, seed if c.rank == 0 else None, 1, 8, 10.0) for c in sorted(grown, key=lambda c: c.rank)]
     m3[0].remove_node(1)
