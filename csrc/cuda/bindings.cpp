@@ -96,6 +96,7 @@ void all_reduce(const CommPtr& c, const at::Tensor& in, const at::Tensor& out, i
     check_launch(launch_all_reduce(c->dev(), in.data_ptr(), out.data_ptr(), dti, dto, op, n,
                                    (float)scale, kAlgoOneShot, -1, c->max_blocks, s), "all_reduce");
     count_launch(1);
+    c->last_allreduce_algo = 0;
     return;
   }
   // NVLS (switch-side reduction) for large messages; in place with no staging
@@ -108,6 +109,7 @@ void all_reduce(const CommPtr& c, const at::Tensor& in, const at::Tensor& out, i
                                         c->max_blocks, s),
                  "all_reduce(nvls)");
     count_launch(1);
+    c->last_allreduce_algo = noff >= 0 ? 4 : 3;
     return;
   }
   TORCH_CHECK(algo != kAlgoNvls, "all_reduce: NVLS path unavailable for this message (needs an active NVLS region, "
@@ -123,8 +125,10 @@ void all_reduce(const CommPtr& c, const at::Tensor& in, const at::Tensor& out, i
     check_launch(launch_all_reduce(c->dev(), in.data_ptr(), out.data_ptr(), dti, dto, op, n,
                                    (float)scale, algo, sym, c->max_blocks, s), "all_reduce");
     count_launch(1);
+    c->last_allreduce_algo = 5;
     return;
   }
+  c->last_allreduce_algo = algo == kAlgoOneShot ? 1 : 2;
   const unsigned long long per = round_down(c->slot_bytes() / std::max(esi, eso), 256);
   for (unsigned long long off = 0; off < n; off += per) {
     const unsigned long long m = std::min(per, n - off);
@@ -484,6 +488,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
       .def_property("timeout_us", &DeviceComm::timeout_us, &DeviceComm::set_timeout_us)
       .def_readwrite("max_blocks", &DeviceComm::max_blocks)
       .def_readwrite("nvls_min_bytes", &DeviceComm::nvls_min_bytes)
+      .def_readonly("last_allreduce_algo", &DeviceComm::last_allreduce_algo)
       .def_readwrite("nvls_min_rs_bytes", &DeviceComm::nvls_min_rs_bytes)
       .def_readwrite("nvls_min_ag_bytes", &DeviceComm::nvls_min_ag_bytes)
       .def_readwrite("nvls_min_bcast_bytes", &DeviceComm::nvls_min_bcast_bytes)

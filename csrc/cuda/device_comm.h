@@ -71,6 +71,9 @@ class DeviceComm {
   uint64_t nvls_min_rs_bytes = 16ull << 20;
   uint64_t nvls_min_ag_bytes = ~0ull;
   uint64_t nvls_min_bcast_bytes = 1ull << 20;
+  // Algorithm of the last all_reduce call (observability): 1 one-shot,
+  // 2 two-shot, 3 NVLS staged, 4 NVLS in place, 5 two-shot in place, 0 local.
+  int last_allreduce_algo = 0;
 
   // ---- NVLS (NVSwitch multicast), multi-process only; see nvls.cpp.
   // Setup order on every rank: rank 0 nvls_create() and hands the returned

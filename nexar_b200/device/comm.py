@@ -22,6 +22,7 @@ times out records it in a host-mapped status word and returns, and
 """
 from __future__ import annotations
 
+import functools
 import os
 from typing import Callable, List, Optional, Sequence
 
@@ -68,6 +69,36 @@ class DeviceHandle:
         return self._event.query()
 
 
+_NVTX = os.environ.get("NEXAR_NVTX", "0") == "1"
+_AR_ALGO_NAMES = {0: "local", 1: "one_shot", 2: "two_shot", 3: "nvls_staged", 4: "nvls_in_place",
+                  5: "two_shot_in_place"}
+
+
+def _observed(op: str):
+    """Count calls and bytes per collective; NVTX range around it with NEXAR_NVTX=1."""
+    def deco(fn):
+        @functools.wraps(fn)
+        def wrapper(self, *args, **kwargs):
+            t = args[0] if args and isinstance(args[0], torch.Tensor) else None
+            st = self._stats.setdefault(op, {"calls": 0, "bytes": 0})
+            st["calls"] += 1
+            if t is not None:
+                st["bytes"] += t.numel() * t.element_size()
+            if _NVTX:
+                torch.cuda.nvtx.range_push(f"nexar.{op}")
+            try:
+                return fn(self, *args, **kwargs)
+            finally:
+                if _NVTX:
+                    torch.cuda.nvtx.range_pop()
+                if op == "all_reduce":
+                    name = _AR_ALGO_NAMES.get(self._comm.last_allreduce_algo, "?")
+                    algos = self._stats.setdefault("all_reduce_algorithms", {})
+                    algos[name] = algos.get(name, 0) + 1
+        return wrapper
+    return deco
+
+
 class DeviceCommunicator:
     """Symmetric-memory communicator over the GPUs of one box."""
 
@@ -112,6 +143,7 @@ class DeviceCommunicator:
             barrier()  # every rank has mapped its peers before any kernel runs
         self._side_stream = None
         self._C = C
+        self._stats = {}
 
     # ----------------------------------------------------------- construction
     @classmethod
@@ -183,10 +215,16 @@ class DeviceCommunicator:
     def status(self) -> dict:
         return self._comm.status()
 
+    def stats(self) -> dict:
+        """Per-collective call and byte counts, and how often each all-reduce algorithm ran."""
+        import copy
+        return copy.deepcopy(self._stats)
+
     def clear_status(self):
         self._comm.clear_status()
 
     # ----------------------------------------------------------- collectives
+    @_observed("all_reduce")
     def all_reduce(self, t: torch.Tensor, op="sum", out: Optional[torch.Tensor] = None,
                    scale: Optional[float] = None, algo: str = "auto") -> torch.Tensor:
         """Reduce ``t`` across ranks. In place unless ``out`` is given.
@@ -199,6 +237,7 @@ class DeviceCommunicator:
                            1.0 if scale is None else float(scale), _ALGOS[algo], self.oneshot_max_bytes)
         return out
 
+    @_observed("reduce_scatter")
     def reduce_scatter(self, inp: torch.Tensor, out: Optional[torch.Tensor] = None, op="sum",
                        scale: Optional[float] = None) -> torch.Tensor:
         """``inp`` holds world*count elements; rank r receives the reduction of chunk r."""
@@ -210,50 +249,59 @@ class DeviceCommunicator:
         self._C.reduce_scatter(self._comm, inp, out, int(ReduceOp.parse(op)), 1.0 if scale is None else float(scale))
         return out
 
+    @_observed("all_gather")
     def all_gather(self, inp: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
         if out is None:
             out = torch.empty(inp.numel() * self.world_size, dtype=inp.dtype, device=inp.device)
         self._C.all_gather(self._comm, inp, out)
         return out
 
+    @_observed("all_to_all")
     def all_to_all(self, inp: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
         out = torch.empty_like(inp) if out is None else out
         self._C.all_to_all(self._comm, inp, out)
         return out
 
+    @_observed("broadcast")
     def broadcast(self, t: torch.Tensor, root: int = 0, out: Optional[torch.Tensor] = None) -> torch.Tensor:
         out = t if out is None else out
         self._C.broadcast(self._comm, t, out, int(root))
         return out
 
+    @_observed("reduce")
     def reduce(self, t: torch.Tensor, root: int = 0, op="sum", out: Optional[torch.Tensor] = None,
                scale: Optional[float] = None) -> torch.Tensor:
         out = t if out is None else out
         self._C.reduce(self._comm, t, out, int(root), int(ReduceOp.parse(op)), 1.0 if scale is None else float(scale))
         return out
 
+    @_observed("gather")
     def gather(self, inp: torch.Tensor, root: int = 0, out: Optional[torch.Tensor] = None) -> torch.Tensor:
         if out is None:
             out = torch.empty(inp.numel() * self.world_size, dtype=inp.dtype, device=inp.device)
         self._C.gather(self._comm, inp, out, int(root))
         return out
 
+    @_observed("scatter")
     def scatter(self, inp: torch.Tensor, root: int = 0, out: Optional[torch.Tensor] = None) -> torch.Tensor:
         if out is None:
             out = torch.empty(inp.numel() // self.world_size, dtype=inp.dtype, device=inp.device)
         self._C.scatter(self._comm, inp, out, int(root))
         return out
 
+    @_observed("scan")
     def scan(self, inp: torch.Tensor, op="sum", out: Optional[torch.Tensor] = None) -> torch.Tensor:
         out = torch.empty_like(inp) if out is None else out
         self._C.scan(self._comm, inp, out, int(ReduceOp.parse(op)), False)
         return out
 
+    @_observed("exclusive_scan")
     def exclusive_scan(self, inp: torch.Tensor, op="sum", out: Optional[torch.Tensor] = None) -> torch.Tensor:
         out = torch.empty_like(inp) if out is None else out
         self._C.scan(self._comm, inp, out, int(ReduceOp.parse(op)), True)
         return out
 
+    @_observed("barrier")
     def barrier(self):
         self._C.barrier(self._comm)
 

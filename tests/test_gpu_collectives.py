@@ -176,6 +176,9 @@ def test_world1_allreduce_scale_cast(cuda0):
     comm.all_reduce(x, out=out, scale=0.5)
     torch.testing.assert_close(out, x.float() * 0.5)
     comm.check()
+    st = comm.stats()
+    assert st["all_reduce"] == {"calls": 1, "bytes": 4097 * 2}
+    assert st["all_reduce_algorithms"] == {"local": 1}
 
 
 def test_device_wait_timeout_reports_error(cuda0):
