@@ -101,7 +101,13 @@ void reduce_int(T* __restrict d, const T* __restrict s, size_t n, ReduceOp op) {
 // Float loops: the compiler vectorises these; target_clones picks the widest
 // ISA the CPU supports at load time (AVX-512F, AVX2, or baseline SSE2).
 #if defined(__x86_64__) && defined(__GNUC__) && !defined(__clang__)
+#if defined(__SANITIZE_THREAD__) || defined(__SANITIZE_ADDRESS__)
+// target_clones resolves through IFUNC during relocation, before a sanitizer
+// runtime is initialised: sanitizer builds use the default clone only.
+#define NEXAR_CLONES
+#else
 #define NEXAR_CLONES __attribute__((target_clones("avx512f", "avx2", "default")))
+#endif
 #else
 #define NEXAR_CLONES
 #endif

@@ -12,6 +12,7 @@
 
 #include <fcntl.h>
 #include <poll.h>
+#include <signal.h>
 #include <sys/socket.h>
 #include <unistd.h>
 
@@ -231,7 +232,25 @@ class TlsStream : public Stream {
   std::atomic<bool> closed_{false};
 };
 
+// OpenSSL's socket BIO writes with write(), not send(MSG_NOSIGNAL) like the
+// plain transport, so a write to a peer that already closed raises SIGPIPE,
+// whose default action ends the process. Ignore it, unless the embedding
+// program installed its own handler (Python already ignores it).
+void ignore_sigpipe_once() {
+  static std::once_flag once;
+  std::call_once(once, [] {
+    struct sigaction cur;
+    if (sigaction(SIGPIPE, nullptr, &cur) == 0 && cur.sa_handler == SIG_DFL) {
+      struct sigaction sa;
+      std::memset(&sa, 0, sizeof(sa));
+      sa.sa_handler = SIG_IGN;
+      sigaction(SIGPIPE, &sa, nullptr);
+    }
+  });
+}
+
 SSL_CTX* make_ctx(bool server, const TlsIdentity& id, bool verify_peer) {
+  ignore_sigpipe_once();
   SSL_CTX* ctx = SSL_CTX_new(server ? TLS_server_method() : TLS_client_method());
   if (!ctx) tls_fail("SSL_CTX_new");
   SSL_CTX_set_min_proto_version(ctx, TLS1_3_VERSION);
