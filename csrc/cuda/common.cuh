@@ -53,6 +53,14 @@ NEXAR_D uint4 ld16_volatile(const void* p) {
                : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p) : "memory");
   return v;
 }
+// L2-coherent 16-byte load (bypasses L1): for data another GPU or CTA
+// published through a release/acquire flag that this CTA already observed.
+NEXAR_D uint4 ld16_cg(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.cg.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
+  return v;
+}
 NEXAR_D uint4 ld16_nc(const void* p) {
   uint4 v;
   asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"

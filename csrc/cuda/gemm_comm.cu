@@ -167,31 +167,58 @@ struct EpiPeerRS {
       if (!__syncthreads_and(ok)) break;
       const int ltm = j / tiles_n, tn = j % tiles_n;
       const int cols = min(BN, N - tn * BN);
-      const int packs = BM * (cols / 8);
-      for (int idx = threadIdx.x; idx < packs; idx += blockDim.x) {
-        const int r = idx / (cols / 8), c8 = idx % (cols / 8);
-        const long long row = (long long)ltm * BM + r;
-        const int col = tn * BN + c8 * 8;
-        float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-        for (int src = 0; src < c.world; ++src) {
-          const uint4 v = ld16_volatile(slot0 + ((long long)src * rpr + row) * N + col);
-          const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
+      const int cpr = cols / 8;  // 16-byte packs per row
+      const int packs = BM * cpr;
+      // Four packs per thread in flight for every source rank: the loads of
+      // one pass are independent, so the reduction streams instead of paying
+      // one L2/NVLink round trip per pack (plain L2 loads: the tile flags
+      // observed above order them after the producers' stores).
+      constexpr int U = 4;
+      const int step = (int)blockDim.x;
+      for (int base = threadIdx.x; base < packs; base += U * step) {
+        float acc[U][8];
+        long long row[U];
+        int col[U];
+        bool live[U];
 #pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            const float2 f = __bfloat1622float2(h[k]);
-            acc[2 * k] += f.x;
-            acc[2 * k + 1] += f.y;
+        for (int u = 0; u < U; ++u) {
+          const int idx = base + u * step;
+          live[u] = idx < packs;
+          const int r = live[u] ? idx / cpr : 0, c8 = live[u] ? idx % cpr : 0;
+          row[u] = (long long)ltm * BM + r;
+          col[u] = tn * BN + c8 * 8;
+#pragma unroll
+          for (int k = 0; k < 8; ++k) acc[u][k] = 0.f;
+        }
+        for (int src = 0; src < c.world; ++src) {
+          uint4 v[U];
+#pragma unroll
+          for (int u = 0; u < U; ++u)
+            v[u] = live[u] ? ld16_cg(slot0 + ((long long)src * rpr + row[u]) * N + col[u]) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+          for (int u = 0; u < U; ++u) {
+            const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v[u]);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const float2 f = __bfloat1622float2(h[k]);
+              acc[u][2 * k] += f.x;
+              acc[u][2 * k + 1] += f.y;
+            }
           }
         }
-        if (bias) {
 #pragma unroll
-          for (int k = 0; k < 8; ++k) acc[k] += __bfloat162float(bias[col + k]);
+        for (int u = 0; u < U; ++u) {
+          if (!live[u]) continue;
+          if (bias) {
+#pragma unroll
+            for (int k = 0; k < 8; ++k) acc[u][k] += __bfloat162float(bias[col[u] + k]);
+          }
+          uint4 o;
+          __nv_bfloat162* oh = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+          for (int k = 0; k < 4; ++k) oh[k] = __floats2bfloat162_rn(acc[u][2 * k], acc[u][2 * k + 1]);
+          *reinterpret_cast<uint4*>(out + row[u] * ldo + col[u]) = o;
         }
-        uint4 o;
-        __nv_bfloat162* oh = reinterpret_cast<__nv_bfloat162*>(&o);
-#pragma unroll
-        for (int k = 0; k < 4; ++k) oh[k] = __floats2bfloat162_rn(acc[2 * k], acc[2 * k + 1]);
-        *reinterpret_cast<uint4*>(out + row * ldo + col) = o;
       }
       __syncthreads();
     }
