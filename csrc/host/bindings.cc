@@ -413,6 +413,51 @@ PYBIND11_MODULE(_host, m) {
         const uint64_t tag = c->next_collective_tag();
         return c->spawn([c, p, n, dt, op, tag] { c->all_reduce_tagged(P(p), n, (DataType)dt, (ReduceOp)op, tag); });
       })
+      .def("all_reduce_bucketed_nb", [](std::shared_ptr<NexarClient> c, const std::vector<std::pair<uint64_t, size_t>>& es,
+                                        int dt, int op) {
+        std::vector<std::pair<void*, size_t>> v;
+        for (auto& e : es) v.emplace_back(P(e.first), e.second);
+        const uint64_t tag = c->next_collective_tag();
+        return c->spawn([c, v, dt, op, tag] { c->all_reduce_bucketed_tagged(v, (DataType)dt, (ReduceOp)op, tag); });
+      })
+      .def("all_reduce_compressed_nb", [](std::shared_ptr<NexarClient> c, uint64_t p, size_t n, int dt, int op,
+                                          std::shared_ptr<Compressor> comp, uint64_t residual) {
+        const uint64_t tag = c->next_collective_tag();
+        return c->spawn([c, p, n, dt, op, comp, residual, tag] {
+          c->all_reduce_compressed_tagged(P(p), n, (DataType)dt, (ReduceOp)op, *comp, P(residual), tag);
+        });
+      })
+      .def("peer_info", [](const NexarClient& c, Rank r) {
+        // Direct link to communicator rank r (nexar's client.peer(rank)); raises UnknownPeer otherwise.
+        if (r >= c.world_size() || !c.has_direct_peer(r))
+          fail(Err::UnknownPeer, "unknown peer: rank " + std::to_string(r) + " has no direct connection");
+        auto conn = c.mesh()->conn(c.mesh_rank(r));
+        py::dict d;
+        d["rank"] = r;
+        d["mesh_rank"] = c.mesh_rank(r);
+        d["alive"] = conn && conn->alive();
+        d["encrypted"] = conn && conn->encrypted();
+        return d;
+      })
+      .def("recv_message_from", [](NexarClient& c, Rank src, uint32_t tag, double timeout_s) {
+        // The oldest data message with `tag` from `src` on the root
+        // communicator (what send_message_to / send deliver).
+        const Rank m = c.mesh_rank(src);
+        const double t = timeout_s < 0 ? c.config().collective_timeout_s : timeout_s;
+        Bytes b;
+        {
+          py::gil_scoped_release nogil;
+          b = std::move(c.mesh()->box(m)->pop_data(tag, Clock::now() + std::chrono::microseconds((int64_t)(t * 1e6))).msg.payload);
+        }
+        return py::bytes(reinterpret_cast<const char*>(b.data()), b.size());
+      }, py::arg("src"), py::arg("tag"), py::arg("timeout_s") = -1.0)
+      .def("send_message_to", [](NexarClient& c, Rank dest, uint32_t tag, const py::bytes& payload, int prio) {
+        // One framed data message to `dest` (received with recv_message_from(src, tag) or recv).
+        const std::string s = payload;
+        Message m = Message::data(tag, c.mesh()->rank(), Bytes(s.begin(), s.end()));
+        py::gil_scoped_release nogil;
+        c.send_message_to(dest, m, (Priority)prio);
+      }, py::arg("dest"), py::arg("tag"), py::arg("payload"), py::arg("priority") = 0)
       .def("spawn_collective", [](std::shared_ptr<NexarClient> c, const std::string& op, py::tuple args) {
         // Generic non-blocking launcher for the other collectives. The
         // collective's tag is reserved here (call order), so concurrent

@@ -227,6 +227,10 @@ class NexarClient : public std::enable_shared_from_this<NexarClient> {
   // at call time so concurrent collectives are isolated).
   uint64_t next_collective_tag() { return collective_tag_.fetch_add(1); }
   void all_reduce_tagged(void* ptr, size_t count, DataType dt, ReduceOp op, uint64_t tag);
+  void all_reduce_bucketed_tagged(const std::vector<std::pair<void*, size_t>>& entries, DataType dt, ReduceOp op,
+                                  uint64_t tag);
+  void all_reduce_compressed_tagged(void* ptr, size_t count, DataType dt, ReduceOp op, Compressor& comp,
+                                    void* residual, uint64_t tag);
   CollectiveHandle spawn(std::function<void()> fn);
 
   // ---- communicator management

@@ -537,6 +537,11 @@ void NexarClient::all_reduce_rs_ag(void* ptr, size_t count, DataType dt, ReduceO
 }
 
 void NexarClient::all_reduce_bucketed(const std::vector<std::pair<void*, size_t>>& entries, DataType dt, ReduceOp op) {
+  all_reduce_bucketed_tagged(entries, dt, op, next_collective_tag());
+}
+
+void NexarClient::all_reduce_bucketed_tagged(const std::vector<std::pair<void*, size_t>>& entries, DataType dt,
+                                             ReduceOp op, uint64_t tag) {
   // Gather the (ptr, count) list into one buffer, one all-reduce, scatter back
   // (nexar/src/collective/bucketed_allreduce.rs:23-75).
   const size_t es = dtype_size(dt);
@@ -548,7 +553,6 @@ void NexarClient::all_reduce_bucketed(const std::vector<std::pair<void*, size_t>
     adapter_->stage_for_send(e.first, e.second * es, flat.data() + off);
     off += e.second * es;
   }
-  const uint64_t tag = next_collective_tag();
   if (total * es >= config().large_msg_bytes) coll::pipelined_ring_allreduce(*this, flat.data(), total, dt, op, tag);
   else coll::ring_allreduce(*this, flat.data(), total, dt, op, tag);
   off = 0;
@@ -559,7 +563,11 @@ void NexarClient::all_reduce_bucketed(const std::vector<std::pair<void*, size_t>
 }
 
 void NexarClient::all_reduce_compressed(void* ptr, size_t count, DataType dt, ReduceOp op, Compressor& comp, void* residual) {
-  const uint64_t tag = next_collective_tag();
+  all_reduce_compressed_tagged(ptr, count, dt, op, comp, residual, next_collective_tag());
+}
+
+void NexarClient::all_reduce_compressed_tagged(void* ptr, size_t count, DataType dt, ReduceOp op, Compressor& comp,
+                                               void* residual, uint64_t tag) {
   with_staging(*this, ptr, count * dtype_size(dt), [&](uint8_t* b) {
     coll::compressed_allreduce(*this, b, count, dt, op, comp, static_cast<uint8_t*>(residual), tag);
   });

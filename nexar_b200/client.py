@@ -18,7 +18,7 @@ from __future__ import annotations
 from typing import Iterable, List, Optional, Sequence, Tuple
 
 from . import _native
-from .core import DataType, ReduceOp
+from .core import DataType, Priority, ReduceOp
 
 _H = None
 
@@ -123,6 +123,41 @@ class NexarClient:
         cfg = config if config is not None else _h().Config.from_env()
         return NexarClient(_h().NexarClient.bootstrap_worker(seed_addr, token, cfg, bind_host))
 
+    @staticmethod
+    def bootstrap_elastic(initial_world: int, min_world: int = 1, max_world: int = 0, config=None,
+                          checkpoint_timeout_s: float = 60.0) -> "ElasticBootstrap":
+        """In-process cluster with elastic scaling (nexar/src/client/bootstrap.rs:41).
+
+        A local seed forms ``initial_world`` ranks, then keeps accepting joiners
+        (``ElasticManager.join(seed_addr, ...)`` from any process) up to
+        ``max_world`` (0 = unbounded); each rank gets an ElasticManager (rank 0's
+        owns the seed) whose ``elastic_checkpoint()`` admits joiners and applies
+        ``remove_node`` requests at a step boundary.
+        """
+        import threading
+        H = _h()
+        cfg = config if config is not None else H.Config()
+        seed = H.SeedNode.bind_local(bool(getattr(cfg, "tls", False)))
+        natives = [None] * initial_world
+        errs = []
+
+        def boot(i):
+            try:
+                natives[i] = H.NexarClient.bootstrap_worker(seed.local_addr(), None, cfg, "127.0.0.1")
+            except Exception as e:  # noqa: BLE001
+                errs.append(e)
+        ts = [threading.Thread(target=boot, args=(i,)) for i in range(initial_world)]
+        [t.start() for t in ts]
+        seed.form_cluster(initial_world)
+        [t.join() for t in ts]
+        if errs:
+            raise errs[0]
+        natives.sort(key=lambda c: c.rank)
+        seed.accept_elastic(max_world)
+        mgrs = [H.ElasticManager(c, seed if c.rank == 0 else None, min_world, max_world, checkpoint_timeout_s)
+                for c in natives]
+        return ElasticBootstrap(seed, [NexarClient(c) for c in natives], mgrs)
+
     # ------------------------------------------------------------ identity
     @property
     def rank(self) -> int:
@@ -198,6 +233,22 @@ class NexarClient:
 
     def stop_rpc_server(self):
         self._c.stop_rpc_server()
+
+    def rpc_dispatcher(self) -> "RpcDispatcher":
+        """The dispatcher that serves this client's registered RPC handlers."""
+        return RpcDispatcher(self)
+
+    # ------------------------------------------------------------ peers / raw messages
+    def peer(self, rank: int) -> dict:
+        """Direct connection to ``rank``: {rank, mesh_rank, alive, encrypted}; UnknownPeer if none."""
+        return self._c.peer_info(rank)
+
+    def send_message_to(self, dest: int, tag: int, payload: bytes, priority=Priority.Critical):
+        """One framed data message to ``dest`` (root communicator); see ``recv_message_from``."""
+        self._c.send_message_to(dest, tag, payload, int(priority))
+
+    def recv_message_from(self, src: int, tag: int, timeout_s: float = -1.0) -> bytes:
+        return self._c.recv_message_from(src, tag, timeout_s)
 
     # ------------------------------------------------------------ collectives (pointer API)
     def all_reduce(self, ptr: int, count: int, dtype, op=ReduceOp.Sum):
@@ -285,10 +336,22 @@ class NexarClient:
     def barrier_nb(self):
         return self._nb("barrier")
 
+    def all_reduce_bucketed_nb(self, entries: Sequence[Tuple[int, int]], dtype, op=ReduceOp.Sum):
+        return CollectiveHandle(self._c.all_reduce_bucketed_nb(list(entries), int(dtype), int(ReduceOp.parse(op))))
+
+    def all_reduce_compressed_nb(self, ptr: int, count: int, dtype, op, compressor, residual_ptr: int):
+        return CollectiveHandle(self._c.all_reduce_compressed_nb(ptr, count, int(dtype), int(ReduceOp.parse(op)),
+                                                                 compressor, residual_ptr))
+
     # ------------------------------------------------------------ typed host helpers
     def all_reduce_host(self, buf, op=ReduceOp.Sum):
         p, n, dt = _buf(buf)
         self.all_reduce(p, n, dt, op)
+        return buf
+
+    def all_reduce_rs_ag_host(self, buf, op=ReduceOp.Sum):
+        p, n, dt = _buf(buf)
+        self.all_reduce_rs_ag(p, n, dt, op)
         return buf
 
     def broadcast_host(self, buf, root: int):
@@ -437,6 +500,38 @@ class NexarClient:
 
 
 # The C++ API is synchronous, so the blocking client is the same object.
+class RpcDispatcher:
+    """Serves the RPC handlers registered on a client (nexar's RpcDispatcher)."""
+
+    def __init__(self, client: "NexarClient"):
+        self._client = client
+
+    def register(self, fn_id: int, handler):
+        self._client.register_rpc(fn_id, handler)
+
+    def serve_once(self, src: int, timeout_s: float = -1.0):
+        self._client.serve_rpc_once(src, timeout_s)
+
+    def start(self):
+        self._client.start_rpc_server()
+
+    def stop(self):
+        self._client.stop_rpc_server()
+
+
+class ElasticBootstrap:
+    """Result of ``NexarClient.bootstrap_elastic``: the seed, the initial clients, their managers."""
+
+    def __init__(self, seed, clients, managers):
+        self.seed = seed
+        self.clients = clients
+        self.managers = managers
+
+    @property
+    def seed_addr(self) -> str:
+        return self.seed.local_addr()
+
+
 SyncClient = NexarClient
 
 

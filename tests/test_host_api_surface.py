@@ -1,0 +1,74 @@
+"""The reference's public client API names on the Python client (peer, raw messages,
+rpc_dispatcher, non-blocking bucketed / compressed all-reduce, rs_ag host variant,
+bootstrap_elastic)."""
+import threading
+
+import numpy as np
+import pytest
+
+from helpers_host import run_collective
+
+
+def test_peer_messages_and_rpc_dispatcher():
+    from nexar_b200.client import NexarClient
+    from nexar_b200.core import NexarError
+    cs = NexarClient.bootstrap_local(3)
+    p = cs[0].peer(1)
+    assert p["rank"] == 1 and p["alive"] and not p["encrypted"]
+    with pytest.raises(NexarError):
+        cs[0].peer(7)
+    cs[0].send_message_to(2, 42, b"hello")
+    assert cs[2].recv_message_from(0, 42, 5.0) == b"hello"
+    d = cs[1].rpc_dispatcher()
+    d.register(5, lambda b: b[::-1])
+    t = threading.Thread(target=d.serve_once, args=(0, 5.0))
+    t.start()
+    assert cs[0].rpc(1, 5, b"abc", 5.0) == b"cba"
+    t.join()
+
+
+def test_nonblocking_bucketed_and_compressed_and_rs_ag_host():
+    from nexar_b200.client import NexarClient
+    from nexar_b200.core import DataType
+    from nexar_b200 import _native
+    cs = NexarClient.bootstrap_local(4)
+    a = [np.full(100, float(c.rank + 1), np.float32) for c in cs]
+    b = [np.full(37, float(2 * c.rank), np.float32) for c in cs]
+    hs = {}
+
+    def start(c):
+        hs[c.rank] = c.all_reduce_bucketed_nb([(a[c.rank].ctypes.data, 100), (b[c.rank].ctypes.data, 37)],
+                                              DataType.F32)
+        hs[c.rank].wait()
+    run_collective(cs, start)
+    assert all((x == 10).all() for x in a) and all((x == 12).all() for x in b)
+    g = [np.random.default_rng(c.rank).standard_normal(1000).astype(np.float32) for c in cs]
+    res = [np.zeros(1000, np.float32) for _ in cs]
+    comp = _native.host().TopKCompressor(0.1)
+
+    def cmp(c):
+        c.all_reduce_compressed_nb(g[c.rank].ctypes.data, 1000, DataType.F32, "sum", comp,
+                                   res[c.rank].ctypes.data).wait()
+    run_collective(cs, cmp)
+    assert all(np.allclose(g[0], x) for x in g)  # every rank holds the same (sparse) sum
+    v = [np.full(64, float(c.rank), np.float32) for c in cs]
+    run_collective(cs, lambda c: c.all_reduce_rs_ag_host(v[c.rank]))
+    assert all((x == 6).all() for x in v)
+
+
+def test_bootstrap_elastic_grows():
+    from nexar_b200.client import Config, NexarClient
+    from nexar_b200 import _native
+    H = _native.host()
+    eb = NexarClient.bootstrap_elastic(2, max_world=4, config=Config(heartbeat_interval_s=0.1))
+    joined = {}
+    jt = threading.Thread(target=lambda: joined.setdefault(
+        "c", H.ElasticManager.join(eb.seed_addr, None, Config(heartbeat_interval_s=0.1), 20.0)))
+    jt.start()
+    import time
+    time.sleep(0.5)
+    assert run_collective(eb.managers, lambda m: m.elastic_checkpoint()) == [True, True]
+    jt.join(20)
+    grown = [NexarClient(m.client()) for m in eb.managers] + [NexarClient(joined["c"])]
+    assert sorted(c.world_size for c in grown) == [3, 3, 3]
+    eb.seed.close()
