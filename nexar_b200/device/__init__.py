@@ -1,2 +1,2 @@
 """Device (GPU) side of nexar_b200: symmetric memory and peer-memory collectives."""
-from .comm import DeviceCommunicator, DeviceHandle  # noqa: F401
+from .comm import DeviceCommunicator, GlobalPtr, DeviceHandle  # noqa: F401

@@ -99,6 +99,23 @@ def _observed(op: str):
     return deco
 
 
+class GlobalPtr:
+    """(rank, heap offset, bytes) of a symmetric allocation (nexar's GlobalPtr,
+    nexar/src/memory/global_ptr.rs:8-41, which the reference defines but never
+    uses). Here it resolves: ``address()`` is the device virtual address of
+    rank ``rank``'s copy, mapped into this process (peer memory over NVLink),
+    usable by kernels that load or store another GPU's buffer directly."""
+
+    def __init__(self, comm: "DeviceCommunicator", rank: int, offset: int, nbytes: int):
+        self.comm, self.rank, self.offset, self.nbytes = comm, rank, offset, nbytes
+
+    def address(self) -> int:
+        return int(self.comm.native.peer_ptr(self.rank)) + self.offset
+
+    def __repr__(self):
+        return f"GlobalPtr(rank={self.rank}, offset={self.offset}, nbytes={self.nbytes})"
+
+
 class DeviceCommunicator:
     """Symmetric-memory communicator over the GPUs of one box."""
 
@@ -194,6 +211,15 @@ class DeviceCommunicator:
             return self._C.nvls_tensor(self._comm, off, list(shape), int(DataType.from_torch(dtype)))
         off = self._comm.alloc_symmetric(nbytes, align)
         return self._C.symmetric_tensor(self._comm, off, list(shape), int(DataType.from_torch(dtype)))
+
+    def global_ptr(self, t: torch.Tensor, rank: int) -> GlobalPtr:
+        """GlobalPtr to rank ``rank``'s copy of symmetric-heap tensor ``t``."""
+        off = self._comm.symmetric_offset(t)
+        if off < 0:
+            raise ValueError("global_ptr needs a tensor from symmetric_empty() (peer-mapped heap)")
+        if not 0 <= rank < self.world_size:
+            raise ValueError(f"rank {rank} out of range")
+        return GlobalPtr(self, rank, int(off), t.numel() * t.element_size())
 
     def is_symmetric(self, t: torch.Tensor) -> bool:
         return self._comm.symmetric_offset(t) >= 0 or (self.nvls and self._comm.nvls_offset(t) >= 0)

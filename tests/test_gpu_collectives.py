@@ -179,6 +179,9 @@ def test_world1_allreduce_scale_cast(cuda0):
     st = comm.stats()
     assert st["all_reduce"] == {"calls": 1, "bytes": 4097 * 2}
     assert st["all_reduce_algorithms"] == {"local": 1}
+    sym = comm.symmetric_empty([1024], torch.float32)
+    gp = comm.global_ptr(sym, 0)
+    assert gp.address() == sym.data_ptr() and gp.nbytes == 4096
 
 
 def test_device_wait_timeout_reports_error(cuda0):
