@@ -91,3 +91,74 @@ def test_compressed_multi_gpu_identical_on_all_ranks():
         assert err == [], f"rank {r}: {err}"
         sums.add(s)
     assert len(sums) == 1  # bitwise-identical results on every rank
+
+
+def _distinct_magnitudes(n, device, seed):
+    """n values whose |v| differ in the top 24 bits of the fp32 pattern, in random order and sign."""
+    i = torch.arange(n, device=device)
+    v = torch.ldexp(1.0 + (i % 32768).float() / 32768.0, (i // 32768 - 5).int())
+    g = torch.Generator(device=device).manual_seed(seed)
+    perm = torch.randperm(n, device=device, generator=g)
+    sign = torch.where(torch.rand(n, device=device, generator=g) < 0.5, -1.0, 1.0)
+    return v[perm] * sign
+
+
+def _run_compress(C, grad, res, k):
+    dev = grad.device
+    blob = torch.zeros(C.compress_blob_bytes(k), dtype=torch.uint8, device=dev)
+    work = torch.empty(C.compress_workspace_bytes(grad.numel()), dtype=torch.uint8, device=dev)
+    C.topk_fp8_compress(grad, res, k, blob, work)
+    torch.cuda.synchronize()
+    scale = blob[:4].view(torch.float32).item()
+    idx = blob[16:16 + 4 * k].view(torch.int32).long()
+    val = blob[16 + 4 * k:16 + 5 * k].view(torch.float8_e4m3fn).float() * scale
+    return idx, val, scale
+
+
+@pytest.mark.parametrize("n,offset", [(1 << 20, 0), (300_007, 0), (300_007, 1), (4097, 3)])
+def test_topk_blob_exact_order_and_residual(cuda0, n, offset):
+    """Exact selection when magnitudes are distinct: ascending indices, e4m3 values, residual.
+
+    offset > 0 passes views that are not 16-byte aligned (the scalar load path)."""
+    from nexar_b200 import _native
+    C = _native.cuda()
+    k = max(1, n // 50)
+    store = torch.zeros(n + offset, device=cuda0)
+    store[offset:] = _distinct_magnitudes(n, cuda0, seed=n)
+    gstore = torch.zeros(n + offset, device=cuda0, dtype=torch.bfloat16)
+    res, grad = store[offset:], gstore[offset:]
+    r = res.clone()
+    idx, val, scale = _run_compress(C, grad, res, k)
+    want_idx = torch.topk(r.abs(), k).indices.sort().values
+    assert torch.equal(idx, want_idx)
+    want_scale = r.abs().max().item() / 448.0
+    assert abs(scale - want_scale) <= 1e-6 * want_scale
+    q = (r[want_idx] / scale).to(torch.float8_e4m3fn).float() * scale
+    # r * (1/scale) on the device may round to the neighbouring e4m3 value at a
+    # rounding boundary: allow a few one-step differences.
+    off = (val - q).abs() > 1e-6 * q.abs()
+    assert off.sum().item() <= 2 + k // 1000
+    assert ((val - q).abs() <= 0.13 * q.abs()).all()
+    want_res = r.clone()
+    want_res[want_idx] -= val
+    torch.testing.assert_close(res, want_res, rtol=0, atol=1e-5)  # device fuses r - q * scale
+
+
+def test_topk_ties_taken_in_index_order(cuda0):
+    """Mostly-zero input (an embedding gradient's unused rows): the k-th value is a tie
+    shared by ~all elements; the lowest indices among the ties are taken."""
+    from nexar_b200 import _native
+    C = _native.cuda()
+    n, k = 1 << 20, 1000
+    g = torch.Generator(device=cuda0).manual_seed(3)
+    nz = torch.randperm(n, device=cuda0, generator=g)[:100]
+    res = torch.zeros(n, device=cuda0)
+    res[nz] = torch.rand(100, device=cuda0, generator=g) + 1.0
+    grad = torch.zeros(n, device=cuda0, dtype=torch.bfloat16)
+    idx, val, _ = _run_compress(C, grad, res.clone(), k)
+    zero_mask = torch.ones(n, dtype=torch.bool, device=cuda0)
+    zero_mask[nz] = False
+    first_zeros = torch.nonzero(zero_mask).flatten()[:k - 100]
+    want = torch.cat([nz, first_zeros]).sort().values
+    assert torch.equal(idx, want)
+    assert (val[torch.isin(idx, nz)] > 0).all()
