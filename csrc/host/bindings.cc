@@ -507,12 +507,28 @@ PYBIND11_MODULE(_host, m) {
       .def_readonly("new_rank", &RecoveryEvent::new_rank)
       .def_readonly("new_world_size", &RecoveryEvent::new_world_size)
       .def_readonly("dead_ranks", &RecoveryEvent::dead_ranks);
+  py::class_<EventSubscription<RecoveryEvent>, std::shared_ptr<EventSubscription<RecoveryEvent>>>(
+      m, "RecoveryEventReceiver")
+      .def("recv", [](EventSubscription<RecoveryEvent>& s, double timeout) -> py::object {
+        RecoveryEvent e;
+        bool ok;
+        {
+          py::gil_scoped_release r;
+          ok = s.recv(timeout, &e);
+        }
+        if (!ok) return py::none();
+        return py::cast(e);
+      }, py::arg("timeout_s") = -1.0)
+      .def_property_readonly("pending", &EventSubscription<RecoveryEvent>::pending)
+      .def_property_readonly("dropped", &EventSubscription<RecoveryEvent>::dropped);
   py::class_<RecoveryOrchestrator>(m, "RecoveryOrchestrator")
       .def(py::init([](std::shared_ptr<NexarClient> c, int policy) {
         return new RecoveryOrchestrator(c, (RecoveryPolicy)policy);
       }))
       .def_static("from_config", &RecoveryOrchestrator::from_config)
       .def("start", &RecoveryOrchestrator::start)
+      .def("run", &RecoveryOrchestrator::run, GR())
+      .def("subscribe", &RecoveryOrchestrator::subscribe)
       .def("shutdown", &RecoveryOrchestrator::shutdown, GR())
       .def("recover", &RecoveryOrchestrator::recover, GR())
       .def("client", &RecoveryOrchestrator::client)
@@ -533,6 +549,20 @@ PYBIND11_MODULE(_host, m) {
       .def_readonly("new_world_size", &ElasticEvent::new_world_size)
       .def_readonly("joined", &ElasticEvent::joined)
       .def_readonly("left", &ElasticEvent::left);
+  py::class_<EventSubscription<ElasticEvent>, std::shared_ptr<EventSubscription<ElasticEvent>>>(
+      m, "ElasticEventReceiver")
+      .def("recv", [](EventSubscription<ElasticEvent>& s, double timeout) -> py::object {
+        ElasticEvent e;
+        bool ok;
+        {
+          py::gil_scoped_release r;
+          ok = s.recv(timeout, &e);
+        }
+        if (!ok) return py::none();
+        return py::cast(e);
+      }, py::arg("timeout_s") = -1.0)
+      .def_property_readonly("pending", &EventSubscription<ElasticEvent>::pending)
+      .def_property_readonly("dropped", &EventSubscription<ElasticEvent>::dropped);
   py::class_<ElasticManager>(m, "ElasticManager")
       .def(py::init<std::shared_ptr<NexarClient>, std::shared_ptr<SeedNode>, uint32_t, uint32_t, double>(),
            py::arg("client"), py::arg("seed") = nullptr, py::arg("min_world") = 1, py::arg("max_world") = 0,
@@ -541,6 +571,7 @@ PYBIND11_MODULE(_host, m) {
       .def("client", &ElasticManager::client)
       .def("remove_node", &ElasticManager::remove_node)
       .def("events", &ElasticManager::events)
+      .def("subscribe", &ElasticManager::subscribe)
       .def_property_readonly("epoch", &ElasticManager::epoch)
       .def_static("join", [](const std::string& seed, const py::object& token, const Config& cfg, double timeout) {
         Bytes t = token.is_none() ? Bytes() : to_bytes(token.cast<py::bytes>());

@@ -48,10 +48,17 @@ void RecoveryOrchestrator::start() {
   thr_ = std::thread([this] { loop(); });
 }
 
+void RecoveryOrchestrator::run() {
+  if (thr_.joinable()) fail(Err::Recovery, "run(): the watch loop already runs (start())");
+  stop_ = false;
+  loop();
+}
+
 void RecoveryOrchestrator::shutdown() {
   stop_ = true;
   cv_.notify_all();
   if (thr_.joinable()) thr_.join();
+  channel_.close();
 }
 
 std::shared_ptr<NexarClient> RecoveryOrchestrator::client() const {
@@ -60,6 +67,7 @@ std::shared_ptr<NexarClient> RecoveryOrchestrator::client() const {
 }
 
 void RecoveryOrchestrator::emit(RecoveryEvent e) {
+  channel_.emit(e);
   {
     std::lock_guard<std::mutex> g(mu_);
     events_.push_back(std::move(e));
@@ -274,6 +282,7 @@ bool ElasticManager::elastic_checkpoint() {
   if (!ack.leaving.empty()) {
     if (me_leaving) {
       events_.push_back(ElasticEvent{ack.epoch, 0, ack.new_world_size, joined, ack.leaving});
+      channel_.emit(events_.back());
       client_ = nullptr;
       return true;
     }
@@ -281,6 +290,7 @@ bool ElasticManager::elastic_checkpoint() {
   }
   client_ = nc;
   events_.push_back(ElasticEvent{ack.epoch, nc->rank(), nc->world_size(), joined, ack.leaving});
+  channel_.emit(events_.back());
   return true;
 }
 

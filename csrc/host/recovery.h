@@ -20,6 +20,7 @@
 #include <map>
 
 #include "client.h"
+#include "events.h"
 
 namespace nexar {
 
@@ -37,6 +38,11 @@ class RecoveryOrchestrator {
   ~RecoveryOrchestrator();
   // Start the watch loop on a background thread.
   void start();
+  // Run the watch loop on the calling thread until shutdown() (the
+  // reference's `run`); throws if the loop already runs on start()'s thread.
+  void run();
+  // Broadcast receiver: sees every event emitted after this call.
+  std::shared_ptr<EventSubscription<RecoveryEvent>> subscribe() { return channel_.subscribe(); }
   void shutdown();
   // Run one recovery synchronously for an observed dead set (used by run()).
   void recover(std::vector<Rank> dead);
@@ -57,6 +63,7 @@ class RecoveryOrchestrator {
   std::shared_ptr<NexarClient> client_;
   RecoveryPolicy policy_;
   std::deque<RecoveryEvent> events_;
+  EventChannel<RecoveryEvent> channel_;
   std::string error_;
   // Leader side: the latest vote of each survivor, kept across agreement
   // attempts (a vote consumed by an attempt that a later failure interrupted
@@ -87,6 +94,8 @@ class ElasticManager {
   // Coordinator (rank 0): schedule a rank to leave at the next checkpoint.
   void remove_node(Rank r);
   std::vector<ElasticEvent> events() const { return events_; }
+  // Broadcast receiver: sees every membership change after this call.
+  std::shared_ptr<EventSubscription<ElasticEvent>> subscribe() { return channel_.subscribe(); }
   uint64_t epoch() const { return epoch_; }
 
   // Joiner side: connect to the seed, accept the existing ranks' connections,
@@ -102,6 +111,7 @@ class ElasticManager {
   uint64_t epoch_ = 0;
   std::vector<Rank> pending_leave_;
   std::vector<ElasticEvent> events_;
+  EventChannel<ElasticEvent> channel_;
 };
 
 }  // namespace nexar

@@ -11,7 +11,9 @@ Layers:
                              AdamW, tcgen05 GEMM, fused GEMM+collective kernels).
   * ``nexar_b200.models``    GPT-2, Llama MLP (TP) and MoE (EP) model definitions.
   * ``nexar_b200.parallel``  data-parallel, tensor-parallel and expert-parallel
-                             training entry points.
+                             training entry points; the hierarchical (node x
+                             cross-node) communicator.
+  * ``nexar_b200.memory``    BufferRef<Host|Device>, the tiered host buffer pool.
 """
 from .core import DataType, ReduceOp, NexarError  # noqa: F401
 

@@ -550,3 +550,106 @@ def RandomKCompressor(ratio: float):
 
 def NoCompression():
     return _h().NoCompression()
+
+
+class RecoveryPolicy:
+    """Recovery policy codes (nexar/src/config.rs RecoveryPolicy)."""
+    Automatic = 0
+    Manual = 1
+    Abort = 2
+
+
+class RecoveryOrchestrator:
+    """Failure watch + agreement + rebuild (nexar/src/cluster/recovery.rs:16-355),
+    over the native orchestrator.
+
+    ``new(client, policy)`` returns ``(orchestrator, receiver)`` like the
+    reference; ``subscribe()`` adds broadcast receivers (``recv(timeout_s)``
+    returns the next RecoveryEvent or None). ``run()`` blocks on the calling
+    thread until ``shutdown()``; ``start()`` runs the same loop on a native
+    thread."""
+
+    def __init__(self, client: "NexarClient", policy: int = RecoveryPolicy.Automatic):
+        self._o = _h().RecoveryOrchestrator(client.native, int(policy))
+
+    @classmethod
+    def new(cls, client: "NexarClient", policy: int = RecoveryPolicy.Automatic):
+        o = cls(client, policy)
+        return o, o.subscribe()
+
+    @classmethod
+    def from_config(cls, client: "NexarClient"):
+        o = cls.__new__(cls)
+        o._o = _h().RecoveryOrchestrator.from_config(client.native)
+        return o, o.subscribe()
+
+    def subscribe(self):
+        return self._o.subscribe()
+
+    def client(self) -> "NexarClient":
+        return NexarClient(self._o.client())
+
+    def start(self):
+        self._o.start()
+
+    def run(self):
+        self._o.run()
+
+    def shutdown(self):
+        self._o.shutdown()
+
+    def next_event(self, timeout_s: float):
+        return self._o.next_event(timeout_s)
+
+    def error(self) -> str:
+        return self._o.error()
+
+    @property
+    def native(self):
+        return self._o
+
+
+class ElasticManager:
+    """Elastic membership at training-step boundaries (nexar/src/cluster/elastic.rs),
+    over the native manager: ``elastic_checkpoint()`` (collective), ``subscribe()``,
+    ``client()``, ``remove_node(rank)`` (coordinator), ``events()``.
+    Joiners call ``ElasticManager.join(seed_addr, token)``."""
+
+    def __init__(self, client: "NexarClient", seed=None, min_world: int = 1, max_world: int = 0,
+                 timeout_s: float = 60.0):
+        self._m = _h().ElasticManager(client.native, seed, min_world, max_world, timeout_s)
+
+    @classmethod
+    def wrap(cls, native) -> "ElasticManager":
+        m = cls.__new__(cls)
+        m._m = native
+        return m
+
+    @staticmethod
+    def join(seed_addr: str, token: Optional[bytes] = None, config=None, timeout_s: float = 60.0) -> "NexarClient":
+        cfg = config if config is not None else _h().Config()
+        return NexarClient(_h().ElasticManager.join(seed_addr, token, cfg, timeout_s))
+
+    def elastic_checkpoint(self) -> bool:
+        return self._m.elastic_checkpoint()
+
+    def subscribe(self):
+        return self._m.subscribe()
+
+    def client(self) -> Optional["NexarClient"]:
+        c = self._m.client()
+        return None if c is None else NexarClient(c)
+
+    def remove_node(self, rank: int):
+        self._m.remove_node(rank)
+
+    def events(self):
+        return self._m.events()
+
+    @property
+    def epoch(self) -> int:
+        return self._m.epoch
+
+    @property
+    def native(self):
+        return self._m

@@ -240,7 +240,10 @@ def test_elastic_noop_checkpoint_and_grow_and_shrink(tls):
     # shrink: rank 1 leaves at the next checkpoint
     m3 = [H.ElasticManager(c.native, seed if c.rank == 0 else None, 1, 8, 10.0) for c in sorted(grown, key=lambda c: c.rank)]
     m3[0].remove_node(1)
+    subs = [m.subscribe() for m in m3]
     assert run_collective(m3, lambda m: m.elastic_checkpoint()) == [True, True, True]
+    evs = [s.recv(5.0) for s in subs]
+    assert all(e is not None and e.left == [1] and e.new_world_size == 2 for e in evs)
     assert m3[1].client() is None
     rest = [NexarClient(m3[0].client()), NexarClient(m3[2].client())]
     assert sorted(c.world_size for c in rest) == [2, 2]
@@ -298,3 +301,30 @@ def test_seed_rejects_wrong_token():
     t.join(30)
     assert errs
     seed.close()
+
+
+def test_recovery_run_subscribe_broadcast():
+    """run() blocks on its thread until shutdown; every subscriber sees the event
+    (broadcast receivers, nexar/src/cluster/recovery.rs:56-81)."""
+    import threading
+    from nexar_b200.client import RecoveryOrchestrator, RecoveryPolicy
+    from nexar_b200.core import NexarError
+    cs = bootstrap(3, **FAST)
+    (o0, r0a), (o1, r1) = RecoveryOrchestrator.new(cs[0]), RecoveryOrchestrator.new(cs[1], RecoveryPolicy.Automatic)
+    r0b = o0.subscribe()
+    t = threading.Thread(target=o0.run, daemon=True)
+    t.start()
+    o1.start()
+    with pytest.raises(NexarError):
+        o1.run()  # its loop already runs on start()'s thread
+    cs[2].close()
+    evs = [r.recv(10.0) for r in (r0a, r0b, r1)]
+    assert all(e is not None and e.dead_ranks == [2] and e.new_world_size == 2 for e in evs)
+    assert r0a.recv(0.05) is None and r0a.dropped == 0
+    new = [o0.client(), o1.client()]
+    run_collective(new, lambda c: c.barrier())
+    o0.shutdown()
+    t.join(5.0)
+    assert not t.is_alive()
+    assert r0a.recv(0.05) is None  # closed and drained
+    o1.shutdown()

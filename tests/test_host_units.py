@@ -227,3 +227,27 @@ def test_config_defaults_and_env(monkeypatch):
     e = H.Config.from_env()
     assert e.collective_timeout_s == 7 and e.topology == "hypercube" and e.recovery_policy == 2
     assert e.ring_max_world == 3
+
+
+def test_memory_buffer_refs_and_pool_builder():
+    """BufferRef memory-space markers and the pool builder (nexar/src/memory/buffer.rs,
+    transport/buffer_pool.rs)."""
+    import numpy as np
+    import torch
+    from nexar_b200.core import DataType
+    from nexar_b200.memory import BufferPool, BufferRef, Device, Host, PoolBuilder, PoolProfile, TierConfig
+    a = np.zeros(12, np.float32)
+    r = BufferRef.host(a)
+    assert r.space is Host and r.len_bytes() == 48 and r.count() == 12 and r.as_u64() == a.ctypes.data
+    assert r.dtype == DataType.F32 and not r.is_empty()
+    t = torch.zeros(5, dtype=torch.bfloat16)
+    assert BufferRef(t).len_bytes() == 10 and BufferRef(t).space is Host
+    with pytest.raises(ValueError):
+        BufferRef.device(t)  # a CPU tensor is host memory
+    raw = BufferRef(address=0x1000, nbytes=64, dtype=DataType.F64, space=Device)
+    assert raw.count() == 8 and raw.ptr().space is Device
+    pool = PoolBuilder().small(TierConfig(2, 1024)).large(TierConfig(1, 1 << 20)).build()
+    b = pool.checkout(100)
+    assert b.size == 100 and b.tier == 0
+    assert pool.tier_for_size(2000) == 1
+    assert BufferPool.with_profile(PoolProfile.Inference).free_count(0) >= 0
