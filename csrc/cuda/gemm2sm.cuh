@@ -14,14 +14,21 @@
 //   both CTAs            warp 0 lane 0 loads A and B into the CTA's own shared
 //                        memory with TMA; the bytes are counted on the
 //                        leader's "full" barrier (no multicast: each load reads
-//                        this GPU's memory into one CTA). Warps 2-5 drain their
+//                        this GPU's memory into one CTA). Warps 2-9 drain their
 //                        CTA's half of the accumulator (same epilogue sinks as
-//                        the 1-SM kernel) and arrive on the leader's
-//                        "TMEM empty" barrier.
+//                        the 1-SM kernel): warp w reads TMEM lane quarter w % 4
+//                        and the tile's column half (w - 2) / 4, so two warps
+//                        share each SM sub-partition and hide each other's
+//                        TMEM-load, operand-load and TMA-store latencies (the
+//                        short-K GEMMs of a transformer block are epilogue-bound
+//                        with one). All arrive on the leader's "TMEM empty"
+//                        barrier.
 // The leader's MMA commits arrive on both CTAs' "stage empty" / "TMEM full"
 // barriers (tcgen05.commit multicast). Every mbarrier wait is bounded; a wait
 // that gives up sets *err and the CTA unwinds to the final cluster barrier.
 #pragma once
+#include <type_traits>
+
 #include "gemm.cuh"
 
 namespace nexar {
@@ -29,12 +36,12 @@ namespace gemm2 {
 
 using gemm::BK;
 using gemm::EPI_BUF_BYTES;
-using gemm::EPI_BYTES;
-using gemm::EPI_WARPS;
 using gemm::kWaitLimit;
 constexpr int TM = 256;                    // pair tile rows
 constexpr int HM = 128;                    // per-CTA share of A rows
-constexpr int STAGES = 6, THREADS = 192;
+constexpr int EPI_WARPS = 8;                       // 2 per TMEM lane quarter
+constexpr int STAGES = 6, THREADS = 64 + 32 * EPI_WARPS;
+constexpr int EPI_BYTES = EPI_WARPS * EPI_BUF_BYTES;  // one 32x64 bf16 staging block per warp (32 KB)
 constexpr int A_BYTES = HM * BK * 2;
 // Pair tile width TN (256; 128 compiles and is correct but measured slower);
 // each CTA stages TN / 2 columns of B.
@@ -189,11 +196,11 @@ k_gemm_bf16_2sm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
     }
   } else {
     const int ew = warp - 2;
-    const int q = warp & 3;
-    uint8_t* bufs = epi_smem + ew * 2 * EPI_BUF_BYTES;
+    const int q = warp & 3;                    // TMEM lane quarter (hardware: warp % 4)
+    const int c_lo = (ew >> 2) * (TN / 2);     // this warp's column half of the tile
+    uint8_t* buf = epi_smem + ew * EPI_BUF_BYTES;
     int acc = 0;
     uint32_t acc_phase = 0;
-    int nb = 0;
     for (int t = pair; t < ntiles; t += npairs) {
       int tm, tn;
       sched.coords(t, tm, tn);
@@ -213,26 +220,44 @@ k_gemm_bf16_2sm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
       const int row = row0 + lane;
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * TN);
 #pragma unroll 1
-      for (int c0 = 0; c0 < TN; c0 += 64) {
+      for (int c0 = c_lo; c0 < c_lo + TN / 2; c0 += 64) {
         if (tn * TN + c0 >= N) break;
         uint32_t r0[32], r1[32];
         tmem_ld_32x32b_x32(tbase + c0, r0);
         tmem_ld_32x32b_x32(tbase + c0 + 32, r1);
         tmem_ld_wait();
-        float v[64], pre[64];
+        float v[64];
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
           v[i] = __uint_as_float(r0[i]);
           v[32 + i] = __uint_as_float(r1[i]);
         }
-        epi.math(row, tn * TN + c0, v, M, N, pre);
+        if constexpr (std::is_same<Epi, gemm::EpiStore>::value) {
+          // Two phases: the pre-activation block is staged and stored from v
+          // itself before the activation runs (no second 64-value array).
+          epi.math_pre(row, tn * TN + c0, v, M, N);
+          if (epi.has_pre) {
+            if (lane == 0) tma_store_wait_read<0>();
+            __syncwarp();
+            gemm::stage_row64(buf, lane, v);
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              tma_store_2d(&tmPre, buf, tn * TN + c0, row0);
+              tma_store_commit();
+            }
+          }
+          epi.math_post(row, tn * TN + c0, v, M, N);
+        } else {
+          float pre[64];
+          epi.math(row, tn * TN + c0, v, M, N, pre);
+        }
         if constexpr (gemm::EpiTraits<Epi>::f32_split) {
           const int ks = sched.split_of(t);
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
-            if (lane == 0) tma_store_wait_read<1>();
+            if (lane == 0) tma_store_wait_read<0>();
             __syncwarp();
-            uint8_t* buf = bufs + nb * EPI_BUF_BYTES;
             if (h == 0) gemm::stage_row32f<0>(buf, lane, v);
             else gemm::stage_row32f<1>(buf, lane, v);
             fence_proxy_async_smem();
@@ -241,30 +266,16 @@ k_gemm_bf16_2sm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
               tma_store_3d(&tmOut, buf, tn * TN + c0 + 32 * h, row0, ks);
               tma_store_commit();
             }
-            nb ^= 1;
           }
           continue;
         }
-        if (lane == 0) tma_store_wait_read<1>();
+        if (lane == 0) tma_store_wait_read<0>();
         __syncwarp();
-        uint8_t* buf = bufs + nb * EPI_BUF_BYTES;
         gemm::stage_row64(buf, lane, v);
         fence_proxy_async_smem();
         __syncwarp();
         epi.store_block(&tmOut, buf, row0, tn * TN + c0, lane);
-        if (epi.has_pre) {
-          if (lane == 0) {
-            tma_store_commit();
-            tma_store_wait_read<0>();
-          }
-          __syncwarp();
-          gemm::stage_row64(buf, lane, pre);
-          fence_proxy_async_smem();
-          __syncwarp();
-          if (lane == 0) tma_store_2d(&tmPre, buf, tn * TN + c0, row0);
-        }
         if (lane == 0) tma_store_commit();
-        nb ^= 1;
       }
       tc_fence_before();
       __syncwarp();

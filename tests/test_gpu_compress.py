@@ -141,7 +141,9 @@ def test_topk_blob_exact_order_and_residual(cuda0, n, offset):
     assert ((val - q).abs() <= 0.13 * q.abs()).all()
     want_res = r.clone()
     want_res[want_idx] -= val
-    torch.testing.assert_close(res, want_res, rtol=0, atol=1e-5)  # device fuses r - q * scale
+    # the device fuses r - q * scale (one rounding); torch rounds q * scale
+    # first: they differ by at most an ulp of |r| (magnitudes reach 2^26 here)
+    assert ((res - want_res).abs() <= 2.0 ** -22 * r.abs() + 1e-6).all()
 
 
 def test_topk_ties_taken_in_index_order(cuda0):
