@@ -46,15 +46,11 @@ py::dict msg_to_dict(const Message& m) {
 }
 }  // namespace
 
-// TLS check over a local socket pair: a server with an identity from CA
-// `a` and a client with one from CA `a` (same_ca) or from an unrelated CA;
-// both verify the peer. Returns true if the handshake and an echo succeed.
-static bool tls_pair_check(bool same_ca) {
+// TLS check over a local socket pair between two identities; both sides
+// verify the peer. Returns true if the handshake and an echo succeed.
+static bool tls_identities_check(const TlsIdentity& sid, const TlsIdentity& cid) {
   int sv[2];
   if (socketpair(AF_UNIX, SOCK_STREAM, 0, sv) != 0) fail(Err::ConnectionFailed, "socketpair failed");
-  auto ca_a = ClusterCA::generate("ca-a");
-  auto ca_b = same_ca ? ca_a : ClusterCA::generate("ca-b");
-  TlsIdentity sid = ca_a->issue("server"), cid = ca_b->issue("client");
   bool server_ok = false;
   std::thread srv([&] {
     try {
@@ -77,6 +73,14 @@ static bool tls_pair_check(bool same_ca) {
   }
   srv.join();
   return server_ok && client_ok;
+}
+
+// A server with an identity from CA `a` and a client with one from CA `a`
+// (same_ca) or from an unrelated CA.
+static bool tls_pair_check(bool same_ca) {
+  auto ca_a = ClusterCA::generate("ca-a");
+  auto ca_b = same_ca ? ca_a : ClusterCA::generate("ca-b");
+  return tls_identities_check(ca_a->issue("server"), ca_b->issue("client"));
 }
 
 PYBIND11_MODULE(_host, m) {
@@ -278,6 +282,18 @@ PYBIND11_MODULE(_host, m) {
       .def("__len__", &CollectiveGroup::size);
 
   // ------------------------------------------------------------ seed / worker
+  py::class_<TlsIdentity>(m, "TlsIdentity")
+      .def_readonly("ca_cert_pem", &TlsIdentity::ca_cert_pem)
+      .def_readonly("cert_pem", &TlsIdentity::cert_pem)
+      .def("valid", &TlsIdentity::valid);
+  py::class_<ClusterCA, std::shared_ptr<ClusterCA>>(m, "ClusterCA")
+      .def_static("generate", &ClusterCA::generate, py::arg("name") = "nexar-cluster-ca")
+      .def_static("from_pem", [](const std::string& key, const std::string& cert) { return ClusterCA::from_pem(key, cert); })
+      .def("issue", &ClusterCA::issue)
+      .def("cert_pem", &ClusterCA::cert_pem)
+      .def("key_pem", &ClusterCA::key_pem);
+  m.def("tls_identities_check", &tls_identities_check, py::arg("server"), py::arg("client"),
+        py::call_guard<py::gil_scoped_release>());
   py::class_<SeedNode, std::shared_ptr<SeedNode>>(m, "SeedNode")
       .def_static("bind", [](const std::string& addr, const py::object& token, bool tls) {
         Bytes t = token.is_none() ? token_from_env() : to_bytes(token.cast<py::bytes>());
@@ -288,6 +304,8 @@ PYBIND11_MODULE(_host, m) {
       .def("local_addr", &SeedNode::local_addr)
       .def("token", [](const SeedNode& s) { return from_bytes(s.token()); })
       .def("with_formation_timeout", [](std::shared_ptr<SeedNode> s, double t) { s->set_formation_timeout(t); return s; })
+      .def("use_ca", &SeedNode::use_ca)
+      .def("ca", &SeedNode::ca)
       .def("form_cluster", &SeedNode::form_cluster, GR())
       .def("accept_elastic", &SeedNode::accept_elastic)
       .def("close", &SeedNode::close, GR());

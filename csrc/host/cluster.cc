@@ -197,6 +197,13 @@ namespace {
 constexpr double kTlsHandshakeTimeoutS = 10.0;
 }
 
+void SeedNode::use_ca(std::shared_ptr<ClusterCA> ca) {
+  if (!ca_) fail(Err::Tls, "use_ca: the seed was bound without TLS");
+  if (!ca) fail(Err::Tls, "use_ca: no CA");
+  ca_ = std::move(ca);
+  seed_id_ = ca_->issue("nexar-seed");
+}
+
 std::shared_ptr<Stream> SeedNode::accept_bootstrap(int fd) {
   if (!ca_) return plain_stream(fd);
   // Workers do not verify the seed (they hold no CA yet): the cluster token

@@ -91,6 +91,10 @@ class SeedNode {
   std::string local_addr() const { return addr_; }
   const Bytes& token() const { return token_; }
   void set_formation_timeout(double s) { formation_timeout_s_ = s; }
+  // Replace the cluster CA of a TLS seed with a restored one (before
+  // form_cluster); identities issued afterwards chain to it.
+  void use_ca(std::shared_ptr<ClusterCA> ca);
+  std::shared_ptr<ClusterCA> ca() const { return ca_; }
 
   // Accept `world` workers, assign ranks in join order, send every worker its
   // Welcome. Returns the peer table (rank -> listen addr).

@@ -301,6 +301,27 @@ std::shared_ptr<ClusterCA> ClusterCA::generate(const std::string& name) {
   return ca;
 }
 
+std::shared_ptr<ClusterCA> ClusterCA::from_pem(const std::string& key_pem, const std::string& cert_pem) {
+  BIO* kb = BIO_new_mem_buf(key_pem.data(), (int)key_pem.size());
+  BIO* cb = BIO_new_mem_buf(cert_pem.data(), (int)cert_pem.size());
+  EVP_PKEY* k = kb ? PEM_read_bio_PrivateKey(kb, nullptr, nullptr, nullptr) : nullptr;
+  X509* c = cb ? PEM_read_bio_X509(cb, nullptr, nullptr, nullptr) : nullptr;
+  if (kb) BIO_free(kb);
+  if (cb) BIO_free(cb);
+  if (!k || !c || X509_check_private_key(c, k) != 1) {
+    if (k) EVP_PKEY_free(k);
+    if (c) X509_free(c);
+    fail(Err::Tls, "ClusterCA::from_pem: unreadable key / certificate or the key does not match");
+  }
+  std::shared_ptr<ClusterCA> ca(new ClusterCA());
+  ca->key_ = k;
+  ca->cert_ = c;
+  ca->ca_pem_ = pem_of_cert(c);
+  return ca;
+}
+
+std::string ClusterCA::key_pem() const { return pem_of_key(static_cast<EVP_PKEY*>(key_)); }
+
 ClusterCA::~ClusterCA() {
   X509_free(static_cast<X509*>(cert_));
   EVP_PKEY_free(static_cast<EVP_PKEY*>(key_));

@@ -31,9 +31,16 @@ class ClusterCA {
   // New P-256 key and self-signed CA certificate.
   static std::shared_ptr<ClusterCA> generate(const std::string& name = "nexar-cluster-ca");
   ~ClusterCA();
+  // Restore a CA saved with key_pem() / cert_pem() (certificate rotation
+  // without re-trusting: nexar/src/transport/tls.rs:122-143 persists the CA
+  // key pair the same way). Throws if the key does not match the certificate.
+  static std::shared_ptr<ClusterCA> from_pem(const std::string& key_pem, const std::string& cert_pem);
   // New P-256 key and a leaf certificate signed by this CA (CN = common_name).
   TlsIdentity issue(const std::string& common_name) const;
   const std::string& cert_pem() const { return ca_pem_; }
+  // The CA's private key, PKCS#8 PEM (unencrypted: store it with file
+  // permissions that only the operator can read).
+  std::string key_pem() const;
 
  private:
   ClusterCA() = default;

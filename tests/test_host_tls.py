@@ -4,6 +4,7 @@ import multiprocessing as mp
 import os
 
 import numpy as np
+import pytest
 
 from helpers_host import run_collective
 
@@ -63,3 +64,57 @@ def test_multiprocess_seed_worker_tls():
         seed.close()
     assert [r[0] for r in res] == [0, 1, 2]
     assert all(r[1] == 6.0 and r[2] for r in res)
+
+
+def test_cluster_ca_persist_and_restore():
+    """The CA key pair survives a PEM round trip; identities issued by the
+    restored CA are trusted by holders of the original's (tls.rs:122-143)."""
+    from nexar_b200 import _native
+    H = _native.host()
+    ca = H.ClusterCA.generate("persisted-ca")
+    key, cert = ca.key_pem(), ca.cert_pem()
+    assert "PRIVATE KEY" in key and "BEGIN CERTIFICATE" in cert
+    back = H.ClusterCA.from_pem(key, cert)
+    assert back.cert_pem() == cert
+    old_id, new_id = ca.issue("old-node"), back.issue("new-node")
+    assert H.tls_identities_check(old_id, new_id) and H.tls_identities_check(new_id, old_id)
+    other = H.ClusterCA.generate("other")
+    assert not H.tls_identities_check(old_id, other.issue("x"))
+    with pytest.raises(Exception):
+        H.ClusterCA.from_pem(other.key_pem(), cert)  # key of another CA
+
+
+def test_seed_reuses_persisted_ca():
+    """A TLS seed given a restored CA forms a cluster whose mesh links chain to it."""
+    import threading
+    from nexar_b200 import _native
+    from nexar_b200.client import NexarClient
+    H = _native.host()
+    ca = H.ClusterCA.generate("site-ca")
+    saved = (ca.key_pem(), ca.cert_pem())
+    seed = H.SeedNode.bind("127.0.0.1:0", b"tok", True)
+    seed.use_ca(H.ClusterCA.from_pem(*saved))
+    assert seed.ca().cert_pem() == saved[1]
+    cfg = H.Config()
+    cfg.tls = True
+    out = {}
+
+    def worker(i):
+        out[i] = H.NexarClient.bootstrap_worker(seed.local_addr(), b"tok", cfg, "127.0.0.1")
+
+    ts = [threading.Thread(target=worker, args=(i,)) for i in range(2)]
+    for t in ts:
+        t.start()
+    seed.form_cluster(2)
+    for t in ts:
+        t.join(30)
+    cs = [NexarClient(out[i]) for i in range(2)]
+    assert all(c.native.transport_encrypted() for c in cs)
+    import numpy as np
+    bufs = [np.full(3, float(c.rank + 1), np.float32) for c in cs]
+    from helpers_host import run_collective
+    run_collective(cs, lambda c: c.all_reduce_host(bufs[c.rank]))
+    assert (bufs[0] == 3).all()
+    for c in cs:
+        c.close()
+    seed.close()
