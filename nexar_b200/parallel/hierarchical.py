@@ -169,6 +169,7 @@ class HierarchicalComm:
     one over the node sub-communicator); CPU tensors need none."""
 
     SMALL_BYTES = 256 << 10  # below this, all_reduce takes the lead path (as the reference)
+    PINNED_CACHE = 8         # pinned staging buffers kept (by dtype and size, least recently used out)
 
     def __init__(self, client, topology: Optional[NodeTopology] = None, hostname: Optional[str] = None,
                  attach_device: bool = False, device: Optional[int] = None, small_bytes: Optional[int] = None,
@@ -231,10 +232,12 @@ class HierarchicalComm:
         if not t.is_cuda:
             return t
         key = (t.dtype, t.numel())
-        h = self._pinned.get(key)
+        h = self._pinned.pop(key, None)
         if h is None:
             h = torch.empty(t.numel(), dtype=t.dtype, pin_memory=True)
-            self._pinned[key] = h
+            while len(self._pinned) >= self.PINNED_CACHE:
+                self._pinned.pop(next(iter(self._pinned)))  # least recently used
+        self._pinned[key] = h
         h.copy_(t.reshape(-1), non_blocking=True)
         torch.cuda.current_stream(t.device).synchronize()
         return h
