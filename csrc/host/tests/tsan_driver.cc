@@ -6,6 +6,7 @@
 //   g++ -std=c++17 -O1 -g -fsanitize=thread -I csrc/host csrc/host/<runtime .cc files>
 //       csrc/host/tests/tsan_driver.cc -lssl -lcrypto -pthread -o tsan_driver
 //   ./tsan_driver            (exit 0 and no "WARNING: ThreadSanitizer" report)
+#include <atomic>
 #include <cstdio>
 #include <cstdlib>
 #include <functional>
@@ -77,6 +78,14 @@ void recovery() {
   std::vector<std::unique_ptr<RecoveryOrchestrator>> orch;
   for (int r = 0; r < 4; ++r)
     if (r != 2) orch.push_back(std::make_unique<RecoveryOrchestrator>(cs[r], RecoveryPolicy::Automatic));
+  // A broadcast receiver drained on its own thread while the orchestrator
+  // thread emits into it.
+  auto sub = orch[0]->subscribe();
+  std::atomic<bool> got{false};
+  std::thread listener([&] {
+    RecoveryEvent e;
+    if (sub->recv(15.0, &e)) got = e.dead_ranks.size() == 1 && e.dead_ranks[0] == 2;
+  });
   for (auto& o : orch) o->start();
   cs[2]->close();
   std::vector<std::shared_ptr<NexarClient>> survivors;
@@ -85,6 +94,8 @@ void recovery() {
     check(o->next_event(15.0, &e), "recovery event");
     survivors.push_back(o->client());
   }
+  listener.join();
+  check(got.load(), "subscribed recovery event");
   std::vector<std::vector<float>> bufs(3, std::vector<float>(64, 1.0f));
   run_all(survivors, [&](NexarClient& c) { c.all_reduce(bufs[c.rank()].data(), 64, DataType::F32, ReduceOp::Sum); });
   for (auto& b : bufs) check(b[0] == 3.0f, "all_reduce after recovery");
