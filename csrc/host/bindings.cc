@@ -117,6 +117,7 @@ PYBIND11_MODULE(_host, m) {
       .def_readwrite("barrier_timeout_s", &Config::barrier_timeout_s)
       .def_readwrite("rpc_timeout_s", &Config::rpc_timeout_s)
       .def_readwrite("large_msg_bytes", &Config::large_msg_bytes)
+      .def_readwrite("small_msg_bytes", &Config::small_msg_bytes)
       .def_readwrite("pipeline_segment_bytes", &Config::pipeline_segment_bytes)
       .def_readwrite("ring_max_world", &Config::ring_max_world)
       .def_readwrite("enable_tcp_bulk_sidecar", &Config::enable_tcp_bulk_sidecar)

@@ -281,6 +281,7 @@ struct ChunkLayout {
 };
 void ring_allreduce(NexarClient& c, uint8_t* buf, size_t count, DataType dt, ReduceOp op, uint64_t tag);
 void halving_doubling_allreduce(NexarClient& c, uint8_t* buf, size_t count, DataType dt, ReduceOp op, uint64_t tag);
+void recursive_doubling_allreduce(NexarClient& c, uint8_t* buf, size_t count, DataType dt, ReduceOp op, uint64_t tag);
 void pipelined_ring_allreduce(NexarClient& c, uint8_t* buf, size_t count, DataType dt, ReduceOp op, uint64_t tag);
 void rs_ag_allreduce(NexarClient& c, uint8_t* buf, size_t count, DataType dt, ReduceOp op, uint64_t tag);
 void ring_allgather(NexarClient& c, const uint8_t* send, uint8_t* recv, size_t count, DataType dt, uint64_t tag);

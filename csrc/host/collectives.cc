@@ -46,6 +46,14 @@ static void check_len(const Bytes& b, size_t expect, const char* op, Rank src) {
                                          std::to_string(b.size()));
 }
 
+// Segment tags of the pipelined ring collectives: [63:48] outer & 0xFFFF,
+// [47:32] step, [31:16] segment, [15:0] phase (the pipelined all-reduce's
+// packing, nexar/src/collective/pipelined_allreduce.rs:27-29; reduce-scatter
+// uses phase 2, all-gather phase 3).
+static uint64_t seg_tag(uint64_t tag, uint64_t step, uint64_t seg, uint64_t phase) {
+  return ((tag & 0xffffull) << 48) | ((step & 0xffffull) << 32) | ((seg & 0xffffull) << 16) | (phase & 0xffffull);
+}
+
 // ------------------------------------------------------------------ all-reduce
 void ring_allreduce(NexarClient& c, uint8_t* buf, size_t count, DataType dt, ReduceOp op, uint64_t tag) {
   const uint32_t N = c.world_size();
@@ -143,6 +151,58 @@ void halving_doubling_allreduce(NexarClient& c, uint8_t* buf, size_t count, Data
   }
 }
 
+// Latency-optimal all-reduce for small messages: log2(p) exchanges of the
+// whole buffer with rank ^ 2^k (recursive doubling), against 2(N-1) steps of
+// the ring. Ranks beyond the largest power of two fold their buffer into a
+// partner first and receive the result last. Each pair computes
+// mine op theirs on both sides; IEEE add, mul, min and max are commutative, so
+// every rank ends with the same bits.
+void recursive_doubling_allreduce(NexarClient& c, uint8_t* buf, size_t count, DataType dt, ReduceOp op,
+                                  uint64_t tag) {
+  const uint32_t N = c.world_size();
+  if (N <= 1 || count == 0) return;
+  const Rank r = c.rank();
+  const size_t nb = count * dtype_size(dt);
+  uint32_t p2 = 1;
+  while (p2 * 2 <= N) p2 *= 2;
+  const uint32_t excess = N - p2;
+  if (r < excess) {
+    Bytes in = c.coll_recv(r + p2, step_tag(tag, 0), "allreduce");
+    check_len(in, nb, "allreduce", r + p2);
+    reduce_slice(buf, in.data(), count, dt, op);
+  } else if (r >= p2) {
+    c.coll_send(r - p2, step_tag(tag, 0), buf, nb, "allreduce");
+  }
+  if (r < p2) {
+    const uint32_t log2 = (uint32_t)__builtin_ctz(p2);
+    for (uint32_t round = 0; round < log2; ++round) {
+      const Rank partner = r ^ (1u << round);
+      const uint64_t t = step_tag(tag, 1 + round);
+      c.coll_send(partner, t, buf, nb, "allreduce");
+      Bytes in = c.coll_recv(partner, t, "allreduce");
+      check_len(in, nb, "allreduce", partner);
+      reduce_slice(buf, in.data(), count, dt, op);
+    }
+  }
+  const uint64_t t_out = step_tag(tag, 999);
+  if (r < excess) {
+    c.coll_send(r + p2, t_out, buf, nb, "allreduce");
+  } else if (r >= p2) {
+    Bytes in = c.coll_recv(r - p2, t_out, "allreduce");
+    check_len(in, nb, "allreduce", r - p2);
+    std::memcpy(buf, in.data(), nb);
+  }
+}
+
+// Large all-reduce: the ring's 2(N-1) steps (N-1 reduce-scatter steps, then
+// N-1 all-gather steps over the same ChunkLayout) run as one pipeline of
+// segments. The chunk received at stage t is the chunk sent at stage t+1, so
+// each received segment is reduced (or stored) in place and forwarded at once:
+// the last reduce-scatter stage feeds the first all-gather stage directly.
+// Every chunk is reduced along the ring in the same order as the unpipelined
+// ring and then copied, so all ranks end with the same bits. Segment tags use
+// the reference's packing (nexar/src/collective/pipelined_allreduce.rs:27-29)
+// with the stage in the low field.
 void pipelined_ring_allreduce(NexarClient& c, uint8_t* buf, size_t count, DataType dt, ReduceOp op, uint64_t tag) {
   const uint32_t N = c.world_size();
   if (N <= 1 || count == 0) return;
@@ -151,41 +211,28 @@ void pipelined_ring_allreduce(NexarClient& c, uint8_t* buf, size_t count, DataTy
   const size_t seg = std::max<size_t>(1, c.config().pipeline_segment_bytes / es);
   ChunkLayout L(count, N);
   const Rank next = (r + 1) % N, prev = (r + N - 1) % N;
-  // Packed tags [63:48] outer & 0xFFFF, [47:32] step, [31:16] segment, [15:0]
-  // phase (nexar/src/collective/pipelined_allreduce.rs:27-29).
-  auto pack = [&](uint64_t s, uint64_t k, uint64_t phase) {
-    return ((tag & 0xffffull) << 48) | ((s & 0xffffull) << 32) | ((k & 0xffffull) << 16) | (phase & 0xffffull);
+  const uint32_t stages = 2 * (N - 1);
+  auto recv_chunk = [&](uint32_t t) -> uint32_t {
+    return t < N - 1 ? (r + 2 * N - t - 1) % N : (r + 2 * N - (t - (N - 1))) % N;
   };
-  for (int phase = 0; phase < 2; ++phase) {
-    for (uint32_t s = 0; s + 1 < N; ++s) {
-      const uint32_t send_c = phase == 0 ? (r + N - s) % N : (r + 1 + N - s) % N;
-      const uint32_t recv_c = phase == 0 ? (r + N - s - 1) % N : (r + N - s) % N;
-      const size_t sl = L.chunk(send_c), rl = L.chunk(recv_c);
-      const size_t nseg = std::max((sl + seg - 1) / seg, (rl + seg - 1) / seg);
-      // Send every segment (the peer's router drains the socket), and reduce
-      // segment k on a helper thread while segment k+1 is being received.
-      for (size_t k = 0; k < nseg; ++k) {
-        const size_t off = k * seg;
-        if (off < sl)
-          c.coll_send(next, pack(s, k, phase), buf + (L.offset(send_c) + off) * es, std::min(seg, sl - off) * es,
-                      "allreduce");
-      }
-      std::future<void> pending;
-      for (size_t k = 0; k < nseg; ++k) {
-        const size_t off = k * seg;
-        if (off >= rl) break;
-        Bytes in = c.coll_recv(prev, pack(s, k, phase), "allreduce");
-        const size_t m = std::min(seg, rl - off);
-        check_len(in, m * es, "allreduce", prev);
-        if (pending.valid()) pending.get();
-        uint8_t* dst = buf + (L.offset(recv_c) + off) * es;
-        if (phase == 0) {
-          pending = std::async(std::launch::async, [dst, d = std::move(in), m, dt, op]() { reduce_slice(dst, d.data(), m, dt, op); });
-        } else {
-          std::memcpy(dst, in.data(), in.size());
-        }
-      }
-      if (pending.valid()) pending.get();
+  auto send_segments = [&](uint32_t t, uint32_t chunk) {
+    const size_t len = L.chunk(chunk);
+    for (size_t k = 0, off = 0; off < len; ++k, off += seg)
+      c.coll_send(next, seg_tag(tag, 0, k, t), buf + (L.offset(chunk) + off) * es, std::min(seg, len - off) * es,
+                  "allreduce");
+  };
+  send_segments(0, r);
+  for (uint32_t t = 0; t < stages; ++t) {
+    const uint32_t rc = recv_chunk(t);
+    const size_t len = L.chunk(rc);
+    for (size_t k = 0, off = 0; off < len; ++k, off += seg) {
+      const size_t m = std::min(seg, len - off);
+      Bytes in = c.coll_recv(prev, seg_tag(tag, 0, k, t), "allreduce");
+      check_len(in, m * es, "allreduce", prev);
+      uint8_t* dst = buf + (L.offset(rc) + off) * es;
+      if (t < N - 1) reduce_slice(dst, in.data(), m, dt, op);
+      else std::memcpy(dst, in.data(), m * es);
+      if (t + 1 < stages) c.coll_send(next, seg_tag(tag, 0, k, t + 1), dst, m * es, "allreduce");
     }
   }
 }
@@ -221,10 +268,31 @@ void rs_ag_allreduce(NexarClient& c, uint8_t* buf, size_t count, DataType dt, Re
 void ring_allgather(NexarClient& c, const uint8_t* send, uint8_t* recv, size_t count, DataType dt, uint64_t tag) {
   const uint32_t N = c.world_size();
   const Rank r = c.rank();
-  const size_t nb = count * dtype_size(dt);
+  const size_t es = dtype_size(dt), nb = count * es;
   if (send != recv + r * nb) std::memmove(recv + r * nb, send, nb);
   if (N <= 1) return;
   const Rank next = (r + 1) % N, prev = (r + N - 1) % N;
+  const size_t seg = std::max<size_t>(1, c.config().pipeline_segment_bytes / es);
+  if (count >= 2 * seg) {
+    // Pipelined: each received segment is stored and forwarded at once.
+    const size_t nseg = (count + seg - 1) / seg;
+    for (size_t k = 0; k < nseg; ++k) {
+      const size_t off = k * seg, m = std::min(seg, count - off);
+      c.coll_send(next, seg_tag(tag, 0, k, 3), recv + r * nb + off * es, m * es, "allgather");
+    }
+    for (uint32_t s = 0; s + 1 < N; ++s) {
+      const uint32_t recv_i = (r + N - s - 1) % N;
+      for (size_t k = 0; k < nseg; ++k) {
+        const size_t off = k * seg, m = std::min(seg, count - off);
+        Bytes in = c.coll_recv(prev, seg_tag(tag, s, k, 3), "allgather");
+        check_len(in, m * es, "allgather", prev);
+        uint8_t* dst = recv + recv_i * nb + off * es;
+        std::memcpy(dst, in.data(), m * es);
+        if (s + 2 < N) c.coll_send(next, seg_tag(tag, s + 1, k, 3), dst, m * es, "allgather");
+      }
+    }
+    return;
+  }
   for (uint32_t s = 0; s + 1 < N; ++s) {
     const uint32_t send_i = (r + N - s) % N, recv_i = (r + N - s - 1) % N;
     c.coll_send(next, step_tag(tag, s), recv + send_i * nb, nb, "allgather");
@@ -243,17 +311,53 @@ void ring_reduce_scatter(NexarClient& c, const uint8_t* send, uint8_t* recv, siz
     std::memmove(recv, send, nb);
     return;
   }
-  Bytes work(send, send + nb * N);
   const Rank next = (r + 1) % N, prev = (r + N - 1) % N;
-  // Start one chunk "behind" so the final accumulated chunk is chunk r.
+  const size_t seg = std::max<size_t>(1, c.config().pipeline_segment_bytes / es);
+  if (count >= 2 * seg) {
+    // Pipelined: every segment of a partial sum is forwarded as soon as it is
+    // reduced, so receiving, reducing and sending overlap across ring steps.
+    const size_t nseg = (count + seg - 1) / seg;
+    const uint32_t first = (r + N - 1) % N;
+    for (size_t k = 0; k < nseg; ++k) {
+      const size_t off = k * seg, m = std::min(seg, count - off);
+      c.coll_send(next, seg_tag(tag, 0, k, 2), send + (first * count + off) * es, m * es, "reduce_scatter");
+    }
+    if (recv != send + r * nb) std::memmove(recv, send + r * nb, nb);
+    for (uint32_t s = 0; s + 1 < N; ++s) {
+      const uint32_t recv_i = (r + N - s - 2) % N;
+      for (size_t k = 0; k < nseg; ++k) {
+        const size_t off = k * seg, m = std::min(seg, count - off);
+        Bytes in = c.coll_recv(prev, seg_tag(tag, s, k, 2), "reduce_scatter");
+        check_len(in, m * es, "reduce_scatter", prev);
+        if (s + 2 == N) {
+          reduce_slice(recv + off * es, in.data(), m, dt, op);
+        } else {
+          reduce_slice(in.data(), send + (recv_i * count + off) * es, m, dt, op);
+          c.coll_send(next, seg_tag(tag, s + 1, k, 2), in.data(), m * es, "reduce_scatter");
+        }
+      }
+    }
+    return;
+  }
+  // Start one chunk "behind" so the final accumulated chunk is chunk r. The
+  // partial sum travels: step 0 sends this rank's own chunk straight from
+  // `send`; every later step forwards the chunk received (and reduced) in the
+  // step before, so no copy of the whole send buffer is made.
+  Bytes acc;
   for (uint32_t s = 0; s + 1 < N; ++s) {
     const uint32_t send_i = (r + N - s - 1) % N, recv_i = (r + N - s - 2) % N;
-    c.coll_send(next, step_tag(tag, s), work.data() + send_i * nb, nb, "reduce_scatter");
+    const uint8_t* out = s == 0 ? send + send_i * nb : acc.data();
+    c.coll_send(next, step_tag(tag, s), out, nb, "reduce_scatter");
     Bytes in = c.coll_recv(prev, step_tag(tag, s), "reduce_scatter");
     check_len(in, nb, "reduce_scatter", prev);
-    reduce_slice(work.data() + recv_i * nb, in.data(), count, dt, op);
+    if (s + 2 == N) {  // recv_i == r: the last partial lands in the output
+      if (recv != send + r * nb) std::memmove(recv, send + r * nb, nb);
+      reduce_slice(recv, in.data(), count, dt, op);
+    } else {
+      reduce_slice(in.data(), send + recv_i * nb, count, dt, op);
+      acc = std::move(in);
+    }
   }
-  std::memcpy(recv, work.data() + r * nb, nb);
 }
 
 // ------------------------------------------------------------------ broadcast / reduce
@@ -522,6 +626,7 @@ void NexarClient::all_reduce_tagged(void* ptr, size_t count, DataType dt, Reduce
   with_staging(*this, ptr, nb, [&](uint8_t* b) {
     // dispatch (nexar/src/collective/allreduce.rs:21-55)
     if (nb >= config().large_msg_bytes) coll::pipelined_ring_allreduce(*this, b, count, dt, op, tag);
+    else if (nb <= config().small_msg_bytes) coll::recursive_doubling_allreduce(*this, b, count, dt, op, tag);
     else if (world_ <= config().ring_max_world || count < world_) coll::ring_allreduce(*this, b, count, dt, op, tag);
     else coll::halving_doubling_allreduce(*this, b, count, dt, op, tag);
   });
@@ -554,6 +659,7 @@ void NexarClient::all_reduce_bucketed_tagged(const std::vector<std::pair<void*, 
     off += e.second * es;
   }
   if (total * es >= config().large_msg_bytes) coll::pipelined_ring_allreduce(*this, flat.data(), total, dt, op, tag);
+  else if (total * es <= config().small_msg_bytes) coll::recursive_doubling_allreduce(*this, flat.data(), total, dt, op, tag);
   else coll::ring_allreduce(*this, flat.data(), total, dt, op, tag);
   off = 0;
   for (auto& e : entries) {

@@ -94,6 +94,7 @@ Config Config::from_env() {
   c.barrier_timeout_s = env_f("NEXAR_BARRIER_TIMEOUT_SECS", c.barrier_timeout_s);
   c.rpc_timeout_s = env_f("NEXAR_RPC_TIMEOUT_SECS", c.rpc_timeout_s);
   c.large_msg_bytes = env_u("NEXAR_LARGE_MSG_BYTES", c.large_msg_bytes);
+  c.small_msg_bytes = env_u("NEXAR_SMALL_MSG_BYTES", c.small_msg_bytes);
   c.pipeline_segment_bytes = env_u("NEXAR_PIPELINE_SEGMENT_BYTES", c.pipeline_segment_bytes);
   c.ring_max_world = (uint32_t)env_u("NEXAR_RING_MAX_WORLD", c.ring_max_world);
   c.enable_tcp_bulk_sidecar = env_b("NEXAR_ENABLE_TCP_BULK_SIDECAR", c.enable_tcp_bulk_sidecar);

@@ -18,7 +18,25 @@
 namespace nexar {
 
 using Rank = uint32_t;
-using Bytes = std::vector<uint8_t>;
+
+// Allocator that leaves bytes uninitialised on value-less construction:
+// `Bytes b(n)` / `b.resize(n)` do not zero-fill (receive buffers are written
+// in full by the socket read; zeroing a 16 MB payload costs as much as a
+// tenth of its transfer). `Bytes b(n, 0)` / `assign(n, 0)` still zero.
+template <class T>
+struct NoInitAllocator : std::allocator<T> {
+  template <class U> struct rebind { using other = NoInitAllocator<U>; };
+  NoInitAllocator() noexcept = default;
+  template <class U> NoInitAllocator(const NoInitAllocator<U>&) noexcept {}
+  template <class U> void construct(U* p) noexcept { ::new (static_cast<void*>(p)) U; }
+  template <class U, class... A> void construct(U* p, A&&... a) { ::new (static_cast<void*>(p)) U(std::forward<A>(a)...); }
+};
+template <class T, class U>
+bool operator==(const NoInitAllocator<T>&, const NoInitAllocator<U>&) noexcept { return true; }
+template <class T, class U>
+bool operator!=(const NoInitAllocator<T>&, const NoInitAllocator<U>&) noexcept { return false; }
+
+using Bytes = std::vector<uint8_t, NoInitAllocator<uint8_t>>;
 using Clock = std::chrono::steady_clock;
 
 constexpr uint16_t kProtocolVersion = 1;
@@ -82,6 +100,9 @@ struct Config {
   double barrier_timeout_s = 30.0;
   double rpc_timeout_s = 30.0;
   uint64_t large_msg_bytes = 8ull << 20;
+  // All-reduces up to this size use recursive doubling (log2 N exchanges of
+  // the whole buffer) instead of the ring's 2(N-1) steps (new; 0 disables).
+  uint64_t small_msg_bytes = 256ull << 10;
   uint64_t pipeline_segment_bytes = 2ull << 20;
   uint32_t ring_max_world = 8;
   bool enable_tcp_bulk_sidecar = true;

@@ -110,6 +110,10 @@ class PlainStream : public Stream {
   ~PlainStream() override { close_fd(fd_); }
   void write_all(const void* p, size_t n) override { nexar::write_all(fd_, p, n); }
   bool read_exact(void* p, size_t n) override { return nexar::read_exact(fd_, p, n); }
+  size_t read_some(void* p, size_t n) override { return nexar::read_some(fd_, p, n); }
+  void write_pair(const void* a, size_t na, const void* b, size_t nb) override {
+    nexar::write_pair(fd_, a, na, b, nb);
+  }
   void shutdown() override { ::shutdown(fd_, SHUT_RDWR); }
   int fd() const override { return fd_; }
 
@@ -215,6 +219,40 @@ class TlsStream : public Stream {
       }
     }
     return true;
+  }
+
+  size_t read_some(void* p, size_t n) override {
+    while (true) {
+      if (closed_) return 0;
+      int r, e;
+      {
+        std::lock_guard<std::mutex> g(mu_);
+        r = SSL_read(ssl_, p, (int)std::min<size_t>(n, 1u << 30));
+        e = r > 0 ? SSL_ERROR_NONE : SSL_get_error(ssl_, r);
+      }
+      if (r > 0) return (size_t)r;
+      if (e == SSL_ERROR_WANT_READ) {
+        wait_fd(fd_, POLLIN, 50);
+      } else if (e == SSL_ERROR_WANT_WRITE) {
+        wait_fd(fd_, POLLOUT, 50);
+      } else {
+        ERR_clear_error();
+        return 0;
+      }
+    }
+  }
+
+  // A small frame goes out as one TLS record.
+  void write_pair(const void* a, size_t na, const void* b, size_t nb) override {
+    if (na + nb <= 16384) {
+      uint8_t tmp[16384];
+      std::memcpy(tmp, a, na);
+      if (nb) std::memcpy(tmp + na, b, nb);
+      write_all(tmp, na + nb);
+      return;
+    }
+    write_all(a, na);
+    if (nb) write_all(b, nb);
   }
 
   void shutdown() override {

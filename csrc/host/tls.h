@@ -55,6 +55,13 @@ class Stream {
   virtual ~Stream() = default;
   virtual void write_all(const void* p, size_t n) = 0;  // throws NexarError(PeerDisconnected)
   virtual bool read_exact(void* p, size_t n) = 0;       // false on EOF / error
+  // Up to n bytes (at least one); 0 on EOF / error.
+  virtual size_t read_some(void* p, size_t n) = 0;
+  // Two buffers back to back (a frame header and its payload).
+  virtual void write_pair(const void* a, size_t na, const void* b, size_t nb) {
+    write_all(a, na);
+    if (nb) write_all(b, nb);
+  }
   virtual void shutdown() = 0;                          // wakes a blocked reader
   virtual int fd() const = 0;
   virtual bool encrypted() const { return false; }

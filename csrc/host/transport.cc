@@ -1,5 +1,7 @@
 #include "transport.h"
 
+#include <sys/uio.h>
+
 #include <arpa/inet.h>
 #include <cerrno>
 #include <fcntl.h>
@@ -102,6 +104,39 @@ void write_all(int fd, const void* p, size_t n) {
     }
     c += w;
     n -= (size_t)w;
+  }
+}
+
+void write_pair(int fd, const void* a, size_t na, const void* b, size_t nb) {
+  iovec v[2] = {{const_cast<void*>(a), na}, {const_cast<void*>(b), nb}};
+  int first = 0;
+  while (first < 2) {
+    msghdr m{};
+    m.msg_iov = v + first;
+    m.msg_iovlen = 2 - first;
+    ssize_t w = ::sendmsg(fd, &m, MSG_NOSIGNAL);
+    if (w < 0) {
+      if (errno == EINTR) continue;
+      fail(Err::PeerDisconnected, std::string("send failed: ") + strerror(errno));
+    }
+    size_t left = (size_t)w;
+    while (first < 2 && left >= v[first].iov_len) {
+      left -= v[first].iov_len;
+      ++first;
+    }
+    if (first < 2) {
+      v[first].iov_base = static_cast<char*>(v[first].iov_base) + left;
+      v[first].iov_len -= left;
+    }
+  }
+}
+
+size_t read_some(int fd, void* p, size_t n) {
+  while (true) {
+    ssize_t r = ::recv(fd, p, n, 0);
+    if (r > 0) return (size_t)r;
+    if (r < 0 && errno == EINTR) continue;
+    return 0;
   }
 }
 
@@ -268,8 +303,7 @@ void PeerConnection::send_frame(uint8_t kind, const uint64_t* prefix, int nprefi
   }
   std::lock_guard<std::mutex> g(write_mu_);
   try {
-    io_->write_all(hdr, h);
-    if (n) io_->write_all(p, n);
+    io_->write_pair(hdr, h, p, n);
   } catch (const NexarError&) {
     alive_ = false;
     throw NexarError(Err::PeerDisconnected, "peer " + std::to_string(peer_) + " disconnected unexpectedly");
@@ -357,12 +391,55 @@ void PeerRouter::dispatch(Message&& m) {
   }
 }
 
+namespace {
+// Buffered reads for the router: frame headers and small payloads come out
+// of one 64 KB buffer filled by single reads (one system call per burst of
+// small frames instead of three per frame); payloads of half the buffer or
+// more are read straight into their destination.
+class FrameReader {
+ public:
+  explicit FrameReader(PeerConnection& c) : c_(c), buf_(kCap) {}
+  bool read_exact(void* p, size_t n) {
+    uint8_t* d = static_cast<uint8_t*>(p);
+    const size_t have = end_ - pos_;
+    if (have >= n) {
+      std::memcpy(d, buf_.data() + pos_, n);
+      pos_ += n;
+      return true;
+    }
+    std::memcpy(d, buf_.data() + pos_, have);
+    pos_ = end_ = 0;
+    d += have;
+    n -= have;
+    if (n >= kCap / 2) return c_.read_exact(d, n);
+    while (n > 0) {
+      const size_t r = c_.read_some(buf_.data(), kCap);
+      if (r == 0) return false;
+      const size_t take = std::min(r, n);
+      std::memcpy(d, buf_.data(), take);
+      d += take;
+      n -= take;
+      pos_ = take;
+      end_ = r;
+    }
+    return true;
+  }
+
+ private:
+  static constexpr size_t kCap = 64 << 10;
+  PeerConnection& c_;
+  Bytes buf_;
+  size_t pos_ = 0, end_ = 0;
+};
+}  // namespace
+
 void PeerRouter::run() {
   const Rank peer = conn_->peer();
+  FrameReader in(*conn_);
   try {
     while (true) {
       uint8_t kind;
-      if (!conn_->read_exact(&kind, 1)) break;
+      if (!in.read_exact(&kind, 1)) break;
       uint64_t pre[3] = {0, 0, 0};
       int np = 0;
       switch (kind) {
@@ -374,7 +451,7 @@ void PeerRouter::run() {
           goto done;
       }
       uint8_t buf[24];
-      if (!conn_->read_exact(buf, 8 * np)) break;
+      if (!in.read_exact(buf, 8 * np)) break;
       for (int i = 0; i < np; ++i) pre[i] = get_le(buf + 8 * i, 8);
       const uint64_t len = pre[np - 1];
       if (len > kMaxMessageBytes) {
@@ -382,7 +459,7 @@ void PeerRouter::run() {
         break;
       }
       Bytes payload(len);
-      if (len && !conn_->read_exact(payload.data(), len)) break;
+      if (len && !in.read_exact(payload.data(), len)) break;
       last_seen_ns_ = now_ns();
       switch (kind) {
         case kFrameMessage: {

@@ -51,7 +51,10 @@ int tcp_listen(const std::string& host, int port, int* bound_port);
 int tcp_accept(int listen_fd, double timeout_s);  // -1 on timeout
 int tcp_connect(const std::string& host, int port, double timeout_s);
 void write_all(int fd, const void* p, size_t n);
+// a then b with one sendmsg per attempt (header + payload of a frame).
+void write_pair(int fd, const void* a, size_t na, const void* b, size_t nb);
 bool read_exact(int fd, void* p, size_t n);  // false on EOF
+size_t read_some(int fd, void* p, size_t n);  // >= 1 byte, 0 on EOF / error
 void close_fd(int fd);
 
 // Read/write one framed message (kind 0x01) on a bootstrap socket.
@@ -118,6 +121,7 @@ class PeerConnection {
   bool encrypted() const { return io_->encrypted(); }
   // Reader side (the router thread): false on EOF or error.
   bool read_exact(void* p, size_t n) { return io_->read_exact(p, n); }
+  size_t read_some(void* p, size_t n) { return io_->read_some(p, n); }
 
   void send_message(const Message& m, Priority prio);
   void send_raw(const void* p, size_t n);

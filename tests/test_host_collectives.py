@@ -87,7 +87,7 @@ def test_allreduce_f64_and_bf16(c2):
 def test_pipelined_and_halving_doubling_paths():
     # ring_max_world=0 forces halving-doubling at 5 ranks; a tiny
     # large_msg_bytes forces the pipelined ring (tests/sparse.rs:292-316).
-    cs = bootstrap(5, ring_max_world=0)
+    cs = bootstrap(5, ring_max_world=0, small_msg_bytes=0)
     xs = [data(r, 1000) for r in range(5)]
     bufs = [x.copy() for x in xs]
     run_collective(cs, lambda c: c.all_reduce_host(bufs[c.rank]))
@@ -102,7 +102,7 @@ def test_pipelined_and_halving_doubling_paths():
 
 
 def test_halving_doubling_pow2():
-    cs = bootstrap(8, ring_max_world=0)
+    cs = bootstrap(8, ring_max_world=0, small_msg_bytes=0)
     xs = [data(r, 333) for r in range(8)]
     bufs = [x.copy() for x in xs]
     run_collective(cs, lambda c: c.all_reduce_host(bufs[c.rank]))
@@ -368,3 +368,57 @@ def test_all_gather_bytes(c3):
     res = run_collective(c3, lambda c: c.all_gather_bytes(b"x" * (c.rank + 1)))
     for r in res:
         assert r == [b"x", b"xx", b"xxx"]
+
+
+ALGOS = {
+    "recursive_doubling": dict(small_msg_bytes=1 << 30),
+    "ring": dict(small_msg_bytes=0),
+    "halving_doubling": dict(small_msg_bytes=0, ring_max_world=0),
+    "pipelined": dict(small_msg_bytes=0, large_msg_bytes=1024, pipeline_segment_bytes=256),
+}
+
+
+@pytest.mark.parametrize("world", [3, 4, 5])
+@pytest.mark.parametrize("algo", sorted(ALGOS))
+def test_allreduce_every_algorithm(world, algo):
+    """Each all-reduce algorithm forced through the config: close to the oracle,
+    bitwise identical on every rank, for an uneven count."""
+    cs = bootstrap(world, **ALGOS[algo])
+    try:
+        xs = [data(r, 1003, seed=7) for r in range(world)]
+        bufs = [x.copy() for x in xs]
+        run_collective(cs, lambda c: c.all_reduce_host(bufs[c.rank]))
+        for b in bufs:
+            np.testing.assert_allclose(b, oracle(xs, "sum"), rtol=1e-5, atol=1e-5)
+            assert np.array_equal(b, bufs[0])
+        for op in ("max", "min", "prod"):
+            ys = [data(r, 37, dtype=np.int32, seed=3) % 5 + 1 for r in range(world)]
+            bs = [y.copy() for y in ys]
+            run_collective(cs, lambda c: c.all_reduce_host(bs[c.rank], op))
+            for b in bs:
+                assert np.array_equal(b, oracle(ys, op).astype(np.int32)), (algo, op)
+    finally:
+        for c in cs:
+            c.close()
+
+
+@pytest.mark.parametrize("world", [3, 4])
+def test_pipelined_reduce_scatter_and_all_gather(world):
+    """Chunks of several segments take the pipelined rings (segments are
+    forwarded as soon as they are reduced / stored)."""
+    cs = bootstrap(world, pipeline_segment_bytes=256)
+    try:
+        count = 1000  # 16 segments of 64 f32 per chunk
+        xs = [data(r, count * world, seed=11) for r in range(world)]
+        outs = [np.zeros(count, np.float32) for _ in range(world)]
+        run_collective(cs, lambda c: c.reduce_scatter_host(xs[c.rank], outs[c.rank]))
+        full = oracle(xs, "sum")
+        for r in range(world):
+            np.testing.assert_allclose(outs[r], full[r * count:(r + 1) * count], rtol=1e-5, atol=1e-5)
+        gs = [np.zeros(count * world, np.float32) for _ in range(world)]
+        run_collective(cs, lambda c: c.all_gather_host(outs[c.rank], gs[c.rank]))
+        for g in gs:
+            assert np.array_equal(g, np.concatenate(outs))
+    finally:
+        for c in cs:
+            c.close()
