@@ -271,6 +271,19 @@ void ring_allgather(NexarClient& c, const uint8_t* send, uint8_t* recv, size_t c
   const size_t es = dtype_size(dt), nb = count * es;
   if (send != recv + r * nb) std::memmove(recv + r * nb, send, nb);
   if (N <= 1) return;
+  if (nb * N <= c.config().small_msg_bytes && !c.is_sparse()) {
+    // Small: direct exchange over the full mesh, the same bytes as the ring
+    // in one hop instead of N-1.
+    for (uint32_t s = 1; s < N; ++s)
+      c.coll_send((r + s) % N, step_tag(tag, 0), recv + r * nb, nb, "allgather");
+    for (uint32_t s = 1; s < N; ++s) {
+      const Rank src = (r + N - s) % N;
+      Bytes in = c.coll_recv(src, step_tag(tag, 0), "allgather");
+      check_len(in, nb, "allgather", src);
+      std::memcpy(recv + src * nb, in.data(), nb);
+    }
+    return;
+  }
   const Rank next = (r + 1) % N, prev = (r + N - 1) % N;
   const size_t seg = std::max<size_t>(1, c.config().pipeline_segment_bytes / es);
   if (count >= 2 * seg) {
@@ -309,6 +322,28 @@ void ring_reduce_scatter(NexarClient& c, const uint8_t* send, uint8_t* recv, siz
   const size_t es = dtype_size(dt), nb = count * es;
   if (N <= 1) {
     std::memmove(recv, send, nb);
+    return;
+  }
+  if (nb * N <= c.config().small_msg_bytes && !c.is_sparse()) {
+    // Small: every rank sends block j to rank j directly (the ring's bytes in
+    // one hop) and reduces the blocks it receives in rank order.
+    for (uint32_t s = 1; s < N; ++s) {
+      const Rank dst = (r + s) % N;
+      c.coll_send(dst, step_tag(tag, 0), send + dst * nb, nb, "reduce_scatter");
+    }
+    std::vector<Bytes> got(N);
+    for (uint32_t s = 1; s < N; ++s) {
+      const Rank src = (r + N - s) % N;
+      got[src] = c.coll_recv(src, step_tag(tag, 0), "reduce_scatter");
+      check_len(got[src], nb, "reduce_scatter", src);
+    }
+    Bytes acc(nb);
+    for (Rank p = 0; p < N; ++p) {
+      const uint8_t* blk = p == r ? send + r * nb : got[p].data();
+      if (p == 0) std::memcpy(acc.data(), blk, nb);
+      else reduce_slice(acc.data(), blk, count, dt, op);
+    }
+    std::memcpy(recv, acc.data(), nb);
     return;
   }
   const Rank next = (r + 1) % N, prev = (r + N - 1) % N;
@@ -431,10 +466,16 @@ void alltoall(NexarClient& c, const uint8_t* send, uint8_t* recv, size_t count, 
   const Rank r = c.rank();
   const size_t nb = count * dtype_size(dt);
   std::memmove(recv + r * nb, send + r * nb, nb);
-  // pairwise exchange: step s sends to r+s and receives from r-s
+  // Pairwise order (step s: to r+s, from r-s). Every block is posted before
+  // the first receive: peers' router threads drain their sockets, so the
+  // sends cannot block on a peer that is itself sending, and the exchange
+  // costs one network hop instead of N-1.
   for (uint32_t s = 1; s < N; ++s) {
-    const Rank dst = (r + s) % N, src = (r + N - s) % N;
+    const Rank dst = (r + s) % N;
     c.coll_send(dst, step_tag(tag, s), send + dst * nb, nb, "alltoall");
+  }
+  for (uint32_t s = 1; s < N; ++s) {
+    const Rank src = (r + N - s) % N;
     Bytes in = c.coll_recv(src, step_tag(tag, s), "alltoall");
     check_len(in, nb, "alltoall", src);
     std::memcpy(recv + src * nb, in.data(), nb);

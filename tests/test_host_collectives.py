@@ -402,11 +402,19 @@ def test_allreduce_every_algorithm(world, algo):
             c.close()
 
 
+RS_AG_PATHS = {
+    "pipelined": dict(pipeline_segment_bytes=256),   # chunks of 16 segments
+    "ring": dict(small_msg_bytes=0),                 # one message per ring step
+    "direct": dict(),                                # small: one hop over the full mesh
+}
+
+
 @pytest.mark.parametrize("world", [3, 4])
-def test_pipelined_reduce_scatter_and_all_gather(world):
-    """Chunks of several segments take the pipelined rings (segments are
-    forwarded as soon as they are reduced / stored)."""
-    cs = bootstrap(world, pipeline_segment_bytes=256)
+@pytest.mark.parametrize("path", sorted(RS_AG_PATHS))
+def test_reduce_scatter_and_all_gather_paths(world, path):
+    """Pipelined rings (segments forwarded as soon as they are reduced /
+    stored), plain rings and the direct small-message exchange."""
+    cs = bootstrap(world, **RS_AG_PATHS[path])
     try:
         count = 1000  # 16 segments of 64 f32 per chunk
         xs = [data(r, count * world, seed=11) for r in range(world)]
