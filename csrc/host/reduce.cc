@@ -4,6 +4,10 @@
 #include <cmath>
 #include <limits>
 
+#if defined(__x86_64__) && defined(__GNUC__)
+#include <immintrin.h>
+#endif
+
 namespace nexar {
 
 // ------------------------------------------------------------ conversions
@@ -139,22 +143,147 @@ inline float apply_f(float a, float b, ReduceOp op) {
   return a;
 }
 
-NEXAR_CLONES void reduce_bf16(uint16_t* __restrict d, const uint16_t* __restrict s, size_t n, ReduceOp op) {
-  constexpr size_t kBlk = 256;
-  float a[kBlk], b[kBlk];
-  for (size_t base = 0; base < n; base += kBlk) {
-    const size_t m = std::min(kBlk, n - base);
-    for (size_t i = 0; i < m; ++i) {
-      a[i] = bf16_to_f32(d[base + i]);
-      b[i] = bf16_to_f32(s[base + i]);
+// bf16 <-> f32: widen = shift left by 16; narrow = round to nearest even on
+// the top 16 bits, NaN kept quiet (f32_to_bf16). The scalar loop is the
+// fallback; the x86 paths below do the same integer steps 16 or 8 lanes wide.
+void reduce_bf16_scalar(uint16_t* d, const uint16_t* s, size_t n, ReduceOp op) {
+  for (size_t i = 0; i < n; ++i) d[i] = f32_to_bf16(apply_f(bf16_to_f32(d[i]), bf16_to_f32(s[i]), op));
+}
+
+#if defined(__x86_64__) && defined(__GNUC__)
+__attribute__((target("avx512f"))) inline __m512 bf16x16_to_f32(const uint16_t* p) {
+  const __m512i w = _mm512_cvtepu16_epi32(_mm256_loadu_si256(reinterpret_cast<const __m256i*>(p)));
+  return _mm512_castsi512_ps(_mm512_slli_epi32(w, 16));
+}
+__attribute__((target("avx512f"))) void reduce_bf16_avx512(uint16_t* d, const uint16_t* s, size_t n, ReduceOp op) {
+  const __m512i bias = _mm512_set1_epi32(0x7fff), one = _mm512_set1_epi32(1);
+  const __m512i absmask = _mm512_set1_epi32(0x7fffffff), inf = _mm512_set1_epi32(0x7f800000);
+  const __m512i quiet = _mm512_set1_epi32(0x40);
+  size_t i = 0;
+  for (; i + 16 <= n; i += 16) {
+    const __m512 a = bf16x16_to_f32(d + i), b = bf16x16_to_f32(s + i);
+    __m512 r;
+    switch (op) {
+      case ReduceOp::Sum: r = _mm512_add_ps(a, b); break;
+      case ReduceOp::Prod: r = _mm512_mul_ps(a, b); break;
+      case ReduceOp::Min: r = _mm512_min_ps(b, a); break;
+      default: r = _mm512_max_ps(b, a); break;
     }
-    reduce_float_body(a, b, m, op);
-    for (size_t i = 0; i < m; ++i) d[base + i] = f32_to_bf16(a[i]);
+    const __m512i x = _mm512_castps_si512(r);
+    const __m512i lsb = _mm512_and_si512(_mm512_srli_epi32(x, 16), one);
+    const __m512i rne = _mm512_srli_epi32(_mm512_add_epi32(x, _mm512_add_epi32(bias, lsb)), 16);
+    const __m512i qnan = _mm512_or_si512(_mm512_srli_epi32(x, 16), quiet);
+    const __mmask16 isnan = _mm512_cmpgt_epi32_mask(_mm512_and_si512(x, absmask), inf);
+    const __m512i h = _mm512_mask_blend_epi32(isnan, rne, qnan);
+    _mm256_storeu_si256(reinterpret_cast<__m256i*>(d + i), _mm512_cvtepi32_epi16(h));
   }
+  reduce_bf16_scalar(d + i, s + i, n - i, op);
+}
+__attribute__((target("avx2"))) inline __m256 bf16x8_to_f32(const uint16_t* p) {
+  const __m256i w = _mm256_cvtepu16_epi32(_mm_loadu_si128(reinterpret_cast<const __m128i*>(p)));
+  return _mm256_castsi256_ps(_mm256_slli_epi32(w, 16));
+}
+__attribute__((target("avx2"))) void reduce_bf16_avx2(uint16_t* d, const uint16_t* s, size_t n, ReduceOp op) {
+  const __m256i bias = _mm256_set1_epi32(0x7fff), one = _mm256_set1_epi32(1);
+  const __m256i absmask = _mm256_set1_epi32(0x7fffffff), inf = _mm256_set1_epi32(0x7f800000);
+  const __m256i quiet = _mm256_set1_epi32(0x40);
+  size_t i = 0;
+  for (; i + 8 <= n; i += 8) {
+    const __m256 a = bf16x8_to_f32(d + i), b = bf16x8_to_f32(s + i);
+    __m256 r;
+    switch (op) {
+      case ReduceOp::Sum: r = _mm256_add_ps(a, b); break;
+      case ReduceOp::Prod: r = _mm256_mul_ps(a, b); break;
+      case ReduceOp::Min: r = _mm256_min_ps(b, a); break;
+      default: r = _mm256_max_ps(b, a); break;
+    }
+    const __m256i x = _mm256_castps_si256(r);
+    const __m256i lsb = _mm256_and_si256(_mm256_srli_epi32(x, 16), one);
+    const __m256i rne = _mm256_srli_epi32(_mm256_add_epi32(x, _mm256_add_epi32(bias, lsb)), 16);
+    const __m256i qnan = _mm256_or_si256(_mm256_srli_epi32(x, 16), quiet);
+    const __m256i isnan = _mm256_cmpgt_epi32(_mm256_and_si256(x, absmask), inf);
+    const __m256i h = _mm256_blendv_epi8(rne, qnan, isnan);
+    // 8 x u32 (each <= 0xffff) -> 8 x u16: pack within 128-bit lanes, then
+    // bring the two lanes' low halves together.
+    const __m256i packed = _mm256_permute4x64_epi64(_mm256_packus_epi32(h, h), 0x08);
+    _mm_storeu_si128(reinterpret_cast<__m128i*>(d + i), _mm256_castsi256_si128(packed));
+  }
+  reduce_bf16_scalar(d + i, s + i, n - i, op);
+}
+#endif
+
+using Half16Fn = void (*)(uint16_t*, const uint16_t*, size_t, ReduceOp);
+Half16Fn pick_bf16() {
+#if defined(__x86_64__) && defined(__GNUC__)
+  __builtin_cpu_init();
+  if (__builtin_cpu_supports("avx512f")) return reduce_bf16_avx512;
+  if (__builtin_cpu_supports("avx2")) return reduce_bf16_avx2;
+#endif
+  return reduce_bf16_scalar;
+}
+
+void reduce_bf16(uint16_t* d, const uint16_t* s, size_t n, ReduceOp op) {
+  static const Half16Fn fn = pick_bf16();
+  fn(d, s, n, op);
+}
+
+void reduce_f16_scalar(uint16_t* d, const uint16_t* s, size_t n, ReduceOp op) {
+  for (size_t i = 0; i < n; ++i) d[i] = f32_to_f16(apply_f(f16_to_f32(d[i]), f16_to_f32(s[i]), op));
+}
+
+#if defined(__x86_64__) && defined(__GNUC__)
+// Hardware binary16 conversions (vcvtph2ps / vcvtps2ph, round to nearest
+// even; the result equals f32_to_f16 except for NaN payload bits). Min / max
+// keep the scalar rule `b < a ? b : a`: the x86 min / max return their second
+// operand on equality or NaN.
+__attribute__((target("avx512f"))) void reduce_f16_avx512(uint16_t* d, const uint16_t* s, size_t n, ReduceOp op) {
+  size_t i = 0;
+  for (; i + 16 <= n; i += 16) {
+    const __m512 a = _mm512_cvtph_ps(_mm256_loadu_si256(reinterpret_cast<const __m256i*>(d + i)));
+    const __m512 b = _mm512_cvtph_ps(_mm256_loadu_si256(reinterpret_cast<const __m256i*>(s + i)));
+    __m512 r;
+    switch (op) {
+      case ReduceOp::Sum: r = _mm512_add_ps(a, b); break;
+      case ReduceOp::Prod: r = _mm512_mul_ps(a, b); break;
+      case ReduceOp::Min: r = _mm512_min_ps(b, a); break;
+      default: r = _mm512_max_ps(b, a); break;
+    }
+    _mm256_storeu_si256(reinterpret_cast<__m256i*>(d + i),
+                        _mm512_cvtps_ph(r, _MM_FROUND_TO_NEAREST_INT | _MM_FROUND_NO_EXC));
+  }
+  reduce_f16_scalar(d + i, s + i, n - i, op);
+}
+__attribute__((target("avx2,f16c"))) void reduce_f16_avx2(uint16_t* d, const uint16_t* s, size_t n, ReduceOp op) {
+  size_t i = 0;
+  for (; i + 8 <= n; i += 8) {
+    const __m256 a = _mm256_cvtph_ps(_mm_loadu_si128(reinterpret_cast<const __m128i*>(d + i)));
+    const __m256 b = _mm256_cvtph_ps(_mm_loadu_si128(reinterpret_cast<const __m128i*>(s + i)));
+    __m256 r;
+    switch (op) {
+      case ReduceOp::Sum: r = _mm256_add_ps(a, b); break;
+      case ReduceOp::Prod: r = _mm256_mul_ps(a, b); break;
+      case ReduceOp::Min: r = _mm256_min_ps(b, a); break;
+      default: r = _mm256_max_ps(b, a); break;
+    }
+    _mm_storeu_si128(reinterpret_cast<__m128i*>(d + i),
+                     _mm256_cvtps_ph(r, _MM_FROUND_TO_NEAREST_INT | _MM_FROUND_NO_EXC));
+  }
+  reduce_f16_scalar(d + i, s + i, n - i, op);
+}
+#endif
+
+Half16Fn pick_f16() {
+#if defined(__x86_64__) && defined(__GNUC__)
+  __builtin_cpu_init();
+  if (__builtin_cpu_supports("avx512f")) return reduce_f16_avx512;
+  if (__builtin_cpu_supports("avx2") && __builtin_cpu_supports("f16c")) return reduce_f16_avx2;
+#endif
+  return reduce_f16_scalar;
 }
 
 void reduce_f16(uint16_t* d, const uint16_t* s, size_t n, ReduceOp op) {
-  for (size_t i = 0; i < n; ++i) d[i] = f32_to_f16(apply_f(f16_to_f32(d[i]), f16_to_f32(s[i]), op));
+  static const Half16Fn fn = pick_f16();
+  fn(d, s, n, op);
 }
 
 template <typename T> void fill(void* dst, size_t n, T v) {

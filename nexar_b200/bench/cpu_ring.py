@@ -5,7 +5,7 @@ all_gather and reduce_scatter; every rank must equal the elementwise sum),
 timed over message sizes.
 
     python -m nexar_b200.bench.cpu_ring [--ranks 4] [--min-bytes 4096] [--max-bytes 67108864]
-                                        [--iters 20] [--warmup 3] [--out sweep.jsonl]
+                                        [--iters 20] [--warmup 3] [--dtype f32|bf16] [--out sweep.jsonl]
 
 One thread per rank in one process (as the reference's tests and this
 config). Each size: a barrier, ``iters`` back-to-back calls per rank, the
@@ -62,23 +62,32 @@ def check_config(clients, n=1024):
     return ok_ar and ok_ag and ok_rs
 
 
-def time_op(clients, op, nbytes, iters, warmup):
+def _values(r, n, dtype):
+    x = np.random.RandomState(r).uniform(-1, 1, n).astype(np.float32)
+    if dtype == "bf16":  # top 16 bits of the f32 pattern, held as uint16 (the client maps it to BF16)
+        return (x.view(np.uint32) >> 16).astype(np.uint16)
+    return x
+
+
+def time_op(clients, op, nbytes, iters, warmup, dtype="f32"):
     W = len(clients)
-    count = max(W, nbytes // 4 // W * W)
+    es = 2 if dtype == "bf16" else 4
+    npt = np.uint16 if dtype == "bf16" else np.float32
+    count = max(W, nbytes // es // W * W)
     if op == "all_reduce":
-        bufs = [np.random.RandomState(r).uniform(-1, 1, count).astype(np.float32) for r in range(W)]
+        bufs = [_values(r, count, dtype) for r in range(W)]
 
         def call(c):
             c.all_reduce_host(bufs[c.rank])
     elif op == "all_gather":
-        send = [np.random.RandomState(r).uniform(-1, 1, count // W).astype(np.float32) for r in range(W)]
-        recv = [np.empty(count, np.float32) for _ in range(W)]
+        send = [_values(r, count // W, dtype) for r in range(W)]
+        recv = [np.empty(count, npt) for _ in range(W)]
 
         def call(c):
             c.all_gather_host(send[c.rank], recv[c.rank])
     elif op == "reduce_scatter":
-        send = [np.random.RandomState(r).uniform(-1, 1, count).astype(np.float32) for r in range(W)]
-        recv = [np.empty(count // W, np.float32) for _ in range(W)]
+        send = [_values(r, count, dtype) for r in range(W)]
+        recv = [np.empty(count // W, npt) for _ in range(W)]
 
         def call(c):
             c.reduce_scatter_host(send[c.rank], recv[c.rank])
@@ -95,9 +104,9 @@ def time_op(clients, op, nbytes, iters, warmup):
         return time.perf_counter() - t0
 
     t = max(_run(clients, body)) / iters
-    total = count * 4
+    total = count * es
     factor = 2 * (W - 1) / W if op == "all_reduce" else (W - 1) / W
-    return {"op": op, "ranks": W, "bytes": total, "us": round(t * 1e6, 1),
+    return {"op": op, "ranks": W, "dtype": dtype, "bytes": total, "us": round(t * 1e6, 1),
             "algbw_gbs": round(total / t / 1e9, 3), "busbw_gbs": round(factor * total / t / 1e9, 3)}
 
 
@@ -109,6 +118,7 @@ def main():
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--ops", default="all_reduce,all_gather,reduce_scatter")
+    ap.add_argument("--dtype", default="f32", choices=["f32", "bf16"])
     ap.add_argument("--out", default=None)
     args = ap.parse_args()
     from nexar_b200.client import NexarClient
@@ -120,7 +130,7 @@ def main():
         while size <= args.max_bytes:
             for op in args.ops.split(","):
                 iters = args.iters if size <= (4 << 20) else max(3, args.iters // 4)
-                rec = time_op(clients, op, size, iters, args.warmup)
+                rec = time_op(clients, op, size, iters, args.warmup, args.dtype)
                 line = json.dumps(rec)
                 print(line, flush=True)
                 if out:

@@ -251,3 +251,40 @@ def test_memory_buffer_refs_and_pool_builder():
     assert b.size == 100 and b.tier == 0
     assert pool.tier_for_size(2000) == 1
     assert BufferPool.with_profile(PoolProfile.Inference).free_count(0) >= 0
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "f16"])
+@pytest.mark.parametrize("op", [0, 1, 2, 3])  # Sum, Prod, Min, Max
+def test_half_reduce_vector_paths_match_scalar_definition(dtype, op):
+    """The SIMD bf16 / f16 reductions (16 or 8 lanes wide plus a scalar tail)
+    agree bit for bit with the scalar conversion rules on every class of
+    input: normals, subnormals, +-0, +-inf, NaN (any NaN matches any NaN)."""
+    import numpy as np
+    H = _native.host()
+    rs = np.random.RandomState(op * 7 + (dtype == "f16"))
+    n = 4099  # vector blocks and a tail
+    a = rs.randint(0, 1 << 16, n).astype(np.uint16)
+    b = rs.randint(0, 1 << 16, n).astype(np.uint16)
+    # special values in both operands
+    if dtype == "bf16":
+        specials = [0x0000, 0x8000, 0x7f80, 0xff80, 0x7fc1, 0x0001, 0x8001, 0x3f80, 0x7f7f]
+    else:
+        specials = [0x0000, 0x8000, 0x7c00, 0xfc00, 0x7e01, 0x0001, 0x8001, 0x3c00, 0x7bff]
+    a[:len(specials)] = specials
+    b[len(specials):2 * len(specials)] = specials
+    to_f = H.bf16_to_f32 if dtype == "bf16" else H.f16_to_f32
+    from_f = H.f32_to_bf16 if dtype == "bf16" else H.f32_to_f16
+    fns = [lambda x, y: x + y, lambda x, y: x * y, lambda x, y: y if y < x else x, lambda x, y: y if y > x else x]
+    with np.errstate(all="ignore"):  # inf / NaN results are part of the test
+        want = np.array([from_f(float(np.float32(fns[op](np.float32(to_f(int(x))), np.float32(to_f(int(y)))))))
+                         for x, y in zip(a, b)], np.uint16)
+    got = a.copy()
+    code = DataType.BF16 if dtype == "bf16" else DataType.F16
+    H.reduce_slice(got.ctypes.data, b.ctypes.data, n, int(code), op)
+    if dtype == "bf16":
+        is_nan = lambda v: ((v & 0x7f80) == 0x7f80) & ((v & 0x007f) != 0)
+    else:
+        is_nan = lambda v: ((v & 0x7c00) == 0x7c00) & ((v & 0x03ff) != 0)
+    both_nan = is_nan(got) & is_nan(want)
+    mism = (got != want) & ~both_nan
+    assert not mism.any(), [(int(a[i]), int(b[i]), int(got[i]), int(want[i])) for i in np.nonzero(mism)[0][:5]]
