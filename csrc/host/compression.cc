@@ -92,10 +92,26 @@ TopKCompressor::TopKCompressor(double ratio) : ratio_(ratio) {
   if (!(ratio > 0.0 && ratio <= 1.0)) fail(Err::Elastic, "ratio must be in (0.0, 1.0]");
 }
 
+namespace {
+// fp32 bit pattern of |x| (for non-negative floats the pattern orders like the
+// value; a NaN sorts above infinity).
+inline uint32_t mag_key(const uint8_t* p, DataType dt) {
+  const float m = magnitude(p, dt);
+  uint32_t b;
+  std::memcpy(&b, &m, 4);
+  return b & 0x7fffffffu;
+}
+inline uint32_t f32_key(float v) {
+  uint32_t b;
+  std::memcpy(&b, &v, 4);
+  return b & 0x7fffffffu;
+}
+}  // namespace
+
 CompressedTensor TopKCompressor::compress(const uint8_t* input, size_t count, DataType dt, uint8_t* residual) {
-  accumulate(residual, input, count, dt);
   const bool is_float = dt == DataType::F32 || dt == DataType::F64 || dt == DataType::BF16 || dt == DataType::F16;
   if (!is_float || count == 0) {
+    accumulate(residual, input, count, dt);
     // Integer tensors are sent whole (magnitude ranking is not meaningful).
     std::vector<uint32_t> idx(count);
     std::iota(idx.begin(), idx.end(), 0u);
@@ -103,14 +119,89 @@ CompressedTensor TopKCompressor::compress(const uint8_t* input, size_t count, Da
   }
   const size_t es = dtype_size(dt);
   const size_t k = topk_count(count, ratio_);
-  std::vector<uint32_t> idx(count);
-  std::iota(idx.begin(), idx.end(), 0u);
-  std::vector<float> mag(count);
-  for (size_t i = 0; i < count; ++i) mag[i] = magnitude(residual + i * es, dt);
-  auto better = [&](uint32_t a, uint32_t b) { return mag[a] > mag[b] || (mag[a] == mag[b] && a < b); };
-  if (k < count) std::nth_element(idx.begin(), idx.begin() + k, idx.end(), better);
-  idx.resize(k);
-  std::sort(idx.begin(), idx.end());
+  // Radix select on the magnitude keys (mag_key). Pass 1 (fused with the
+  // error-feedback accumulation for f32): a histogram of the keys' top 11
+  // bits, four interleaved copies so runs of equal bins do not serialise on
+  // one counter. The bin holding the k-th largest key follows from the
+  // counts. Pass 2 collects, in index order, the indices of every key in a
+  // higher bin and the (index, key) pairs of that bin; nth_element over the
+  // bin's keys gives the threshold, and a merge of the two ascending lists
+  // yields the k largest magnitudes, ties broken towards the lower index.
+  uint32_t hist4[4][2048] = {};
+  if (dt == DataType::F32) {
+    float* r = reinterpret_cast<float*>(residual);
+    const float* x = reinterpret_cast<const float*>(input);
+    size_t i = 0;
+    for (; i + 4 <= count; i += 4) {
+      const float v0 = r[i] + x[i], v1 = r[i + 1] + x[i + 1], v2 = r[i + 2] + x[i + 2], v3 = r[i + 3] + x[i + 3];
+      r[i] = v0;
+      r[i + 1] = v1;
+      r[i + 2] = v2;
+      r[i + 3] = v3;
+      ++hist4[0][f32_key(v0) >> 20];
+      ++hist4[1][f32_key(v1) >> 20];
+      ++hist4[2][f32_key(v2) >> 20];
+      ++hist4[3][f32_key(v3) >> 20];
+    }
+    for (; i < count; ++i) {
+      r[i] += x[i];
+      ++hist4[0][f32_key(r[i]) >> 20];
+    }
+  } else {
+    accumulate(residual, input, count, dt);
+    for (size_t i = 0; i < count; ++i) ++hist4[i & 3][mag_key(residual + i * es, dt) >> 20];
+  }
+  if (k >= count) {
+    std::vector<uint32_t> all(count);
+    std::iota(all.begin(), all.end(), 0u);
+    return gather_and_clear(all, residual, count, dt);
+  }
+  size_t above = 0;
+  uint32_t bin = 2047;
+  for (; bin > 0; --bin) {
+    const size_t h = (size_t)hist4[0][bin] + hist4[1][bin] + hist4[2][bin] + hist4[3][bin];
+    if (above + h >= k) break;
+    above += h;
+  }
+  std::vector<uint32_t> hi_idx, c_idx, c_key;
+  hi_idx.reserve(above);
+  auto visit = [&](size_t i, uint32_t v) {
+    const uint32_t b = v >> 20;
+    if (b > bin) {
+      hi_idx.push_back((uint32_t)i);
+    } else if (b == bin) {
+      c_idx.push_back((uint32_t)i);
+      c_key.push_back(v);
+    }
+  };
+  if (dt == DataType::F32) {
+    const uint32_t* rb = reinterpret_cast<const uint32_t*>(residual);
+    const uint32_t lo = bin << 20;  // keys below `lo` are skipped without a branch-heavy path
+    for (size_t i = 0; i < count; ++i) {
+      const uint32_t v = rb[i] & 0x7fffffffu;
+      if (v >= lo) visit(i, v);
+    }
+  } else {
+    for (size_t i = 0; i < count; ++i) visit(i, mag_key(residual + i * es, dt));
+  }
+  const size_t need = k - above;  // >= 1 keys from the threshold bin
+  std::vector<uint32_t> sorted_keys(c_key);
+  std::nth_element(sorted_keys.begin(), sorted_keys.begin() + (need - 1), sorted_keys.end(), std::greater<uint32_t>());
+  const uint32_t thr = sorted_keys[need - 1];
+  size_t ties = need;
+  for (uint32_t v : c_key)
+    if (v > thr) --ties;
+  std::vector<uint32_t> idx;
+  idx.reserve(k);
+  size_t a = 0;
+  for (size_t j = 0; j < c_idx.size(); ++j) {
+    const uint32_t v = c_key[j];
+    if (!(v > thr || (v == thr && ties))) continue;
+    if (v == thr) --ties;
+    while (a < hi_idx.size() && hi_idx[a] < c_idx[j]) idx.push_back(hi_idx[a++]);
+    idx.push_back(c_idx[j]);
+  }
+  while (a < hi_idx.size()) idx.push_back(hi_idx[a++]);
   return gather_and_clear(idx, residual, count, dt);
 }
 

@@ -5,9 +5,11 @@
 //
 // TopK keeps the k = max(1, ceil(n * ratio)) entries of largest |residual|
 // (residual += input first; chosen entries are zeroed in the residual). This
-// implementation selects with nth_element (O(n)) and breaks ties towards the
-// lower index, so every run picks the same set; it compresses f32, f64, bf16
-// and f16 (the reference passes anything but f32/f64 through uncompressed).
+// implementation selects by radix select on the magnitudes' fp32 bit
+// patterns (two streaming passes plus a partial sort of one histogram bin)
+// and breaks ties towards the lower index, so every run picks the same set;
+// it compresses f32, f64, bf16 and f16 (the reference passes anything but
+// f32/f64 through uncompressed).
 // RandomK samples k distinct indices with a generator seeded from a hash of
 // the residual; NoCompression sends every element.
 #pragma once

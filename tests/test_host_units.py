@@ -288,3 +288,26 @@ def test_half_reduce_vector_paths_match_scalar_definition(dtype, op):
     both_nan = is_nan(got) & is_nan(want)
     mism = (got != want) & ~both_nan
     assert not mism.any(), [(int(a[i]), int(b[i]), int(got[i]), int(want[i])) for i in np.nonzero(mism)[0][:5]]
+
+
+@pytest.mark.parametrize("dtype", [np.float32, np.float64, np.float16])
+@pytest.mark.parametrize("n,ratio", [(1, 0.5), (7, 0.3), (10_003, 0.01), (10_003, 0.999), (10_003, 1.0), (4096, 0.25)])
+def test_topk_selection_matches_sort_reference(dtype, n, ratio):
+    """The radix-select top-k equals a full sort by (|r| desc, index asc) for
+    random data with many repeated magnitudes, odd lengths, k = 1 .. n."""
+    import math
+    code = {np.float32: DataType.F32, np.float64: DataType.F64, np.float16: DataType.F16}[dtype]
+    rs = np.random.RandomState(n + int(ratio * 1000))
+    x = (rs.randint(-40, 41, n) / 8.0).astype(dtype)  # few distinct magnitudes: ties everywhere
+    res = (rs.randn(n) * (rs.rand(n) < 0.5)).astype(dtype)
+    r_before = (res.astype(np.float64) + x.astype(np.float64)).astype(dtype)  # residual += input
+    k = max(1, math.ceil(n * ratio))
+    mag = np.abs(r_before.astype(np.float32))
+    order = np.lexsort((np.arange(n), -mag))  # magnitude desc, then index asc
+    want = np.sort(order[:k])
+    ct = H.TopKCompressor(ratio).compress(x.ctypes.data, n, int(code), res.ctypes.data)
+    assert ct.k == k
+    assert ct.indices == want.tolist()
+    left = r_before.copy()
+    left[want] = 0
+    np.testing.assert_array_equal(res, left)
