@@ -7,7 +7,11 @@
 The NCCL arm issues the same call sequence as the reference's nexar-nccl
 single-node path (ncclAllReduce / ncclReduceScatter / ncclAllGather /
 ncclBroadcast in place on one stream; all_to_all as grouped send/recv),
-through torch.distributed's NCCL backend. The ``nexar_sym`` arm runs the same
+through torch.distributed's NCCL backend. The ``nccl_group`` arm issues it through
+``nexar_b200.device.nccl.NcclGroup`` (raw ncclAllReduce / ncclReduceScatter /
+ncclAllGather / ncclBroadcast on device pointers, in place where the reference
+is, on the timed stream; nexar-nccl has no device all_to_all, so that arm
+skips it). The ``nexar_sym`` arm runs the same
 calls on buffers allocated in symmetric memory (the NVSwitch multicast region
 when NVLS is the preferred path, else the peer-mapped heap), the equivalent of NCCL's
 registered buffers: no staging copies. Both arms are timed the same way:
@@ -39,7 +43,8 @@ def main(argv=None):
     ap.add_argument("--step", type=int, default=2, help="size multiplier between points")
     ap.add_argument("--iters", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=20)
-    ap.add_argument("--impls", default="nexar,nexar_sym,nccl")
+    ap.add_argument("--impls", default="nexar,nexar_sym,nccl",
+                    help="comma list of nexar, nexar_sym, nccl, nccl_group")
     ap.add_argument("--algo", default="auto")
     ap.add_argument("--out", default=None)
     args = ap.parse_args(argv)
@@ -79,6 +84,21 @@ def main(argv=None):
 
     ops = args.ops.split(",")
     impls = args.impls.split(",")
+    group = None
+    if "nccl_group" in impls:
+        from nexar_b200.core import DataType
+        from nexar_b200.device import nccl as nccl_mod
+        uid = [nccl_mod.unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        group = nccl_mod.NcclGroup(rank, world, uid[0], device=local, stream=torch.cuda.current_stream(dev))
+        gdt = DataType.from_torch(dtype)
+
+    def pick(impl, ours, torch_nccl, raw=None):
+        if impl == "nexar":
+            return ours
+        if impl == "nccl":
+            return torch_nccl
+        return raw
 
     def sym_buf(numel):
         return comm.symmetric_empty([numel], dtype, nvls=comm.nvls_preferred)
@@ -118,27 +138,33 @@ def main(argv=None):
                     nbytes = n * es
                 elif op == "all_reduce":
                     t = big.clone()
-                    fn = (lambda: comm.all_reduce(t, algo=args.algo)) if impl == "nexar" else (lambda: dist.all_reduce(t))
+                    fn = pick(impl, lambda: comm.all_reduce(t, algo=args.algo), lambda: dist.all_reduce(t),
+                              lambda: group.allreduce_inplace(t.data_ptr(), n, gdt))
                     nbytes = n * es
                 elif op == "reduce_scatter":
                     out = torch.empty(n // world, dtype=dtype, device=dev)
-                    fn = (lambda: comm.reduce_scatter(big, out)) if impl == "nexar" else (lambda: dist.reduce_scatter_tensor(out, big))
+                    fn = pick(impl, lambda: comm.reduce_scatter(big, out), lambda: dist.reduce_scatter_tensor(out, big),
+                              lambda: group.reduce_scatter_ptr(big.data_ptr(), out.data_ptr(), n // world, gdt))
                     nbytes = n * es
                 elif op == "all_gather":
                     inp = big[: n // world].clone()
                     out = torch.empty(n, dtype=dtype, device=dev)
-                    fn = (lambda: comm.all_gather(inp, out)) if impl == "nexar" else (lambda: dist.all_gather_into_tensor(out, inp))
+                    fn = pick(impl, lambda: comm.all_gather(inp, out), lambda: dist.all_gather_into_tensor(out, inp),
+                              lambda: group.allgather(inp.data_ptr(), out.data_ptr(), n // world, gdt))
                     nbytes = n * es
                 elif op == "all_to_all":
                     out = torch.empty_like(big)
-                    fn = (lambda: comm.all_to_all(big, out)) if impl == "nexar" else (lambda: dist.all_to_all_single(out, big))
+                    fn = pick(impl, lambda: comm.all_to_all(big, out), lambda: dist.all_to_all_single(out, big))
                     nbytes = n * es
                 elif op == "broadcast":
                     t = big.clone()
-                    fn = (lambda: comm.broadcast(t, 0)) if impl == "nexar" else (lambda: dist.broadcast(t, 0))
+                    fn = pick(impl, lambda: comm.broadcast(t, 0), lambda: dist.broadcast(t, 0),
+                              lambda: group.broadcast_inplace(t.data_ptr(), n, gdt, 0))
                     nbytes = n * es
                 else:
                     raise SystemExit(f"unknown op {op}")
+                if fn is None:
+                    continue
                 ms = time_it(fn)
                 if impl == "nexar_sym":
                     torch.cuda.synchronize()
@@ -154,6 +180,8 @@ def main(argv=None):
         del big
         size *= args.step
     comm.check()
+    if group is not None:
+        group.destroy()
     dist.barrier()
     dist.destroy_process_group()
     return 0

@@ -419,12 +419,17 @@ class NexarClient:
         return buf
 
     # ------------------------------------------------------------ device (CUDA adapter)
-    def attach_device(self, device: Optional[int] = None, **kw):
+    def attach_device(self, device: Optional[int] = None, nccl: bool = False, **kw):
         """Attach the CUDA DeviceAdapter: maps the symmetric heaps of every rank
         (handles travel over this client's mesh) so ``*_device`` calls run the
-        sm_100a peer-memory kernels."""
+        sm_100a peer-memory kernels. ``nccl=True`` also forms an NCCL
+        communicator over this client (id sent by rank 0 over the mesh) that
+        carries device ``send`` / ``recv`` without ``torch.distributed``."""
         from .device import DeviceCommunicator
         self._device = DeviceCommunicator.from_client(self, device=device, **kw)
+        if nccl:
+            from .device.nccl import nccl_group_for_client
+            self._device.attach_nccl(nccl_group_for_client(self, device=self._device.device))
         return self._device
 
     @property

@@ -161,6 +161,7 @@ class DeviceCommunicator:
         self._side_stream = None
         self._C = C
         self._stats = {}
+        self._nccl = None
 
     # ----------------------------------------------------------- construction
     @classmethod
@@ -476,19 +477,51 @@ class DeviceCommunicator:
         return self._nb(self.barrier, (), None)
 
     # ----------------------------------------------------------- p2p (NCCL)
+    def attach_nccl(self, group) -> None:
+        """Carry ``send`` / ``recv`` on ``group`` (a
+        :class:`~nexar_b200.device.nccl.NcclGroup` over the same ranks in the
+        same order) instead of ``torch.distributed``."""
+        if group.local_world != self.world_size or group.local_rank != self.rank:
+            raise ValueError(f"NCCL group is rank {group.local_rank} of {group.local_world}, "
+                             f"this communicator rank {self.rank} of {self.world_size}")
+        self._nccl = group
+
+    @property
+    def nccl(self):
+        """The attached NCCL group (None: p2p goes through ``torch.distributed``)."""
+        return self._nccl
+
     def send(self, t: torch.Tensor, dst: int, group=None):
-        """Pipeline-style device send; stays on NCCL p2p (torch.distributed)."""
+        """Pipeline-style device send; stays on NCCL p2p (the attached
+        ``NcclGroup``, else ``torch.distributed``)."""
+        if self._nccl is not None and group is None:
+            self._nccl.send(t, dst)
+            return
         import torch.distributed as dist
         dist.send(t, dst, group=group)
 
     def recv(self, t: torch.Tensor, src: int, group=None):
+        if self._nccl is not None and group is None:
+            self._nccl.recv(t, src)
+            return
         import torch.distributed as dist
         dist.recv(t, src, group=group)
 
     def isend(self, t: torch.Tensor, dst: int, group=None):
+        """Non-blocking send: an ``NcclHandle`` with an attached group, else a torch ``Work``."""
+        if self._nccl is not None and group is None:
+            return self._nccl.send_nb(t, dst)
         import torch.distributed as dist
         return dist.isend(t, dst, group=group)
 
     def irecv(self, t: torch.Tensor, src: int, group=None):
+        if self._nccl is not None and group is None:
+            return self._nccl.recv_nb(t, src)
         import torch.distributed as dist
         return dist.irecv(t, src, group=group)
+
+    def send_nb(self, t: torch.Tensor, dst: int):
+        return self.isend(t, dst)
+
+    def recv_nb(self, t: torch.Tensor, src: int):
+        return self.irecv(t, src)

@@ -166,14 +166,16 @@ class HierarchicalComm:
     """Node-aware collectives over a flat ``NexarClient`` (collective construction:
     every rank calls it in the same order). ``device_comm`` is the node's
     ``DeviceCommunicator`` for CUDA tensors (``attach_device=True`` builds
-    one over the node sub-communicator); CPU tensors need none."""
+    one over the node sub-communicator; ``nccl=True`` adds the node's NCCL
+    communicator for device send / recv, its id sent by the node's lead);
+    CPU tensors need none."""
 
     SMALL_BYTES = 256 << 10  # below this, all_reduce takes the lead path (as the reference)
     PINNED_CACHE = 8         # pinned staging buffers kept (by dtype and size, least recently used out)
 
     def __init__(self, client, topology: Optional[NodeTopology] = None, hostname: Optional[str] = None,
                  attach_device: bool = False, device: Optional[int] = None, small_bytes: Optional[int] = None,
-                 **device_kw):
+                 nccl: bool = False, **device_kw):
         self.client = client
         self.topo = topology or discover_topology(client, hostname)
         t = self.topo
@@ -186,7 +188,7 @@ class HierarchicalComm:
         self.cross = _HostTensorComm(self.cross_client)
         self.device_comm = None
         if attach_device:
-            self.device_comm = self.local_client.attach_device(device, **device_kw)
+            self.device_comm = self.local_client.attach_device(device, nccl=nccl, **device_kw)
         self.small_bytes = self.SMALL_BYTES if small_bytes is None else int(small_bytes)
         self._pinned: Dict[Tuple[torch.dtype, int], torch.Tensor] = {}
 

@@ -2,11 +2,13 @@
 
     python setup.py build_ext --inplace
 
-Two extension modules:
+Three extension modules:
   * nexar_b200._host  - C++17 host runtime (control plane, CPU collectives,
                         compression, cluster management). No CUDA, no torch.
   * nexar_b200._cuda  - CUDA runtime for sm_100a (symmetric heap, peer-memory
                         collectives, fused GEMM+collective kernels, model ops).
+  * nexar_b200._nccl  - NCCL communicator (libnccl resolved at run time) for
+                        device point-to-point and the NCCL comparator.
 
 Device code is compiled for sm_100a only.
 """
@@ -52,6 +54,13 @@ ext_modules.append(CUDAExtension(
     cuda_sources,
     include_dirs=[os.path.join(ROOT, "csrc", "cuda")],
     extra_compile_args={"cxx": CXX_FLAGS, "nvcc": NVCC_FLAGS},
+))
+
+ext_modules.append(CUDAExtension(
+    "nexar_b200._nccl",
+    rel(glob.glob(os.path.join(ROOT, "csrc", "nccl", "*.cpp"))),
+    extra_compile_args={"cxx": CXX_FLAGS},
+    libraries=["dl"],
 ))
 
 setup(

@@ -1,0 +1,105 @@
+"""NcclGroup on the GPU: every call of the reference's NcclGroup
+(nexar-nccl/src/group.rs) plus grouped send / recv, on one GPU (a
+one-rank communicator: results equal the inputs, self send / recv is a copy),
+and ring send / recv plus all-reduce over two GPUs when the box has them.
+The expected values are plain PyTorch fp32 computations."""
+import threading
+
+import pytest
+import torch
+
+from conftest import gpu_count
+from nexar_b200.core import DataType, ReduceOp
+from nexar_b200.device import DeviceCommunicator
+from nexar_b200.device import nccl
+
+pytestmark = pytest.mark.gpu
+
+
+def test_nccl_group_one_gpu(cuda0):
+    g = nccl.NcclGroup(0, 1, nccl.unique_id(), device=0)
+    assert (g.local_rank, g.local_world, g.device) == (0, 1, 0) and not g.closed
+    gen = torch.Generator(device="cuda").manual_seed(1)
+    x = torch.randn(4097, device=cuda0, generator=gen)
+    ref = x.clone()
+
+    out = torch.empty_like(x)
+    assert g.all_reduce(x, "sum", out=out) is out
+    torch.testing.assert_close(out, ref, rtol=0, atol=0)
+    g.all_reduce(x, "max")
+    g.broadcast(x, root=0)
+    g.reduce(x, root=0, op="sum")
+    ag = torch.empty_like(x)
+    g.all_gather(x, ag)
+    rs = torch.empty_like(x)
+    g.reduce_scatter(x, rs)
+    torch.testing.assert_close(x, ref, rtol=0, atol=0)
+    torch.testing.assert_close(ag, ref, rtol=0, atol=0)
+    torch.testing.assert_close(rs, ref, rtol=0, atol=0)
+
+    xb = x.to(torch.bfloat16)
+    yb = torch.zeros_like(xb)
+    g.send_recv(xb, 0, yb, 0)
+    torch.testing.assert_close(yb.float(), ref.to(torch.bfloat16).float(), rtol=0, atol=0)
+
+    y = torch.zeros_like(x)
+    h = g.send_recv_nb(x, 0, y, 0)
+    assert h.wait() is y
+    h.synchronize()
+    assert h.is_finished()
+    torch.testing.assert_close(y, ref, rtol=0, atol=0)
+
+    # raw-pointer calls on the group's stream, ordered by events
+    z = ref.clone()
+    torch.cuda.synchronize()
+    g.allreduce_inplace(z.data_ptr(), z.numel(), DataType.F32, ReduceOp.Sum)
+    ev = g.create_event()
+    g.record_event(ev)
+    g.stream_wait_event(ev, torch.cuda.current_stream())
+    g.synchronize()
+    assert g.event_query(ev)
+    g.destroy_event(ev)
+    torch.testing.assert_close(z, ref, rtol=0, atol=0)
+    assert g.async_error() == 0
+
+    comm = DeviceCommunicator(0, 1, 0, exchange=lambda h_: [h_], slot_bytes=1 << 20)
+    comm.attach_nccl(g)
+    assert comm.nccl is g
+    g.destroy()
+    assert g.closed
+    with pytest.raises(nccl.NcclCommError, match="destroyed"):
+        g.all_reduce(x)
+
+
+def test_nccl_group_two_gpus_ring():
+    if gpu_count() < 2:
+        pytest.skip("needs two GPUs")
+    from helpers_host import bootstrap, run_collective
+    clients = bootstrap(2)
+    n = 1 << 16
+
+    def go(c):
+        torch.cuda.set_device(c.rank)
+        g = nccl.nccl_group_for_client(c, device=c.rank)
+        dev = torch.device("cuda", c.rank)
+        gen = torch.Generator(device=dev).manual_seed(10 + c.rank)
+        x = torch.randn(n, device=dev, generator=gen)
+        got = torch.empty_like(x)
+        peer = 1 - c.rank
+        g.send_recv(x, peer, got, peer)
+        s = x.clone()
+        g.all_reduce(s)
+        torch.cuda.synchronize(dev)
+        g.destroy()
+        return x.cpu(), got.cpu(), s.cpu()
+
+    try:
+        res = run_collective(clients, go, timeout=120)
+    finally:
+        for c in clients:
+            c.close()
+    (x0, got0, s0), (x1, got1, s1) = res
+    torch.testing.assert_close(got0, x1, rtol=0, atol=0)
+    torch.testing.assert_close(got1, x0, rtol=0, atol=0)
+    torch.testing.assert_close(s0, x0 + x1, rtol=1e-6, atol=1e-6)
+    torch.testing.assert_close(s1, s0, rtol=0, atol=0)
