@@ -83,6 +83,38 @@ static bool tls_pair_check(bool same_ca) {
   return tls_identities_check(ca_a->issue("server"), ca_b->issue("client"));
 }
 
+// Python subclasses of DeviceAdapter (the reference's DeviceAdapter trait is
+// public so applications can bring their own memory). Buffers cross as
+// integer addresses; the override runs with the GIL taken, from whichever
+// thread runs the collective.
+class PyDeviceAdapter : public DeviceAdapter {
+ public:
+  std::string name() const override { PYBIND11_OVERRIDE_PURE(std::string, DeviceAdapter, name); }
+  bool supports_host_offload() const override {
+    PYBIND11_OVERRIDE(bool, DeviceAdapter, supports_host_offload);
+  }
+  bool host_addressable() const override { PYBIND11_OVERRIDE(bool, DeviceAdapter, host_addressable); }
+  void stage_for_send(const void* ptr, size_t n, uint8_t* out) override {
+    py::gil_scoped_acquire gil;
+    py::function f = py::get_override(static_cast<const DeviceAdapter*>(this), "stage_for_send");
+    if (!f) fail(Err::DeviceError, "DeviceAdapter subclass lacks stage_for_send");
+    f(reinterpret_cast<uint64_t>(ptr), n, reinterpret_cast<uint64_t>(out));
+  }
+  void receive_to_device(const uint8_t* src, size_t n, void* ptr) override {
+    py::gil_scoped_acquire gil;
+    py::function f = py::get_override(static_cast<const DeviceAdapter*>(this), "receive_to_device");
+    if (!f) fail(Err::DeviceError, "DeviceAdapter subclass lacks receive_to_device");
+    f(reinterpret_cast<uint64_t>(src), n, reinterpret_cast<uint64_t>(ptr));
+  }
+  void reduce_inplace(void* dst, const void* src, size_t count, DataType dt, ReduceOp op) override {
+    py::gil_scoped_acquire gil;
+    py::function f = py::get_override(static_cast<const DeviceAdapter*>(this), "reduce_inplace");
+    if (!f) fail(Err::DeviceError, "DeviceAdapter subclass lacks reduce_inplace");
+    f(reinterpret_cast<uint64_t>(dst), reinterpret_cast<uint64_t>(src), count, static_cast<int>(dt),
+      static_cast<int>(op));
+  }
+};
+
 PYBIND11_MODULE(_host, m) {
   m.def("tls_pair_check", &tls_pair_check, py::arg("same_ca"), py::call_guard<py::gil_scoped_release>());
   m.doc() = "nexar_b200 host runtime (C++): TCP control plane, CPU collectives, cluster management";
@@ -311,6 +343,27 @@ PYBIND11_MODULE(_host, m) {
       .def("accept_elastic", &SeedNode::accept_elastic)
       .def("close", &SeedNode::close, GR());
 
+  // ------------------------------------------------------------ device adapters
+  py::class_<DeviceAdapter, PyDeviceAdapter, std::shared_ptr<DeviceAdapter>>(m, "DeviceAdapter")
+      .def(py::init<>())
+      .def("name", &DeviceAdapter::name)
+      .def("supports_host_offload", &DeviceAdapter::supports_host_offload)
+      .def("supports_device_collectives", &DeviceAdapter::supports_device_collectives)
+      .def("host_addressable", &DeviceAdapter::host_addressable)
+      .def("stage_for_send", [](DeviceAdapter& a, uint64_t ptr, size_t n, uint64_t out) {
+        a.stage_for_send(P(ptr), n, static_cast<uint8_t*>(P(out)));
+      }, GR())
+      .def("receive_to_device", [](DeviceAdapter& a, uint64_t src, size_t n, uint64_t ptr) {
+        a.receive_to_device(static_cast<const uint8_t*>(P(src)), n, P(ptr));
+      }, GR())
+      .def("reduce_inplace", [](DeviceAdapter& a, uint64_t dst, uint64_t src, size_t count, int dt, int op) {
+        a.reduce_inplace(P(dst), P(src), count, static_cast<DataType>(dt), static_cast<ReduceOp>(op));
+      }, GR());
+  py::class_<CpuAdapter, DeviceAdapter, std::shared_ptr<CpuAdapter>>(m, "CpuAdapter").def(py::init<>());
+  py::class_<CudaStagingAdapter, DeviceAdapter, std::shared_ptr<CudaStagingAdapter>>(m, "CudaAdapter")
+      .def(py::init<>())
+      .def_static("runtime_available", &CudaStagingAdapter::runtime_available);
+
   // ------------------------------------------------------------ client
   py::class_<NexarClient, std::shared_ptr<NexarClient>>(m, "NexarClient")
       .def_static("bootstrap_local", &NexarClient::bootstrap_local, GR())
@@ -327,6 +380,8 @@ PYBIND11_MODULE(_host, m) {
       .def_property_readonly("rank_map", &NexarClient::rank_map)
       .def_property_readonly("mesh_rank_of_self", [](const NexarClient& c) { return c.mesh()->rank(); })
       .def_property_readonly("adapter_name", [](const NexarClient& c) { return c.adapter()->name(); })
+      .def("adapter", &NexarClient::adapter)
+      .def("set_adapter", &NexarClient::set_adapter)
       .def("has_direct_peer", &NexarClient::has_direct_peer)
       .def("transport_encrypted", [](const NexarClient& c) { return c.mesh()->all_encrypted(); })
       .def("is_sparse", &NexarClient::is_sparse)

@@ -423,13 +423,26 @@ std::shared_ptr<NexarClient> NexarClient::bootstrap_worker(const std::string& se
 }
 
 // ------------------------------------------------------------ p2p
+void NexarClient::set_adapter(std::shared_ptr<DeviceAdapter> a) {
+  adapter_ = a ? std::move(a) : std::make_shared<CpuAdapter>();
+}
+
+// Point to point moves the buffer through the adapter: staged to the host
+// before sending, written back after receiving (nexar/src/client/async_client.rs:312-379).
 void NexarClient::send(const void* ptr, size_t size, Rank dest, uint32_t tag) {
   const Rank m = mesh_rank(dest);
+  const uint8_t* src = static_cast<const uint8_t*>(ptr);
+  Bytes staged;
+  if (!adapter_->host_addressable()) {
+    staged.resize(size);
+    adapter_->stage_for_send(ptr, size, staged.data());
+    src = staged.data();
+  }
   if (comm_id_ == 0) {
-    Bytes payload(static_cast<const uint8_t*>(ptr), static_cast<const uint8_t*>(ptr) + size);
+    Bytes payload = adapter_->host_addressable() ? Bytes(src, src + size) : std::move(staged);
     mesh_->send_message(m, Message::data(tag, mesh_->rank(), std::move(payload)), Priority::Bulk);
   } else {
-    mesh_->send_tagged(m, comm_id_, kP2PTagBit | tag, ptr, size);
+    mesh_->send_tagged(m, comm_id_, kP2PTagBit | tag, src, size);
   }
 }
 
@@ -446,31 +459,32 @@ void NexarClient::recv(void* ptr, size_t size, Rank src, uint32_t tag) {
   }
   if (payload.size() != size)
     fail(Err::BufferSizeMismatch, "buffer size mismatch: expected " + std::to_string(size) + " bytes, got " + std::to_string(payload.size()));
-  std::memcpy(ptr, payload.data(), size);
+  if (adapter_->host_addressable()) std::memcpy(ptr, payload.data(), size);
+  else adapter_->receive_to_device(payload.data(), size, ptr);
 }
 
 void NexarClient::send_iov(const std::vector<std::pair<const void*, size_t>>& iov, Rank dest, uint32_t tag) {
   size_t total = 0;
   for (auto& e : iov) total += e.second;
   Bytes b(total);
-  size_t off = 0;
-  for (auto& e : iov) {
-    std::memcpy(b.data() + off, e.first, e.second);
-    off += e.second;
-  }
-  send(b.data(), b.size(), dest, tag);
+  adapter_->stage_for_send_iov(iov, b.data());
+  // b is host memory now: send it without a second staging pass.
+  const Rank m = mesh_rank(dest);
+  if (comm_id_ == 0) mesh_->send_message(m, Message::data(tag, mesh_->rank(), std::move(b)), Priority::Bulk);
+  else mesh_->send_tagged(m, comm_id_, kP2PTagBit | tag, b.data(), b.size());
 }
 
 void NexarClient::recv_iov(const std::vector<std::pair<void*, size_t>>& iov, Rank src, uint32_t tag) {
   size_t total = 0;
   for (auto& e : iov) total += e.second;
-  Bytes b(total);
-  recv(b.data(), total, src, tag);
-  size_t off = 0;
-  for (auto& e : iov) {
-    std::memcpy(e.first, b.data() + off, e.second);
-    off += e.second;
-  }
+  const Rank m = mesh_rank(src);
+  auto dl = deadline_in(collective_timeout());
+  Bytes payload;
+  if (comm_id_ == 0) payload = std::move(mesh_->box(m)->pop_data(tag, dl).msg.payload);
+  else payload = std::move(mesh_->box(m)->pop(LaneKey{LaneKind::Tagged, comm_id_, kP2PTagBit | tag}, dl).bytes);
+  if (payload.size() != total)
+    fail(Err::BufferSizeMismatch, "buffer size mismatch: expected " + std::to_string(total) + " bytes, got " + std::to_string(payload.size()));
+  adapter_->receive_to_device_iov(payload.data(), iov);
 }
 
 void NexarClient::send_bytes(Rank dest, const void* p, size_t n) { mesh_->send_raw(mesh_rank(dest), comm_id_, p, n); }

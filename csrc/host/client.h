@@ -36,20 +36,56 @@ class DeviceAdapter {
   virtual bool supports_host_offload() const { return true; }
   // Kernels on the device itself perform collectives (no host staging).
   virtual bool supports_device_collectives() const { return false; }
+  // Buffers are ordinary host memory: collectives and p2p read and write them
+  // in place, without staging copies.
+  virtual bool host_addressable() const { return false; }
   virtual void stage_for_send(const void* ptr, size_t nbytes, uint8_t* out) = 0;
   virtual void receive_to_device(const uint8_t* src, size_t nbytes, void* ptr) = 0;
   virtual void reduce_inplace(void* dst, const void* src, size_t count, DataType dt, ReduceOp op) = 0;
+  // Gather / scatter forms (nexar/src/device/adapter.rs: stage_for_send_iov,
+  // receive_to_device_iov): regions are packed back to back in `out` / `src`.
+  virtual void stage_for_send_iov(const std::vector<std::pair<const void*, size_t>>& iov, uint8_t* out) {
+    size_t off = 0;
+    for (auto& e : iov) {
+      stage_for_send(e.first, e.second, out + off);
+      off += e.second;
+    }
+  }
+  virtual void receive_to_device_iov(const uint8_t* src, const std::vector<std::pair<void*, size_t>>& iov) {
+    size_t off = 0;
+    for (auto& e : iov) {
+      receive_to_device(src + off, e.second, e.first);
+      off += e.second;
+    }
+  }
 };
 
 // Host pointers used directly (nexar/src/device/cpu.rs:7-52).
 class CpuAdapter : public DeviceAdapter {
  public:
   std::string name() const override { return "cpu"; }
+  bool host_addressable() const override { return true; }
   void stage_for_send(const void* ptr, size_t n, uint8_t* out) override { std::memcpy(out, ptr, n); }
   void receive_to_device(const uint8_t* src, size_t n, void* ptr) override { std::memcpy(ptr, src, n); }
   void reduce_inplace(void* dst, const void* src, size_t count, DataType dt, ReduceOp op) override {
     reduce_slice(dst, src, count, dt, op);
   }
+};
+
+// CUDA device memory staged through host memory (nexar-rdma/src/cuda_adapter.rs:14-139):
+// copies go through the CUDA runtime (libcudart, resolved at first use, so this
+// module needs no CUDA at build or load time); reduce_inplace brings both
+// operands to the host, reduces there and writes the result back. This is the
+// path for device pointers that cross hosts; on one box, device pointers go to
+// the peer-memory kernels of the device communicator instead.
+class CudaStagingAdapter : public DeviceAdapter {
+ public:
+  std::string name() const override { return "cuda"; }
+  void stage_for_send(const void* ptr, size_t n, uint8_t* out) override;
+  void receive_to_device(const uint8_t* src, size_t n, void* ptr) override;
+  void reduce_inplace(void* dst, const void* src, size_t count, DataType dt, ReduceOp op) override;
+  // Whether libcudart could be resolved in this process (no device needed).
+  static bool runtime_available();
 };
 
 // ------------------------------------------------------------------ mesh
@@ -178,6 +214,9 @@ class NexarClient : public std::enable_shared_from_this<NexarClient> {
   std::shared_ptr<Mesh> mesh() const { return mesh_; }
   const std::vector<Rank>& rank_map() const { return rank_map_; }
   std::shared_ptr<DeviceAdapter> adapter() const { return adapter_; }
+  // Replace the adapter; call before the first operation that uses it.
+  // Communicators derived later by split / rebuild inherit it.
+  void set_adapter(std::shared_ptr<DeviceAdapter> a);
   Rank mesh_rank(Rank r) const;
   bool has_direct_peer(Rank r) const { return mesh_->has_direct(mesh_rank(r)); }
   bool is_sparse() const { return mesh_->sparse(); }

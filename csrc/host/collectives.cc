@@ -651,7 +651,7 @@ void compressed_allreduce(NexarClient& c, uint8_t* buf, size_t count, DataType d
 namespace {
 template <typename F> void with_staging(NexarClient& c, void* ptr, size_t nbytes, F&& f) {
   auto ad = c.adapter();
-  if (ad->name() == "cpu") {
+  if (ad->host_addressable()) {
     f(static_cast<uint8_t*>(ptr));
     return;
   }
@@ -659,6 +659,32 @@ template <typename F> void with_staging(NexarClient& c, void* ptr, size_t nbytes
   ad->stage_for_send(ptr, nbytes, tmp.data());
   f(tmp.data());
   ad->receive_to_device(tmp.data(), nbytes, ptr);
+}
+
+// Out-of-place form: `send` (send_bytes) is staged in, `recv` (recv_bytes)
+// written back after the algorithm; a null buffer or zero size is skipped
+// (gather's and scatter's non-root sides).
+template <typename F>
+void with_staging2(NexarClient& c, const void* send, size_t send_bytes, void* recv, size_t recv_bytes, F&& f) {
+  auto ad = c.adapter();
+  if (ad->host_addressable()) {
+    f(static_cast<const uint8_t*>(send), static_cast<uint8_t*>(recv));
+    return;
+  }
+  Bytes in, out;
+  const uint8_t* s = nullptr;
+  uint8_t* r = nullptr;
+  if (send && send_bytes) {
+    in.resize(send_bytes);
+    ad->stage_for_send(send, send_bytes, in.data());
+    s = in.data();
+  }
+  if (recv && recv_bytes) {
+    out.resize(recv_bytes);
+    r = out.data();
+  }
+  f(s, r);
+  if (r) ad->receive_to_device(out.data(), recv_bytes, recv);
 }
 }  // namespace
 
@@ -727,12 +753,19 @@ void NexarClient::broadcast(void* ptr, size_t count, DataType dt, Rank root) {
 }
 
 void NexarClient::all_gather(const void* send, void* recv, size_t count, DataType dt) {
-  coll::ring_allgather(*this, static_cast<const uint8_t*>(send), static_cast<uint8_t*>(recv), count, dt, next_collective_tag());
+  const uint64_t tag = next_collective_tag();
+  const size_t nb = count * dtype_size(dt);
+  with_staging2(*this, send, nb, recv, nb * world_, [&](const uint8_t* s, uint8_t* r) {
+    coll::ring_allgather(*this, s, r, count, dt, tag);
+  });
 }
 
 void NexarClient::reduce_scatter(const void* send, void* recv, size_t count, DataType dt, ReduceOp op) {
-  coll::ring_reduce_scatter(*this, static_cast<const uint8_t*>(send), static_cast<uint8_t*>(recv), count, dt, op,
-                            next_collective_tag());
+  const uint64_t tag = next_collective_tag();
+  const size_t nb = count * dtype_size(dt);
+  with_staging2(*this, send, nb * world_, recv, nb, [&](const uint8_t* s, uint8_t* r) {
+    coll::ring_reduce_scatter(*this, s, r, count, dt, op, tag);
+  });
 }
 
 void NexarClient::reduce(void* ptr, size_t count, DataType dt, ReduceOp op, Rank root) {
@@ -741,15 +774,27 @@ void NexarClient::reduce(void* ptr, size_t count, DataType dt, ReduceOp op, Rank
 }
 
 void NexarClient::all_to_all(const void* send, void* recv, size_t count, DataType dt) {
-  coll::alltoall(*this, static_cast<const uint8_t*>(send), static_cast<uint8_t*>(recv), count, dt, next_collective_tag());
+  const uint64_t tag = next_collective_tag();
+  const size_t nb = count * dtype_size(dt) * world_;
+  with_staging2(*this, send, nb, recv, nb, [&](const uint8_t* s, uint8_t* r) { coll::alltoall(*this, s, r, count, dt, tag); });
 }
 
 void NexarClient::gather(const void* send, void* recv, size_t count, DataType dt, Rank root) {
-  coll::gather(*this, static_cast<const uint8_t*>(send), static_cast<uint8_t*>(recv), count, dt, root, next_collective_tag());
+  const uint64_t tag = next_collective_tag();
+  const size_t nb = count * dtype_size(dt);
+  // Only the root's receive buffer (count x world) is written.
+  with_staging2(*this, send, nb, rank_ == root ? recv : nullptr, nb * world_, [&](const uint8_t* s, uint8_t* r) {
+    coll::gather(*this, s, r, count, dt, root, tag);
+  });
 }
 
 void NexarClient::scatter(const void* send, void* recv, size_t count, DataType dt, Rank root) {
-  coll::scatter(*this, static_cast<const uint8_t*>(send), static_cast<uint8_t*>(recv), count, dt, root, next_collective_tag());
+  const uint64_t tag = next_collective_tag();
+  const size_t nb = count * dtype_size(dt);
+  // Only the root's send buffer (count x world) is read.
+  with_staging2(*this, rank_ == root ? send : nullptr, nb * world_, recv, nb, [&](const uint8_t* s, uint8_t* r) {
+    coll::scatter(*this, s, r, count, dt, root, tag);
+  });
 }
 
 void NexarClient::scan(void* ptr, size_t count, DataType dt, ReduceOp op) {

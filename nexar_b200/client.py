@@ -42,6 +42,59 @@ def config_from_env():
     return _h().Config.from_env()
 
 
+def CpuAdapter():
+    """Host buffers used in place (nexar/src/device/cpu.rs)."""
+    return _h().CpuAdapter()
+
+
+def CudaAdapter():
+    """CUDA device buffers staged through host memory for host collectives and
+    p2p (nexar-rdma/src/cuda_adapter.rs): the cross-host path for device
+    pointers. On one box, ``attach_device`` runs device collectives on the
+    peer-memory kernels instead."""
+    return _h().CudaAdapter()
+
+
+def _adapter(a):
+    """A native adapter from None / "cpu" / "cuda" / an adapter object."""
+    if a is None or a == "cpu":
+        return CpuAdapter()
+    if a == "cuda":
+        return CudaAdapter()
+    if isinstance(a, _h().DeviceAdapter):
+        if type(a).__module__ != _h().__name__:
+            # A Python subclass: the native clients keep only the C++ part
+            # alive, so its Python half (the overrides) is kept here for the
+            # life of the process.
+            _PY_ADAPTERS.append(a)
+        return a
+    raise TypeError(f"not a DeviceAdapter: {a!r}")
+
+
+_PY_ADAPTERS: list = []
+
+
+def __getattr__(name):
+    # DeviceAdapter: subclass it in Python to bring another memory space
+    # (override name, stage_for_send, receive_to_device, reduce_inplace and,
+    # for plain host memory, host_addressable). Resolved lazily so importing
+    # this module does not load the extension.
+    if name == "DeviceAdapter":
+        return _h().DeviceAdapter
+    raise AttributeError(name)
+
+
+def _host_buf(x) -> Tuple[int, int, DataType]:
+    """``_buf`` for the typed ``*_host`` calls: host memory only."""
+    try:
+        import torch
+        if isinstance(x, torch.Tensor) and x.is_cuda:
+            raise TypeError("*_host calls take host buffers; use the *_device call for CUDA tensors")
+    except ImportError:  # pragma: no cover
+        pass
+    return _buf(x)
+
+
 def _buf(x) -> Tuple[int, int, DataType]:
     """(address, numel, dtype) of a contiguous numpy array or torch tensor."""
     try:
@@ -111,17 +164,25 @@ class NexarClient:
 
     # ------------------------------------------------------------ bootstrap
     @staticmethod
-    def bootstrap_local(world_size: int, config=None) -> List["NexarClient"]:
+    def bootstrap_local(world_size: int, config=None, adapter=None) -> List["NexarClient"]:
+        """``world_size`` ranks in this process over loopback (nexar/src/client/bootstrap.rs:22).
+        ``adapter`` ("cpu", "cuda" or a DeviceAdapter) is shared by every rank."""
         cfg = config if config is not None else _h().Config()
-        return [NexarClient(c) for c in _h().NexarClient.bootstrap_local(world_size, cfg)]
+        ad = _adapter(adapter)
+        natives = _h().NexarClient.bootstrap_local(world_size, cfg)
+        for c in natives:
+            c.set_adapter(ad)
+        return [NexarClient(c) for c in natives]
 
     bootstrap_local_with_config = bootstrap_local
 
     @staticmethod
     def bootstrap(seed_addr: str, token: Optional[bytes] = None, config=None,
-                  bind_host: str = "127.0.0.1") -> "NexarClient":
+                  bind_host: str = "127.0.0.1", adapter=None) -> "NexarClient":
         cfg = config if config is not None else _h().Config.from_env()
-        return NexarClient(_h().NexarClient.bootstrap_worker(seed_addr, token, cfg, bind_host))
+        c = _h().NexarClient.bootstrap_worker(seed_addr, token, cfg, bind_host)
+        c.set_adapter(_adapter(adapter))
+        return NexarClient(c)
 
     @staticmethod
     def bootstrap_elastic(initial_world: int, min_world: int = 1, max_world: int = 0, config=None,
@@ -186,6 +247,15 @@ class NexarClient:
 
     def adapter(self) -> str:
         return "cuda" if self._device is not None else self._c.adapter_name
+
+    def device_adapter(self):
+        """The native DeviceAdapter host collectives and p2p stage through."""
+        return self._c.adapter()
+
+    def set_adapter(self, adapter):
+        """Replace the adapter ("cpu", "cuda" or a DeviceAdapter) before the
+        operations that should use it; split / rebuild children inherit it."""
+        self._c.set_adapter(_adapter(adapter))
 
     # ------------------------------------------------------------ p2p
     def send(self, ptr: int, size: int, dest: int, tag: int):
@@ -345,62 +415,62 @@ class NexarClient:
 
     # ------------------------------------------------------------ typed host helpers
     def all_reduce_host(self, buf, op=ReduceOp.Sum):
-        p, n, dt = _buf(buf)
+        p, n, dt = _host_buf(buf)
         self.all_reduce(p, n, dt, op)
         return buf
 
     def all_reduce_rs_ag_host(self, buf, op=ReduceOp.Sum):
-        p, n, dt = _buf(buf)
+        p, n, dt = _host_buf(buf)
         self.all_reduce_rs_ag(p, n, dt, op)
         return buf
 
     def broadcast_host(self, buf, root: int):
-        p, n, dt = _buf(buf)
+        p, n, dt = _host_buf(buf)
         self.broadcast(p, n, dt, root)
         return buf
 
     def all_gather_host(self, send, recv):
-        ps, n, dt = _buf(send)
-        pr, _, _ = _buf(recv)
+        ps, n, dt = _host_buf(send)
+        pr, _, _ = _host_buf(recv)
         self.all_gather(ps, pr, n, dt)
         return recv
 
     def reduce_scatter_host(self, send, recv, op=ReduceOp.Sum):
-        ps, _, dt = _buf(send)
-        pr, n, _ = _buf(recv)
+        ps, _, dt = _host_buf(send)
+        pr, n, _ = _host_buf(recv)
         self.reduce_scatter(ps, pr, n, dt, op)
         return recv
 
     def reduce_host(self, buf, op, root: int):
-        p, n, dt = _buf(buf)
+        p, n, dt = _host_buf(buf)
         self.reduce(p, n, dt, op, root)
         return buf
 
     def all_to_all_host(self, send, recv):
-        ps, n, dt = _buf(send)
-        pr, _, _ = _buf(recv)
+        ps, n, dt = _host_buf(send)
+        pr, _, _ = _host_buf(recv)
         self.all_to_all(ps, pr, n // self.world_size, dt)
         return recv
 
     def gather_host(self, send, recv, root: int):
-        ps, n, dt = _buf(send)
-        pr = _buf(recv)[0] if recv is not None else 0
+        ps, n, dt = _host_buf(send)
+        pr = _host_buf(recv)[0] if recv is not None else 0
         self.gather(ps, pr, n, dt, root)
         return recv
 
     def scatter_host(self, send, recv, root: int):
-        pr, n, dt = _buf(recv)
-        ps = _buf(send)[0] if send is not None else 0
+        pr, n, dt = _host_buf(recv)
+        ps = _host_buf(send)[0] if send is not None else 0
         self.scatter(ps, pr, n, dt, root)
         return recv
 
     def scan_host(self, buf, op=ReduceOp.Sum):
-        p, n, dt = _buf(buf)
+        p, n, dt = _host_buf(buf)
         self.scan(p, n, dt, op)
         return buf
 
     def exclusive_scan_host(self, buf, op=ReduceOp.Sum):
-        p, n, dt = _buf(buf)
+        p, n, dt = _host_buf(buf)
         self.exclusive_scan(p, n, dt, op)
         return buf
 
@@ -438,34 +508,115 @@ class NexarClient:
             raise RuntimeError("no CUDA device attached; call attach_device()")
         return self._device
 
+    def _staged(self, *tensors) -> bool:
+        """True when ``*_device`` calls go through the adapter's host staging
+        (no device communicator attached, an adapter that is not host memory):
+        the cross-host path for device buffers. Pending work on the tensors is
+        finished first; the results are on the device when the call returns."""
+        if self._device is not None:
+            return False
+        if self._c.adapter().host_addressable():
+            raise RuntimeError("no CUDA device attached; call attach_device() or set a CudaAdapter")
+        import torch
+        for t in tensors:
+            if isinstance(t, torch.Tensor) and t.is_cuda:
+                torch.cuda.synchronize(t.device)
+        return True
+
+    def _staged_done(self, *tensors):
+        import torch
+        for t in tensors:
+            if isinstance(t, torch.Tensor) and t.is_cuda:
+                torch.cuda.synchronize(t.device)
+
     def all_reduce_device(self, t, op=ReduceOp.Sum):
+        if self._staged(t):
+            p, n, dt = _buf(t)
+            self.all_reduce(p, n, dt, op)
+            self._staged_done(t)
+            return t
         return self.device.all_reduce(t, op=str(ReduceOp.parse(op)))
 
+    def all_reduce_rs_ag_device(self, t, op=ReduceOp.Sum):
+        """Reduce-scatter then all-gather (nexar/src/collective/rs_ag_allreduce.rs):
+        on the box that is the two-shot peer-memory kernel."""
+        if self._staged(t):
+            p, n, dt = _buf(t)
+            self.all_reduce_rs_ag(p, n, dt, op)
+            self._staged_done(t)
+            return t
+        return self.device.all_reduce(t, op=str(ReduceOp.parse(op)), algo="two_shot")
+
     def broadcast_device(self, t, root: int):
+        if self._staged(t):
+            p, n, dt = _buf(t)
+            self.broadcast(p, n, dt, root)
+            self._staged_done(t)
+            return t
         return self.device.broadcast(t, root)
 
     def all_gather_device(self, send, recv):
+        if self._staged(send, recv):
+            ps, n, dt = _buf(send)
+            self.all_gather(ps, _buf(recv)[0], n, dt)
+            self._staged_done(recv)
+            return recv
         return self.device.all_gather(send, recv)
 
     def reduce_scatter_device(self, send, recv, op=ReduceOp.Sum):
+        if self._staged(send, recv):
+            pr, n, dt = _buf(recv)
+            self.reduce_scatter(_buf(send)[0], pr, n, dt, op)
+            self._staged_done(recv)
+            return recv
         return self.device.reduce_scatter(send, recv, op=str(ReduceOp.parse(op)))
 
     def reduce_device(self, t, op, root: int):
+        if self._staged(t):
+            p, n, dt = _buf(t)
+            self.reduce(p, n, dt, op, root)
+            self._staged_done(t)
+            return t
         return self.device.reduce(t, root, op=str(ReduceOp.parse(op)))
 
     def all_to_all_device(self, send, recv):
+        if self._staged(send, recv):
+            ps, n, dt = _buf(send)
+            self.all_to_all(ps, _buf(recv)[0], n // self.world_size, dt)
+            self._staged_done(recv)
+            return recv
         return self.device.all_to_all(send, recv)
 
     def gather_device(self, send, recv, root: int):
+        if self._staged(send, recv):
+            ps, n, dt = _buf(send)
+            self.gather(ps, _buf(recv)[0] if recv is not None else 0, n, dt, root)
+            self._staged_done(recv)
+            return recv
         return self.device.gather(send, root, recv)
 
     def scatter_device(self, send, recv, root: int):
+        if self._staged(send, recv):
+            pr, n, dt = _buf(recv)
+            self.scatter(_buf(send)[0] if send is not None else 0, pr, n, dt, root)
+            self._staged_done(recv)
+            return recv
         return self.device.scatter(send, root, recv)
 
     def scan_device(self, t, op=ReduceOp.Sum):
+        if self._staged(t):
+            p, n, dt = _buf(t)
+            self.scan(p, n, dt, op)
+            self._staged_done(t)
+            return t
         return t.copy_(self.device.scan(t, op=str(ReduceOp.parse(op))))
 
     def exclusive_scan_device(self, t, op=ReduceOp.Sum):
+        if self._staged(t):
+            p, n, dt = _buf(t)
+            self.exclusive_scan(p, n, dt, op)
+            self._staged_done(t)
+            return t
         return t.copy_(self.device.exclusive_scan(t, op=str(ReduceOp.parse(op))))
 
     # ------------------------------------------------------------ helpers for the device layer
