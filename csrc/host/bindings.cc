@@ -5,6 +5,7 @@
 // release the GIL. NexarError is raised as the matching nexar_b200.core
 // exception class.
 #include <sys/socket.h>
+#include <unistd.h>
 
 #include <cstring>
 #include <pybind11/functional.h>
@@ -343,6 +344,30 @@ PYBIND11_MODULE(_host, m) {
       .def("accept_elastic", &SeedNode::accept_elastic)
       .def("close", &SeedNode::close, GR());
 
+  // ------------------------------------------------------------ worker (nexar/src/cluster/worker.rs)
+  // WorkerNode.connect binds the mesh listener, joins through the seed and
+  // returns what the Welcome carried; NexarClient.from_worker_info then builds
+  // the mesh (bootstrap_worker does both in one call).
+  py::class_<WorkerInfo, std::shared_ptr<WorkerInfo>>(m, "WorkerInfo")
+      .def_property_readonly("rank", [](const WorkerInfo& w) { return w.rank; })
+      .def_property_readonly("world_size", [](const WorkerInfo& w) { return w.world_size; })
+      .def_property_readonly("peers", [](const WorkerInfo& w) { return w.peers; })
+      .def_property_readonly("listen_addr", [](const WorkerInfo& w) { return w.listen_addr; })
+      .def_property_readonly("has_certificate", [](const WorkerInfo& w) { return w.tls.valid(); })
+      .def_property_readonly("consumed", [](const WorkerInfo& w) { return w.listen_fd < 0; })
+      .def("close", [](WorkerInfo& w) {
+        if (w.listen_fd >= 0) ::close(w.listen_fd);
+        w.listen_fd = -1;
+      });
+  struct WorkerNodeApi {};
+  py::class_<WorkerNodeApi>(m, "WorkerNode")
+      .def_static("connect", [](const std::string& seed, const py::object& token, const std::string& host, bool tls) {
+        Bytes t = token.is_none() ? token_from_env() : to_bytes(token.cast<py::bytes>());
+        py::gil_scoped_release r;
+        return std::make_shared<WorkerInfo>(WorkerNode::connect(seed, t, host, tls));
+      }, py::arg("seed_addr"), py::arg("token") = py::none(), py::arg("bind_host") = "127.0.0.1",
+         py::arg("tls") = false);
+
   // ------------------------------------------------------------ device adapters
   py::class_<DeviceAdapter, PyDeviceAdapter, std::shared_ptr<DeviceAdapter>>(m, "DeviceAdapter")
       .def(py::init<>())
@@ -374,6 +399,13 @@ PYBIND11_MODULE(_host, m) {
         return NexarClient::bootstrap_worker(seed, t, cfg, host);
       }, py::arg("seed_addr"), py::arg("token") = py::none(), py::arg("config") = Config(),
          py::arg("bind_host") = "127.0.0.1")
+      .def_static("from_worker_info", [](std::shared_ptr<WorkerInfo> info, const Config& cfg) {
+        if (!info || info->listen_fd < 0) fail(Err::ConnectionFailed, "worker info already used or closed");
+        WorkerInfo w = *info;
+        info->listen_fd = -1;  // the mesh owns the listener now
+        py::gil_scoped_release r;
+        return NexarClient::from_worker_info(std::move(w), cfg);
+      }, py::arg("info"), py::arg("config") = Config())
       .def_property_readonly("rank", &NexarClient::rank)
       .def_property_readonly("world_size", &NexarClient::world_size)
       .def_property_readonly("comm_id", &NexarClient::comm_id)

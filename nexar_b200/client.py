@@ -185,8 +185,18 @@ class NexarClient:
         return NexarClient(c)
 
     @staticmethod
+    def from_worker(info, config=None, adapter=None) -> "NexarClient":
+        """Build the mesh from a ``WorkerNode.connect`` result (the second half
+        of ``bootstrap``); ``config`` must match the cluster's (TLS, topology)."""
+        cfg = config if config is not None else _h().Config.from_env()
+        c = _h().NexarClient.from_worker_info(info, cfg)
+        c.set_adapter(_adapter(adapter))
+        return NexarClient(c)
+
+    @staticmethod
     def bootstrap_elastic(initial_world: int, min_world: int = 1, max_world: int = 0, config=None,
-                          checkpoint_timeout_s: float = 60.0) -> "ElasticBootstrap":
+                          checkpoint_timeout_s: float = 60.0, elastic: Optional["ElasticConfig"] = None,
+                          adapter=None) -> "ElasticBootstrap":
         """In-process cluster with elastic scaling (nexar/src/client/bootstrap.rs:41).
 
         A local seed forms ``initial_world`` ranks, then keeps accepting joiners
@@ -196,8 +206,12 @@ class NexarClient:
         ``remove_node`` requests at a step boundary.
         """
         import threading
+        if elastic is not None:
+            min_world, max_world = elastic.min_world_size, elastic.max_world_size
+            checkpoint_timeout_s = elastic.checkpoint_timeout_s
         H = _h()
         cfg = config if config is not None else H.Config()
+        ad = _adapter(adapter)
         seed = H.SeedNode.bind_local(bool(getattr(cfg, "tls", False)))
         natives = [None] * initial_world
         errs = []
@@ -214,6 +228,8 @@ class NexarClient:
         if errs:
             raise errs[0]
         natives.sort(key=lambda c: c.rank)
+        for c in natives:
+            c.set_adapter(ad)
         seed.accept_elastic(max_world)
         mgrs = [H.ElasticManager(c, seed if c.rank == 0 else None, min_world, max_world, checkpoint_timeout_s)
                 for c in natives]
@@ -675,6 +691,21 @@ class RpcDispatcher:
         self._client.stop_rpc_server()
 
 
+class ElasticConfig:
+    """Elastic membership bounds (nexar/src/cluster/elastic.rs:21-35):
+    ``min_world_size`` (shrinks below it are refused), ``max_world_size``
+    (0 = unbounded joins), ``checkpoint_timeout_s``."""
+
+    def __init__(self, min_world_size: int = 1, max_world_size: int = 0, checkpoint_timeout_s: float = 60.0):
+        self.min_world_size = int(min_world_size)
+        self.max_world_size = int(max_world_size)
+        self.checkpoint_timeout_s = float(checkpoint_timeout_s)
+
+    def __repr__(self):
+        return (f"ElasticConfig(min_world_size={self.min_world_size}, max_world_size={self.max_world_size}, "
+                f"checkpoint_timeout_s={self.checkpoint_timeout_s})")
+
+
 class ElasticBootstrap:
     """Result of ``NexarClient.bootstrap_elastic``: the seed, the initial clients, their managers."""
 
@@ -689,6 +720,18 @@ class ElasticBootstrap:
 
 
 SyncClient = NexarClient
+
+
+class WorkerNode:
+    """Joins a cluster through its seed (nexar/src/cluster/worker.rs:10-149)."""
+
+    @staticmethod
+    def connect(seed_addr: str, token: Optional[bytes] = None, bind_host: str = "127.0.0.1", tls: bool = False):
+        """Bind this rank's mesh listener on ``bind_host`` (advertised to the
+        others), send Hello with ``token`` (``NEXAR_CLUSTER_TOKEN`` if None),
+        wait for Welcome. Returns a ``WorkerInfo`` (rank, world_size, peers,
+        listen_addr) for ``NexarClient.from_worker``."""
+        return _h().WorkerNode.connect(seed_addr, token, bind_host, tls)
 
 
 def SeedNode(addr: str = "127.0.0.1:0", token: Optional[bytes] = None, local: bool = False):

@@ -72,3 +72,46 @@ def test_bootstrap_elastic_grows():
     grown = [NexarClient(m.client()) for m in eb.managers] + [NexarClient(joined["c"])]
     assert sorted(c.world_size for c in grown) == [3, 3, 3]
     eb.seed.close()
+
+
+def test_worker_node_connect_then_from_worker():
+    """Seed / worker bootstrap in two steps (nexar/src/cluster/worker.rs:34,
+    nexar/src/client/bootstrap.rs): WorkerNode.connect, then the mesh."""
+    from nexar_b200.client import Config, NexarClient, SeedNode, WorkerNode
+    seed = SeedNode(local=True)
+    infos = [None] * 3
+    ts = [threading.Thread(target=lambda i=i: infos.__setitem__(i, WorkerNode.connect(seed.local_addr())))
+          for i in range(3)]
+    [t.start() for t in ts]
+    seed.form_cluster(3)
+    [t.join(30) for t in ts]
+    assert sorted(i.rank for i in infos) == [0, 1, 2]
+    assert all(i.world_size == 3 and len(i.peers) == 3 and not i.consumed for i in infos)
+    clients = [None] * 3
+    ts = [threading.Thread(target=lambda k=k: clients.__setitem__(k, NexarClient.from_worker(infos[k], Config())))
+          for k in range(3)]
+    [t.start() for t in ts]
+    [t.join(30) for t in ts]
+    assert all(i.consumed for i in infos)
+    with pytest.raises(Exception):
+        NexarClient.from_worker(infos[0], Config())
+    bufs = {c.rank: np.full(5, float(c.rank), np.float32) for c in clients}
+    run_collective(clients, lambda c: c.all_reduce_host(bufs[c.rank]))
+    assert all((b == 3).all() for b in bufs.values())
+    for c in clients:
+        c.close()
+    seed.close()
+
+
+def test_crate_root_exports_and_elastic_config():
+    import nexar_b200 as nx
+    for name in list(nx._EXPORTS) + ["TopologyStrategy", "Compressor", "RecoveryEvent", "ElasticEvent"]:
+        assert getattr(nx, name) is not None, name
+    assert nx.IoVec(16, 4) == (16, 4) and nx.Rank is int
+    with pytest.raises(AttributeError):
+        nx.NoSuchThing  # noqa: B018
+    ec = nx.ElasticConfig(min_world_size=2, max_world_size=3, checkpoint_timeout_s=5.0)
+    eb = nx.NexarClient.bootstrap_elastic(2, elastic=ec, adapter="cpu")
+    assert [c.world_size for c in eb.clients] == [2, 2]
+    assert run_collective(eb.managers, lambda m: m.elastic_checkpoint()) == [False, False]
+    eb.seed.close()
