@@ -2,6 +2,9 @@
 
 #include <sys/uio.h>
 
+#include <algorithm>
+#include <cstdlib>
+
 #include <arpa/inet.h>
 #include <cerrno>
 #include <fcntl.h>
@@ -209,15 +212,44 @@ Message read_framed(int fd) {
 }
 
 // ------------------------------------------------------------------ mailbox
+namespace {
+// Spin window of a waiting pop (NEXAR_SPIN_US, default 50 us; 0 turns it off).
+std::chrono::microseconds mailbox_spin() {
+  static const std::chrono::microseconds v = [] {
+    const char* e = std::getenv("NEXAR_SPIN_US");
+    long us = e && *e ? std::strtol(e, nullptr, 10) : 50;
+    return std::chrono::microseconds(us < 0 ? 0 : us);
+  }();
+  return v;
+}
+
+inline void cpu_relax() {
+#if defined(__x86_64__) || defined(__i386__)
+  __builtin_ia32_pause();
+#endif
+}
+}  // namespace
+
+void Mailbox::spin_until_changed(uint64_t seen, Clock::time_point until) const {
+  for (uint32_t i = 1; version_.load(std::memory_order_acquire) == seen; ++i) {
+    cpu_relax();
+    if ((i & 63) == 0 && Clock::now() >= until) return;
+  }
+}
+
 void Mailbox::push(const LaneKey& k, Item it) {
+  bool wake;
   {
     std::lock_guard<std::mutex> g(mu_);
     lanes_[k].push_back(std::move(it));
+    version_.fetch_add(1, std::memory_order_release);
+    wake = waiters_ > 0;
   }
-  cv_.notify_all();
+  if (wake) cv_.notify_all();
 }
 
 Item Mailbox::pop(const LaneKey& k, Clock::time_point deadline) {
+  const auto spin_end = std::min(deadline, Clock::now() + mailbox_spin());
   std::unique_lock<std::mutex> lk(mu_);
   while (true) {
     auto it = lanes_.find(k);
@@ -228,7 +260,17 @@ Item Mailbox::pop(const LaneKey& k, Clock::time_point deadline) {
       return v;
     }
     if (closed_) fail(close_code_, close_msg_);
-    if (cv_.wait_until(lk, deadline) == std::cv_status::timeout) {
+    if (Clock::now() < spin_end) {
+      const uint64_t seen = version_.load(std::memory_order_acquire);
+      lk.unlock();
+      spin_until_changed(seen, spin_end);
+      lk.lock();
+      continue;
+    }
+    ++waiters_;
+    const auto st = cv_.wait_until(lk, deadline);
+    --waiters_;
+    if (st == std::cv_status::timeout) {
       auto it2 = lanes_.find(k);
       if (it2 != lanes_.end() && !it2->second.empty()) continue;
       if (closed_) fail(close_code_, close_msg_);
@@ -239,6 +281,7 @@ Item Mailbox::pop(const LaneKey& k, Clock::time_point deadline) {
 
 Item Mailbox::pop_data(uint32_t tag, Clock::time_point deadline) {
   const LaneKey k{LaneKind::Data, 0, 0};
+  const auto spin_end = std::min(deadline, Clock::now() + mailbox_spin());
   std::unique_lock<std::mutex> lk(mu_);
   while (true) {
     auto it = lanes_.find(k);
@@ -253,7 +296,17 @@ Item Mailbox::pop_data(uint32_t tag, Clock::time_point deadline) {
       }
     }
     if (closed_) fail(close_code_, close_msg_);
-    if (cv_.wait_until(lk, deadline) == std::cv_status::timeout) {
+    if (Clock::now() < spin_end) {
+      const uint64_t seen = version_.load(std::memory_order_acquire);
+      lk.unlock();
+      spin_until_changed(seen, spin_end);
+      lk.lock();
+      continue;
+    }
+    ++waiters_;
+    const auto st = cv_.wait_until(lk, deadline);
+    --waiters_;
+    if (st == std::cv_status::timeout) {
       if (closed_) fail(close_code_, close_msg_);
       fail(Err::Timeout, "timed out waiting for data (tag " + std::to_string(tag) + ") from rank " +
                              std::to_string(src_));
@@ -268,6 +321,7 @@ void Mailbox::close(Err code, const std::string& why) {
     closed_ = true;
     close_code_ = code;
     close_msg_ = why;
+    version_.fetch_add(1, std::memory_order_release);
   }
   cv_.notify_all();
 }

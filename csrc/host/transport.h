@@ -101,10 +101,17 @@ class Mailbox {
   Rank src() const { return src_; }
 
  private:
+  // Spin on version_ for a short window before sleeping on cv_: a reply
+  // that arrives within microseconds is taken without a futex sleep / wake.
+  // Returns once version_ moved away from `seen` or at `until`.
+  void spin_until_changed(uint64_t seen, Clock::time_point until) const;
+
   Rank src_;
   mutable std::mutex mu_;
   std::condition_variable cv_;
   std::map<LaneKey, std::deque<Item>> lanes_;
+  std::atomic<uint64_t> version_{0};  // bumped by every push and close
+  int waiters_ = 0;                   // threads asleep on cv_ (guarded by mu_)
   bool closed_ = false;
   Err close_code_ = Err::PeerDisconnected;
   std::string close_msg_;
