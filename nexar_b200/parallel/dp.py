@@ -15,6 +15,7 @@ all-reduce, nexar/src/collective/bucketed_allreduce.rs:23-75).
 """
 from __future__ import annotations
 
+import dataclasses
 import time
 from typing import List, Optional
 
@@ -181,3 +182,60 @@ class DataParallelTrainer:
     def release(self):
         """Drop the captured graph (call before tearing down the process group)."""
         self.graph = None
+
+    # ---------------------------------------------------------------- checkpoint / resume
+    CHECKPOINT_FORMAT = "nexar_b200.dp_trainer/1"
+
+    def state_dict(self) -> dict:
+        """Everything a resumed run needs, as CPU tensors and plain values:
+        fp32 master weights, both AdamW moments, the step counter, the learning
+        rate, the optimizer settings, the model shape and the flat layout.
+        Data-parallel ranks hold identical state, so one rank saves it."""
+        torch.cuda.synchronize(self.device)
+        flat = self.model.flat
+        return {
+            "format": self.CHECKPOINT_FORMAT,
+            "config": dataclasses.asdict(self.cfg),
+            "layout": [[e.name, list(e.shape), e.offset, e.numel] for e in flat.entries],
+            "master": flat.master.detach().cpu(),
+            "exp_avg": flat.exp_avg.detach().cpu(),
+            "exp_avg_sq": flat.exp_avg_sq.detach().cpu(),
+            "step": int(self.step_dev.item()),
+            "lr": float(self.lr_dev.item()),
+            "optim": {"betas": list(self.betas), "eps": self.eps, "weight_decay": self.wd, "grad_clip": self.clip},
+        }
+
+    def load_state_dict(self, sd: dict) -> None:
+        """Restore a :meth:`state_dict` into this trainer's buffers, in place
+        (a captured CUDA graph keeps working). The model shape and flat layout
+        must match; the bf16 working weights are re-derived from the fp32
+        master weights."""
+        if sd.get("format") != self.CHECKPOINT_FORMAT:
+            raise ValueError(f"not a {self.CHECKPOINT_FORMAT} checkpoint: {sd.get('format')!r}")
+        if sd["config"] != dataclasses.asdict(self.cfg):
+            raise ValueError(f"checkpoint is for model {sd['config']}, this trainer runs {dataclasses.asdict(self.cfg)}")
+        flat = self.model.flat
+        layout = [[e.name, list(e.shape), e.offset, e.numel] for e in flat.entries]
+        if [list(x) for x in sd["layout"]] != layout:
+            raise ValueError("checkpoint flat-parameter layout differs from this trainer's")
+        torch.cuda.synchronize(self.device)
+        flat.master.copy_(sd["master"])
+        flat.exp_avg.copy_(sd["exp_avg"])
+        flat.exp_avg_sq.copy_(sd["exp_avg_sq"])
+        flat.param_bf16.copy_(flat.master)
+        self.step_dev.fill_(int(sd["step"]))
+        self.lr_dev.fill_(float(sd["lr"]))
+        o = sd.get("optim", {})
+        self.betas = tuple(o.get("betas", self.betas))
+        self.eps = o.get("eps", self.eps)
+        self.wd = o.get("weight_decay", self.wd)
+        self.clip = o.get("grad_clip", self.clip)
+        torch.cuda.synchronize(self.device)
+
+    def save(self, path: str) -> None:
+        """Write :meth:`state_dict` to ``path`` (call on one rank)."""
+        torch.save(self.state_dict(), path)
+
+    def load(self, path: str) -> None:
+        """Read a checkpoint written by :meth:`save` (every rank loads the same file)."""
+        self.load_state_dict(torch.load(path, map_location="cpu", weights_only=True))
