@@ -9,6 +9,9 @@ names:
   gemm_rs      fused GEMM -> reduce-scatter with a one-rank communicator
                (8192 x 4096 x 1792: the epilogue stores into the rank's
                staging slot and the kernel reduces it, as on W ranks)
+  ag_gemm      fused all-gather -> GEMM with a one-rank communicator
+               (8192 x 3584 x 4096 bf16, the TP=8 gate + up projection per GPU:
+               the copy warps stage the local shard, the MMA waits on it)
   compress     top-1 % + e4m3 compression of 64 Mi bf16 values
   ln_bwd       LayerNorm backward, 8192 x 768 with the bias-gradient sums
 
@@ -70,6 +73,16 @@ def main():
         B = (0.05 * torch.randn(N, K, device=dev, generator=g)).to(torch.bfloat16)
         out = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
         ms = _time(lambda: comm.gemm_reduce_scatter(A, B, out=out), args.iters)
+        comm.check()
+        rec.update(M=M, N=N, K=K, us=round(ms * 1e3, 1), tflops=round(2 * M * N * K / ms / 1e9, 1))
+    elif args.name == "ag_gemm":
+        from nexar_b200.device import DeviceCommunicator
+        comm = DeviceCommunicator(0, 1, 0, exchange=lambda h: [h])
+        M, N, K = 8192, 14336 // 8 * 2, 4096
+        x = torch.randn(M, K, device=dev, generator=g).to(torch.bfloat16)
+        B = (0.05 * torch.randn(N, K, device=dev, generator=g)).to(torch.bfloat16)
+        out = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
+        ms = _time(lambda: comm.all_gather_gemm(x, B, out=out), args.iters)
         comm.check()
         rec.update(M=M, N=N, K=K, us=round(ms * 1e3, 1), tflops=round(2 * M * N * K / ms / 1e9, 1))
     elif args.name == "compress":
