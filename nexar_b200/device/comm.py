@@ -112,8 +112,24 @@ class GlobalPtr:
     def address(self) -> int:
         return int(self.comm.native.peer_ptr(self.rank)) + self.offset
 
+    def is_local(self, rank: Optional[int] = None) -> bool:
+        """Whether the memory is on ``rank`` (default: the communicator's own rank)."""
+        return self.rank == (self.comm.rank if rank is None else rank)
+
+    def _key(self):
+        return (id(self.comm), self.rank, self.offset, self.nbytes)
+
+    def __eq__(self, other):
+        return isinstance(other, GlobalPtr) and self._key() == other._key()
+
+    def __hash__(self):
+        return hash(self._key())
+
     def __repr__(self):
         return f"GlobalPtr(rank={self.rank}, offset={self.offset}, nbytes={self.nbytes})"
+
+    def __str__(self):  # the reference's Display: rank and address range
+        return f"rank {self.rank} [+{self.offset:#x}, {self.nbytes} bytes]"
 
 
 class DeviceCommunicator:

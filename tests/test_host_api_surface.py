@@ -115,3 +115,46 @@ def test_crate_root_exports_and_elastic_config():
     assert [c.world_size for c in eb.clients] == [2, 2]
     assert run_collective(eb.managers, lambda m: m.elastic_checkpoint()) == [False, False]
     eb.seed.close()
+
+
+def test_single_rank_bootstrap_and_collectives():
+    """nexar/src/client/bootstrap.rs test_bootstrap_single_node, sync_client.rs test_sync_client_single_node."""
+    from nexar_b200.client import NexarClient
+    (c,) = NexarClient.bootstrap_local(1)
+    a = np.arange(5, dtype=np.float32)
+    c.all_reduce_host(a)
+    assert (a == np.arange(5)).all()
+    out = np.zeros(5, np.float32)
+    c.all_gather_host(a, out)
+    assert (out == a).all()
+    c.barrier()
+    assert c.split(0, 0).world_size == 1
+    c.close()
+
+
+def test_rpc_handler_overwrite():
+    """nexar/src/rpc/registry.rs test_overwrite_handler: the last registration wins."""
+    from nexar_b200.client import NexarClient
+    cs = NexarClient.bootstrap_local(2)
+    d = cs[1].rpc_dispatcher()
+    d.register(3, lambda b: b"first")
+    d.register(3, lambda b: b"second")
+    t = threading.Thread(target=d.serve_once, args=(0, 5.0))
+    t.start()
+    assert cs[0].rpc(1, 3, b"", 5.0) == b"second"
+    t.join()
+    for c in cs:
+        c.close()
+
+
+def test_global_ptr_identity():
+    """nexar/src/memory/global_ptr.rs: construction, is_local, display, eq / hash."""
+    from nexar_b200.device.comm import GlobalPtr
+
+    class FakeComm:
+        rank = 1
+    comm = FakeComm()
+    a, b, c = GlobalPtr(comm, 1, 256, 64), GlobalPtr(comm, 1, 256, 64), GlobalPtr(comm, 2, 256, 64)
+    assert a == b and hash(a) == hash(b) and a != c and len({a, b, c}) == 2
+    assert a.is_local() and not c.is_local() and c.is_local(2)
+    assert "rank 1" in str(a) and "64 bytes" in str(a)
