@@ -233,6 +233,7 @@ void register_ops(py::module& m) {
 // ---------------------------------------------------------------- GEMM (tcgen05)
 #include "gemm_api.h"
 #include "compress_api.h"
+#include "attention_api.h"
 namespace nexar {
 void op_gemm(const at::Tensor& A, const at::Tensor& B, const at::Tensor& C, const c10::optional<at::Tensor>& bias,
              const c10::optional<at::Tensor>& residual, const c10::optional<at::Tensor>& pre, int64_t act,
@@ -404,6 +405,48 @@ void register_gemm_ops(py::module& m) {
                               stream_of(out)),
         "decompress_accumulate");
     count_launch(1);
+  });
+  // ---- self-attention (head dimension 64, tcgen05): qkv [B*T, 3C] -> y [B*T, C]
+  m.def("attn_supported", [](int64_t B, int64_t T, int64_t H, int64_t hd) {
+    return attention_supported((int)B, (int)T, (int)H, (int)hd);
+  });
+  m.def("attn_bwd_workspace_floats", [](int64_t B, int64_t T, int64_t H) {
+    return (int64_t)attention_bwd_workspace_floats((int)B, (int)T, (int)H);
+  });
+  m.def("attn_fwd", [](const at::Tensor& qkv, const at::Tensor& y, const at::Tensor& lse, int64_t B, int64_t T,
+                       int64_t H, bool causal) {
+    need_bf16(qkv, "qkv");
+    need_bf16(y, "y");
+    need_f32(lse, "lse");
+    TORCH_CHECK(attention_supported((int)B, (int)T, (int)H, 64), "attn_fwd: needs head dim 64 and T % 128 == 0");
+    const int64_t C = H * 64;
+    TORCH_CHECK(qkv.numel() == B * T * 3 * C && y.numel() == B * T * C && lse.numel() == B * H * T,
+                "attn_fwd: shape mismatch");
+    c10::cuda::CUDAGuard g(qkv.get_device());
+    chk(attention_fwd(bf(qkv), bf(y), lse.data_ptr<float>(), (int)B, (int)T, (int)H, causal, stream_of(qkv)),
+        "attn_fwd");
+    count_launch(1);
+  });
+  m.def("attn_bwd", [](const at::Tensor& qkv, const at::Tensor& y, const at::Tensor& dy, const at::Tensor& lse,
+                       const at::Tensor& dqkv, const at::Tensor& ws, int64_t B, int64_t T, int64_t H, bool causal) {
+    need_bf16(qkv, "qkv");
+    need_bf16(y, "y");
+    need_bf16(dy, "dy");
+    need_bf16(dqkv, "dqkv");
+    need_f32(lse, "lse");
+    need_f32(ws, "ws");
+    TORCH_CHECK(attention_supported((int)B, (int)T, (int)H, 64), "attn_bwd: needs head dim 64 and T % 128 == 0");
+    const int64_t C = H * 64;
+    TORCH_CHECK(qkv.numel() == B * T * 3 * C && dqkv.numel() == qkv.numel() && y.numel() == B * T * C &&
+                    dy.numel() == y.numel() && lse.numel() == B * H * T,
+                "attn_bwd: shape mismatch");
+    TORCH_CHECK(ws.numel() >= (int64_t)attention_bwd_workspace_floats((int)B, (int)T, (int)H),
+                "attn_bwd: workspace too small");
+    c10::cuda::CUDAGuard g(qkv.get_device());
+    chk(attention_bwd(bf(qkv), bf(y), bf(dy), lse.data_ptr<float>(), bf(dqkv), ws.data_ptr<float>(), (int)B,
+                      (int)T, (int)H, causal, stream_of(qkv)),
+        "attn_bwd");
+    count_launch(3);
   });
 }
 }  // namespace nexar

@@ -8,7 +8,9 @@ Kernels per layer: fused residual-add (+ the residual branch's bias) +
 LayerNorm (its backward also yields that bias's gradient), QKV / proj / FC /
 FC-proj GEMMs on the tcgen05 kernel (forward K-major; backward reads dY^T,
 X^T and W as MN-major operands, split-K for the weight gradients; bias and
-GELU fused into the FC epilogue), causal flash attention (torch SDPA). The
+GELU fused into the FC epilogue), causal flash attention: torch SDPA by
+default, the tcgen05 attention kernels of nexar_b200 with
+NEXAR_ATTENTION=nexar (or own_attention=True; T a multiple of 128). The
 head is the tied embedding GEMM followed by the fused softmax-cross-entropy
 kernel that writes its gradient in place of the logits. Weight gradients
 are stored straight into the flat gradient buffer (no zero-fill, no
@@ -17,6 +19,7 @@ per-parameter accumulation).
 from __future__ import annotations
 
 import math
+import os
 from dataclasses import dataclass
 from typing import Dict, List, Optional, Tuple
 
@@ -65,9 +68,13 @@ def param_specs(cfg: GPT2Config) -> List[Tuple[str, Tuple[int, ...], bool]]:
 
 
 class GPT2(torch.nn.Module):
-    def __init__(self, cfg: GPT2Config, device, grad_alloc=None, seed: int = 0):
+    def __init__(self, cfg: GPT2Config, device, grad_alloc=None, seed: int = 0,
+                 own_attention: Optional[bool] = None):
         super().__init__()
         self.cfg = cfg
+        if own_attention is None:
+            own_attention = os.environ.get("NEXAR_ATTENTION", "sdpa") == "nexar"
+        self.own_attention = bool(own_attention)
         self.flat = FlatParams(param_specs(cfg), device, grad_alloc=grad_alloc)
         self._init_weights(seed)
         self.p: Dict[str, torch.nn.Parameter] = self.flat.params()
@@ -105,11 +112,14 @@ class GPT2(torch.nn.Module):
         for l in range(cfg.n_layer):
             q = f"h{l}."
             qkv = ops.linear(h, p[q + "attn.w"], p[q + "attn.b"])
-            qkv = qkv.view(B, T, 3, H, hd)
-            qh, kh, vh = qkv.unbind(2)
-            y = F.scaled_dot_product_attention(qh.transpose(1, 2), kh.transpose(1, 2), vh.transpose(1, 2),
-                                               is_causal=True)
-            y = y.transpose(1, 2).reshape(B * T, C)
+            if self.own_attention and ops.attention_supported(B, T, H, hd):
+                y = ops.attention(qkv, B, T, H, causal=True)
+            else:
+                qkv = qkv.view(B, T, 3, H, hd)
+                qh, kh, vh = qkv.unbind(2)
+                y = F.scaled_dot_product_attention(qh.transpose(1, 2), kh.transpose(1, 2), vh.transpose(1, 2),
+                                                   is_causal=True)
+                y = y.transpose(1, 2).reshape(B * T, C)
             # projection bias is folded into the residual add of the next LayerNorm
             a = ops.linear(y, p[q + "proj.w"])
             x, h = ops.residual_layer_norm(x, a, p[q + "ln2.w"], p[q + "ln2.b"], cfg.ln_eps, rbias=p[q + "proj.b"])

@@ -313,6 +313,50 @@ def swiglu(gu):
     return _SwiGLU.apply(gu)
 
 
+class _Attention(torch.autograd.Function):
+    """Multi-head self-attention on the tcgen05 kernels (head dimension 64).
+
+    qkv: [B*T, 3C] bf16 ([B, T, 3, H, 64] flattened, the QKV projection's
+    output); returns y [B*T, C] bf16 ([B, T, H, 64]). The forward saves the
+    per-row log-sum-exp; the backward recomputes the probabilities from it and
+    writes the gradient of qkv in one buffer."""
+
+    @staticmethod
+    def forward(ctx, qkv, B: int, T: int, H: int, causal: bool):
+        qkv = qkv.contiguous()
+        C = H * 64
+        y = torch.empty(B * T, C, dtype=qkv.dtype, device=qkv.device)
+        lse = torch.empty(B * H * T, dtype=torch.float32, device=qkv.device)
+        _native.cuda().attn_fwd(qkv, y, lse, B, T, H, causal)
+        ctx.save_for_backward(qkv, y, lse)
+        ctx.shape = (B, T, H, causal)
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        qkv, y, lse = ctx.saved_tensors
+        B, T, H, causal = ctx.shape
+        C = _native.cuda()
+        dqkv = torch.empty_like(qkv)
+        ws = _SCRATCH.get((qkv.device, "attn_ws"))
+        need = C.attn_bwd_workspace_floats(B, T, H)
+        if ws is None or ws.numel() < need:
+            ws = torch.empty(need, dtype=torch.float32, device=qkv.device)
+            _SCRATCH[(qkv.device, "attn_ws")] = ws
+        C.attn_bwd(qkv, y, dy.contiguous(), lse, dqkv, ws, B, T, H, causal)
+        return dqkv, None, None, None, None
+
+
+def attention_supported(B: int, T: int, H: int, head_dim: int) -> bool:
+    """Shapes the tcgen05 attention kernels take: head dimension 64, T a multiple of 128."""
+    return bool(_native.cuda().attn_supported(B, T, H, head_dim))
+
+
+def attention(qkv, B: int, T: int, H: int, causal: bool = True):
+    """softmax(Q K^T / 8 [+ causal mask]) V for every head of qkv [B*T, 3C]; returns [B*T, C]."""
+    return _Attention.apply(qkv, B, T, H, causal)
+
+
 class _Embedding(torch.autograd.Function):
     @staticmethod
     def forward(ctx, tok, wte, wpe):
