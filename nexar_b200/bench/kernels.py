@@ -12,6 +12,9 @@ names:
   ag_gemm      fused all-gather -> GEMM with a one-rank communicator
                (8192 x 3584 x 4096 bf16, the TP=8 gate + up projection per GPU:
                the copy warps stage the local shard, the MMA waits on it)
+  attn         causal self-attention forward + backward of one GPT-2 layer
+               (B 8, T 1024, 12 heads of 64) on the tcgen05 kernels, with the
+               same on torch SDPA (cuDNN) for comparison
   compress     top-1 % + e4m3 compression of 64 Mi bf16 values
   ln_bwd       LayerNorm backward, 8192 x 768 with the bias-gradient sums
 
@@ -85,6 +88,27 @@ def main():
         ms = _time(lambda: comm.all_gather_gemm(x, B, out=out), args.iters)
         comm.check()
         rec.update(M=M, N=N, K=K, us=round(ms * 1e3, 1), tflops=round(2 * M * N * K / ms / 1e9, 1))
+    elif args.name == "attn":
+        Bn, T, Hn = 8, 1024, 12
+        Cn = Hn * 64
+        qkv = torch.randn(Bn * T, 3 * Cn, device=dev, generator=g).to(torch.bfloat16).requires_grad_(True)
+        dy = torch.randn(Bn * T, Cn, device=dev, generator=g).to(torch.bfloat16)
+
+        def ours():
+            y = ops.attention(qkv, Bn, T, Hn, causal=True)
+            y.backward(dy)
+
+        def sdpa():
+            x = qkv.view(Bn, T, 3, Hn, 64)
+            q, k, v = (t.transpose(1, 2) for t in x.unbind(2))
+            y = torch.nn.functional.scaled_dot_product_attention(q, k, v, is_causal=True)
+            y.transpose(1, 2).reshape(Bn * T, Cn).backward(dy)
+
+        ms = _time(ours, args.iters)
+        ms_ref = _time(sdpa, args.iters)
+        flops = 3.5 * 4 * Bn * Hn * T * T * 64 / 2  # fwd (1) + bwd (2.5) x causal half
+        rec.update(B=Bn, T=T, H=Hn, us=round(ms * 1e3, 1), tflops=round(flops / ms / 1e9, 1),
+                   sdpa_us=round(ms_ref * 1e3, 1), sdpa_tflops=round(flops / ms_ref / 1e9, 1))
     elif args.name == "compress":
         n = 64 << 20
         grad = torch.randn(n, device=dev, generator=g).to(torch.bfloat16)
