@@ -5,7 +5,7 @@ all_gather and reduce_scatter; every rank must equal the elementwise sum),
 timed over message sizes.
 
     python -m nexar_b200.bench.cpu_ring [--ranks 4] [--min-bytes 4096] [--max-bytes 67108864]
-                                        [--iters 20] [--warmup 3] [--dtype f32|bf16] [--out sweep.jsonl]
+                                        [--iters 20] [--warmup 3] [--dtype f32|bf16] [--tls] [--out sweep.jsonl]
 
 One thread per rank in one process (as the reference's tests and this
 config). Each size: a barrier, ``iters`` back-to-back calls per rank, the
@@ -120,12 +120,14 @@ def main():
     ap.add_argument("--ops", default="all_reduce,all_gather,reduce_scatter")
     ap.add_argument("--dtype", default="f32", choices=["f32", "bf16"])
     ap.add_argument("--out", default=None)
+    ap.add_argument("--tls", action="store_true", help="mutually authenticated TLS 1.3 on every mesh link")
     args = ap.parse_args()
-    from nexar_b200.client import NexarClient
-    clients = NexarClient.bootstrap_local(args.ranks)
+    from nexar_b200.client import Config, NexarClient
+    clients = NexarClient.bootstrap_local(args.ranks, Config(tls=True) if args.tls else None)
     out = open(args.out, "w") if args.out else None
     try:
-        print(json.dumps({"config": "cpu_ring", "ranks": args.ranks, "correct": check_config(clients)}), flush=True)
+        print(json.dumps({"config": "cpu_ring", "ranks": args.ranks, "tls": args.tls,
+                          "correct": check_config(clients)}), flush=True)
         size = args.min_bytes
         while size <= args.max_bytes:
             for op in args.ops.split(","):
