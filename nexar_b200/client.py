@@ -518,6 +518,23 @@ class NexarClient:
             self._device.attach_nccl(nccl_group_for_client(self, device=self._device.device))
         return self._device
 
+    def reattach_device(self, old=None, device: Optional[int] = None, nccl: Optional[bool] = None, **kw):
+        """Device communicator for a rebuilt client (after ``rebuild_excluding``
+        / ``rebuild_adding``, a recovery or an elastic resize): closes ``old``
+        (the parent's DeviceCommunicator: its mappings of departed ranks go
+        away) and maps the heaps of this client's ranks. Every rank of this
+        client calls it together. ``device`` and ``nccl`` default to the old
+        communicator's settings. A job that relies on recovery keeps NVLS off
+        (``NEXAR_NVLS=0``): a multicast object whose member died cannot be
+        unbound safely."""
+        if old is not None:
+            if device is None:
+                device = old.device
+            if nccl is None:
+                nccl = old.nccl is not None
+            old.close()
+        return self.attach_device(device, nccl=bool(nccl), **kw)
+
     @property
     def device(self):
         if self._device is None:

@@ -246,6 +246,26 @@ class DeviceCommunicator:
         return self._comm
 
     # ----------------------------------------------------------- status
+    def close(self):
+        """Release this communicator's device resources now (symmetric heap,
+        peer mappings, NVLS region) instead of at garbage collection. Every
+        rank closes together; tensors from ``symmetric_empty`` must not be
+        used afterwards. The recovery and elastic paths close the old
+        communicator before attaching one over the rebuilt client
+        (``NexarClient.reattach_device``)."""
+        if self._comm is None:
+            return
+        torch.cuda.synchronize(self.device)
+        if self._nccl is not None:
+            self._nccl.destroy()
+            self._nccl = None
+        self._side_stream = None
+        self._comm = None
+
+    @property
+    def closed(self) -> bool:
+        return self._comm is None
+
     def check(self):
         """Raise CollectiveFailed if any device wait of this communicator timed out."""
         st = self._comm.status()
