@@ -1,7 +1,7 @@
 """TP Llama-MLP block step: fused all-gather->GEMM / GEMM->reduce-scatter kernels
 vs NCCL + cuBLAS (TP=8, d=4096, ffn=14336, 8192 tokens).
 
-    torchrun --nproc-per-node N --master-addr 127.0.0.1 -m nexar_b200.bench.tp_mlp [--tokens 8192]
+    torchrun --nproc-per-node N --master-addr 127.0.0.1 -m nexar_b200.bench.tp_mlp [--tokens 8192] [--train]
 
 Also times each fused kernel alone against its roofline: the slower of
 (FLOPs at the measured bf16 GEMM peak) and (bytes that must cross NVLink at
@@ -21,6 +21,7 @@ def main():
     ap.add_argument("--tokens", type=int, default=8192)
     ap.add_argument("--iters", type=int, default=30)
     ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--train", action="store_true", help="also time forward + backward (train_step)")
     args = ap.parse_args()
     import torch
     import torch.distributed as dist
@@ -75,7 +76,20 @@ def main():
     peak = peaks["bf16_tflops"] * 1e12
     roof_ag = max(flops_ag / peak, bytes_ag / link if W > 1 else 0) * 1e3
     roof_rs = max(flops_rs / peak, bytes_rs / link if W > 1 else 0) * 1e3
+    ms_train = ms_train_base = None
+    if args.train:
+        dy = torch.randn_like(x)
+        ms_train = timeit(lambda: mlp.train_step(x, dy))
+        ms_train_base = timeit(lambda: mlp.train_step_baseline(x, dy))
     comm.check()
+    if rank == 0 and args.train:
+        print(json.dumps({
+            "bench": "tp_llama_mlp_train_step", "n_gpus": W, "tokens": T, "d": d, "ffn": F, "dtype": "bf16",
+            "ms_fused": round(ms_train, 4), "ms_nccl_cublas": round(ms_train_base, 4),
+            "speedup": round(ms_train_base / ms_train, 3),
+            "tokens_per_s_fused": round(T / (ms_train / 1e3), 1),
+            "tflops_fused": round(3 * mlp.flops() / (ms_train / 1e3) / 1e12, 1),
+        }), flush=True)
     if rank == 0:
         print(json.dumps({
             "bench": "tp_llama_mlp_fwd", "n_gpus": W, "tokens": T, "d": d, "ffn": F, "dtype": "bf16",

@@ -449,6 +449,14 @@ class DeviceCommunicator:
         self._C.all_gather_gemm(self._comm, x, B, out, afull, cnt, bias, 1 if act == "gelu" else 0, pre, float(alpha))
         return out
 
+    def gathered(self, M: int, K: int) -> torch.Tensor:
+        """The gathered [M, K] input of the last ``all_gather_gemm`` of that
+        shape (its local workspace; valid until the next call of the shape)."""
+        ws = getattr(self, "_ag_ws", {}).get((M, K))
+        if ws is None:
+            raise RuntimeError(f"no all_gather_gemm of shape [{M}, {K}] has run on this communicator")
+        return ws[0].view(M, K)
+
     def _ag_workspace(self, M: int, K: int, device):
         key = (M, K)
         ws = getattr(self, "_ag_ws", None)

@@ -8,6 +8,12 @@ row-parallel down projection ([d, F/W] per rank) runs as one fused
 GEMM->reduce-scatter kernel. `forward_baseline` is the same block with NCCL
 collectives and cuBLAS GEMMs (the comparator).
 
+`train_step` runs forward and backward (nexar_b200.parallel.tensor): the
+backward reuses the fused kernels (all-gather -> GEMM for the input
+gradient of the down projection, GEMM -> reduce-scatter for the block's input
+gradient) and reads the weight-gradient GEMM operands MN-major;
+`train_step_baseline` is its NCCL + cuBLAS comparator.
+
 `forward_fp8` is the block-scaled fp8 variant of config 4: weights are kept
 as e4m3 with 128x128 block scales; the input shard is quantised per 1x128
 block, all-gathered as fp8 bytes + fp32 scales (half the NVLink bytes of
@@ -79,6 +85,47 @@ class TPLlamaMLP:
         gu = ops.matmul_fp8(xq_full, xs_full, wuq, wus)             # [T, 2F/W]
         hq, hs = ops.swiglu_quant_fp8(gu)                          # [T, F/W] e4m3
         return self.comm.gemm_fp8_reduce_scatter(hq, hs, wdq, wds)  # [T/W, d]
+
+    def train_step(self, x_shard: torch.Tensor, dy_shard: torch.Tensor):
+        """Forward and backward of the block on the fused kernels
+        (nexar_b200.parallel.tensor): returns (y_shard, dx_shard, dw_gu, dw_down)."""
+        from ..parallel.tensor import DeviceTP, tp_mlp
+        xs = x_shard.detach().requires_grad_(True)
+        wg = self.w_up.detach().requires_grad_(True)
+        wd = self.w_down.detach().requires_grad_(True)
+        y = tp_mlp(xs, wg, wd, DeviceTP(self.comm))
+        y.backward(dy_shard)
+        return y.detach(), xs.grad, wg.grad, wd.grad
+
+    def train_step_baseline(self, x_shard: torch.Tensor, dy_shard: torch.Tensor, group=None):
+        """The same forward and backward with NCCL all-gather / reduce-scatter and cuBLAS GEMMs."""
+        import torch.distributed as dist
+        T, d, F = self.cfg.tokens, self.cfg.d_model, self.F
+
+        def ag(t):
+            full = torch.empty(T, t.shape[1], dtype=t.dtype, device=t.device)
+            dist.all_gather_into_tensor(full, t.contiguous(), group=group)
+            return full
+
+        def rs(t):
+            out = torch.empty(T // self.W, t.shape[1], dtype=t.dtype, device=t.device)
+            dist.reduce_scatter_tensor(out, t.contiguous(), group=group)
+            return out
+
+        xf = ag(x_shard)
+        gu = torch.matmul(xf, self.w_up.t())
+        g, u = gu[:, :F], gu[:, F:]
+        sg = torch.sigmoid(g)
+        silu = g * sg
+        h = silu * u
+        y = rs(torch.matmul(h, self.w_down.t()))
+        dyf = ag(dy_shard)
+        dh = torch.matmul(dyf, self.w_down)
+        dw_down = torch.matmul(dyf.t(), h)
+        dgu = torch.cat([dh * u * (sg * (1 + g * (1 - sg))), dh * silu], dim=1)
+        dx = rs(torch.matmul(dgu, self.w_up))
+        dw_gu = torch.matmul(dgu.t(), xf)
+        return y, dx, dw_gu, dw_down
 
     def forward_baseline(self, x_shard: torch.Tensor, group=None) -> torch.Tensor:
         """Same block with NCCL all_gather / reduce_scatter and cuBLAS GEMMs."""
