@@ -74,8 +74,54 @@ _AR_ALGO_NAMES = {0: "local", 1: "one_shot", 2: "two_shot", 3: "nvls_staged", 4:
                   5: "two_shot_in_place"}
 
 
+_TIMING = os.environ.get("NEXAR_COMM_TIMING", "0") == "1"
+
+
+class DeviceTimeHistogram:
+    """Device time of every collective call, from CUDA events recorded around
+    the launch on its stream and read back lazily (no synchronisation on the
+    call path). Buckets are counts of calls up to each bound in microseconds
+    (the last bucket is everything above the largest bound)."""
+
+    EDGES_US = (10, 30, 100, 300, 1000, 3000, 10000)
+
+    def __init__(self):
+        self.pending: list = []
+        self.per_op: dict = {}
+
+    def record(self, op: str, start, end):
+        self.pending.append((op, start, end))
+
+    def resolve(self):
+        keep = []
+        for op, start, end in self.pending:
+            if not end.query():
+                keep.append((op, start, end))
+                continue
+            us = start.elapsed_time(end) * 1e3
+            h = self.per_op.setdefault(op, {"count": 0, "total_us": 0.0, "min_us": float("inf"), "max_us": 0.0,
+                                            "buckets": [0] * (len(self.EDGES_US) + 1)})
+            h["count"] += 1
+            h["total_us"] += us
+            h["min_us"] = min(h["min_us"], us)
+            h["max_us"] = max(h["max_us"], us)
+            b = 0
+            while b < len(self.EDGES_US) and us > self.EDGES_US[b]:
+                b += 1
+            h["buckets"][b] += 1
+        self.pending = keep
+
+    def summary(self) -> dict:
+        self.resolve()
+        out = {}
+        for op, h in self.per_op.items():
+            out[op] = dict(h, mean_us=h["total_us"] / h["count"], bucket_edges_us=list(self.EDGES_US))
+        return out
+
+
 def _observed(op: str):
-    """Count calls and bytes per collective; NVTX range around it with NEXAR_NVTX=1."""
+    """Count calls and bytes per collective; NVTX range around it with NEXAR_NVTX=1;
+    device time per call with NEXAR_COMM_TIMING=1 (``stats()["device_time"]``)."""
     def deco(fn):
         @functools.wraps(fn)
         def wrapper(self, *args, **kwargs):
@@ -86,9 +132,17 @@ def _observed(op: str):
                 st["bytes"] += t.numel() * t.element_size()
             if _NVTX:
                 torch.cuda.nvtx.range_push(f"nexar.{op}")
+            timed = self._timer is not None and not torch.cuda.is_current_stream_capturing()
+            if timed:
+                ev0 = torch.cuda.Event(enable_timing=True)
+                ev0.record()
             try:
                 return fn(self, *args, **kwargs)
             finally:
+                if timed:
+                    ev1 = torch.cuda.Event(enable_timing=True)
+                    ev1.record()
+                    self._timer.record(op, ev0, ev1)
                 if _NVTX:
                     torch.cuda.nvtx.range_pop()
                 if op == "all_reduce":
@@ -178,6 +232,7 @@ class DeviceCommunicator:
         self._C = C
         self._stats = {}
         self._nccl = None
+        self._timer = DeviceTimeHistogram() if _TIMING else None
 
     # ----------------------------------------------------------- construction
     @classmethod
@@ -279,9 +334,19 @@ class DeviceCommunicator:
         return self._comm.status()
 
     def stats(self) -> dict:
-        """Per-collective call and byte counts, and how often each all-reduce algorithm ran."""
+        """Per-collective call and byte counts, how often each all-reduce
+        algorithm ran and, with timing on, each collective's device-time
+        histogram (``device_time``)."""
         import copy
-        return copy.deepcopy(self._stats)
+        out = copy.deepcopy(self._stats)
+        if self._timer is not None:
+            out["device_time"] = self._timer.summary()
+        return out
+
+    def enable_timing(self, on: bool = True):
+        """Record the device time of every collective call from now on
+        (``NEXAR_COMM_TIMING=1`` turns it on at construction)."""
+        self._timer = (self._timer or DeviceTimeHistogram()) if on else None
 
     def clear_status(self):
         self._comm.clear_status()
