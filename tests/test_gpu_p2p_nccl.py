@@ -103,3 +103,53 @@ def test_nccl_group_two_gpus_ring():
     torch.testing.assert_close(got1, x0, rtol=0, atol=0)
     torch.testing.assert_close(s0, x0 + x1, rtol=1e-6, atol=1e-6)
     torch.testing.assert_close(s1, s0, rtol=0, atol=0)
+
+
+def test_pipeline_1f1b_two_gpus():
+    """Two pipeline stages on two GPUs, activations and gradients over NCCL p2p,
+    against the whole model on the CPU (fp32)."""
+    if gpu_count() < 2:
+        pytest.skip("needs two GPUs")
+    import copy
+
+    from helpers_host import bootstrap, run_collective
+    from nexar_b200.parallel.pipeline import NcclP2P, run_1f1b
+    d, rows, M = 64, 16, 5
+    torch.manual_seed(0)
+    stages = [torch.nn.Sequential(torch.nn.Linear(d, d), torch.nn.Tanh()) for _ in range(2)]
+    ref = copy.deepcopy(stages)
+    g = torch.Generator().manual_seed(1)
+    mbs = [torch.randn(rows, d, generator=g) for _ in range(M)]
+    tgts = [torch.randn(rows, d, generator=g) for _ in range(M)]
+    whole = torch.nn.Sequential(*ref)
+    ref_losses = []
+    for x, t in zip(mbs, tgts):
+        loss = ((whole(x) - t) ** 2).mean()
+        loss.backward()
+        ref_losses.append(float(loss.detach()))
+
+    clients = bootstrap(2)
+
+    def go(c):
+        torch.cuda.set_device(c.rank)
+        dev = torch.device("cuda", c.rank)
+        grp = nccl.nccl_group_for_client(c, device=c.rank)
+        mod = stages[c.rank].to(dev)
+        inputs = [x.to(dev) for x in mbs] if c.rank == 0 else [None] * M
+        tg = [t.to(dev) for t in tgts]
+        losses = run_1f1b(mod, NcclP2P(grp), inputs, (rows, d), torch.float32,
+                          loss_fn=lambda y, i: ((y - tg[i]) ** 2).mean())
+        torch.cuda.synchronize(dev)
+        grads = [p.grad.cpu() for p in mod.parameters()]
+        grp.destroy()
+        return losses, grads
+
+    try:
+        out = run_collective(clients, go, timeout=120)
+    finally:
+        for c in clients:
+            c.close()
+    assert out[1][0] == pytest.approx(ref_losses, rel=1e-4, abs=1e-5)
+    for s in range(2):
+        for got, p in zip(out[s][1], ref[s].parameters()):
+            torch.testing.assert_close(got, p.grad, rtol=1e-4, atol=1e-5)
