@@ -526,6 +526,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_route", &moe_route_op);
   m.def("moe_dispatch", &moe_dispatch_op);
   m.def("moe_combine", &moe_combine_op);
+  m.def("moe_dispatch_rows", &moe_dispatch_rows_op, py::arg("comm"), py::arg("g"), py::arg("slot_expert"),
+        py::arg("slot_pos"), py::arg("slot_scale"), py::arg("dst"), py::arg("ticket"));
   m.def("all_gather_gemm", &ag_gemm);
   m.def("gemm_fp8_reduce_scatter", &gemm_fp8_rs);
   register_ops(m);

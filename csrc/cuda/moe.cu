@@ -169,6 +169,64 @@ __global__ void __launch_bounds__(kMoeThreads) k_moe_dispatch(CommDev c, const _
   finish_call(c, call);
 }
 
+// Backward of combine (one warp per slot): slot (t, k) stores scale[slot] *
+// g[t] into global row slot_pos[slot] of expert slot_expert[slot]'s buffer
+// (rows already placed by the forward dispatch; -1 = dropped, skipped), then
+// the same "dispatch done" handshake as k_moe_dispatch.
+__global__ void __launch_bounds__(kMoeThreads) k_moe_dispatch_rows(CommDev c, const __nv_bfloat16* __restrict__ g,
+                                                                   int T, int d, const int* __restrict__ slot_expert,
+                                                                   const int* __restrict__ slot_pos,
+                                                                   const float* __restrict__ slot_scale,
+                                                                   unsigned long long dst_off, int capacity,
+                                                                   unsigned int* ticket) {
+  const unsigned long long call = call_index(c);
+  const unsigned long long epoch = epoch_of(call, 0);
+  const int lane = threadIdx.x & 31;
+  const int warps = gridDim.x * (kMoeThreads / 32);
+  const int packs = d / 8;
+  for (int slot = (blockIdx.x * kMoeThreads + threadIdx.x) >> 5; slot < 2 * T; slot += warps) {
+    const int e = slot_expert[slot];
+    const int pos = slot_pos[slot];
+    if (pos < 0 || pos >= capacity || e < 0 || e >= c.world) continue;
+    const float sc = slot_scale ? slot_scale[slot] : 1.f;
+    const __nv_bfloat16* src = g + (size_t)(slot >> 1) * d;
+    __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(c.peer_base[e] + dst_off) + (size_t)pos * d;
+    for (int i = lane; i < packs; i += 32) {
+      const uint4 a = ld16(src + i * 8);
+      const __nv_bfloat162* ha = reinterpret_cast<const __nv_bfloat162*>(&a);
+      uint4 r;
+      __nv_bfloat162* hr = reinterpret_cast<__nv_bfloat162*>(&r);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float2 f = __bfloat1622float2(ha[k]);
+        hr[k] = __floats2bfloat162_rn(sc * f.x, sc * f.y);
+      }
+      st16(dst + i * 8, r);
+    }
+  }
+  __syncthreads();
+  __shared__ unsigned int t;
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    t = atomicAdd(ticket, 1u);
+  }
+  __syncthreads();
+  if (t == gridDim.x - 1) {
+    if (threadIdx.x == 0) {
+      *ticket = 0u;
+      fence_sys();
+    }
+    __syncthreads();
+    if ((int)threadIdx.x < c.world) {
+      const int p = threadIdx.x;
+      st_release_sys(moe_flag(c, p, kMoeDispatchDoneOff, c.rank), epoch);
+      if (!wait_ge(moe_flag(c, c.rank, kMoeDispatchDoneOff, p), epoch, c.timeout_ns))
+        record_timeout(c, p, kOpMoeDispatch, epoch);
+    }
+  }
+  finish_call(c, call);
+}
+
 // One warp per token: out[t] = g1 * E_{e1}[pos1] + g2 * E_{e2}[pos2].
 __global__ void __launch_bounds__(kMoeThreads) k_moe_combine(CommDev c, __nv_bfloat16* __restrict__ out, int T, int d,
                                                              const int* __restrict__ slot_expert,
@@ -238,6 +296,17 @@ cudaError_t moe_dispatch(const CommDev& c, const __nv_bfloat16* x, int T, int d,
   if (blocks > 148 * 4) blocks = 148 * 4;
   k_moe_dispatch<<<blocks, kMoeThreads, 0, s>>>(c, x, T, d, slot_expert, slot_pos, counts_all, recv_off, capacity,
                                                 ticket);
+  return cudaGetLastError();
+}
+
+cudaError_t moe_dispatch_rows(const CommDev& c, const __nv_bfloat16* g, int T, int d, const int* slot_expert,
+                              const int* slot_pos, const float* slot_scale, unsigned long long dst_off, int capacity,
+                              unsigned int* ticket, cudaStream_t s) {
+  if (d % 8) return cudaErrorInvalidValue;
+  int blocks = (2 * T * 32 + kMoeThreads - 1) / kMoeThreads;
+  if (blocks > 148 * 4) blocks = 148 * 4;
+  k_moe_dispatch_rows<<<blocks, kMoeThreads, 0, s>>>(c, g, T, d, slot_expert, slot_pos, slot_scale, dst_off, capacity,
+                                                     ticket);
   return cudaGetLastError();
 }
 

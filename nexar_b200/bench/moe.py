@@ -1,7 +1,7 @@
 """Expert-parallel MoE layer forward: fused dispatch/combine kernels vs
 NCCL all_to_all_single + torch permutation + cuBLAS (the MoE benchmark configuration).
 
-    torchrun --nproc-per-node N --master-addr 127.0.0.1 -m nexar_b200.bench.moe [--tokens 16384]
+    torchrun --nproc-per-node N --master-addr 127.0.0.1 -m nexar_b200.bench.moe [--tokens 16384] [--train]
 """
 from __future__ import annotations
 
@@ -17,6 +17,7 @@ def main():
     ap.add_argument("--tokens", type=int, default=16384)
     ap.add_argument("--iters", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--train", action="store_true", help="also time forward + backward (train_step)")
     args = ap.parse_args()
     import torch
     import torch.distributed as dist
@@ -29,8 +30,10 @@ def main():
     os.environ.setdefault("NEXAR_SYMM_USER_BYTES", str(3 << 30))
     from nexar_b200.device import DeviceCommunicator
     from nexar_b200.models.moe import ExpertParallelMoE, MoEConfig
+    nbuf = 4 if args.train else 2  # receive / expert-output buffers (+ their gradients when training)
     comm = DeviceCommunicator.from_torch(slot_bytes=64 << 20,
-                                         heap_bytes=(1 << 20) + (128 << 20) + 2 * (2 * args.tokens * 2) * args.d * 2 + (64 << 20))
+                                         heap_bytes=(1 << 20) + (128 << 20) + nbuf * (2 * args.tokens * 2) * args.d * 2
+                                         + (64 << 20))
     cfg = MoEConfig(args.d, args.ffn, args.tokens)
     moe = ExpertParallelMoE(cfg, comm)
     g = torch.Generator(device=dev).manual_seed(rank)
@@ -54,6 +57,11 @@ def main():
 
     ms_fused = timeit(lambda: moe.forward(x, logits))
     ms_base = timeit(lambda: moe.forward_baseline(x, logits))
+    ms_train = ms_train_base = None
+    if args.train:
+        dout = torch.randn(cfg.tokens_per_gpu, cfg.d_model, device=dev, generator=g).to(torch.bfloat16)
+        ms_train = timeit(lambda: moe.train_step(x, logits, dout))
+        ms_train_base = timeit(lambda: moe.train_step_baseline(x, logits, dout))
     rows = torch.tensor([float(moe.last_rows)], device=dev)
     dist.all_reduce(rows)
     comm.check()
@@ -66,6 +74,15 @@ def main():
             "speedup": round(ms_base / ms_fused, 3),
             "tokens_per_s_fused": round(T / (ms_fused / 1e3), 1),
             "expert_tflops_per_gpu": round(moe.flops(rows.item() / world) / (ms_fused / 1e3) / 1e12, 1),
+        }), flush=True)
+    if rank == 0 and args.train:
+        T = cfg.tokens_per_gpu * world
+        print(json.dumps({
+            "bench": "moe_ep_layer_train_step", "n_gpus": world, "experts": world,
+            "tokens_per_gpu": cfg.tokens_per_gpu, "d": cfg.d_model, "ffn": cfg.ffn, "top_k": 2, "dtype": "bf16",
+            "ms_fused": round(ms_train, 4), "ms_nccl_torch": round(ms_train_base, 4),
+            "speedup": round(ms_train_base / ms_train, 3),
+            "tokens_per_s_fused": round(T / (ms_train / 1e3), 1),
         }), flush=True)
     dist.barrier()
     dist.destroy_process_group()

@@ -8,6 +8,10 @@ forward():          route kernel -> device all-gather of the per-expert counts
                     gate scaling and top-2 sum).
 forward_baseline(): the same layer with torch routing/permutation, NCCL
                     all_to_all_single and cuBLAS GEMMs (the comparator).
+train_step():       forward and backward (nexar_b200.parallel.expert): the
+                    output gradient goes to the experts with a gate-scaled
+                    fused dispatch, input and gate gradients come back with
+                    fused combines; train_step_baseline() is its comparator.
 """
 from __future__ import annotations
 
@@ -79,6 +83,70 @@ class ExpertParallelMoE:
         out = torch.empty_like(x)
         C.moe_combine(comm.native, out, self.slot_expert, self.slot_pos, self.slot_gate, self.eout)
         return out
+
+    def train_step(self, x: torch.Tensor, logits: torch.Tensor, dout: torch.Tensor):
+        """Forward and backward of the layer on the fused kernels
+        (nexar_b200.parallel.expert): returns a dict with out, dx, dlogits,
+        dw_up and dw_down. The first call allocates the gradient buffers in
+        symmetric memory (every rank calls it together)."""
+        from ..parallel.expert import DeviceEP, moe_train_step
+        if getattr(self, "_ep", None) is None:
+            self._ep = DeviceEP(self)
+        return moe_train_step(x, logits, dout, self.w_up, self.w_down, self._ep)
+
+    def train_step_baseline(self, x: torch.Tensor, logits: torch.Tensor, dout: torch.Tensor, group=None):
+        """The same forward and backward with torch routing / permutation, NCCL
+        all_to_all_single and cuBLAS GEMMs (the comparator)."""
+        import torch.distributed as dist
+        T, d = x.shape
+        E, F = self.E, self.cfg.ffn
+        top_v, top_i = torch.topk(logits.float(), 2, dim=-1)
+        gates = torch.softmax(top_v, dim=-1)
+        flat_e = top_i.reshape(-1)
+        order = torch.argsort(flat_e, stable=True)
+        send = x.repeat_interleave(2, dim=0)[order]
+        send_counts = torch.bincount(flat_e, minlength=E)
+        recv_counts = torch.empty_like(send_counts)
+        dist.all_to_all_single(recv_counts, send_counts, group=group)
+        sc, rc = send_counts.tolist(), recv_counts.tolist()
+
+        def a2a(t, out_rows, out_splits, in_splits):
+            out = torch.empty(out_rows, d, dtype=t.dtype, device=t.device)
+            dist.all_to_all_single(out, t.contiguous(), out_splits, in_splits, group=group)
+            return out
+
+        recv = a2a(send, sum(rc), rc, sc)
+        gu = torch.matmul(recv, self.w_up.t())
+        g, u = gu[:, :F], gu[:, F:]
+        sg = torch.sigmoid(g)
+        silu = g * sg
+        hh = silu * u
+        eo = torch.matmul(hh, self.w_down.t())
+        back = a2a(eo, 2 * T, sc, rc)
+        unperm = torch.empty_like(back)
+        unperm[order] = back
+        unperm = unperm.view(T, 2, d).float()
+        out = (unperm * gates.unsqueeze(-1)).sum(1).to(x.dtype)
+        # backward
+        df = dout.float()
+        dg = (unperm * df.unsqueeze(1)).sum(-1)                       # [T, 2]
+        d_unperm = (gates.unsqueeze(-1) * df.unsqueeze(1)).to(x.dtype).view(2 * T, d)
+        d_eo = a2a(d_unperm[order], sum(rc), rc, sc)
+        dhh = torch.matmul(d_eo, self.w_down)
+        dw_down = torch.matmul(d_eo.t(), hh)
+        dgu = torch.cat([dhh * u * (sg * (1 + g * (1 - sg))), dhh * silu], dim=1)
+        d_recv = torch.matmul(dgu, self.w_up)
+        dw_up = torch.matmul(dgu.t(), recv)
+        d_send = a2a(d_recv, 2 * T, sc, rc)
+        d_rep = torch.empty_like(d_send)
+        d_rep[order] = d_send
+        dx = d_rep.view(T, 2, d).float().sum(1).to(x.dtype)
+        c = gates[:, 0] * gates[:, 1] * (dg[:, 0] - dg[:, 1])
+        dlogits = torch.zeros(T, E, dtype=torch.float32, device=x.device)
+        ar = torch.arange(T, device=x.device)
+        dlogits[ar, top_i[:, 0]] += c
+        dlogits[ar, top_i[:, 1]] -= c
+        return {"out": out, "dx": dx, "dlogits": dlogits, "dw_up": dw_up, "dw_down": dw_down}
 
     def forward_baseline(self, x: torch.Tensor, logits: torch.Tensor, group=None) -> torch.Tensor:
         import torch.distributed as dist
