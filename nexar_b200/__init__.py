@@ -6,12 +6,14 @@ Layers:
                              (seed/worker bootstrap, tagged p2p, host collectives,
                              RPC, split, rebuild, recovery, elastic, sparse overlays).
   * ``nexar_b200.device``    DeviceCommunicator: symmetric heap over NVLink and the
-                             sm_100a peer-memory collectives.
+                             sm_100a peer-memory collectives; NcclGroup (device
+                             point-to-point over NCCL).
   * ``nexar_b200.ops``       model kernels (LayerNorm, GELU, SwiGLU, cross-entropy,
                              AdamW, tcgen05 GEMM, fused GEMM+collective kernels).
   * ``nexar_b200.models``    GPT-2, Llama MLP (TP) and MoE (EP) model definitions.
-  * ``nexar_b200.parallel``  data-parallel, tensor-parallel and expert-parallel
-                             training entry points; the hierarchical (node x
+  * ``nexar_b200.parallel``  data, tensor, expert, sequence (Ulysses), context
+                             (ring attention) and pipeline (1F1B) parallel
+                             training steps; the hierarchical (node x
                              cross-node) communicator.
   * ``nexar_b200.memory``    BufferRef<Host|Device>, the tiered host buffer pool.
 """

@@ -1,2 +1,14 @@
-"""Parallel training entry points: data (dp), tensor (tp) and expert (ep)
-parallel, and the two-level node x cross-node communicator (hierarchical)."""
+"""Parallel training entry points.
+
+  dp            data parallel (the GPT-2 trainer: bucketed gradient all-reduce
+                overlapped with backward, CUDA graph)
+  tensor        tensor parallel SwiGLU MLP step (fused all-gather -> GEMM and
+                GEMM -> reduce-scatter, forward and backward)
+  expert        expert parallel MoE step (fused dispatch / combine, forward and
+                backward)
+  sequence      Ulysses sequence parallelism (all-to-all around head-sharded
+                attention)
+  context       ring attention (context parallelism)
+  pipeline      1F1B pipeline schedule over point-to-point transfers
+  hierarchical  the two-level node x cross-node communicator
+"""
