@@ -49,9 +49,10 @@ def moe_train_step(x: torch.Tensor, logits: torch.Tensor, dout: torch.Tensor, w_
     rows = slots["rows"]
     recv = ep.dispatch(x, slots)
     eout = ep.expert_buffer()
-    gu = ep.nt(recv, w_up)
-    h = ep.swiglu(gu)
-    ep.nt(h, w_down, out=eout[:rows])
+    if rows > 0:
+        gu = ep.nt(recv, w_up)
+        h = ep.swiglu(gu)
+        ep.nt(h, w_down, out=eout[:rows])
     out = ep.combine(eout, slots, slots["gate"], T, d)
 
     first, second, ones = _gate_masks(T, x.device)
@@ -60,12 +61,15 @@ def moe_train_step(x: torch.Tensor, logits: torch.Tensor, dout: torch.Tensor, w_
     r2 = ep.combine(eout, slots, second, T, d).float()
     df = dout.float()
     dg1, dg2 = (df * r1).sum(1), (df * r2).sum(1)
-    dh = ep.nn(d_eout, w_down)
-    dw_down = ep.tn(d_eout, h)
-    dgu = ep.swiglu_bwd(gu, dh)
     d_recv = ep.grad_buffer()
-    ep.nn(dgu, w_up, out=d_recv[:rows])
-    dw_up = ep.tn(dgu, recv)
+    if rows > 0:
+        dh = ep.nn(d_eout, w_down)
+        dw_down = ep.tn(d_eout, h)
+        dgu = ep.swiglu_bwd(gu, dh)
+        ep.nn(dgu, w_up, out=d_recv[:rows])
+        dw_up = ep.tn(dgu, recv)
+    else:  # no token chose this expert
+        dw_down, dw_up = torch.zeros_like(w_down), torch.zeros_like(w_up)
     dx = ep.combine(d_recv, slots, ones, T, d)
 
     gate = slots["gate"].float()
