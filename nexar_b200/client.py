@@ -84,38 +84,46 @@ def __getattr__(name):
     raise AttributeError(name)
 
 
-def _host_buf(x) -> Tuple[int, int, DataType]:
-    """``_buf`` for the typed ``*_host`` calls: host memory only."""
-    try:
-        import torch
-        if isinstance(x, torch.Tensor) and x.is_cuda:
-            raise TypeError("*_host calls take host buffers; use the *_device call for CUDA tensors")
-    except ImportError:  # pragma: no cover
-        pass
-    return _buf(x)
+_NP_CODES = None
 
 
-def _buf(x) -> Tuple[int, int, DataType]:
-    """(address, numel, dtype) of a contiguous numpy array or torch tensor."""
-    try:
-        import torch
-        if isinstance(x, torch.Tensor):
-            if not x.is_contiguous():
-                raise ValueError("tensor must be contiguous")
-            return x.data_ptr(), x.numel(), DataType.from_torch(x.dtype)
-    except ImportError:  # pragma: no cover
-        pass
-    import numpy as np
-    if isinstance(x, np.ndarray):
+def _np_codes():
+    """numpy dtype -> DataType (bf16 travels as raw uint16 bits)."""
+    global _NP_CODES
+    if _NP_CODES is None:
+        import numpy as np
+        _NP_CODES = {np.dtype(np.float32): DataType.F32, np.dtype(np.float64): DataType.F64,
+                     np.dtype(np.float16): DataType.F16, np.dtype(np.int8): DataType.I8,
+                     np.dtype(np.int32): DataType.I32, np.dtype(np.int64): DataType.I64,
+                     np.dtype(np.uint8): DataType.U8, np.dtype(np.uint32): DataType.U32,
+                     np.dtype(np.uint64): DataType.U64, np.dtype(np.uint16): DataType.BF16}
+    return _NP_CODES
+
+
+def _buf(x, host_only: bool = False) -> Tuple[int, int, DataType]:
+    """(address, numel, dtype) of a contiguous numpy array or torch tensor
+    (host_only: reject CUDA tensors)."""
+    iface = getattr(x, "__array_interface__", None)
+    if iface is not None and not hasattr(x, "data_ptr"):  # numpy array: the fast path
         if not x.flags["C_CONTIGUOUS"]:
             raise ValueError("array must be C-contiguous")
-        table = {np.dtype(np.float32): DataType.F32, np.dtype(np.float64): DataType.F64,
-                 np.dtype(np.float16): DataType.F16, np.dtype(np.int8): DataType.I8,
-                 np.dtype(np.int32): DataType.I32, np.dtype(np.int64): DataType.I64,
-                 np.dtype(np.uint8): DataType.U8, np.dtype(np.uint32): DataType.U32,
-                 np.dtype(np.uint64): DataType.U64, np.dtype(np.uint16): DataType.BF16}
-        return x.ctypes.data, x.size, table[x.dtype]
+        try:
+            return iface["data"][0], x.size, _np_codes()[x.dtype]
+        except KeyError:
+            raise TypeError(f"unsupported array dtype {x.dtype}") from None
+    import torch
+    if isinstance(x, torch.Tensor):
+        if host_only and x.is_cuda:
+            raise TypeError("*_host calls take host buffers; use the *_device call for CUDA tensors")
+        if not x.is_contiguous():
+            raise ValueError("tensor must be contiguous")
+        return x.data_ptr(), x.numel(), DataType.from_torch(x.dtype)
     raise TypeError(f"unsupported buffer type {type(x)}")
+
+
+def _host_buf(x) -> Tuple[int, int, DataType]:
+    """``_buf`` for the typed ``*_host`` calls: host memory only."""
+    return _buf(x, host_only=True)
 
 
 class CollectiveHandle:
