@@ -1,7 +1,8 @@
 // Native driver for a ThreadSanitizer build of the host control plane (no
 // Python): every thread below is a rank of one in-process cluster, so TSAN
 // sees the transport's router threads, the senders, the heartbeat monitor,
-// the recovery orchestrator and the TLS streams interleave for real.
+// the recovery orchestrator, the TLS streams and a device adapter shared by
+// every rank's thread interleave for real.
 //
 //   g++ -std=c++17 -O1 -g -fsanitize=thread -I csrc/host csrc/host/<runtime .cc files>
 //       csrc/host/tests/tsan_driver.cc -lssl -lcrypto -pthread -o tsan_driver
@@ -9,6 +10,7 @@
 #include <atomic>
 #include <cstdio>
 #include <cstdlib>
+#include <cstring>
 #include <functional>
 #include <thread>
 #include <vector>
@@ -104,11 +106,62 @@ void recovery() {
   for (auto& c : cs) c->close();
 }
 
+// An adapter whose buffers are not host-addressable (the staging paths of
+// every collective and of p2p run), shared by all ranks' threads; it counts
+// the bytes it stages from several threads at once.
+class CountingStagingAdapter : public DeviceAdapter {
+ public:
+  std::string name() const override { return "staging-test"; }
+  void stage_for_send(const void* ptr, size_t n, uint8_t* out) override {
+    std::memcpy(out, ptr, n);
+    staged += n;
+  }
+  void receive_to_device(const uint8_t* src, size_t n, void* ptr) override {
+    std::memcpy(ptr, src, n);
+    received += n;
+  }
+  void reduce_inplace(void* dst, const void* src, size_t count, DataType dt, ReduceOp op) override {
+    reduce_slice(dst, src, count, dt, op);
+  }
+  std::atomic<uint64_t> staged{0}, received{0};
+};
+
+void staged_collectives() {
+  Config cfg;
+  cfg.heartbeat_interval_s = 0.05;
+  auto cs = NexarClient::bootstrap_local(3, cfg);
+  auto ad = std::make_shared<CountingStagingAdapter>();
+  for (auto& c : cs) c->set_adapter(ad);
+  std::vector<std::vector<float>> bufs(3, std::vector<float>(3000));
+  run_all(cs, [&](NexarClient& c) {
+    auto& b = bufs[c.rank()];
+    for (auto& x : b) x = (float)(c.rank() + 1);
+    c.all_reduce(b.data(), b.size(), DataType::F32, ReduceOp::Sum);
+    std::vector<float> out(3 * 100), rs(1000), a2a(3 * 100);
+    c.all_gather(b.data(), out.data(), 100, DataType::F32);
+    c.reduce_scatter(b.data(), rs.data(), rs.size(), DataType::F32, ReduceOp::Sum);
+    c.all_to_all(b.data(), a2a.data(), 100, DataType::F32);
+    std::vector<float> g(c.rank() == 1 ? 300 : 0);
+    c.gather(b.data(), c.rank() == 1 ? g.data() : nullptr, 100, DataType::F32, 1);
+    c.scan(b.data(), 100, DataType::F32, ReduceOp::Sum);
+    const Rank peer = (c.rank() + 1) % 3, from = (c.rank() + 2) % 3;
+    std::vector<char> msg(4096, (char)c.rank()), got(4096);
+    std::thread tx([&] { c.send(msg.data(), msg.size(), peer, 9); });
+    c.recv(got.data(), got.size(), from, 9);
+    tx.join();
+    check(got[7] == (char)from, "staged p2p payload");
+  });
+  check(bufs[0][2000] == 6.0f, "staged all_reduce");
+  check(ad->staged.load() > 0 && ad->received.load() > 0, "adapter used");
+  for (auto& c : cs) c->close();
+}
+
 }  // namespace
 
 int main() {
   collectives(false);
   collectives(true);
+  staged_collectives();
   recovery();
   std::printf("tsan driver: ok\n");
   return 0;
