@@ -35,6 +35,8 @@ def parse():
     ap.add_argument("--seq-len", type=int, default=SEQ_LEN)
     ap.add_argument("--no-graph", action="store_true")
     ap.add_argument("--model", default="small", choices=["small", "tiny"])
+    ap.add_argument("--attention", default="sdpa", choices=["sdpa", "nexar"],
+                    help="attention kernels: torch SDPA (default) or this package's tcgen05 kernels")
     return ap.parse_args()
 
 
@@ -64,6 +66,8 @@ def main():
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}; launch N>1 with torchrun")
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
+    if args.attention == "nexar":
+        os.environ["NEXAR_ATTENTION"] = "nexar"
     if world > 1:
         from datetime import timedelta
         dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=120),
@@ -146,6 +150,7 @@ def main():
                        "global_batch": B * world, "micro_batch_per_gpu": B, "seq_len": T,
                        "parallelism": f"dp{world}", "grad_bucket_mb": 25,
                        "cuda_graph": trainer.graph is not None,
+                       "attention": "nexar tcgen05" if trainer.model.own_attention else "torch sdpa",
                        "l2": "no flush: per-step working set (weights+grads+optimizer 2 GB, activations ~5 GB) "
                              "exceeds the 126 MB L2"},
             "model_tflops_per_gpu": round(flops / world / 1e12, 1),
