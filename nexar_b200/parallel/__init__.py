@@ -2,6 +2,7 @@
 
   dp            data parallel (the GPT-2 trainer: bucketed gradient all-reduce
                 overlapped with backward, CUDA graph)
+  zero          sharded data parallel optimizer (ZeRO stage 1/2) for any module
   tensor        tensor parallel SwiGLU MLP step (fused all-gather -> GEMM and
                 GEMM -> reduce-scatter, forward and backward)
   expert        expert parallel MoE step (fused dispatch / combine, forward and
