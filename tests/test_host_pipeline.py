@@ -58,3 +58,21 @@ def test_1f1b_matches_whole_model(W, M):
     for s in range(W):
         for p, q in zip(stages[s].parameters(), ref[s].parameters()):
             torch.testing.assert_close(p.grad, q.grad, rtol=1e-10, atol=1e-12)
+
+
+def test_pipeline_dead_stage_errors_not_hangs():
+    """A stage that leaves makes its neighbour's transfer fail within the
+    collective timeout (the reference's fault-injection rule: error, not deadlock)."""
+    import time
+
+    from nexar_b200.core import NexarError
+    d, rows, M = 4, 2, 3
+    stages = _stages(2, d)
+    clients = bootstrap(2, collective_timeout_s=2.0, heartbeat_interval_s=0.1, heartbeat_timeout_s=0.5)
+    clients[1].close()
+    mbs = [torch.randn(rows, d, dtype=torch.float64) for _ in range(M)]
+    t0 = time.time()
+    with pytest.raises(NexarError):
+        run_1f1b(stages[0], HostP2P(clients[0]), mbs, (rows, d), torch.float64)
+    assert time.time() - t0 < 30
+    clients[0].close()
