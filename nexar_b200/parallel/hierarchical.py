@@ -399,6 +399,52 @@ class HierarchicalComm:
             return t
         return self._all_reduce_lead(t, op)
 
+    # The collectives below run over the flat client (host transport, CUDA
+    # tensors staged through host memory): correct for every node layout,
+    # without a two-level schedule. nexar-nccl's facade has none of them.
+    @staticmethod
+    def _to_host(t: torch.Tensor) -> torch.Tensor:
+        return t.detach().contiguous().reshape(-1).cpu() if t.is_cuda else t.contiguous().reshape(-1)
+
+    def all_to_all(self, inp: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+        """Rank r's out chunk q = rank q's inp chunk r (world_size equal chunks)."""
+        hi = self._to_host(inp)
+        ho = torch.empty_like(hi)
+        self.client.all_to_all_host(hi, ho)
+        out.view(-1).copy_(ho)
+        return out
+
+    def gather(self, inp: torch.Tensor, out: Optional[torch.Tensor], root: int = 0) -> Optional[torch.Tensor]:
+        """The root's out (world_size x inp) receives every rank's inp in rank order."""
+        hi = self._to_host(inp)
+        ho = torch.empty(hi.numel() * self.world_size, dtype=hi.dtype) if self.rank == root else None
+        self.client.gather_host(hi, ho, root)
+        if self.rank == root:
+            out.view(-1).copy_(ho)
+        return out
+
+    def scatter(self, inp: Optional[torch.Tensor], out: torch.Tensor, root: int = 0) -> torch.Tensor:
+        """Rank r's out receives chunk r of the root's inp."""
+        hi = self._to_host(inp) if self.rank == root else None
+        ho = torch.empty(out.numel(), dtype=out.dtype)
+        self.client.scatter_host(hi, ho, root)
+        out.view(-1).copy_(ho)
+        return out
+
+    def scan(self, t: torch.Tensor, op="sum") -> torch.Tensor:
+        """In place: rank r holds op over ranks 0..r."""
+        h = self._to_host(t).clone()
+        self.client.scan_host(h, ReduceOp.parse(op))
+        t.view(-1).copy_(h)
+        return t
+
+    def exclusive_scan(self, t: torch.Tensor, op="sum") -> torch.Tensor:
+        """In place: rank r holds op over ranks 0..r-1 (the identity on rank 0)."""
+        h = self._to_host(t).clone()
+        self.client.exclusive_scan_host(h, ReduceOp.parse(op))
+        t.view(-1).copy_(h)
+        return t
+
     def barrier(self):
         self.local.barrier()
         if self.topo.is_lead and self.cross.world_size > 1:

@@ -75,6 +75,25 @@ def test_hierarchical_collectives(layout):
             outs = run_collective(comms, lambda c: c.reduce(_val(c.rank, 19, 4), root))
             assert torch.equal(outs[root], sum(_val(r, 19, 4) for r in range(W))), (layout, root)
 
+        # the collectives the reference's facade lacks (carried by the flat client)
+        k = 5
+        outs = run_collective(comms, lambda c: c.all_to_all(_val(c.rank, W * k, 5), torch.empty(W * k)))
+        for r, o in enumerate(outs):
+            assert torch.equal(o, torch.cat([_val(q, W * k, 5)[r * k:(r + 1) * k] for q in range(W)])), layout
+        outs = run_collective(comms, lambda c: c.gather(_val(c.rank, k, 6), torch.empty(W * k) if c.rank == 1
+                                                        else None, root=1))
+        assert torch.equal(outs[1], torch.cat([_val(q, k, 6) for q in range(W)]))
+        outs = run_collective(comms, lambda c: c.scatter(_val(c.rank, W * k, 7) if c.rank == 2 else None,
+                                                         torch.empty(k), root=2))
+        for r, o in enumerate(outs):
+            assert torch.equal(o, _val(2, W * k, 7)[r * k:(r + 1) * k])
+        outs = run_collective(comms, lambda c: c.scan(_val(c.rank, k, 8)))
+        for r, o in enumerate(outs):
+            assert torch.equal(o, sum(_val(q, k, 8) for q in range(r + 1)))
+        outs = run_collective(comms, lambda c: c.exclusive_scan(_val(c.rank, k, 9)))
+        assert torch.equal(outs[0], torch.zeros(k))
+        assert torch.equal(outs[W - 1], sum(_val(q, k, 9) for q in range(W - 1)))
+
         run_collective(comms, lambda c: c.barrier())
     finally:
         for c in clients:
