@@ -2,6 +2,8 @@
 
   dp            data parallel (the GPT-2 trainer: bucketed gradient all-reduce
                 overlapped with backward, CUDA graph)
+  ddp           data parallel wrapper for any module (bucketed all-reduce
+                overlapping backward)
   zero          sharded data parallel optimizer (ZeRO stage 1/2) for any module
   tensor        tensor parallel SwiGLU MLP step (fused all-gather -> GEMM and
                 GEMM -> reduce-scatter, forward and backward)
