@@ -1,6 +1,6 @@
 """In-place all-reduce (sum) over four ranks in one process.
 
-    python examples/allreduce.py
+    PYTHONPATH=. python examples/allreduce.py
 """
 import numpy as np
 

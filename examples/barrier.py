@@ -1,6 +1,6 @@
 """Barrier: no rank leaves before every rank has arrived.
 
-    python examples/barrier.py
+    PYTHONPATH=. python examples/barrier.py
 """
 import threading
 import time

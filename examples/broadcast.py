@@ -1,6 +1,6 @@
 """Broadcast from a non-zero root over four ranks.
 
-    python examples/broadcast.py
+    PYTHONPATH=. python examples/broadcast.py
 """
 import numpy as np
 

@@ -1,6 +1,6 @@
 """Remote procedure call: rank 1 serves function 7, rank 0 calls it.
 
-    python examples/rpc.py
+    PYTHONPATH=. python examples/rpc.py
 """
 import threading
 

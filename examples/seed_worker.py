@@ -1,7 +1,7 @@
 """Cluster set-up the way it runs across machines: a seed node assigns ranks,
 workers join through it, then every worker builds its part of the mesh.
 
-    python examples/seed_worker.py                 # all roles in this process
+    PYTHONPATH=. python examples/seed_worker.py                 # all roles in this process
     # or, across processes / machines:
     python -c "from nexar_b200 import SeedNode; s = SeedNode('0.0.0.0:5000'); s.form_cluster(2)"
     NEXAR_CLUSTER_TOKEN=<token> python -c "from nexar_b200 import NexarClient; \\

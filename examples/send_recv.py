@@ -1,6 +1,6 @@
 """Tagged point-to-point between two ranks in one process.
 
-    python examples/send_recv.py
+    PYTHONPATH=. python examples/send_recv.py
 """
 import numpy as np
 

@@ -6,7 +6,7 @@ import sys
 import pytest
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-EXAMPLES = ["send_recv", "allreduce", "broadcast", "barrier", "rpc", "seed_worker"]
+EXAMPLES = ["send_recv", "allreduce", "broadcast", "barrier", "rpc", "seed_worker", "parallel_cpu"]
 
 
 @pytest.mark.parametrize("name", EXAMPLES)
