@@ -1,6 +1,8 @@
 """Checkpoint / resume of the data-parallel GPT-2 trainer: a trainer restored
 from another trainer's checkpoint takes the same next step (same loss, same
 fp32 master weights after AdamW) as the original."""
+import os
+
 import pytest
 import torch
 
@@ -8,6 +10,11 @@ from nexar_b200.models.gpt2 import GPT2Config
 from nexar_b200.parallel.dp import DataParallelTrainer
 
 pytestmark = pytest.mark.gpu
+
+# Paths that have not yet run on a B200: opt-in until their first validation
+# run (NEXAR_TEST_UNVALIDATED=1), so the validated suite runs unchanged.
+UNVALIDATED = pytest.mark.skipif(os.environ.get("NEXAR_TEST_UNVALIDATED") != "1",
+                                 reason="not yet validated on B200s (NEXAR_TEST_UNVALIDATED=1)")
 
 
 def _batch(cfg, seed):
@@ -17,6 +24,7 @@ def _batch(cfg, seed):
     return idx, tgt
 
 
+@UNVALIDATED
 def test_resume_matches_uninterrupted_run(cuda0, tmp_path):
     cfg = GPT2Config.tiny()
     a = DataParallelTrainer(cfg, micro_batch=2, seq_len=cfg.block_size, use_cuda_graph=False, seed=0)
