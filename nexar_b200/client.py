@@ -187,6 +187,7 @@ class NexarClient:
     @staticmethod
     def bootstrap(seed_addr: str, token: Optional[bytes] = None, config=None,
                   bind_host: str = "127.0.0.1", adapter=None) -> "NexarClient":
+        """Join a cluster through the seed at `seed_addr` (one process per rank)."""
         cfg = config if config is not None else _h().Config.from_env()
         c = _h().NexarClient.bootstrap_worker(seed_addr, token, cfg, bind_host)
         c.set_adapter(_adapter(adapter))
@@ -261,15 +262,19 @@ class NexarClient:
         return self._c
 
     def config(self):
+        """The NexarConfig this communicator was built with."""
         return self._c.config()
 
     def has_direct_peer(self, rank: int) -> bool:
+        """Whether `rank` has a direct connection (False when a sparse topology relays to it)."""
         return self._c.has_direct_peer(rank)
 
     def is_sparse(self) -> bool:
+        """Whether this communicator runs on a sparse topology (k-regular or hypercube)."""
         return self._c.is_sparse()
 
     def adapter(self) -> str:
+        """Name of the memory adapter in use ("cuda" when a device communicator is attached)."""
         return "cuda" if self._device is not None else self._c.adapter_name
 
     def device_adapter(self):
@@ -283,27 +288,35 @@ class NexarClient:
 
     # ------------------------------------------------------------ p2p
     def send(self, ptr: int, size: int, dest: int, tag: int):
+        """Send `size` bytes at `ptr` to rank `dest` under `tag` (staged through the adapter for non-host memory)."""
         self._c.send(ptr, size, dest, tag)
 
     def recv(self, ptr: int, size: int, src: int, tag: int):
+        """Receive the oldest message from `src` with `tag` into `size` bytes at `ptr`; the size must match."""
         self._c.recv(ptr, size, src, tag)
 
     def send_iov(self, iov: Sequence[Tuple[int, int]], dest: int, tag: int):
+        """Send the (ptr, len) regions back to back as one tagged message."""
         self._c.send_iov(list(iov), dest, tag)
 
     def recv_iov(self, iov: Sequence[Tuple[int, int]], src: int, tag: int):
+        """Receive one tagged message and scatter it over the (ptr, len) regions."""
         self._c.recv_iov(list(iov), src, tag)
 
     def send_bytes(self, dest: int, data: bytes):
+        """Send a byte string to `dest` on this communicator's raw lane."""
         self._c.send_bytes(dest, data)
 
     def recv_bytes(self, src: int) -> bytes:
+        """Receive the next byte string from `src` on the raw lane."""
         return self._c.recv_bytes(src)
 
     def send_bytes_tagged(self, dest: int, tag: int, data: bytes):
+        """Send a byte string to `dest` under a 64-bit tag."""
         self._c.send_bytes_tagged(dest, tag, data)
 
     def recv_bytes_tagged(self, src: int, tag: int, timeout_s: float = -1.0) -> bytes:
+        """Receive the byte string from `src` with `tag` (timeout_s < 0: the collective timeout)."""
         return self._c.recv_bytes_tagged(src, tag, timeout_s)
 
     # ------------------------------------------------------------ rpc
@@ -312,20 +325,25 @@ class NexarClient:
         self._c.register_rpc(fn_id, handler)
 
     def rpc(self, target: int, fn_id: int, args: bytes, timeout_s: float = -1.0) -> bytes:
+        """Call function `fn_id` on rank `target` with `args`; returns its reply (timeout_s < 0: the RPC timeout)."""
         return self._c.rpc(target, fn_id, args, timeout_s)
 
     rpc_with_timeout = rpc
 
     def recv_rpc_request(self, src: int, timeout_s: float = -1.0) -> dict:
+        """Take the next RPC request from `src` (fields: req_id, fn_id, payload)."""
         return self._c.recv_rpc_request(src, timeout_s)
 
     def serve_rpc_once(self, src: int, timeout_s: float = -1.0):
+        """Serve one RPC request from `src` with the registered handlers."""
         self._c.serve_rpc_once(src, timeout_s)
 
     def start_rpc_server(self):
+        """Serve RPC requests from every peer on a background thread."""
         self._c.start_rpc_server()
 
     def stop_rpc_server(self):
+        """Stop the background RPC server."""
         self._c.stop_rpc_server()
 
     def rpc_dispatcher(self) -> "RpcDispatcher":
@@ -342,49 +360,64 @@ class NexarClient:
         self._c.send_message_to(dest, tag, payload, int(priority))
 
     def recv_message_from(self, src: int, tag: int, timeout_s: float = -1.0) -> bytes:
+        """Receive the payload that `src` sent with ``send_message_to`` under `tag`."""
         return self._c.recv_message_from(src, tag, timeout_s)
 
     # ------------------------------------------------------------ collectives (pointer API)
     def all_reduce(self, ptr: int, count: int, dtype, op=ReduceOp.Sum):
+        """In place: `count` elements at `ptr` become op over all ranks."""
         self._c.all_reduce(ptr, count, int(dtype), int(ReduceOp.parse(op)))
 
     def all_reduce_rs_ag(self, ptr: int, count: int, dtype, op=ReduceOp.Sum):
+        """All-reduce as reduce-scatter then all-gather (uneven counts allowed)."""
         self._c.all_reduce_rs_ag(ptr, count, int(dtype), int(ReduceOp.parse(op)))
 
     def all_reduce_bucketed(self, entries: Sequence[Tuple[int, int]], dtype, op=ReduceOp.Sum):
+        """One all-reduce over several (ptr, count) regions packed together."""
         self._c.all_reduce_bucketed(list(entries), int(dtype), int(ReduceOp.parse(op)))
 
     def all_reduce_compressed(self, ptr: int, count: int, dtype, op, compressor, residual_ptr: int):
+        """All-reduce of compressed contributions (compressor with error feedback in `residual`)."""
         self._c.all_reduce_compressed(ptr, count, int(dtype), int(ReduceOp.parse(op)), compressor, residual_ptr)
 
     def broadcast(self, ptr: int, count: int, dtype, root: int):
+        """In place: every rank's `count` elements at `ptr` become the root's."""
         self._c.broadcast(ptr, count, int(dtype), root)
 
     def all_gather(self, send_ptr: int, recv_ptr: int, count: int, dtype):
+        """recv (count x world) = every rank's send (count) in rank order."""
         self._c.all_gather(send_ptr, recv_ptr, count, int(dtype))
 
     def reduce_scatter(self, send_ptr: int, recv_ptr: int, count: int, dtype, op=ReduceOp.Sum):
+        """recv (count) on rank r = op over ranks of chunk r of send (count x world)."""
         self._c.reduce_scatter(send_ptr, recv_ptr, count, int(dtype), int(ReduceOp.parse(op)))
 
     def reduce(self, ptr: int, count: int, dtype, op, root: int):
+        """In place: the root's buffer becomes op over all ranks (other ranks keep partial results)."""
         self._c.reduce(ptr, count, int(dtype), int(ReduceOp.parse(op)), root)
 
     def all_to_all(self, send_ptr: int, recv_ptr: int, count: int, dtype):
+        """recv chunk q (count) = chunk r of rank q's send (count x world)."""
         self._c.all_to_all(send_ptr, recv_ptr, count, int(dtype))
 
     def gather(self, send_ptr: int, recv_ptr: int, count: int, dtype, root: int):
+        """The root's recv (count x world) receives every rank's send (count) in rank order."""
         self._c.gather(send_ptr, recv_ptr, count, int(dtype), root)
 
     def scatter(self, send_ptr: int, recv_ptr: int, count: int, dtype, root: int):
+        """recv (count) on rank r = chunk r of the root's send (count x world)."""
         self._c.scatter(send_ptr, recv_ptr, count, int(dtype), root)
 
     def scan(self, ptr: int, count: int, dtype, op=ReduceOp.Sum):
+        """In place: rank r holds op over ranks 0..r."""
         self._c.scan(ptr, count, int(dtype), int(ReduceOp.parse(op)))
 
     def exclusive_scan(self, ptr: int, count: int, dtype, op=ReduceOp.Sum):
+        """In place: rank r holds op over ranks 0..r-1 (the identity on rank 0)."""
         self._c.exclusive_scan(ptr, count, int(dtype), int(ReduceOp.parse(op)))
 
     def barrier(self, timeout_s: Optional[float] = None):
+        """Return once every rank of this communicator has entered the barrier."""
         if timeout_s is None:
             self._c.barrier()
         else:
@@ -392,113 +425,139 @@ class NexarClient:
 
     # ------------------------------------------------------------ non-blocking
     def all_reduce_nb(self, ptr: int, count: int, dtype, op=ReduceOp.Sum) -> CollectiveHandle:
+        """Non-blocking ``all_reduce``: starts it on a worker thread and returns a CollectiveHandle."""
         return CollectiveHandle(self._c.all_reduce_nb(ptr, count, int(dtype), int(ReduceOp.parse(op))))
 
     def _nb(self, op: str, *args) -> CollectiveHandle:
         return CollectiveHandle(self._c.spawn_collective(op, tuple(int(a) for a in args)))
 
     def broadcast_nb(self, ptr, count, dtype, root):
+        """Non-blocking ``broadcast``: starts it on a worker thread and returns a CollectiveHandle."""
         return self._nb("broadcast", ptr, count, dtype, root)
 
     def all_gather_nb(self, send_ptr, recv_ptr, count, dtype):
+        """Non-blocking ``all_gather``: starts it on a worker thread and returns a CollectiveHandle."""
         return self._nb("all_gather", send_ptr, recv_ptr, count, dtype)
 
     def reduce_scatter_nb(self, send_ptr, recv_ptr, count, dtype, op=ReduceOp.Sum):
+        """Non-blocking ``reduce_scatter``: starts it on a worker thread and returns a CollectiveHandle."""
         return self._nb("reduce_scatter", send_ptr, recv_ptr, count, dtype, ReduceOp.parse(op))
 
     def reduce_nb(self, ptr, count, dtype, op, root):
+        """Non-blocking ``reduce``: starts it on a worker thread and returns a CollectiveHandle."""
         return self._nb("reduce", ptr, count, dtype, ReduceOp.parse(op), root)
 
     def all_to_all_nb(self, send_ptr, recv_ptr, count, dtype):
+        """Non-blocking ``all_to_all``: starts it on a worker thread and returns a CollectiveHandle."""
         return self._nb("all_to_all", send_ptr, recv_ptr, count, dtype)
 
     def gather_nb(self, send_ptr, recv_ptr, count, dtype, root):
+        """Non-blocking ``gather``: starts it on a worker thread and returns a CollectiveHandle."""
         return self._nb("gather", send_ptr, recv_ptr, count, dtype, root)
 
     def scatter_nb(self, send_ptr, recv_ptr, count, dtype, root):
+        """Non-blocking ``scatter``: starts it on a worker thread and returns a CollectiveHandle."""
         return self._nb("scatter", send_ptr, recv_ptr, count, dtype, root)
 
     def scan_nb(self, ptr, count, dtype, op=ReduceOp.Sum):
+        """Non-blocking ``scan``: starts it on a worker thread and returns a CollectiveHandle."""
         return self._nb("scan", ptr, count, dtype, ReduceOp.parse(op))
 
     def exclusive_scan_nb(self, ptr, count, dtype, op=ReduceOp.Sum):
+        """Non-blocking ``exclusive_scan``: starts it on a worker thread and returns a CollectiveHandle."""
         return self._nb("exclusive_scan", ptr, count, dtype, ReduceOp.parse(op))
 
     def all_reduce_rs_ag_nb(self, ptr, count, dtype, op=ReduceOp.Sum):
+        """Non-blocking ``all_reduce_rs_ag``: starts it on a worker thread and returns a CollectiveHandle."""
         return self._nb("all_reduce_rs_ag", ptr, count, dtype, ReduceOp.parse(op))
 
     def barrier_nb(self):
+        """Non-blocking ``barrier``: starts it on a worker thread and returns a CollectiveHandle."""
         return self._nb("barrier")
 
     def all_reduce_bucketed_nb(self, entries: Sequence[Tuple[int, int]], dtype, op=ReduceOp.Sum):
+        """Non-blocking ``all_reduce_bucketed``: starts it on a worker thread and returns a CollectiveHandle."""
         return CollectiveHandle(self._c.all_reduce_bucketed_nb(list(entries), int(dtype), int(ReduceOp.parse(op))))
 
     def all_reduce_compressed_nb(self, ptr: int, count: int, dtype, op, compressor, residual_ptr: int):
+        """Non-blocking ``all_reduce_compressed``: starts it on a worker thread and returns a CollectiveHandle."""
         return CollectiveHandle(self._c.all_reduce_compressed_nb(ptr, count, int(dtype), int(ReduceOp.parse(op)),
                                                                  compressor, residual_ptr))
 
     # ------------------------------------------------------------ typed host helpers
     def all_reduce_host(self, buf, op=ReduceOp.Sum):
+        """``all_reduce`` on host buffers (numpy arrays or CPU tensors); returns the result buffer."""
         p, n, dt = _host_buf(buf)
         self.all_reduce(p, n, dt, op)
         return buf
 
     def all_reduce_rs_ag_host(self, buf, op=ReduceOp.Sum):
+        """``all_reduce_rs_ag`` on host buffers (numpy arrays or CPU tensors); returns the result buffer."""
         p, n, dt = _host_buf(buf)
         self.all_reduce_rs_ag(p, n, dt, op)
         return buf
 
     def broadcast_host(self, buf, root: int):
+        """``broadcast`` on host buffers (numpy arrays or CPU tensors); returns the result buffer."""
         p, n, dt = _host_buf(buf)
         self.broadcast(p, n, dt, root)
         return buf
 
     def all_gather_host(self, send, recv):
+        """``all_gather`` on host buffers (numpy arrays or CPU tensors); returns the result buffer."""
         ps, n, dt = _host_buf(send)
         pr, _, _ = _host_buf(recv)
         self.all_gather(ps, pr, n, dt)
         return recv
 
     def reduce_scatter_host(self, send, recv, op=ReduceOp.Sum):
+        """``reduce_scatter`` on host buffers (numpy arrays or CPU tensors); returns the result buffer."""
         ps, _, dt = _host_buf(send)
         pr, n, _ = _host_buf(recv)
         self.reduce_scatter(ps, pr, n, dt, op)
         return recv
 
     def reduce_host(self, buf, op, root: int):
+        """``reduce`` on host buffers (numpy arrays or CPU tensors); returns the result buffer."""
         p, n, dt = _host_buf(buf)
         self.reduce(p, n, dt, op, root)
         return buf
 
     def all_to_all_host(self, send, recv):
+        """``all_to_all`` on host buffers (numpy arrays or CPU tensors); returns the result buffer."""
         ps, n, dt = _host_buf(send)
         pr, _, _ = _host_buf(recv)
         self.all_to_all(ps, pr, n // self.world_size, dt)
         return recv
 
     def gather_host(self, send, recv, root: int):
+        """``gather`` on host buffers (numpy arrays or CPU tensors); returns the result buffer."""
         ps, n, dt = _host_buf(send)
         pr = _host_buf(recv)[0] if recv is not None else 0
         self.gather(ps, pr, n, dt, root)
         return recv
 
     def scatter_host(self, send, recv, root: int):
+        """``scatter`` on host buffers (numpy arrays or CPU tensors); returns the result buffer."""
         pr, n, dt = _host_buf(recv)
         ps = _host_buf(send)[0] if send is not None else 0
         self.scatter(ps, pr, n, dt, root)
         return recv
 
     def scan_host(self, buf, op=ReduceOp.Sum):
+        """``scan`` on host buffers (numpy arrays or CPU tensors); returns the result buffer."""
         p, n, dt = _host_buf(buf)
         self.scan(p, n, dt, op)
         return buf
 
     def exclusive_scan_host(self, buf, op=ReduceOp.Sum):
+        """``exclusive_scan`` on host buffers (numpy arrays or CPU tensors); returns the result buffer."""
         p, n, dt = _host_buf(buf)
         self.exclusive_scan(p, n, dt, op)
         return buf
 
     def all_reduce_bucketed_host(self, bufs, op=ReduceOp.Sum):
+        """``all_reduce_bucketed`` on host buffers (numpy arrays or CPU tensors); returns the result buffer."""
         entries = [_buf(b) for b in bufs]
         dts = {e[2] for e in entries}
         if len(dts) != 1:
@@ -507,6 +566,7 @@ class NexarClient:
         return bufs
 
     def all_reduce_compressed_host(self, buf, compressor, residual, op=ReduceOp.Sum):
+        """``all_reduce_compressed`` on host buffers (numpy arrays or CPU tensors); returns the result buffer."""
         p, n, dt = _buf(buf)
         r, _, _ = _buf(residual)
         self.all_reduce_compressed(p, n, dt, op, compressor, r)
@@ -571,6 +631,7 @@ class NexarClient:
                 torch.cuda.synchronize(t.device)
 
     def all_reduce_device(self, t, op=ReduceOp.Sum):
+        """``all_reduce`` on CUDA tensors: the device communicator's kernels, or the adapter's host staging when none is attached."""
         if self._staged(t):
             p, n, dt = _buf(t)
             self.all_reduce(p, n, dt, op)
@@ -589,6 +650,7 @@ class NexarClient:
         return self.device.all_reduce(t, op=str(ReduceOp.parse(op)), algo="two_shot")
 
     def broadcast_device(self, t, root: int):
+        """``broadcast`` on CUDA tensors: the device communicator's kernels, or the adapter's host staging when none is attached."""
         if self._staged(t):
             p, n, dt = _buf(t)
             self.broadcast(p, n, dt, root)
@@ -597,6 +659,7 @@ class NexarClient:
         return self.device.broadcast(t, root)
 
     def all_gather_device(self, send, recv):
+        """``all_gather`` on CUDA tensors: the device communicator's kernels, or the adapter's host staging when none is attached."""
         if self._staged(send, recv):
             ps, n, dt = _buf(send)
             self.all_gather(ps, _buf(recv)[0], n, dt)
@@ -605,6 +668,7 @@ class NexarClient:
         return self.device.all_gather(send, recv)
 
     def reduce_scatter_device(self, send, recv, op=ReduceOp.Sum):
+        """``reduce_scatter`` on CUDA tensors: the device communicator's kernels, or the adapter's host staging when none is attached."""
         if self._staged(send, recv):
             pr, n, dt = _buf(recv)
             self.reduce_scatter(_buf(send)[0], pr, n, dt, op)
@@ -613,6 +677,7 @@ class NexarClient:
         return self.device.reduce_scatter(send, recv, op=str(ReduceOp.parse(op)))
 
     def reduce_device(self, t, op, root: int):
+        """``reduce`` on CUDA tensors: the device communicator's kernels, or the adapter's host staging when none is attached."""
         if self._staged(t):
             p, n, dt = _buf(t)
             self.reduce(p, n, dt, op, root)
@@ -621,6 +686,7 @@ class NexarClient:
         return self.device.reduce(t, root, op=str(ReduceOp.parse(op)))
 
     def all_to_all_device(self, send, recv):
+        """``all_to_all`` on CUDA tensors: the device communicator's kernels, or the adapter's host staging when none is attached."""
         if self._staged(send, recv):
             ps, n, dt = _buf(send)
             self.all_to_all(ps, _buf(recv)[0], n // self.world_size, dt)
@@ -629,6 +695,7 @@ class NexarClient:
         return self.device.all_to_all(send, recv)
 
     def gather_device(self, send, recv, root: int):
+        """``gather`` on CUDA tensors: the device communicator's kernels, or the adapter's host staging when none is attached."""
         if self._staged(send, recv):
             ps, n, dt = _buf(send)
             self.gather(ps, _buf(recv)[0] if recv is not None else 0, n, dt, root)
@@ -637,6 +704,7 @@ class NexarClient:
         return self.device.gather(send, root, recv)
 
     def scatter_device(self, send, recv, root: int):
+        """``scatter`` on CUDA tensors: the device communicator's kernels, or the adapter's host staging when none is attached."""
         if self._staged(send, recv):
             pr, n, dt = _buf(recv)
             self.scatter(_buf(send)[0] if send is not None else 0, pr, n, dt, root)
@@ -645,6 +713,7 @@ class NexarClient:
         return self.device.scatter(send, root, recv)
 
     def scan_device(self, t, op=ReduceOp.Sum):
+        """``scan`` on CUDA tensors: the device communicator's kernels, or the adapter's host staging when none is attached."""
         if self._staged(t):
             p, n, dt = _buf(t)
             self.scan(p, n, dt, op)
@@ -653,6 +722,7 @@ class NexarClient:
         return t.copy_(self.device.scan(t, op=str(ReduceOp.parse(op))))
 
     def exclusive_scan_device(self, t, op=ReduceOp.Sum):
+        """``exclusive_scan`` on CUDA tensors: the device communicator's kernels, or the adapter's host staging when none is attached."""
         if self._staged(t):
             p, n, dt = _buf(t)
             self.exclusive_scan(p, n, dt, op)
@@ -676,12 +746,15 @@ class NexarClient:
 
     # ------------------------------------------------------------ communicators
     def split(self, color: int, key: int) -> "NexarClient":
+        """Sub-communicator of the ranks with the same `color`, ordered by (`key`, rank)."""
         return NexarClient(self._c.split(color, key))
 
     def rebuild_excluding(self, dead_ranks: Iterable[int]) -> "NexarClient":
+        """Communicator of the surviving ranks (renumbered in order) without `dead_ranks`."""
         return NexarClient(self._c.rebuild_excluding(sorted(set(dead_ranks))))
 
     def rebuild_adding(self, new_mesh_ranks: Iterable[int], comm_id: int = 0) -> "NexarClient":
+        """Communicator grown by the given mesh ranks (appended after the current ranks)."""
         return NexarClient(self._c.rebuild_adding(list(new_mesh_ranks), comm_id))
 
     def failure_watch(self) -> List[int]:
@@ -689,6 +762,7 @@ class NexarClient:
         return self._c.dead_ranks()
 
     def wait_failure(self, timeout_s: float) -> List[int]:
+        """Block until a peer is declared dead or `timeout_s` passes; returns the dead ranks."""
         return self._c.wait_failure(timeout_s)
 
     def close(self):
