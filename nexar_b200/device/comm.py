@@ -294,6 +294,7 @@ class DeviceCommunicator:
         return GlobalPtr(self, rank, int(off), t.numel() * t.element_size())
 
     def is_symmetric(self, t: torch.Tensor) -> bool:
+        """Whether t lies in this communicator's symmetric memory (heap or NVLS region)."""
         return self._comm.symmetric_offset(t) >= 0 or (self.nvls and self._comm.nvls_offset(t) >= 0)
 
     @property
@@ -331,6 +332,7 @@ class DeviceCommunicator:
                 f"(block {st['block']}, epoch {st['epoch']})")
 
     def status(self) -> dict:
+        """The host-mapped status word (code, rank, op, block, epoch of the last failed wait)."""
         return self._comm.status()
 
     def stats(self) -> dict:
@@ -349,6 +351,7 @@ class DeviceCommunicator:
         self._timer = (self._timer or DeviceTimeHistogram()) if on else None
 
     def clear_status(self):
+        """Reset the status word after a reported failure."""
         self._comm.clear_status()
 
     # ----------------------------------------------------------- collectives
@@ -379,6 +382,7 @@ class DeviceCommunicator:
 
     @_observed("all_gather")
     def all_gather(self, inp: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """out (world x inp) = every rank's inp in rank order (peer-memory or NVLS kernel)."""
         if out is None:
             out = torch.empty(inp.numel() * self.world_size, dtype=inp.dtype, device=inp.device)
         self._C.all_gather(self._comm, inp, out)
@@ -386,12 +390,14 @@ class DeviceCommunicator:
 
     @_observed("all_to_all")
     def all_to_all(self, inp: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """out chunk q = chunk r of rank q's inp (world equal chunks, peer stores)."""
         out = torch.empty_like(inp) if out is None else out
         self._C.all_to_all(self._comm, inp, out)
         return out
 
     @_observed("broadcast")
     def broadcast(self, t: torch.Tensor, root: int = 0, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """t (or out) on every rank = the root's t (peer loads, scatter + all-gather, or NVLS multicast)."""
         out = t if out is None else out
         self._C.broadcast(self._comm, t, out, int(root))
         return out
@@ -399,12 +405,14 @@ class DeviceCommunicator:
     @_observed("reduce")
     def reduce(self, t: torch.Tensor, root: int = 0, op="sum", out: Optional[torch.Tensor] = None,
                scale: Optional[float] = None) -> torch.Tensor:
+        """The root's t (or out) = op over all ranks' t."""
         out = t if out is None else out
         self._C.reduce(self._comm, t, out, int(root), int(ReduceOp.parse(op)), 1.0 if scale is None else float(scale))
         return out
 
     @_observed("gather")
     def gather(self, inp: torch.Tensor, root: int = 0, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """The root's out (world x inp) = every rank's inp in rank order."""
         if out is None:
             out = torch.empty(inp.numel() * self.world_size, dtype=inp.dtype, device=inp.device)
         self._C.gather(self._comm, inp, out, int(root))
@@ -412,6 +420,7 @@ class DeviceCommunicator:
 
     @_observed("scatter")
     def scatter(self, inp: torch.Tensor, root: int = 0, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """out on rank r = chunk r of the root's inp."""
         if out is None:
             out = torch.empty(inp.numel() // self.world_size, dtype=inp.dtype, device=inp.device)
         self._C.scatter(self._comm, inp, out, int(root))
@@ -419,18 +428,21 @@ class DeviceCommunicator:
 
     @_observed("scan")
     def scan(self, inp: torch.Tensor, op="sum", out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """out on rank r = op over ranks 0..r of inp."""
         out = torch.empty_like(inp) if out is None else out
         self._C.scan(self._comm, inp, out, int(ReduceOp.parse(op)), False)
         return out
 
     @_observed("exclusive_scan")
     def exclusive_scan(self, inp: torch.Tensor, op="sum", out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """out on rank r = op over ranks 0..r-1 of inp (identity on rank 0)."""
         out = torch.empty_like(inp) if out is None else out
         self._C.scan(self._comm, inp, out, int(ReduceOp.parse(op)), True)
         return out
 
     @_observed("barrier")
     def barrier(self):
+        """Device barrier: returns once every rank's stream has reached it (bounded waits)."""
         self._C.barrier(self._comm)
 
     # ----------------------------------------------------------- compressed all-reduce
@@ -534,6 +546,7 @@ class DeviceCommunicator:
 
     # ----------------------------------------------------------- non-blocking
     def side_stream(self) -> torch.cuda.Stream:
+        """The high-priority stream the non-blocking collectives run on."""
         if self._side_stream is None:
             self._side_stream = torch.cuda.Stream(device=self.device, priority=-1)
         return self._side_stream
@@ -552,37 +565,48 @@ class DeviceCommunicator:
         return DeviceHandle(ev, tuple(tensors) + (result,), self)
 
     def all_reduce_nb(self, t, op="sum", out=None, scale=None, algo="auto") -> DeviceHandle:
+        """Non-blocking ``all_reduce`` on the side stream; returns a DeviceHandle."""
         out_ = t if out is None else out
         return self._nb(lambda: self.all_reduce(t, op, out_, scale, algo), (t, out_), out_)
 
     def reduce_scatter_nb(self, inp, out, op="sum", scale=None) -> DeviceHandle:
+        """Non-blocking ``reduce_scatter`` on the side stream; returns a DeviceHandle."""
         return self._nb(lambda: self.reduce_scatter(inp, out, op, scale), (inp, out), out)
 
     def all_gather_nb(self, inp, out) -> DeviceHandle:
+        """Non-blocking ``all_gather`` on the side stream; returns a DeviceHandle."""
         return self._nb(lambda: self.all_gather(inp, out), (inp, out), out)
 
     def all_to_all_nb(self, inp, out) -> DeviceHandle:
+        """Non-blocking ``all_to_all`` on the side stream; returns a DeviceHandle."""
         return self._nb(lambda: self.all_to_all(inp, out), (inp, out), out)
 
     def broadcast_nb(self, t, root=0) -> DeviceHandle:
+        """Non-blocking ``broadcast`` on the side stream; returns a DeviceHandle."""
         return self._nb(lambda: self.broadcast(t, root), (t,), t)
 
     def reduce_nb(self, t, root=0, op="sum") -> DeviceHandle:
+        """Non-blocking ``reduce`` on the side stream; returns a DeviceHandle."""
         return self._nb(lambda: self.reduce(t, root, op), (t,), t)
 
     def gather_nb(self, inp, out, root=0) -> DeviceHandle:
+        """Non-blocking ``gather`` on the side stream; returns a DeviceHandle."""
         return self._nb(lambda: self.gather(inp, root, out), (inp, out), out)
 
     def scatter_nb(self, inp, out, root=0) -> DeviceHandle:
+        """Non-blocking ``scatter`` on the side stream; returns a DeviceHandle."""
         return self._nb(lambda: self.scatter(inp, root, out), (inp, out), out)
 
     def scan_nb(self, inp, out, op="sum") -> DeviceHandle:
+        """Non-blocking ``scan`` on the side stream; returns a DeviceHandle."""
         return self._nb(lambda: self.scan(inp, op, out), (inp, out), out)
 
     def exclusive_scan_nb(self, inp, out, op="sum") -> DeviceHandle:
+        """Non-blocking ``exclusive_scan`` on the side stream; returns a DeviceHandle."""
         return self._nb(lambda: self.exclusive_scan(inp, op, out), (inp, out), out)
 
     def barrier_nb(self) -> DeviceHandle:
+        """Non-blocking ``barrier`` on the side stream; returns a DeviceHandle."""
         return self._nb(self.barrier, (), None)
 
     # ----------------------------------------------------------- p2p (NCCL)
@@ -610,6 +634,7 @@ class DeviceCommunicator:
         dist.send(t, dst, group=group)
 
     def recv(self, t: torch.Tensor, src: int, group=None):
+        """Pipeline-style device receive of t from rank src (NCCL p2p)."""
         if self._nccl is not None and group is None:
             self._nccl.recv(t, src)
             return
@@ -624,13 +649,16 @@ class DeviceCommunicator:
         return dist.isend(t, dst, group=group)
 
     def irecv(self, t: torch.Tensor, src: int, group=None):
+        """Non-blocking receive: an NcclHandle with an attached group, else a torch Work."""
         if self._nccl is not None and group is None:
             return self._nccl.recv_nb(t, src)
         import torch.distributed as dist
         return dist.irecv(t, src, group=group)
 
     def send_nb(self, t: torch.Tensor, dst: int):
+        """Non-blocking send (see isend)."""
         return self.isend(t, dst)
 
     def recv_nb(self, t: torch.Tensor, src: int):
+        """Non-blocking receive (see irecv)."""
         return self.irecv(t, src)

@@ -161,6 +161,7 @@ class NcclHandle:
         return self._keep[-1] if self._keep else None
 
     def synchronize(self):
+        """Block the host until the operation has finished; raises if the communicator reports an error."""
         self._event.synchronize()
         st = self._group.async_error()
         if st != 0:
@@ -232,39 +233,50 @@ class NcclGroup:
 
     # ------------------------------------------------------------ raw pointers (group stream)
     def allreduce_inplace(self, ptr: int, count: int, dtype, op=ReduceOp.Sum):
+        """ncclAllReduce in place on `count` elements at `ptr` (group stream)."""
         _native_call(self._g.all_reduce_inplace, int(ptr), int(count), int(DataType(dtype)), int(ReduceOp.parse(op)))
 
     def allreduce(self, send_ptr: int, recv_ptr: int, count: int, dtype, op=ReduceOp.Sum):
+        """ncclAllReduce from send_ptr into recv_ptr (group stream)."""
         _native_call(self._g.all_reduce, int(send_ptr), int(recv_ptr), int(count), int(DataType(dtype)),
                      int(ReduceOp.parse(op)))
 
     def reduce_scatter_ptr(self, send_ptr: int, recv_ptr: int, recv_count: int, dtype, op=ReduceOp.Sum):
+        """ncclReduceScatter: recv_count elements per rank; rank r receives chunk r."""
         _native_call(self._g.reduce_scatter, int(send_ptr), int(recv_ptr), int(recv_count), int(DataType(dtype)),
                      int(ReduceOp.parse(op)))
 
     def allgather(self, send_ptr: int, recv_ptr: int, send_count: int, dtype):
+        """ncclAllGather: send_count elements per rank into recv in rank order."""
         _native_call(self._g.all_gather, int(send_ptr), int(recv_ptr), int(send_count), int(DataType(dtype)))
 
     def broadcast_inplace(self, ptr: int, count: int, dtype, root: int):
+        """ncclBroadcast in place from `root`."""
         _native_call(self._g.broadcast_inplace, int(ptr), int(count), int(DataType(dtype)), int(root))
 
     def reduce_inplace(self, ptr: int, count: int, dtype, op, root: int):
+        """ncclReduce in place onto `root`."""
         _native_call(self._g.reduce_inplace, int(ptr), int(count), int(DataType(dtype)), int(ReduceOp.parse(op)),
                      int(root))
 
     def send_ptr(self, ptr: int, count: int, dtype, peer: int):
+        """ncclSend of `count` elements to `peer` (group stream)."""
         _native_call(self._g.send, int(ptr), int(count), int(DataType(dtype)), int(peer))
 
     def recv_ptr(self, ptr: int, count: int, dtype, peer: int):
+        """ncclRecv of `count` elements from `peer` (group stream)."""
         _native_call(self._g.recv, int(ptr), int(count), int(DataType(dtype)), int(peer))
 
     def synchronize(self):
+        """Block the host until the group's stream has drained."""
         _native_call(self._g.synchronize)
 
     def create_event(self) -> int:
+        """A CUDA event (no timing) on the group's device; returns its handle."""
         return int(_native_call(self._g.create_event))
 
     def record_event(self, event: int):
+        """Record `event` on the group's stream."""
         _native_call(self._g.record_event, int(event))
 
     def stream_wait_event(self, event: int, stream: Optional[torch.cuda.Stream] = None):
@@ -272,12 +284,15 @@ class NcclGroup:
         _native_call(self._g.stream_wait_event, 0 if stream is None else int(stream.cuda_stream), int(event))
 
     def event_query(self, event: int) -> bool:
+        """Whether `event` has completed."""
         return bool(_native_call(self._g.event_query, int(event)))
 
     def destroy_event(self, event: int):
+        """Destroy an event made by create_event."""
         _native_call(self._g.destroy_event, int(event))
 
     def async_error(self) -> int:
+        """The communicator's asynchronous error state (0 while healthy)."""
         return int(_native_call(self._g.async_error))
 
     def abort(self):
@@ -304,6 +319,7 @@ class NcclGroup:
         return h
 
     def all_reduce(self, t: torch.Tensor, op="sum", out: Optional[torch.Tensor] = None, blocking: bool = True):
+        """All-reduce of t (into out) ordered after the caller's current stream."""
         out_ = t if out is None else out
         if out_.numel() != t.numel() or out_.dtype != t.dtype:
             raise NcclCommError("all_reduce: out must match the input's size and dtype")
@@ -311,6 +327,7 @@ class NcclGroup:
         return self._run(lambda: self.allreduce(_ptr(t), _ptr(out_), t.numel(), dt, op), (t, out_), out_, blocking)
 
     def reduce_scatter(self, inp: torch.Tensor, out: torch.Tensor, op="sum", blocking: bool = True):
+        """Rank r's out = op over ranks of chunk r of inp."""
         if inp.numel() != out.numel() * self.local_world or inp.dtype != out.dtype:
             raise NcclCommError("reduce_scatter: input must hold world_size x out elements of out's dtype")
         dt = DataType.from_torch(out.dtype)
@@ -318,24 +335,29 @@ class NcclGroup:
                          (inp, out), out, blocking)
 
     def all_gather(self, inp: torch.Tensor, out: torch.Tensor, blocking: bool = True):
+        """out (world x inp) = every rank's inp in rank order."""
         if out.numel() != inp.numel() * self.local_world or inp.dtype != out.dtype:
             raise NcclCommError("all_gather: out must hold world_size x input elements of the input's dtype")
         dt = DataType.from_torch(inp.dtype)
         return self._run(lambda: self.allgather(_ptr(inp), _ptr(out), inp.numel(), dt), (inp, out), out, blocking)
 
     def broadcast(self, t: torch.Tensor, root: int = 0, blocking: bool = True):
+        """t on every rank = the root's t."""
         dt = DataType.from_torch(t.dtype)
         return self._run(lambda: self.broadcast_inplace(_ptr(t), t.numel(), dt, root), (t,), t, blocking)
 
     def reduce(self, t: torch.Tensor, root: int = 0, op="sum", blocking: bool = True):
+        """The root's t = op over all ranks' t."""
         dt = DataType.from_torch(t.dtype)
         return self._run(lambda: self.reduce_inplace(_ptr(t), t.numel(), dt, op, root), (t,), t, blocking)
 
     def send(self, t: torch.Tensor, peer: int, blocking: bool = True):
+        """Send t to `peer` (ordered after the caller's current stream)."""
         dt = DataType.from_torch(t.dtype)
         return self._run(lambda: self.send_ptr(_ptr(t), t.numel(), dt, peer), (t,), t, blocking)
 
     def recv(self, t: torch.Tensor, peer: int, blocking: bool = True):
+        """Receive t from `peer`."""
         dt = DataType.from_torch(t.dtype)
         return self._run(lambda: self.recv_ptr(_ptr(t), t.numel(), dt, peer), (t,), t, blocking)
 
@@ -351,15 +373,19 @@ class NcclGroup:
                          (send_t, recv_t), recv_t, blocking)
 
     def all_reduce_nb(self, t, op="sum", out=None) -> NcclHandle:
+        """Non-blocking all_reduce; returns an NcclHandle."""
         return self.all_reduce(t, op, out, blocking=False)
 
     def send_nb(self, t, peer) -> NcclHandle:
+        """Non-blocking send; returns an NcclHandle."""
         return self.send(t, peer, blocking=False)
 
     def recv_nb(self, t, peer) -> NcclHandle:
+        """Non-blocking receive; returns an NcclHandle."""
         return self.recv(t, peer, blocking=False)
 
     def send_recv_nb(self, send_t, send_peer, recv_t, recv_peer) -> NcclHandle:
+        """Non-blocking send_recv; returns an NcclHandle."""
         return self.send_recv(send_t, send_peer, recv_t, recv_peer, blocking=False)
 
 
