@@ -207,9 +207,11 @@ class DataParallelTrainer:
 
     def load_state_dict(self, sd: dict) -> None:
         """Restore a :meth:`state_dict` into this trainer's buffers, in place
-        (a captured CUDA graph keeps working). The model shape and flat layout
-        must match; the bf16 working weights are re-derived from the fp32
-        master weights."""
+        (a captured CUDA graph keeps working, unless the checkpoint's optimizer
+        settings differ from the ones captured: then the graph is dropped and
+        steps run eagerly until :meth:`capture` is called again). The model
+        shape and flat layout must match; the bf16 working weights are
+        re-derived from the fp32 master weights."""
         if sd.get("format") != self.CHECKPOINT_FORMAT:
             raise ValueError(f"not a {self.CHECKPOINT_FORMAT} checkpoint: {sd.get('format')!r}")
         if sd["config"] != dataclasses.asdict(self.cfg):
@@ -226,10 +228,13 @@ class DataParallelTrainer:
         self.step_dev.fill_(int(sd["step"]))
         self.lr_dev.fill_(float(sd["lr"]))
         o = sd.get("optim", {})
-        self.betas = tuple(o.get("betas", self.betas))
-        self.eps = o.get("eps", self.eps)
-        self.wd = o.get("weight_decay", self.wd)
-        self.clip = o.get("grad_clip", self.clip)
+        new = (tuple(o.get("betas", self.betas)), o.get("eps", self.eps), o.get("weight_decay", self.wd),
+               o.get("grad_clip", self.clip))
+        if new != (tuple(self.betas), self.eps, self.wd, self.clip) and self.graph is not None:
+            # these settings are kernel arguments baked into the captured graph:
+            # run eagerly until capture() is called again
+            self.graph = None
+        self.betas, self.eps, self.wd, self.clip = new
         torch.cuda.synchronize(self.device)
 
     def save(self, path: str) -> None:
