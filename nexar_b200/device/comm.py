@@ -236,8 +236,10 @@ class DeviceCommunicator:
 
     # ----------------------------------------------------------- construction
     @classmethod
-    def from_torch(cls, group=None, device: Optional[int] = None, **kw) -> "DeviceCommunicator":
-        """Build from an initialised ``torch.distributed`` process group."""
+    def from_torch(cls, group=None, device: Optional[int] = None, nccl: bool = False,
+                   **kw) -> "DeviceCommunicator":
+        """Build from an initialised ``torch.distributed`` process group
+        (``nccl=True`` also attaches an NcclGroup over it for device send / recv)."""
         import torch.distributed as dist
         rank = dist.get_rank(group)
         world = dist.get_world_size(group)
@@ -251,7 +253,11 @@ class DeviceCommunicator:
         def barrier():
             dist.barrier(group=group)
 
-        return cls(rank, world, dev, exchange, barrier=barrier, **kw)
+        out = cls(rank, world, dev, exchange, barrier=barrier, **kw)
+        if nccl:
+            from .nccl import NcclGroup
+            out.attach_nccl(NcclGroup.from_torch(group, device=dev))
+        return out
 
     @classmethod
     def from_client(cls, client, device: Optional[int] = None, **kw) -> "DeviceCommunicator":

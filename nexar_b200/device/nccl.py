@@ -204,6 +204,18 @@ class NcclGroup:
             raise err from None
         self._stream = stream if stream is not None else torch.cuda.ExternalStream(self._g.stream, device=dev)
 
+    @classmethod
+    def from_torch(cls, group=None, device: Optional[int] = None,
+                   stream: Optional[torch.cuda.Stream] = None) -> "NcclGroup":
+        """Build over an initialised ``torch.distributed`` process group (its
+        rank 0 creates the id; collective over the group)."""
+        import torch.distributed as dist
+        rank, world = dist.get_rank(group), dist.get_world_size(group)
+        holder = [unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(holder, src=dist.get_global_rank(group, 0) if group is not None else 0,
+                                   group=group)
+        return cls(rank, world, holder[0], device=device, stream=stream)
+
     # reference-style constructor name
     @classmethod
     def init(cls, stream: Optional[torch.cuda.Stream], local_rank: int, local_world: int, uid: bytes,
