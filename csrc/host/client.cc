@@ -429,34 +429,29 @@ void NexarClient::set_adapter(std::shared_ptr<DeviceAdapter> a) {
 
 // Point to point moves the buffer through the adapter: staged to the host
 // before sending, written back after receiving (nexar/src/client/async_client.rs:312-379).
+// Messages travel as tagged raw frames on the communicator's p2p tag space
+// (written straight from the caller's buffer, no message encoding), and a
+// receive takes the oldest message with its tag (the reference's lane takes
+// the next message and errors on a tag mismatch).
 void NexarClient::send(const void* ptr, size_t size, Rank dest, uint32_t tag) {
   const Rank m = mesh_rank(dest);
-  const uint8_t* src = static_cast<const uint8_t*>(ptr);
-  Bytes staged;
-  if (!adapter_->host_addressable()) {
-    staged.resize(size);
-    adapter_->stage_for_send(ptr, size, staged.data());
-    src = staged.data();
+  if (adapter_->host_addressable()) {
+    mesh_->send_tagged(m, comm_id_, kP2PTagBit | tag, ptr, size);
+    return;
   }
-  if (comm_id_ == 0) {
-    Bytes payload = adapter_->host_addressable() ? Bytes(src, src + size) : std::move(staged);
-    mesh_->send_message(m, Message::data(tag, mesh_->rank(), std::move(payload)), Priority::Bulk);
-  } else {
-    mesh_->send_tagged(m, comm_id_, kP2PTagBit | tag, src, size);
-  }
+  Bytes staged(size);
+  adapter_->stage_for_send(ptr, size, staged.data());
+  mesh_->send_tagged(m, comm_id_, kP2PTagBit | tag, staged.data(), size);
+}
+
+Bytes NexarClient::recv_p2p(Rank src, uint32_t tag) {
+  const Rank m = mesh_rank(src);
+  auto dl = deadline_in(collective_timeout());
+  return std::move(mesh_->box(m)->pop(LaneKey{LaneKind::Tagged, comm_id_, kP2PTagBit | tag}, dl).bytes);
 }
 
 void NexarClient::recv(void* ptr, size_t size, Rank src, uint32_t tag) {
-  const Rank m = mesh_rank(src);
-  auto dl = deadline_in(collective_timeout());
-  Bytes payload;
-  if (comm_id_ == 0) {
-    // Tag matching: the oldest Data message with this tag (the reference's
-    // lane takes the next message and errors on a tag mismatch).
-    payload = std::move(mesh_->box(m)->pop_data(tag, dl).msg.payload);
-  } else {
-    payload = std::move(mesh_->box(m)->pop(LaneKey{LaneKind::Tagged, comm_id_, kP2PTagBit | tag}, dl).bytes);
-  }
+  Bytes payload = recv_p2p(src, tag);
   if (payload.size() != size)
     fail(Err::BufferSizeMismatch, "buffer size mismatch: expected " + std::to_string(size) + " bytes, got " + std::to_string(payload.size()));
   if (adapter_->host_addressable()) std::memcpy(ptr, payload.data(), size);
@@ -468,20 +463,13 @@ void NexarClient::send_iov(const std::vector<std::pair<const void*, size_t>>& io
   for (auto& e : iov) total += e.second;
   Bytes b(total);
   adapter_->stage_for_send_iov(iov, b.data());
-  // b is host memory now: send it without a second staging pass.
-  const Rank m = mesh_rank(dest);
-  if (comm_id_ == 0) mesh_->send_message(m, Message::data(tag, mesh_->rank(), std::move(b)), Priority::Bulk);
-  else mesh_->send_tagged(m, comm_id_, kP2PTagBit | tag, b.data(), b.size());
+  mesh_->send_tagged(mesh_rank(dest), comm_id_, kP2PTagBit | tag, b.data(), b.size());
 }
 
 void NexarClient::recv_iov(const std::vector<std::pair<void*, size_t>>& iov, Rank src, uint32_t tag) {
   size_t total = 0;
   for (auto& e : iov) total += e.second;
-  const Rank m = mesh_rank(src);
-  auto dl = deadline_in(collective_timeout());
-  Bytes payload;
-  if (comm_id_ == 0) payload = std::move(mesh_->box(m)->pop_data(tag, dl).msg.payload);
-  else payload = std::move(mesh_->box(m)->pop(LaneKey{LaneKind::Tagged, comm_id_, kP2PTagBit | tag}, dl).bytes);
+  Bytes payload = recv_p2p(src, tag);
   if (payload.size() != total)
     fail(Err::BufferSizeMismatch, "buffer size mismatch: expected " + std::to_string(total) + " bytes, got " + std::to_string(payload.size()));
   adapter_->receive_to_device_iov(payload.data(), iov);

@@ -226,6 +226,8 @@ class NexarClient : public std::enable_shared_from_this<NexarClient> {
   void recv(void* ptr, size_t size, Rank src, uint32_t tag);
   void send_iov(const std::vector<std::pair<const void*, size_t>>& iov, Rank dest, uint32_t tag);
   void recv_iov(const std::vector<std::pair<void*, size_t>>& iov, Rank src, uint32_t tag);
+  // The payload of the oldest p2p message from src with this tag.
+  Bytes recv_p2p(Rank src, uint32_t tag);
   void send_bytes(Rank dest, const void* p, size_t n);
   Bytes recv_bytes(Rank src);
   void send_bytes_tagged(Rank dest, uint64_t tag, const void* p, size_t n);
