@@ -7,7 +7,7 @@ namespace nexar {
 
 namespace {
 constexpr uint32_t kMeshMagic = 0x4e584d31;  // "NXM1"
-constexpr uint64_t kP2PTagBit = 1ull << 63;   // p2p send/recv on non-root communicators
+constexpr uint64_t kP2PTagBit = 1ull << 63;   // tag space of p2p send / recv (apart from tagged bytes)
 enum RelayLane : uint8_t { kRelayTagged = 0, kRelayControl = 1, kRelayRaw = 2 };
 
 uint64_t token_hash(const Bytes& t) { return t.empty() ? 0 : fnv1a_comm_id({t}); }
