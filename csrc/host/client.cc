@@ -155,6 +155,15 @@ void Mesh::send_raw(Rank dest, uint64_t comm, const void* p, size_t n) {
   send_message((Rank)hop, Message::relay(rank_, dest, 0, relay_payload(kRelayRaw, comm, p, n)), Priority::Bulk);
 }
 
+void Mesh::send_data(Rank dest, uint32_t tag, const void* p, size_t n) {
+  if (auto c = conn(dest)) {
+    c->send_data(tag, rank_, p, n, Priority::Bulk);
+    return;
+  }
+  const auto* b = static_cast<const uint8_t*>(p);
+  send_message(dest, Message::data(tag, rank_, Bytes(b, b + n)), Priority::Bulk);
+}
+
 void Mesh::send_message(Rank dest, const Message& m, Priority prio) {
   if (auto c = conn(dest)) {
     c->send_message(m, prio);
@@ -429,24 +438,35 @@ void NexarClient::set_adapter(std::shared_ptr<DeviceAdapter> a) {
 
 // Point to point moves the buffer through the adapter: staged to the host
 // before sending, written back after receiving (nexar/src/client/async_client.rs:312-379).
-// Messages travel as tagged raw frames on the communicator's p2p tag space
-// (written straight from the caller's buffer, no message encoding), and a
-// receive takes the oldest message with its tag (the reference's lane takes
-// the next message and errors on a tag mismatch).
-void NexarClient::send(const void* ptr, size_t size, Rank dest, uint32_t tag) {
+// On the root communicator a message is a Data message (tag, source rank,
+// payload), as the reference sends it, so send pairs with recv_message_from and
+// send_message_to with recv; the payload is written straight from the caller's
+// buffer and read straight into its own buffer (no encode / decode copies). A
+// receive takes the oldest Data message with its tag (the reference takes the
+// next one and fails on a tag mismatch). On a split / rebuilt communicator the
+// message travels as a tagged frame keyed by the communicator id, so
+// communicators that share links never see each other's messages (the
+// reference's Data message has no communicator id).
+void NexarClient::p2p_send(const void* ptr, size_t size, Rank dest, uint32_t tag) {
   const Rank m = mesh_rank(dest);
+  if (comm_id_ == 0) mesh_->send_data(m, tag, ptr, size);
+  else mesh_->send_tagged(m, comm_id_, kP2PTagBit | tag, ptr, size);
+}
+
+void NexarClient::send(const void* ptr, size_t size, Rank dest, uint32_t tag) {
   if (adapter_->host_addressable()) {
-    mesh_->send_tagged(m, comm_id_, kP2PTagBit | tag, ptr, size);
+    p2p_send(ptr, size, dest, tag);
     return;
   }
   Bytes staged(size);
   adapter_->stage_for_send(ptr, size, staged.data());
-  mesh_->send_tagged(m, comm_id_, kP2PTagBit | tag, staged.data(), size);
+  p2p_send(staged.data(), size, dest, tag);
 }
 
 Bytes NexarClient::recv_p2p(Rank src, uint32_t tag) {
   const Rank m = mesh_rank(src);
   auto dl = deadline_in(collective_timeout());
+  if (comm_id_ == 0) return std::move(mesh_->box(m)->pop_data(tag, dl).msg.payload);
   return std::move(mesh_->box(m)->pop(LaneKey{LaneKind::Tagged, comm_id_, kP2PTagBit | tag}, dl).bytes);
 }
 
@@ -463,7 +483,7 @@ void NexarClient::send_iov(const std::vector<std::pair<const void*, size_t>>& io
   for (auto& e : iov) total += e.second;
   Bytes b(total);
   adapter_->stage_for_send_iov(iov, b.data());
-  mesh_->send_tagged(mesh_rank(dest), comm_id_, kP2PTagBit | tag, b.data(), b.size());
+  p2p_send(b.data(), b.size(), dest, tag);
 }
 
 void NexarClient::recv_iov(const std::vector<std::pair<void*, size_t>>& iov, Rank src, uint32_t tag) {

@@ -120,6 +120,9 @@ class Mesh : public std::enable_shared_from_this<Mesh> {
   void send_tagged(Rank dest, uint64_t comm, uint64_t tag, const void* p, size_t n);
   void send_raw(Rank dest, uint64_t comm, const void* p, size_t n);
   void send_message(Rank dest, const Message& m, Priority prio);
+  // One Data message (tag, this rank, payload) written from the caller's
+  // buffer on a direct link; relayed as an encoded message otherwise.
+  void send_data(Rank dest, uint32_t tag, const void* p, size_t n);
 
   // Failure detection (nexar/src/cluster/health.rs:11-103): a background
   // thread sends heartbeats every interval and declares a peer dead when a
@@ -293,6 +296,8 @@ class NexarClient : public std::enable_shared_from_this<NexarClient> {
   std::atomic<uint64_t> barrier_epoch_{0};
 
  private:
+  // Root communicator: a Data message; split / rebuilt ones: a tagged frame.
+  void p2p_send(const void* ptr, size_t size, Rank dest, uint32_t tag);
   std::shared_ptr<Mesh> mesh_;
   Rank rank_;
   uint32_t world_;

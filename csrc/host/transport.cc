@@ -369,6 +369,25 @@ void PeerConnection::send_message(const Message& m, Priority prio) {
   uint64_t len = enc.size();
   send_frame(kFrameMessage, &len, 1, enc.data(), enc.size());
 }
+void PeerConnection::send_data(uint32_t tag, Rank src, const void* p, size_t n, Priority prio) {
+  if (!alive_) fail(Err::PeerDisconnected, "peer " + std::to_string(peer_) + " disconnected unexpectedly");
+  constexpr size_t kBody = kDataPrefixBytes - kHeaderSize;  // kind, tag, src, blob length
+  if (n + kBody > 0xffffffffull) fail(Err::EncodeFailed, "message body exceeds u32::MAX bytes");
+  uint8_t hdr[1 + 8 + kDataPrefixBytes];
+  size_t h = 0;
+  hdr[h++] = kFrameMessage;
+  const uint64_t frame_len = kDataPrefixBytes + n;
+  for (int j = 0; j < 8; ++j) hdr[h++] = (frame_len >> (8 * j)) & 0xff;
+  h += encode_data_prefix(tag, src, n, prio, hdr + h);
+  std::lock_guard<std::mutex> g(write_mu_);
+  try {
+    io_->write_pair(hdr, h, p, n);
+  } catch (const NexarError&) {
+    alive_ = false;
+    throw NexarError(Err::PeerDisconnected, "peer " + std::to_string(peer_) + " disconnected unexpectedly");
+  }
+}
+
 void PeerConnection::send_raw(const void* p, size_t n) {
   uint64_t len = n;
   send_frame(kFrameRaw, &len, 1, p, n);
@@ -511,6 +530,36 @@ void PeerRouter::run() {
       if (len > kMaxMessageBytes) {
         NEXAR_LOG(LogLevel::Error, "oversized frame from rank " + std::to_string(peer));
         break;
+      }
+      if (kind == kFrameMessage && len >= kDataPrefixBytes) {
+        // Data messages (p2p send / recv) are parsed from their fixed prefix
+        // and the payload is read straight into its own buffer; any other
+        // message is reassembled and decoded whole.
+        uint8_t head[kDataPrefixBytes];
+        if (!in.read_exact(head, kDataPrefixBytes)) break;
+        uint32_t tag = 0;
+        Rank src = 0;
+        uint64_t plen = 0;
+        if (decode_data_prefix(head, len, &tag, &src, &plen)) {
+          Bytes data(plen);
+          if (plen && !in.read_exact(data.data(), plen)) break;
+          last_seen_ns_ = now_ns();
+          dispatch(Message::data(tag, src, std::move(data)));
+          continue;
+        }
+        Bytes whole(len);
+        std::memcpy(whole.data(), head, kDataPrefixBytes);
+        if (!in.read_exact(whole.data() + kDataPrefixBytes, len - kDataPrefixBytes)) break;
+        last_seen_ns_ = now_ns();
+        Message m;
+        try {
+          m = decode_message(whole.data(), whole.size());
+        } catch (const NexarError& e) {
+          NEXAR_LOG(LogLevel::Warn, std::string("dropping undecodable message: ") + e.what());
+          continue;
+        }
+        dispatch(std::move(m));
+        continue;
       }
       Bytes payload(len);
       if (len && !in.read_exact(payload.data(), len)) break;

@@ -134,6 +134,10 @@ class PeerConnection {
   void send_raw(const void* p, size_t n);
   void send_raw_comm(uint64_t comm_id, const void* p, size_t n);
   void send_raw_tagged(uint64_t comm_id, uint64_t tag, const void* p, size_t n);
+  // One Data message (wire kind 9: tag, source rank, payload blob), framed
+  // and encoded exactly as send_message(Message::data(...)) would, with the
+  // payload written straight from `p` (no encode copy).
+  void send_data(uint32_t tag, Rank src, const void* p, size_t n, Priority prio);
   // Shut the socket down (fault injection / teardown); the reader sees EOF.
   void close();
   bool alive() const { return alive_.load(); }

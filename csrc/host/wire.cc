@@ -190,6 +190,31 @@ Bytes encode_message(const Message& m, Priority prio) {
   return out;
 }
 
+size_t encode_data_prefix(uint32_t tag, Rank src, uint64_t payload_len, Priority prio, uint8_t* out) {
+  Header h;
+  h.payload_length = (uint32_t)(kDataPrefixBytes - kHeaderSize + payload_len);
+  h.priority = (uint8_t)prio;
+  h.encode(out);
+  size_t o = kHeaderSize;
+  out[o++] = (uint8_t)MsgKind::Data;
+  for (int i = 0; i < 4; ++i) out[o++] = (tag >> (8 * i)) & 0xff;
+  for (int i = 0; i < 4; ++i) out[o++] = (src >> (8 * i)) & 0xff;
+  for (int i = 0; i < 8; ++i) out[o++] = (payload_len >> (8 * i)) & 0xff;
+  return o;
+}
+
+bool decode_data_prefix(const uint8_t* p, uint64_t msg_len, uint32_t* tag, Rank* src, uint64_t* payload_len) {
+  Header h;
+  if (!Header::decode(p, &h)) return false;
+  if (p[kHeaderSize] != (uint8_t)MsgKind::Data) return false;
+  const uint64_t plen = get_le(p + kHeaderSize + 9, 8);
+  if ((uint64_t)h.payload_length + kHeaderSize != msg_len || plen + kDataPrefixBytes != msg_len) return false;
+  *tag = (uint32_t)get_le(p + kHeaderSize + 1, 4);
+  *src = (Rank)get_le(p + kHeaderSize + 5, 4);
+  *payload_len = plen;
+  return true;
+}
+
 Message decode_message(const uint8_t* p, size_t n) {
   if (n < kHeaderSize) fail(Err::DecodeFailed, "buffer shorter than the 8-byte header");
   Header h;

@@ -105,4 +105,15 @@ Bytes encode_message(const Message& m, Priority prio);
 // Parse header + body from one contiguous buffer (length checked).
 Message decode_message(const uint8_t* p, size_t n);
 
+// The fixed part of an encoded Data message ahead of its payload: the 8-byte
+// header, the variant byte, tag (u32), source rank (u32) and the payload's
+// blob length (u64). Data messages are written and parsed in two pieces (this
+// prefix, then the payload in place) so a p2p payload is never copied into or
+// out of an encode buffer; the bytes are those encode_message produces.
+constexpr size_t kDataPrefixBytes = kHeaderSize + 1 + 4 + 4 + 8;
+size_t encode_data_prefix(uint32_t tag, Rank src, uint64_t payload_len, Priority prio, uint8_t* out);
+// True if `p` (kDataPrefixBytes long) starts a well-formed Data message whose
+// encoding is `msg_len` bytes in total; fills tag, source and payload length.
+bool decode_data_prefix(const uint8_t* p, uint64_t msg_len, uint32_t* tag, Rank* src, uint64_t* payload_len);
+
 }  // namespace nexar

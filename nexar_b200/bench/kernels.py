@@ -12,9 +12,10 @@ names:
   ag_gemm      fused all-gather -> GEMM with a one-rank communicator
                (8192 x 3584 x 4096 bf16, the TP=8 gate + up projection per GPU:
                the copy warps stage the local shard, the MMA waits on it)
-  attn         causal self-attention forward + backward of one GPT-2 layer
-               (B 8, T 1024, 12 heads of 64) on the tcgen05 kernels, with the
-               same on torch SDPA (cuDNN) for comparison
+  attn         causal self-attention of one GPT-2 layer (B 8, T 1024, 12
+               heads of 64): forward (k_attn_fwd) and backward (k_attn_delta,
+               k_attn_bwd, k_attn_dq_out) timed apart on the tcgen05 kernels,
+               and torch SDPA (cuDNN) forward and forward + backward
   compress     top-1 % + e4m3 compression of 64 Mi bf16 values
   ln_bwd       LayerNorm backward, 8192 x 768 with the bias-gradient sums
 
@@ -91,24 +92,32 @@ def main():
     elif args.name == "attn":
         Bn, T, Hn = 8, 1024, 12
         Cn = Hn * 64
-        qkv = torch.randn(Bn * T, 3 * Cn, device=dev, generator=g).to(torch.bfloat16).requires_grad_(True)
+        qkv = torch.randn(Bn * T, 3 * Cn, device=dev, generator=g).to(torch.bfloat16)
         dy = torch.randn(Bn * T, Cn, device=dev, generator=g).to(torch.bfloat16)
+        y = torch.empty(Bn * T, Cn, device=dev, dtype=torch.bfloat16)
+        lse = torch.empty(Bn * Hn * T, device=dev, dtype=torch.float32)
+        dqkv = torch.empty_like(qkv)
+        ws = torch.empty(C.attn_bwd_workspace_floats(Bn, T, Hn), device=dev, dtype=torch.float32)
+        fwd_ms = _time(lambda: C.attn_fwd(qkv, y, lse, Bn, T, Hn, True), args.iters)
+        bwd_ms = _time(lambda: C.attn_bwd(qkv, y, dy, lse, dqkv, ws, Bn, T, Hn, True), args.iters)
+        qkv_r = qkv.clone().requires_grad_(True)
 
-        def ours():
-            y = ops.attention(qkv, Bn, T, Hn, causal=True)
-            y.backward(dy)
-
-        def sdpa():
-            x = qkv.view(Bn, T, 3, Hn, 64)
+        def sdpa_fwd():
+            x = qkv_r.view(Bn, T, 3, Hn, 64)
             q, k, v = (t.transpose(1, 2) for t in x.unbind(2))
-            y = torch.nn.functional.scaled_dot_product_attention(q, k, v, is_causal=True)
-            y.transpose(1, 2).reshape(Bn * T, Cn).backward(dy)
+            return torch.nn.functional.scaled_dot_product_attention(q, k, v, is_causal=True)
 
-        ms = _time(ours, args.iters)
-        ms_ref = _time(sdpa, args.iters)
-        flops = 3.5 * 4 * Bn * Hn * T * T * 64 / 2  # fwd (1) + bwd (2.5) x causal half
-        rec.update(B=Bn, T=T, H=Hn, us=round(ms * 1e3, 1), tflops=round(flops / ms / 1e9, 1),
-                   sdpa_us=round(ms_ref * 1e3, 1), sdpa_tflops=round(flops / ms_ref / 1e9, 1))
+        def sdpa_both():
+            sdpa_fwd().transpose(1, 2).reshape(Bn * T, Cn).backward(dy)
+
+        with torch.no_grad():
+            sdpa_fwd_ms = _time(sdpa_fwd, args.iters)
+        sdpa_ms = _time(sdpa_both, args.iters)
+        ffl = 4 * Bn * Hn * T * T * 64 / 2  # causal: half of the T x T scores
+        rec.update(B=Bn, T=T, H=Hn, fwd_us=round(fwd_ms * 1e3, 1), bwd_us=round(bwd_ms * 1e3, 1),
+                   fwd_tflops=round(ffl / fwd_ms / 1e9, 1), bwd_tflops=round(2.5 * ffl / bwd_ms / 1e9, 1),
+                   sdpa_fwd_us=round(sdpa_fwd_ms * 1e3, 1), sdpa_fwd_bwd_us=round(sdpa_ms * 1e3, 1),
+                   sdpa_bwd_us_incl_autograd=round((sdpa_ms - sdpa_fwd_ms) * 1e3, 1))
     elif args.name == "compress":
         n = 64 << 20
         grad = torch.randn(n, device=dev, generator=g).to(torch.bfloat16)

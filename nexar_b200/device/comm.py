@@ -132,6 +132,7 @@ def _observed(op: str):
                 st["bytes"] += t.numel() * t.element_size()
             if _NVTX:
                 torch.cuda.nvtx.range_push(f"nexar.{op}")
+            self.order_launch()
             timed = self._timer is not None and not torch.cuda.is_current_stream_capturing()
             if timed:
                 ev0 = torch.cuda.Event(enable_timing=True)
@@ -233,6 +234,7 @@ class DeviceCommunicator:
         self._stats = {}
         self._nccl = None
         self._timer = DeviceTimeHistogram() if _TIMING else None
+        self._last_stream = None
 
     # ----------------------------------------------------------- construction
     @classmethod
@@ -306,6 +308,32 @@ class DeviceCommunicator:
     @property
     def native(self):
         return self._comm
+
+    # ----------------------------------------------------------- launch order
+    def order_launch(self):
+        """Order the next kernel of this communicator after its previous one.
+
+        Every collective kernel of one communicator shares a device call
+        counter, the signal pad and the staging slots, so its kernels must run
+        one after another. Kernels on one stream already do; when this launch
+        goes to another stream than the previous one (a blocking collective on
+        the current stream after a ``*_nb`` on the side stream, or the other
+        way round), the new stream first waits for the old one. Collectives
+        then complete in call order on every rank, as the reference's
+        call-time tags keep concurrent non-blocking collectives apart
+        (nexar/src/client/collectives_nb.rs:33-47). The fused kernels and the
+        MoE dispatch / combine call this too."""
+        cur = torch.cuda.current_stream(self.device)
+        last = self._last_stream
+        if last is not None and last != cur:
+            cap_now = torch.cuda.is_current_stream_capturing()
+            with torch.cuda.stream(last):
+                cap_last = torch.cuda.is_current_stream_capturing()
+            # A capturing stream cannot wait on work outside its capture (and
+            # the reverse): graph replays are ordered by the caller.
+            if cap_now == cap_last:
+                cur.wait_stream(last)
+        self._last_stream = cur
 
     # ----------------------------------------------------------- status
     def close(self):
@@ -499,6 +527,7 @@ class DeviceCommunicator:
         M, N = A.shape[0], B.shape[0]
         if out is None:
             out = torch.empty(M // self.world_size, N, dtype=A.dtype, device=A.device)
+        self.order_launch()
         self._C.gemm_reduce_scatter(self._comm, A, B, out, bias, float(alpha))
         return out
 
@@ -513,6 +542,7 @@ class DeviceCommunicator:
         M, N = A_q.shape[0], B_q.shape[0]
         if out is None:
             out = torch.empty(M // self.world_size, N, dtype=torch.bfloat16, device=A_q.device)
+        self.order_launch()
         self._C.gemm_fp8_reduce_scatter(self._comm, A_q, A_s, B_q, B_s, out, bias, float(alpha))
         return out
 
@@ -529,6 +559,7 @@ class DeviceCommunicator:
         if out is None:
             out = torch.empty(M, B.shape[0], dtype=x.dtype, device=x.device)
         afull, cnt = self._ag_workspace(M, K, x.device)
+        self.order_launch()
         self._C.all_gather_gemm(self._comm, x, B, out, afull, cnt, bias, 1 if act == "gelu" else 0, pre, float(alpha))
         return out
 

@@ -407,16 +407,19 @@ def exchange_nccl_id(client, local_ranks, node_idx: int, lead: int) -> bytes:
     the lead creates it and sends it to every other local rank with tag
     ``0xACC1_0000 | node_idx``; the others receive it from the lead
     (nexar-nccl/src/bootstrap.rs:79-118)."""
+    import numpy as np
     tag = NCCL_ID_TAG_BASE | (int(node_idx) & 0xFFFF)
     if client.rank == lead:
         uid = unique_id()
+        buf = np.frombuffer(uid, dtype=np.uint8).copy()
         for r in local_ranks:
             if r != lead:
-                client.send_bytes_tagged(r, tag, uid)
+                client.send(buf.ctypes.data, buf.nbytes, r, tag)
         return uid
-    data = client.recv_bytes_tagged(lead, tag)
+    buf = np.empty(UNIQUE_ID_BYTES, dtype=np.uint8)
+    client.recv(buf.ctypes.data, buf.nbytes, lead, tag)
     try:
-        return id_from_bytes(data)
+        return id_from_bytes(buf.tobytes())
     except BootstrapError as e:
         raise BootstrapError(f"NCCL id from rank {lead}: {e}") from None
 

@@ -70,6 +70,7 @@ class ExpertParallelMoE:
         self.counts.zero_()
         C.moe_route(logits, self.slot_expert, self.slot_pos, self.slot_gate, self.counts)
         comm.all_gather(self.counts, self.counts_all)
+        comm.order_launch()
         C.moe_dispatch(comm.native, x, self.slot_expert, self.slot_pos, self.counts_all, self.recv, self.ticket)
         # rows this expert received (host read of E*E ints: sizes the GEMM launches)
         rows = int(self.counts_all.view(self.E, self.E)[:, comm.rank].sum().item())
@@ -81,6 +82,7 @@ class ExpertParallelMoE:
             C.swiglu_fwd(gu, h)
             C.gemm(h, self.w_down, self.eout[:rows])
         out = torch.empty_like(x)
+        comm.order_launch()
         C.moe_combine(comm.native, out, self.slot_expert, self.slot_pos, self.slot_gate, self.eout)
         return out
 

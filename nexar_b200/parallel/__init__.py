@@ -4,7 +4,7 @@
                 overlapped with backward, CUDA graph)
   ddp           data parallel wrapper for any module (bucketed all-reduce
                 overlapping backward)
-  zero          sharded data parallel optimizer (ZeRO stage 1/2) for any module
+  zero          sharded data parallel optimizer (ZeRO stage 1: optimizer state) for any module
   tensor        tensor parallel SwiGLU MLP step (fused all-gather -> GEMM and
                 GEMM -> reduce-scatter, forward and backward)
   expert        expert parallel MoE step (fused dispatch / combine, forward and

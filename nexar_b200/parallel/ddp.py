@@ -7,8 +7,12 @@ A post-accumulate hook marks each gradient ready; when a bucket is complete
 its gradients are packed into one flat buffer and a non-blocking all-reduce
 of the bucket starts while backward continues. :meth:`finish` (call it
 before the optimizer step) waits for every bucket and writes the averaged
-gradients back. Every rank must run the same model, so the buckets complete
-in the same order everywhere and the collectives match.
+gradients back. Gradient accumulation: run every backward pass but the last
+of a step under :meth:`no_sync` (gradients only accumulate in ``.grad``); the
+last pass starts the all-reduces of the accumulated sums. A second backward
+outside ``no_sync`` before ``finish()`` raises instead of losing gradients.
+Every rank must run the same model, so the buckets complete in the same
+order everywhere and the collectives match.
 
 Backends: :class:`DeviceBuckets` (the device communicator's all-reduce on its
 side stream, with the 1/W mean fused into the kernel) and
@@ -21,6 +25,7 @@ nexar/src/collective/bucketed_allreduce.rs:23-75).
 """
 from __future__ import annotations
 
+import contextlib
 from typing import List
 
 import torch
@@ -74,6 +79,7 @@ class DistributedDataParallel(torch.nn.Module):
         if cur:
             self.buckets.append(cur)
         self._bucket_of = {id(p): b for b, ps in enumerate(self.buckets) for p in ps}
+        self._sync = True
         self._reset()
         for p in params:
             p.register_post_accumulate_grad_hook(self._hook)
@@ -82,8 +88,24 @@ class DistributedDataParallel(torch.nn.Module):
         self._left = [len(b) for b in self.buckets]
         self._inflight = {}
 
+    @contextlib.contextmanager
+    def no_sync(self):
+        """Backward passes inside this context only accumulate gradients; the
+        next backward outside it reduces the accumulated sums."""
+        old, self._sync = self._sync, False
+        try:
+            yield
+        finally:
+            self._sync = old
+
     def _hook(self, p):
+        if not self._sync:
+            return
         b = self._bucket_of[id(p)]
+        if b in self._inflight:
+            raise RuntimeError(
+                f"a gradient of bucket {b} arrived after its all-reduce had started: a second backward pass "
+                "before finish(); run the accumulation passes under no_sync()")
         self._left[b] -= 1
         if self._left[b] == 0:
             flat = torch.cat([q.grad.reshape(-1) for q in self.buckets[b]])

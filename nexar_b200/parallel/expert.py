@@ -108,12 +108,14 @@ class DeviceEP:
 
     def dispatch(self, x, slots):
         L = self.layer
+        self.comm.order_launch()
         self._C.moe_dispatch(self.comm.native, x.contiguous(), L.slot_expert, L.slot_pos, L.counts_all, L.recv,
                              L.ticket)
         return L.recv[:slots["rows"]]
 
     def dispatch_rows(self, g, slots, scale):
         L = self.layer
+        self.comm.order_launch()
         self._C.moe_dispatch_rows(self.comm.native, g.contiguous(), L.slot_expert, L.slot_pos, scale, self.d_eout,
                                   L.ticket)
         return self.d_eout[:slots["rows"]]
@@ -121,6 +123,7 @@ class DeviceEP:
     def combine(self, buf, slots, gates, T, d):
         L = self.layer
         out = torch.empty(T, d, dtype=torch.bfloat16, device=buf.device)
+        self.comm.order_launch()
         self._C.moe_combine(self.comm.native, out, L.slot_expert, L.slot_pos, gates, buf)
         return out
 

@@ -1,11 +1,14 @@
-"""Sharded data parallelism (ZeRO stage 1/2) for any torch module.
+"""Sharded data parallelism (ZeRO stage 1: optimizer state sharded) for any torch module.
 
-Every rank keeps the full parameters (for forward and backward) but only
-1/W of the optimizer state: after backward the flat gradient is
-reduce-scattered (rank r receives the average over ranks of its shard),
-AdamW updates the fp32 master copy of that shard, and the updated shards
-are all-gathered back into every rank's parameters. Gradient and optimizer
-memory per rank drop by W; the bytes on the wire equal one all-reduce.
+Every rank keeps the full parameters and the full gradients (for forward and
+backward) but only 1/W of the optimizer state: after backward the flat
+gradient is reduce-scattered (rank r receives the average over ranks of its
+shard), AdamW updates the fp32 master copy of that shard, and the updated
+shards are all-gathered back into every rank's parameters. Optimizer memory
+(master weights and both moments) per rank drops by W; gradient memory does
+not (ZeRO stage 2 would also shard the gradients). The bytes on the wire
+equal one all-reduce. All parameters must share one dtype (they travel as
+one flat tensor).
 
 Backends: :class:`DeviceSharding` (a DeviceCommunicator: reduce-scatter and
 all-gather kernels over NVLink peer memory, with the 1/W averaging fused into
@@ -70,6 +73,9 @@ class ShardedAdamW:
     def __init__(self, params: Iterable[torch.nn.Parameter], backend, lr: float = 1e-3, betas=(0.9, 0.999),
                  eps: float = 1e-8, weight_decay: float = 0.0):
         self.params = [p for p in params if p.requires_grad]
+        dtypes = {p.dtype for p in self.params}
+        if len(dtypes) != 1:
+            raise ValueError(f"ShardedAdamW needs parameters of one dtype (one flat tensor), got {sorted(map(str, dtypes))}")
         self.backend = backend
         self.lr, self.betas, self.eps, self.wd = lr, betas, eps, weight_decay
         W, r = backend.world_size, backend.rank

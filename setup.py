@@ -35,7 +35,8 @@ def rel(paths):
     return sorted(os.path.relpath(p, ROOT) for p in paths)
 
 
-host_sources = rel(glob.glob(os.path.join(ROOT, "csrc", "host", "**", "*.cc"), recursive=True))
+# csrc/host/tests/ holds native test drivers (their own main): not part of the extension.
+host_sources = rel(glob.glob(os.path.join(ROOT, "csrc", "host", "*.cc")))
 cuda_sources = rel(glob.glob(os.path.join(ROOT, "csrc", "cuda", "*.cu"))
                    + glob.glob(os.path.join(ROOT, "csrc", "cuda", "*.cpp")))
 

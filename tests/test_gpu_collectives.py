@@ -146,6 +146,28 @@ def _worker(rank, world, port, results):
     h = comm.all_reduce_nb(t)
     h.wait()
     torch.cuda.synchronize()
+    # non-blocking and blocking collectives in flight together: an all_reduce_nb
+    # (side stream), then a blocking all_reduce (current stream) before wait(),
+    # then two overlapping non-blocking ones; each against the fp64 oracle
+    n = 4 << 20
+    xa = [_data(r, n, torch.float32, seed=7) for r in range(world)]
+    xb = [_data(r, n, torch.float32, seed=8) for r in range(world)]
+    xc = [_data(r, n, torch.float32, seed=9) for r in range(world)]
+    xd = [_data(r, n, torch.float32, seed=10) for r in range(world)]
+    a, b, c, d = (v[rank].to(dev) for v in (xa, xb, xc, xd))
+    d_out = torch.empty(n // world, device=dev)
+    ha = comm.all_reduce_nb(a)
+    comm.all_reduce(b, scale=0.5)
+    hc = comm.all_reduce_nb(c, op="max")
+    hd = comm.reduce_scatter_nb(d, d_out)
+    for hh in (ha, hc, hd):
+        hh.wait()
+    torch.cuda.synchronize()
+    check("nb all_reduce (then blocking)", a, _oracle_reduce(xa, "sum"), **_tol(torch.float32, world))
+    check("blocking all_reduce while nb in flight", b, _oracle_reduce(xb, "sum") * 0.5, **_tol(torch.float32, world))
+    check("overlapping nb all_reduce max", c, _oracle_reduce(xc, "max"), atol=0, rtol=0)
+    check("overlapping nb reduce_scatter", d_out, _oracle_reduce(xd, "sum")[rank * (n // world):(rank + 1) * (n // world)],
+          **_tol(torch.float32, world))
     try:
         comm.check()
     except Exception as e:  # noqa: BLE001

@@ -27,6 +27,42 @@ def test_peer_messages_and_rpc_dispatcher():
     t.join()
 
 
+def test_p2p_send_is_a_data_message_on_the_root_communicator():
+    """send / recv on the root communicator carry Data messages (as the
+    reference's client.send), so they pair with send_message_to /
+    recv_message_from; a split communicator's p2p traffic stays apart from the
+    root's even under the same tag."""
+    from nexar_b200.client import NexarClient
+    cs = NexarClient.bootstrap_local(2)
+    # send -> recv_message_from
+    x = np.arange(64, dtype=np.uint8)
+    cs[0].send(x.ctypes.data, x.nbytes, 1, 77)
+    assert cs[1].recv_message_from(0, 77, 5.0) == x.tobytes()
+    # send_message_to -> recv (large enough to take several socket reads)
+    payload = bytes(np.random.default_rng(0).integers(0, 256, 300_000, dtype=np.uint8))
+    cs[1].send_message_to(0, 78, payload)
+    out = np.empty(len(payload), np.uint8)
+    cs[0].recv(out.ctypes.data, out.nbytes, 1, 78)
+    assert out.tobytes() == payload
+    # messages with other tags wait their turn; the oldest with the tag is taken
+    a, b = np.full(8, 1, np.uint8), np.full(8, 2, np.uint8)
+    cs[0].send(a.ctypes.data, 8, 1, 5)
+    cs[0].send(b.ctypes.data, 8, 1, 6)
+    got6, got5 = np.empty(8, np.uint8), np.empty(8, np.uint8)
+    cs[1].recv(got6.ctypes.data, 8, 0, 6)
+    cs[1].recv(got5.ctypes.data, 8, 0, 5)
+    assert (got6 == 2).all() and (got5 == 1).all()
+    # a split communicator's message under the same tag is not the root's
+    subs = run_collective(cs, lambda c: c.split(0, c.rank))
+    s_msg, r_msg = np.full(4, 9, np.uint8), np.full(4, 3, np.uint8)
+    subs[0].send(s_msg.ctypes.data, 4, 1, 11)
+    cs[0].send(r_msg.ctypes.data, 4, 1, 11)
+    root_got, sub_got = np.empty(4, np.uint8), np.empty(4, np.uint8)
+    cs[1].recv(root_got.ctypes.data, 4, 0, 11)
+    subs[1].recv(sub_got.ctypes.data, 4, 0, 11)
+    assert (root_got == 3).all() and (sub_got == 9).all()
+
+
 def test_nonblocking_bucketed_and_compressed_and_rs_ag_host():
     from nexar_b200.client import NexarClient
     from nexar_b200.core import DataType

@@ -51,3 +51,47 @@ def test_ddp_matches_full_batch_sgd(W):
     for m in models:
         for p, q in zip(m.parameters(), ref.parameters()):
             torch.testing.assert_close(p, q, rtol=1e-10, atol=1e-12)
+
+
+def test_ddp_gradient_accumulation_with_no_sync():
+    """Two micro-batches per step (the first under no_sync) follow full-batch
+    SGD over both micro-batches of every rank; a second backward outside
+    no_sync before finish() raises."""
+    W, steps, rows, lr = 2, 2, 4, 0.1
+    g = torch.Generator().manual_seed(11)
+    xs = torch.randn(steps, W, 2, rows, 6, generator=g, dtype=torch.float64)
+    ys = torch.randn(steps, W, 2, rows, 2, generator=g, dtype=torch.float64)
+    ref = _model()
+    opt = torch.optim.SGD(ref.parameters(), lr=lr)
+    for s in range(steps):
+        opt.zero_grad()
+        (sum(((ref(xs[s, r, m]) - ys[s, r, m]) ** 2).mean() for r in range(W) for m in range(2)) / W).backward()
+        opt.step()
+
+    models = [_model() for _ in range(W)]
+    clients = bootstrap(W)
+    try:
+        def rank_fn(c):
+            ddp = DistributedDataParallel(models[c.rank], HostBuckets(c), bucket_bytes=600)
+            sgd = torch.optim.SGD(ddp.parameters(), lr=lr)
+            for s in range(steps):
+                sgd.zero_grad()
+                with ddp.no_sync():
+                    ((ddp(xs[s, c.rank, 0]) - ys[s, c.rank, 0]) ** 2).mean().backward()
+                assert not ddp._inflight
+                ((ddp(xs[s, c.rank, 1]) - ys[s, c.rank, 1]) ** 2).mean().backward()
+                ddp.finish()
+                sgd.step()
+            # a second backward outside no_sync before finish() is refused
+            ((ddp(xs[0, c.rank, 0]) - ys[0, c.rank, 0]) ** 2).mean().backward()
+            with pytest.raises(RuntimeError, match="no_sync"):
+                ((ddp(xs[0, c.rank, 1]) - ys[0, c.rank, 1]) ** 2).mean().backward()
+            return True
+
+        run_collective(clients, rank_fn)
+    finally:
+        for c in clients:
+            c.close()
+    for m in models:
+        for p, q in zip(m.parameters(), ref.parameters()):
+            torch.testing.assert_close(p, q, rtol=1e-10, atol=1e-12)
