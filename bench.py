@@ -2,6 +2,7 @@
 
     python bench.py --gpus N --steps K --warmup W            # nexar_b200 (this repo)
     python bench.py --impl reference ...                     # the reference (unavailable here)
+    python bench.py --impl torch ...                         # plain PyTorch + cuBLAS + NCCL comparator
 
 For N > 1 launch with torchrun (one rank per GPU). Per GPU: micro-batch 8 x
 1024 tokens, bf16, synthetic uniform token ids, random N(0, 0.02) init. The
@@ -54,6 +55,9 @@ def main():
     if args.impl == "reference":
         reference_unavailable(args)
         return 0
+    if args.impl == "torch":
+        from nexar_b200.bench.torch_gpt2 import run
+        return run(args, METRIC)
     if args.warmup < 3:
         args.warmup = 3
     import torch
@@ -112,6 +116,10 @@ def main():
         end.record()
         barrier()
     ms = start.elapsed_time(end)
+    tl = trainer.timeline()  # NEXAR_DP_TIMELINE=1: per-bucket all-reduce timeline of the last step
+    if tl is not None:
+        tl["rank"] = rank
+        print("timeline " + json.dumps(tl), file=sys.stderr, flush=True)
     eager_launches = _native.launch_count() - launches0
     gpu_launches = trainer.graph_launches * args.steps if trainer.graph is not None else eager_launches
     t = torch.tensor([ms], dtype=torch.float64, device=dev)

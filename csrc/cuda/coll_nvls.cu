@@ -350,9 +350,12 @@ __global__ void __launch_bounds__(kNvlsThreads) k_gather_bcast_nvls(CommDev c, c
 
 // Up to kMaxBlocks CTAs (two per SM): while one CTA of an SM waits on a
 // signal, the other copies, so HBM staging overlaps the NVLink phase.
-int nvls_grid(unsigned long long units, unsigned int /*max_blocks*/) {
+// `max_blocks` (the communicator's limit, e.g. a small grid for collectives
+// that overlap compute kernels) caps it further.
+int nvls_grid(unsigned long long units, unsigned int max_blocks) {
   unsigned long long g = units < 1 ? 1 : units;
   if (g > (unsigned long long)kMaxBlocks) g = kMaxBlocks;
+  if (max_blocks > 0 && g > max_blocks) g = max_blocks;
   return (int)g;
 }
 

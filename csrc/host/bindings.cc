@@ -303,7 +303,9 @@ PYBIND11_MODULE(_host, m) {
       })
       .def("checkout", &BufferPool::checkout)
       .def("tier_for_size", [](const BufferPool& b, size_t n) { return (int)b.tier_for_size(n); })
-      .def("free_count", [](const BufferPool& b, int t) { return b.free_count((PoolTier)t); });
+      .def("free_count", [](const BufferPool& b, int t) { return b.free_count((PoolTier)t); })
+      .def("blocks_reused", [](const BufferPool& b, int t) { return b.blocks_reused((PoolTier)t); })
+      .def("blocks_fresh", [](const BufferPool& b, int t) { return b.blocks_fresh((PoolTier)t); });
 
   // ------------------------------------------------------------ handles
   py::class_<CollectiveHandle>(m, "CollectiveHandle")
@@ -391,21 +393,24 @@ PYBIND11_MODULE(_host, m) {
 
   // ------------------------------------------------------------ client
   py::class_<NexarClient, std::shared_ptr<NexarClient>>(m, "NexarClient")
-      .def_static("bootstrap_local", &NexarClient::bootstrap_local, GR())
+      .def_static("bootstrap_local", &NexarClient::bootstrap_local, py::arg("world"), py::arg("config"),
+                  py::arg("pool") = std::shared_ptr<BufferPool>(), GR())
       .def_static("bootstrap_worker", [](const std::string& seed, const py::object& token, const Config& cfg,
-                                         const std::string& host) {
+                                         const std::string& host, std::shared_ptr<BufferPool> pool) {
         Bytes t = token.is_none() ? token_from_env() : to_bytes(token.cast<py::bytes>());
         py::gil_scoped_release r;
-        return NexarClient::bootstrap_worker(seed, t, cfg, host);
+        return NexarClient::bootstrap_worker(seed, t, cfg, host, std::move(pool));
       }, py::arg("seed_addr"), py::arg("token") = py::none(), py::arg("config") = Config(),
-         py::arg("bind_host") = "127.0.0.1")
-      .def_static("from_worker_info", [](std::shared_ptr<WorkerInfo> info, const Config& cfg) {
+         py::arg("bind_host") = "127.0.0.1", py::arg("pool") = std::shared_ptr<BufferPool>())
+      .def_static("from_worker_info", [](std::shared_ptr<WorkerInfo> info, const Config& cfg,
+                                         std::shared_ptr<BufferPool> pool) {
         if (!info || info->listen_fd < 0) fail(Err::ConnectionFailed, "worker info already used or closed");
         WorkerInfo w = *info;
         info->listen_fd = -1;  // the mesh owns the listener now
         py::gil_scoped_release r;
-        return NexarClient::from_worker_info(std::move(w), cfg);
-      }, py::arg("info"), py::arg("config") = Config())
+        return NexarClient::from_worker_info(std::move(w), cfg, std::move(pool));
+      }, py::arg("info"), py::arg("config") = Config(), py::arg("pool") = std::shared_ptr<BufferPool>())
+      .def_property_readonly("pool", [](const NexarClient& c) { return c.mesh()->pool(); })
       .def_property_readonly("rank", &NexarClient::rank)
       .def_property_readonly("world_size", &NexarClient::world_size)
       .def_property_readonly("comm_id", &NexarClient::comm_id)

@@ -1,13 +1,137 @@
 #include "buffer_pool.h"
 
+#include <cstdlib>
+#include <new>
+
 namespace nexar {
+
+namespace {
+// Every allocation made through pool_allocate carries this header in front
+// of the caller's bytes: the owning pool (nullptr for system allocations)
+// and the tier, so a block can be freed on any thread.
+struct alignas(64) BlockHeader {
+  BufferPool* pool;
+  uint32_t tier;
+  uint32_t magic;
+  size_t capacity;
+};
+constexpr uint32_t kBlockMagic = 0x4e58424cu;
+thread_local BufferPool* tls_pool = nullptr;
+
+void* system_block(size_t bytes) {
+  auto* h = static_cast<BlockHeader*>(std::malloc(sizeof(BlockHeader) + bytes));
+  if (!h) throw std::bad_alloc();
+  h->pool = nullptr;
+  h->tier = (uint32_t)PoolTier::Unpooled;
+  h->magic = kBlockMagic;
+  h->capacity = bytes;
+  return h;
+}
+}  // namespace
+
+void* pool_allocate(size_t bytes) {
+  void* block = nullptr;
+  if (tls_pool && bytes >= BufferPool::kPoolMinBytes) block = tls_pool->take_block(bytes);
+  if (!block) block = system_block(bytes);
+  return static_cast<BlockHeader*>(block) + 1;
+}
+
+void pool_deallocate(void* p) noexcept {
+  if (!p) return;
+  BlockHeader* h = static_cast<BlockHeader*>(p) - 1;
+  if (h->pool) h->pool->give_block(h);
+  else std::free(h);
+}
+
+PoolScope::PoolScope(BufferPool* pool) : prev_(tls_pool) { tls_pool = pool; }
+PoolScope::~PoolScope() { tls_pool = prev_; }
+
+struct PoolDeleter {
+  void operator()(BufferPool* p) const noexcept { p->orphan(); }
+};
+
+BufferPool::~BufferPool() {
+  for (auto& fl : free_blocks_)
+    for (void* b : fl) std::free(b);
+}
+
+void BufferPool::orphan() noexcept {
+  bool del;
+  {
+    std::lock_guard<std::mutex> g(mu_);
+    orphaned_ = true;
+    del = live_blocks_ == 0;
+  }
+  if (del) delete this;
+}
+
+void* BufferPool::take_block(size_t bytes) {
+  const PoolTier t = tier_for_size(bytes);
+  if (t == PoolTier::Unpooled) return nullptr;
+  const int ti = (int)t;
+  BlockHeader* h = nullptr;
+  {
+    std::lock_guard<std::mutex> g(mu_);
+    if (!free_blocks_[ti].empty()) {
+      h = static_cast<BlockHeader*>(free_blocks_[ti].back());
+      free_blocks_[ti].pop_back();
+      ++reused_[ti];
+    } else {
+      ++fresh_[ti];
+    }
+    ++live_blocks_;
+  }
+  if (!h) {
+    const size_t cap = tiers_[ti].capacity;
+    h = static_cast<BlockHeader*>(std::malloc(sizeof(BlockHeader) + cap));
+    if (!h) {
+      std::lock_guard<std::mutex> g(mu_);
+      --live_blocks_;
+      throw std::bad_alloc();
+    }
+    h->capacity = cap;
+  }
+  h->pool = this;
+  h->tier = (uint32_t)ti;
+  h->magic = kBlockMagic;
+  return h;
+}
+
+void BufferPool::give_block(void* block) noexcept {
+  auto* h = static_cast<BlockHeader*>(block);
+  const int ti = (int)h->tier;
+  bool del = false, keep = false;
+  {
+    std::lock_guard<std::mutex> g(mu_);
+    --live_blocks_;
+    if (!orphaned_ && free_blocks_[ti].size() < tiers_[ti].count) {
+      free_blocks_[ti].push_back(h);
+      keep = true;
+    }
+    del = orphaned_ && live_blocks_ == 0;
+  }
+  if (!keep) std::free(h);
+  if (del) delete this;
+}
+
+size_t BufferPool::blocks_reused(PoolTier t) const {
+  if (t == PoolTier::Unpooled) return 0;
+  std::lock_guard<std::mutex> g(mu_);
+  return reused_[(int)t];
+}
+
+size_t BufferPool::blocks_fresh(PoolTier t) const {
+  if (t == PoolTier::Unpooled) return 0;
+  std::lock_guard<std::mutex> g(mu_);
+  return fresh_[(int)t];
+}
 
 PooledBuf::~PooledBuf() {
   if (pool_ && tier_ != PoolTier::Unpooled) pool_->return_buf(std::move(buf_), tier_);
 }
 
 std::shared_ptr<BufferPool> BufferPool::from_tiers(TierConfig s, TierConfig l, TierConfig h, TierConfig g) {
-  auto p = std::shared_ptr<BufferPool>(new BufferPool());
+  auto p = std::shared_ptr<BufferPool>(new BufferPool(), PoolDeleter());
   p->tiers_[0] = {std::max<size_t>(s.count, 1), s.capacity};
   p->tiers_[1] = {std::max<size_t>(l.count, 1), l.capacity};
   p->tiers_[2] = {std::max<size_t>(h.count, 1), h.capacity};

@@ -33,8 +33,9 @@ Clock::time_point deadline_in(double s) {
 }  // namespace
 
 // ============================================================ Mesh
-Mesh::Mesh(Rank rank, uint32_t world, Config cfg, Bytes token)
-    : rank_(rank), world_(world), cfg_(std::move(cfg)), token_(std::move(token)) {
+Mesh::Mesh(Rank rank, uint32_t world, Config cfg, Bytes token, std::shared_ptr<BufferPool> pool)
+    : rank_(rank), world_(world), cfg_(std::move(cfg)), token_(std::move(token)),
+      pool_(pool ? std::move(pool) : BufferPool::with_profile(PoolProfile::Training)) {
   for (Rank r = 0; r < world; ++r) boxes_.push_back(std::make_shared<Mailbox>(r));
 }
 
@@ -80,7 +81,8 @@ void Mesh::add_connection(Rank r, std::shared_ptr<Stream> io) {
       },
       [weak](Rank p) {
         if (auto s = weak.lock()) s->mark_dead(p, "connection lost");
-      });
+      },
+      pool_);
   std::lock_guard<std::mutex> g(mu_);
   routers_[r] = std::move(router);
 }
@@ -334,8 +336,9 @@ Rank NexarClient::mesh_rank(Rank r) const {
   return rank_map_[r];
 }
 
-std::shared_ptr<NexarClient> NexarClient::from_worker_info(WorkerInfo info, const Config& cfg) {
-  auto mesh = std::make_shared<Mesh>(info.rank, info.world_size, cfg, info.token);
+std::shared_ptr<NexarClient> NexarClient::from_worker_info(WorkerInfo info, const Config& cfg,
+                                                          std::shared_ptr<BufferPool> pool) {
+  auto mesh = std::make_shared<Mesh>(info.rank, info.world_size, cfg, info.token, std::move(pool));
   mesh->listen_fd = info.listen_fd;
   mesh->listen_addr = info.listen_addr;
   if (cfg.tls) {
@@ -381,7 +384,8 @@ std::shared_ptr<NexarClient> NexarClient::from_worker_info(WorkerInfo info, cons
   return std::make_shared<NexarClient>(mesh, info.rank, info.world_size, 0, rm, nullptr);
 }
 
-std::vector<std::shared_ptr<NexarClient>> NexarClient::bootstrap_local(uint32_t world, const Config& cfg) {
+std::vector<std::shared_ptr<NexarClient>> NexarClient::bootstrap_local(uint32_t world, const Config& cfg,
+                                                                       std::shared_ptr<BufferPool> pool) {
   if (world == 0) fail(Err::InvalidRank, "world size must be >= 1");
   auto seed = SeedNode::bind_local(cfg.tls);
   std::vector<WorkerInfo> infos(world);
@@ -413,7 +417,7 @@ std::vector<std::shared_ptr<NexarClient>> NexarClient::bootstrap_local(uint32_t 
   for (uint32_t i = 0; i < world; ++i) {
     ts.emplace_back([&, i] {
       try {
-        clients[infos[i].rank] = from_worker_info(infos[i], cfg);
+        clients[infos[i].rank] = from_worker_info(infos[i], cfg, pool);
       } catch (...) {
         errs[i] = std::current_exception();
       }
@@ -426,9 +430,10 @@ std::vector<std::shared_ptr<NexarClient>> NexarClient::bootstrap_local(uint32_t 
 }
 
 std::shared_ptr<NexarClient> NexarClient::bootstrap_worker(const std::string& seed_addr, const Bytes& token,
-                                                          const Config& cfg, const std::string& bind_host) {
+                                                          const Config& cfg, const std::string& bind_host,
+                                                          std::shared_ptr<BufferPool> pool) {
   WorkerInfo info = WorkerNode::connect(seed_addr, token, bind_host, cfg.tls);
-  return from_worker_info(std::move(info), cfg);
+  return from_worker_info(std::move(info), cfg, std::move(pool));
 }
 
 // ------------------------------------------------------------ p2p

@@ -91,8 +91,10 @@ class CudaStagingAdapter : public DeviceAdapter {
 // ------------------------------------------------------------------ mesh
 class Mesh : public std::enable_shared_from_this<Mesh> {
  public:
-  Mesh(Rank rank, uint32_t world, Config cfg, Bytes token);
+  // `pool` serves the routers' receive buffers (nullptr: a Training-profile pool).
+  Mesh(Rank rank, uint32_t world, Config cfg, Bytes token, std::shared_ptr<BufferPool> pool = nullptr);
   ~Mesh();
+  const std::shared_ptr<BufferPool>& pool() const { return pool_; }
   Rank rank() const { return rank_; }
   uint32_t world() const { return world_; }
   const Config& config() const { return cfg_; }
@@ -150,6 +152,7 @@ class Mesh : public std::enable_shared_from_this<Mesh> {
   uint32_t world_;
   Config cfg_;
   Bytes token_;
+  std::shared_ptr<BufferPool> pool_;
   TlsIdentity tls_id_;
   mutable std::mutex mu_;
   std::map<Rank, std::shared_ptr<PeerConnection>> conns_;
@@ -203,12 +206,17 @@ class NexarClient : public std::enable_shared_from_this<NexarClient> {
               std::vector<Rank> rank_map, std::shared_ptr<DeviceAdapter> adapter);
 
   // ---- bootstrap
-  static std::vector<std::shared_ptr<NexarClient>> bootstrap_local(uint32_t world, const Config& cfg);
+  // `pool`: receive buffer pool shared by the ranks' routers (nullptr: one
+  // Training-profile pool per rank), the reference's new_with_pool.
+  static std::vector<std::shared_ptr<NexarClient>> bootstrap_local(uint32_t world, const Config& cfg,
+                                                                   std::shared_ptr<BufferPool> pool = nullptr);
   // Multi-process: every process calls this; the process with rank_hint 0
   // may host the seed (`seed` non-null). Builds the full or sparse mesh.
   static std::shared_ptr<NexarClient> bootstrap_worker(const std::string& seed_addr, const Bytes& token,
-                                                       const Config& cfg, const std::string& bind_host);
-  static std::shared_ptr<NexarClient> from_worker_info(WorkerInfo info, const Config& cfg);
+                                                       const Config& cfg, const std::string& bind_host,
+                                                       std::shared_ptr<BufferPool> pool = nullptr);
+  static std::shared_ptr<NexarClient> from_worker_info(WorkerInfo info, const Config& cfg,
+                                                       std::shared_ptr<BufferPool> pool = nullptr);
 
   Rank rank() const { return rank_; }
   uint32_t world_size() const { return world_; }

@@ -23,11 +23,19 @@ using Rank = uint32_t;
 // `Bytes b(n)` / `b.resize(n)` do not zero-fill (receive buffers are written
 // in full by the socket read; zeroing a 16 MB payload costs as much as a
 // tenth of its transfer). `Bytes b(n, 0)` / `assign(n, 0)` still zero.
+// Storage comes from pool_allocate (buffer_pool.cc): a thread inside a
+// PoolScope (the receive routers) draws buffers of 16 KiB and more from its
+// BufferPool's tiers, and they return to their tier when freed on any thread.
+void* pool_allocate(size_t bytes);
+void pool_deallocate(void* p) noexcept;
 template <class T>
 struct NoInitAllocator : std::allocator<T> {
+  using value_type = T;
   template <class U> struct rebind { using other = NoInitAllocator<U>; };
   NoInitAllocator() noexcept = default;
   template <class U> NoInitAllocator(const NoInitAllocator<U>&) noexcept {}
+  T* allocate(size_t n) { return static_cast<T*>(pool_allocate(n * sizeof(T))); }
+  void deallocate(T* p, size_t) noexcept { pool_deallocate(p); }
   template <class U> void construct(U* p) noexcept { ::new (static_cast<void*>(p)) U; }
   template <class U, class... A> void construct(U* p, A&&... a) { ::new (static_cast<void*>(p)) U(std::forward<A>(a)...); }
 };

@@ -416,9 +416,9 @@ static int64_t now_ns() {
 }
 
 PeerRouter::PeerRouter(std::shared_ptr<PeerConnection> conn, std::shared_ptr<Mailbox> box, RelayFn on_relay,
-                       DisconnectFn on_disconnect)
+                       DisconnectFn on_disconnect, std::shared_ptr<BufferPool> pool)
     : conn_(std::move(conn)), box_(std::move(box)), on_relay_(std::move(on_relay)),
-      on_disconnect_(std::move(on_disconnect)), last_seen_ns_(now_ns()) {
+      on_disconnect_(std::move(on_disconnect)), pool_(std::move(pool)), last_seen_ns_(now_ns()) {
   thr_ = std::thread([this] { run(); });
 }
 
@@ -508,6 +508,7 @@ class FrameReader {
 
 void PeerRouter::run() {
   const Rank peer = conn_->peer();
+  PoolScope scope(pool_.get());  // payload buffers come from the mesh's pool
   FrameReader in(*conn_);
   try {
     while (true) {

@@ -36,6 +36,7 @@
 #include <unordered_map>
 
 #include "tls.h"
+#include "buffer_pool.h"
 #include "wire.h"
 
 namespace nexar {
@@ -164,13 +165,14 @@ class PeerConnection {
   std::unordered_map<std::type_index, std::shared_ptr<void>> ext_;
 };
 
-// Reader thread for one connection.
+// Reader thread for one connection; payloads it reads are allocated from
+// `pool` (see PoolScope in buffer_pool.h) when one is given.
 class PeerRouter {
  public:
   using RelayFn = std::function<void(const Message&)>;
   using DisconnectFn = std::function<void(Rank)>;
   PeerRouter(std::shared_ptr<PeerConnection> conn, std::shared_ptr<Mailbox> box, RelayFn on_relay,
-             DisconnectFn on_disconnect);
+             DisconnectFn on_disconnect, std::shared_ptr<BufferPool> pool = nullptr);
   ~PeerRouter();
   void stop();
   double last_seen_s() const;  // seconds since the last frame from this peer
@@ -182,6 +184,7 @@ class PeerRouter {
   std::shared_ptr<Mailbox> box_;
   RelayFn on_relay_;
   DisconnectFn on_disconnect_;
+  std::shared_ptr<BufferPool> pool_;
   std::atomic<int64_t> last_seen_ns_;
   std::thread thr_;
 };

@@ -55,6 +55,18 @@ def CudaAdapter():
     return _h().CudaAdapter()
 
 
+def _pool(p):
+    """A native BufferPool from None / a PoolProfile / a pool object."""
+    if p is None:
+        return None
+    if isinstance(p, _h().BufferPool):
+        return p
+    from .memory import PoolProfile
+    if isinstance(p, (PoolProfile, int)):
+        return _h().BufferPool.with_profile(int(p))
+    raise TypeError(f"not a BufferPool or PoolProfile: {p!r}")
+
+
 def _adapter(a):
     """A native adapter from None / "cpu" / "cuda" / an adapter object."""
     if a is None or a == "cpu":
@@ -172,12 +184,16 @@ class NexarClient:
 
     # ------------------------------------------------------------ bootstrap
     @staticmethod
-    def bootstrap_local(world_size: int, config=None, adapter=None) -> List["NexarClient"]:
+    def bootstrap_local(world_size: int, config=None, adapter=None, pool=None) -> List["NexarClient"]:
         """``world_size`` ranks in this process over loopback (nexar/src/client/bootstrap.rs:22).
-        ``adapter`` ("cpu", "cuda" or a DeviceAdapter) is shared by every rank."""
+        ``adapter`` ("cpu", "cuda" or a DeviceAdapter) is shared by every rank.
+        ``pool``: a :class:`~nexar_b200.memory.BufferPool` (or a ``PoolProfile``)
+        whose tiers serve every rank's receive buffers (the reference's
+        ``new_with_pool`` / ``new_with_profile``); default one Training-profile
+        pool per rank."""
         cfg = config if config is not None else _h().Config()
         ad = _adapter(adapter)
-        natives = _h().NexarClient.bootstrap_local(world_size, cfg)
+        natives = _h().NexarClient.bootstrap_local(world_size, cfg, _pool(pool))
         for c in natives:
             c.set_adapter(ad)
         return [NexarClient(c) for c in natives]
@@ -186,19 +202,20 @@ class NexarClient:
 
     @staticmethod
     def bootstrap(seed_addr: str, token: Optional[bytes] = None, config=None,
-                  bind_host: str = "127.0.0.1", adapter=None) -> "NexarClient":
-        """Join a cluster through the seed at `seed_addr` (one process per rank)."""
+                  bind_host: str = "127.0.0.1", adapter=None, pool=None) -> "NexarClient":
+        """Join a cluster through the seed at `seed_addr` (one process per rank);
+        ``pool`` as in :meth:`bootstrap_local`."""
         cfg = config if config is not None else _h().Config.from_env()
-        c = _h().NexarClient.bootstrap_worker(seed_addr, token, cfg, bind_host)
+        c = _h().NexarClient.bootstrap_worker(seed_addr, token, cfg, bind_host, _pool(pool))
         c.set_adapter(_adapter(adapter))
         return NexarClient(c)
 
     @staticmethod
-    def from_worker(info, config=None, adapter=None) -> "NexarClient":
+    def from_worker(info, config=None, adapter=None, pool=None) -> "NexarClient":
         """Build the mesh from a ``WorkerNode.connect`` result (the second half
         of ``bootstrap``); ``config`` must match the cluster's (TLS, topology)."""
         cfg = config if config is not None else _h().Config.from_env()
-        c = _h().NexarClient.from_worker_info(info, cfg)
+        c = _h().NexarClient.from_worker_info(info, cfg, _pool(pool))
         c.set_adapter(_adapter(adapter))
         return NexarClient(c)
 
@@ -287,6 +304,11 @@ class NexarClient:
         self._c.set_adapter(_adapter(adapter))
 
     # ------------------------------------------------------------ p2p
+    @property
+    def pool(self):
+        """The buffer pool that serves this client's receive buffers."""
+        return self._c.pool
+
     def send(self, ptr: int, size: int, dest: int, tag: int):
         """Send `size` bytes at `ptr` to rank `dest` under `tag` (staged through the adapter for non-host memory)."""
         self._c.send(ptr, size, dest, tag)

@@ -22,6 +22,7 @@ times out records it in a host-mapped status word and returns, and
 """
 from __future__ import annotations
 
+import contextlib
 import functools
 import os
 from typing import Callable, List, Optional, Sequence
@@ -334,6 +335,18 @@ class DeviceCommunicator:
             if cap_now == cap_last:
                 cur.wait_stream(last)
         self._last_stream = cur
+
+    @contextlib.contextmanager
+    def block_limit(self, max_blocks: int):
+        """Launch this communicator's kernels with at most ``max_blocks`` CTAs
+        inside the block (e.g. collectives that overlap persistent compute
+        kernels on the other SMs); the previous limit is restored after."""
+        old = self._comm.max_blocks
+        self._comm.max_blocks = max(1, int(max_blocks))
+        try:
+            yield
+        finally:
+            self._comm.max_blocks = old
 
     # ----------------------------------------------------------- status
     def close(self):

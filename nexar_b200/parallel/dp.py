@@ -5,7 +5,13 @@ symmetric heap, split into ~25 MB buckets (contiguous ranges). A
 post-accumulate hook counts finished parameters per bucket; when a bucket is
 complete its all-reduce (two-shot over NVLink, averaging scale 1/world fused
 into the kernel, in place, no staging copies) is launched on the
-communicator's side stream, overlapping the rest of backward. The optimizer
+communicator's side stream, overlapping the rest of backward. Buckets that
+overlap backward run on a small grid (``overlap_blocks`` CTAs,
+``NEXAR_DP_AR_BLOCKS``) so the persistent GEMM kernels keep their SMs; the
+last buckets, which run after backward has finished, take the whole GPU.
+With ``timeline=True`` (``NEXAR_DP_TIMELINE=1``) CUDA events mark, per
+bucket, when it became ready on the compute stream and when its all-reduce
+started and ended, plus the end of backward (:meth:`timeline`). The optimizer
 step (global-norm clip + fused AdamW over flat fp32 master weights) runs
 after the last bucket joins. The whole step can be captured in one CUDA graph.
 
@@ -16,6 +22,7 @@ all-reduce, nexar/src/collective/bucketed_allreduce.rs:23-75).
 from __future__ import annotations
 
 import dataclasses
+import os
 import time
 from typing import List, Optional
 
@@ -29,7 +36,8 @@ class DataParallelTrainer:
     def __init__(self, cfg: GPT2Config, micro_batch: int, seq_len: int, comm=None, device=None,
                  lr: float = 6e-4, betas=(0.9, 0.95), eps: float = 1e-8, weight_decay: float = 0.1,
                  grad_clip: float = 1.0, bucket_bytes: int = 25 << 20, seed: int = 0,
-                 use_cuda_graph: bool = True):
+                 use_cuda_graph: bool = True, overlap_blocks: Optional[int] = None,
+                 timeline: Optional[bool] = None):
         self.cfg = cfg
         self.B, self.T = micro_batch, seq_len
         self.comm = comm
@@ -67,6 +75,17 @@ class DataParallelTrainer:
             self._bucket_need.append(len(names))
         self._bucket_left: List[int] = list(self._bucket_need)
         self._launched: List[bool] = [False] * len(self.buckets)
+        self.overlap_blocks = int(overlap_blocks if overlap_blocks is not None
+                                  else os.environ.get("NEXAR_DP_AR_BLOCKS", "32"))
+        self.tail_buckets = 2  # launched once backward has (nearly) finished: full grid
+        if timeline is None:
+            timeline = os.environ.get("NEXAR_DP_TIMELINE", "0") == "1"
+        self._tl = None
+        if timeline and self.world > 1:
+            ev = lambda: torch.cuda.Event(enable_timing=True)  # noqa: E731
+            self._tl = {"step0": ev(), "bwd_end": ev(), "step_end": ev(),
+                        "ready": [ev() for _ in self.buckets], "start": [ev() for _ in self.buckets],
+                        "end": [ev() for _ in self.buckets], "order": []}
         # Backward kernels write each gradient straight into the flat buffer
         # and then call the parameter's ready callback (no zero-fill, no
         # accumulation). A parameter that is ever missed falls back to
@@ -107,9 +126,24 @@ class DataParallelTrainer:
     def _launch_bucket(self, bi):
         start, end, _ = self.buckets[bi]
         side = self.comm.side_stream()
-        side.wait_stream(torch.cuda.current_stream(self.device))
+        cur = torch.cuda.current_stream(self.device)
+        tl = self._tl
+        if tl is not None:
+            tl["ready"][bi].record(cur)
+            tl["order"].append(bi)
+        side.wait_stream(cur)
+        n_before = sum(self._launched)
+        tail = n_before >= len(self.buckets) - self.tail_buckets
         with torch.cuda.stream(side):
-            self.comm.all_reduce(self.model.flat.grad[start:end], scale=1.0 / self.world)
+            if tl is not None:
+                tl["start"][bi].record(side)
+            if tail:
+                self.comm.all_reduce(self.model.flat.grad[start:end], scale=1.0 / self.world)
+            else:
+                with self.comm.block_limit(self.overlap_blocks):
+                    self.comm.all_reduce(self.model.flat.grad[start:end], scale=1.0 / self.world)
+            if tl is not None:
+                tl["end"][bi].record(side)
         self._launched[bi] = True
 
     # ---------------------------------------------------------------- step
@@ -120,8 +154,14 @@ class DataParallelTrainer:
         self._seen = set()
         if self._zero_grads:
             flat.grad.zero_()
+        tl = self._tl
+        if tl is not None:
+            tl["order"] = []
+            tl["step0"].record()
         loss = self.model(self.static_idx, self.static_tgt, unit_grad=True)
         loss.backward()
+        if tl is not None:
+            tl["bwd_end"].record()
         if len(self._seen) != len(self.model.p):
             self._zero_grads = True  # some gradient was not written this step: zero-fill from now on
         if self.world > 1:
@@ -137,6 +177,28 @@ class DataParallelTrainer:
                 self.lr, self.betas[0], self.betas[1], self.eps, self.wd, 1, self.clip_coef,
                 self.step_dev, self.lr_dev)
         self.static_loss.copy_(loss.detach())
+        if tl is not None:
+            tl["step_end"].record()
+
+    def timeline(self) -> Optional[dict]:
+        """Milliseconds from the start of the last step (``timeline=True``):
+        end of backward, end of the step, and per bucket (in launch order)
+        its size and when it became ready / its all-reduce started / ended."""
+        tl = self._tl
+        if tl is None:
+            return None
+        torch.cuda.synchronize(self.device)
+        t0 = tl["step0"]
+        out = {"bwd_end_ms": t0.elapsed_time(tl["bwd_end"]), "step_end_ms": t0.elapsed_time(tl["step_end"]),
+               "overlap_blocks": self.overlap_blocks, "buckets": []}
+        for bi in tl["order"]:
+            start, end, names = self.buckets[bi]
+            out["buckets"].append({"bucket": bi, "mb": round((end - start) * 2 / 2**20, 2),
+                                   "first": names[0], "last": names[-1],
+                                   "ready_ms": round(t0.elapsed_time(tl["ready"][bi]), 3),
+                                   "start_ms": round(t0.elapsed_time(tl["start"][bi]), 3),
+                                   "end_ms": round(t0.elapsed_time(tl["end"][bi]), 3)})
+        return out
 
     def capture(self, warmup: int = 3):
         """Warm up eagerly on a side stream, then capture one whole step."""

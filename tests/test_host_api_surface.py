@@ -194,3 +194,30 @@ def test_global_ptr_identity():
     assert a == b and hash(a) == hash(b) and a != c and len({a, b, c}) == 2
     assert a.is_local() and not c.is_local() and c.is_local(2)
     assert "rank 1" in str(a) and "64 bytes" in str(a)
+
+
+def test_receive_buffers_come_from_the_client_pool():
+    """Large receives are served by the client's buffer pool and reuse its
+    blocks (nexar's routers read into pooled buffers; new_with_pool)."""
+    from nexar_b200.client import NexarClient
+    from nexar_b200.memory import BufferPool, PoolBuilder, TierConfig
+    pool = PoolBuilder().small(TierConfig(8, 64 << 10)).large(TierConfig(4, 8 << 20)).build()
+    cs = NexarClient.bootstrap_local(2, pool=pool)
+    assert cs[0].pool is pool and cs[1].pool is pool
+    n = 1 << 20  # large tier
+    x = np.arange(n, dtype=np.uint8)
+    y = np.empty(n, np.uint8)
+    for _ in range(6):
+        cs[0].send(x.ctypes.data, n, 1, 9)
+        cs[1].recv(y.ctypes.data, n, 0, 9)
+        assert (y == x).all()
+    large = 1
+    assert pool.blocks_fresh(large) >= 1
+    assert pool.blocks_reused(large) >= 4  # later receives reuse the freed block
+    # collectives' receives go through the same pool
+    a = [np.full(300_000, float(c.rank + 1), np.float32) for c in cs]
+    run_collective(cs, lambda c: c.all_reduce(a[c.rank].ctypes.data, a[c.rank].size, 0))
+    assert all((v == 3.0).all() for v in a)
+    default = NexarClient.bootstrap_local(2)
+    assert default[0].pool is not default[1].pool  # one Training-profile pool per rank
+    BufferPool.with_profile(0)
