@@ -6,36 +6,46 @@
 // at h*64), y the [B*T, C] attention output, lse the [B, H, T] natural-log
 // softmax normaliser of every query row (scores scaled by 1/sqrt(64)).
 //
-// Forward (k_attn_fwd): one CTA per (128-query block, batch, head).
-//   warp 0      TMA loads: the Q tile once, then K and V tiles of 128 keys
-//               into a 2-deep ring (every load reads this GPU's memory; no
+// Forward (k_attn_fwd): one CTA per (pair of adjacent 128-query tiles A and
+// B, batch, head); the tiles share every K / V load.
+//   warp 0      TMA loads: both Q tiles once, then K and V tiles of 128 keys
+//               into a 3-deep ring (every load reads this GPU's memory; no
 //               multicast);
-//   warp 1      allocates 512 TMEM columns; lane 0 issues S = Q K^T
-//               (M = N = 128, K = 64) into one of two S accumulators and
-//               O_j = P_j V_j (M = 128, N = 64, K = 128) into one of two
-//               O accumulators, one block ahead (S of block j is computed
-//               while the softmax of block j - 1 runs);
-//   warps 4-7   one query row per thread (TMEM lane = row): online softmax in
-//               the exp2 domain, P written as bf16 into 128-byte-swizzled
-//               shared memory (the A operand of the next MMA), and the
-//               running output kept in registers: O = alpha * O + P_j V_j
-//               read back from TMEM one block behind.
+//   warp 1      allocates 512 TMEM columns; lane 0 issues S_t = Q_t K_j^T
+//               (M = N = 128, K = 64) for the next key block of tile t as
+//               soon as tile t's softmax holds the current scores, and
+//               O_t += P_t V_j (M = 128, N = 64, K = 128) once P_t is in
+//               shared memory, polling both tiles' inputs and issuing
+//               whichever MMA is ready (the tensor pipe takes an MMA only as
+//               fast as it runs them, so a fixed issue order would serialise
+//               the tiles); O_A and O_B accumulate in TMEM;
+//   warps 4-7   softmax of tile A, warps 8-11 of tile B, one query row per
+//               thread (TMEM lane = row), in the exp2 domain. The running
+//               maximum is raised lazily (only when a block's maximum exceeds
+//               it by more than 2^8), so the accumulated output is rescaled
+//               in TMEM only on those blocks. A quarter of the exponentials
+//               run on the FMA pipe (exp2_poly2), the rest on the MUFU unit.
+//               P goes to 128-byte-swizzled shared memory as bf16 (the A
+//               operand of the next MMA).
 // Backward (k_attn_bwd): one CTA per (128-key block, batch, head), looping
-// over the query blocks that see it.
-//   warp 0      K_j, V_j once; Q_i, dO_i, lse_i, Delta_i per step (2-deep);
-//   warp 1      S^T = K Q^T and dP^T = V dO^T (M = N = 128, K = 64), then
-//               dV += P^T dO, dK += dS^T Q (M = 128, N = 64, K = 128,
-//               accumulated in TMEM over all steps) and dQ_i = dS K into one
-//               of two TMEM buffers;
-//   warps 4-7   one key row per thread: P^T = exp(S^T * scale - lse),
-//               dS^T = P^T (dP^T - Delta), both as bf16 into swizzled shared
-//               memory (dS^T doubles as the MN-major A operand of dQ);
-//   warps 8-11  drain dQ_i from TMEM into a swizzled shared staging tile and
+// over the query blocks that see it, each as two halves of 64 queries.
+//   warp 0      K_j, V_j once; Q_i, dO_i, lse_i, Delta_i per block (2-deep);
+//   warp 1      S^T = K Q_half^T and dP^T = V dO_half^T (M = 128, N = 64,
+//               K = 64) into one of two TMEM half buffers, two halves ahead;
+//               dV += P^T dO_half, dK += dS^T Q_half (K = 64, accumulated in
+//               TMEM over all steps); after both halves dQ_i = dS K
+//               (M = 128, N = 64, K = 128) into one of two TMEM buffers;
+//   warps 4-11  one key row per thread, 32 query columns of a half per warp:
+//               P^T = exp(S^T * scale - lse), dS^T = P^T (dP^T - Delta), both
+//               as bf16 into swizzled shared memory (dS^T doubles as the
+//               MN-major A operand of dQ); at the end dV (warps 4-7) and dK
+//               (warps 8-11) from TMEM to dqkv;
+//   warps 12-15 drain dQ_i from TMEM into a swizzled shared staging tile and
 //               add it to the fp32 dQ accumulator with two tensor bulk
 //               reductions (cp.reduce.async.bulk.tensor .add, 128 x 32 fp32
-//               boxes) per step.
-// Delta = rowsum(dO * O) comes from k_attn_delta; k_attn_dq_out scales the
-// fp32 dQ accumulator into the Q columns of dqkv.
+//               boxes) per query block.
+// k_attn_prep computes Delta = rowsum(dO * O) and clears the dQ accumulator;
+// k_attn_dq_out scales the fp32 dQ accumulator into the Q columns of dqkv.
 //
 // Every mbarrier wait is bounded (2 s of %globaltimer); a wait that gives up
 // records a code in the GEMM error word (gemm_error_flag), the CTA unwinds and
@@ -135,13 +145,120 @@ NEXAR_D void tmem_ld_x32(uint32_t taddr, uint32_t* r) {
   tmem_ld_32x32b_x32(taddr, *reinterpret_cast<uint32_t(*)[32]>(r));
 }
 
+// Non-blocking phase test (never suspends the thread).
+NEXAR_D bool mbar_test(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity) : "memory");
+  return ok != 0;
+}
+
+// Event timeline of one CTA (SM clock, %clock64) for tuning the pipelines:
+// recorded only when attention_trace_select picked that CTA. Slots: forward
+// softmax of tile t at 512 t + 8 j + k, forward MMA at 1024 + 8 j + 4 t + k,
+// forward loads at 1536 + j; backward softmax at 2048 + 4 u + k, backward MMA
+// at 3072 + 4 u + k.
+constexpr int kTraceSlots = 4096;
+__device__ unsigned long long g_trace[kTraceSlots];
+__device__ int g_trace_cta = -1;
+// `on` is this CTA's (blockIdx.x == g_trace_cta), read once at kernel entry.
+NEXAR_D void trace(bool on, int slot) {
+  if (on && slot >= 0 && slot < kTraceSlots) g_trace[slot] = clock64();
+}
+
+NEXAR_D float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+NEXAR_D float ex2(float x) {
+  float r;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return r;
+}
+
+// Packed fp32 pairs (Blackwell f32x2 pipes): d = a * b + c, a + b, a * b.
+NEXAR_D void ffma2(float& d0, float& d1, float a0, float a1, float b0, float b1, float c0, float c1) {
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
+      "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d0), "=f"(d1) : "f"(a0), "f"(a1), "f"(b0), "f"(b1), "f"(c0), "f"(c1));
+}
+NEXAR_D void fadd2(float& d0, float& d1, float a0, float a1, float b0, float b1) {
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d0), "=f"(d1) : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
+}
+NEXAR_D void fmul2(float& d0, float& d1, float a0, float a1, float b0, float b1) {
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "mul.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d0), "=f"(d1) : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
+}
+
+// 2^x of two values on the FMA pipe, taking part of the exponentials off the
+// MUFU unit (its 16 results per SM clock bound the softmax). Method: the
+// Cody-Waite split x = n + f with n = rint(x) (the 1.5 * 2^23 rounding
+// constant) and |f| <= 1/2; 2^f by a cubic whose coefficients were fitted for
+// this file by Lawson-weighted least squares on [-1/2, 1/2] (maximum relative
+// error 7.5e-5, below the bf16 rounding of P); 2^n by adding n to the exponent
+// field. Inputs below -125 (the masked -inf among them) give exactly 0.
+NEXAR_D void exp2_poly2(float& r0, float& r1, float x0, float x1) {
+  constexpr float kRound = 12582912.f;  // 1.5 * 2^23
+  constexpr float c0 = 0.9999281764f, c1 = 0.6932609677f, c2 = 0.2426097095f, c3 = 0.0551709794f;
+  const float y0 = fmaxf(x0, -125.f), y1 = fmaxf(x1, -125.f);
+  float t0, t1, n0, n1, f0, f1, p0, p1;
+  fadd2(t0, t1, y0, y1, kRound, kRound);
+  fadd2(n0, n1, t0, t1, -kRound, -kRound);
+  fadd2(f0, f1, y0, y1, -n0, -n1);
+  ffma2(p0, p1, c3, c3, f0, f1, c2, c2);
+  ffma2(p0, p1, p0, p1, f0, f1, c1, c1);
+  ffma2(p0, p1, p0, p1, f0, f1, c0, c0);
+  const int e0 = __float_as_int(p0) + (__float_as_int(t0) << 23);
+  const int e1 = __float_as_int(p1) + (__float_as_int(t1) << 23);
+  r0 = x0 < -125.f ? 0.f : __int_as_float(e0);
+  r1 = x1 < -125.f ? 0.f : __int_as_float(e1);
+}
+
+NEXAR_D void tmem_st_x32(uint32_t taddr, const uint32_t* r) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};"
+      :: "r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+         "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]),
+         "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]),
+         "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+NEXAR_D void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
 // ============================================================ forward
-constexpr int F_Q = 0, F_K = TILE, F_V = 3 * TILE, F_P = 5 * TILE;  // P: 2 buffers x 32 KB
+// One CTA per pair of adjacent 128-query tiles (A = 2p, B = 2p + 1) of one
+// (batch, head): the two tiles share every K / V load, and their softmax
+// warpgroups overlap on the SM (one computes exponentials while the tensor
+// cores run the other's MMAs).
+constexpr int F_STAGES = 3;
+constexpr int F_QA = 0;                             // Q_A, Q_B: 2 tiles
+constexpr int F_K = 2 * TILE;                       // K ring
+constexpr int F_V = F_K + F_STAGES * TILE;          // V ring
+constexpr int F_P = F_V + F_STAGES * TILE;          // P_A, P_B: [128][128] bf16 each (two swizzled halves)
 constexpr int F_BAR = F_P + 4 * TILE;
 constexpr int F_SMEM = F_BAR + 256 + 1024;
-constexpr int F_THREADS = 256;
-// TMEM columns: S accumulators at 0 / 128, O accumulators at 256 / 320.
+// Warpgroup 0: TMA (warp 0), MMA (warp 1); warpgroup 1: softmax of tile A;
+// warpgroup 2: softmax of tile B. 168 registers per thread (3 warps per SM
+// sub-partition: 3 x 32 x 168 = 16,128 of its 16,384).
+constexpr int F_THREADS = 384;
+// TMEM columns: S_A 0, S_B 128 (fp32 scores), O_A 256, O_B 320 (fp32 output accumulators).
 constexpr uint32_t T_S = 0, T_O = 256;
+// The running maximum is raised only when a block's maximum exceeds it by
+// more than 2^8: between raises the probabilities stay below 256 (exact in
+// fp32, ample range in bf16) and the output accumulator needs no rescaling.
+constexpr float kRescaleLog2 = 8.f;
 
 __global__ void __launch_bounds__(F_THREADS, 1)
 k_attn_fwd(const __grid_constant__ CUtensorMap tm_qkv, __nv_bfloat16* __restrict__ y, float* __restrict__ lse, int B,
@@ -150,37 +267,45 @@ k_attn_fwd(const __grid_constant__ CUtensorMap tm_qkv, __nv_bfloat16* __restrict
   uint8_t* smem = align1024(smem_raw);
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem + F_BAR);
   uint64_t* q_full = bar;
-  uint64_t* k_full = bar + 1;     // [2]
-  uint64_t* v_full = bar + 3;     // [2]
-  uint64_t* kv_empty = bar + 5;   // [2]
-  uint64_t* s_full = bar + 7;     // [2]
-  uint64_t* p_full = bar + 9;     // [2]
-  uint64_t* o_full = bar + 11;    // [2]
-  uint64_t* o_empty = bar + 13;   // [2]
-  uint64_t* mma_done = bar + 15;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 16);
+  uint64_t* k_full = bar + 1;     // [F_STAGES]
+  uint64_t* v_full = bar + 4;     // [F_STAGES]
+  uint64_t* kv_empty = bar + 7;   // [F_STAGES]
+  uint64_t* s_full = bar + 10;    // [2] per tile: S = Q K^T complete
+  uint64_t* s_free = bar + 12;    // [2] per tile: S read into registers
+  uint64_t* p_full = bar + 14;    // [2] per tile: P in shared memory, O rescaled
+  uint64_t* o_done = bar + 16;    // [2] per tile: O += P V complete
+  uint64_t* mma_done = bar + 18;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 20);
   __shared__ volatile int s_abort;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const bool tron = (int)blockIdx.x == g_trace_cta;
   const int nq = T / BQ;
+  const int npair = (nq + 1) / 2;
   const int BH = B * H;
-  const int qb = nq - 1 - (int)(blockIdx.x / BH);  // most key blocks first (causal)
+  const int pr = npair - 1 - (int)(blockIdx.x / BH);  // most key blocks first (causal)
   const int bh = (int)(blockIdx.x % BH);
   const int b = bh / H, h = bh % H;
   const int C = H * HD;
-  const int nkv = causal ? qb + 1 : nq;
   const int row0 = b * T;
+  const int ntile = (2 * pr + 1 < nq) ? 2 : 1;
+  int nkv[2];
+#pragma unroll
+  for (int t = 0; t < 2; ++t) nkv[t] = causal ? 2 * pr + t + 1 : nq;
+  const int nkv_max = nkv[ntile - 1];
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    for (int s = 0; s < 2; ++s) {
+    for (int s = 0; s < F_STAGES; ++s) {
       mbar_init(k_full + s, 1);
       mbar_init(v_full + s, 1);
       mbar_init(kv_empty + s, 1);
-      mbar_init(s_full + s, 1);
-      mbar_init(p_full + s, 128);
-      mbar_init(o_full + s, 1);
-      mbar_init(o_empty + s, 128);
+    }
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(s_full + t, 1);
+      mbar_init(s_free + t, 128);
+      mbar_init(p_full + t, 128);
+      mbar_init(o_done + t, 1);
     }
     mbar_init(mma_done, 1);
     s_abort = 0;
@@ -198,69 +323,115 @@ k_attn_fwd(const __grid_constant__ CUtensorMap tm_qkv, __nv_bfloat16* __restrict
 
   if (warp == 0) {
     if (lane == 0) {
-      mbar_arrive_expect_tx(q_full, TILE);
-      tma_load_2d(smem + F_Q, &tm_qkv, q_full, h * HD, row0 + qb * BQ);
+      mbar_arrive_expect_tx(q_full, ntile * TILE);
+      for (int t = 0; t < ntile; ++t)
+        tma_load_2d(smem + F_QA + t * TILE, &tm_qkv, q_full, h * HD, row0 + (2 * pr + t) * BQ);
       int issued = 0;
-      for (int j = 0; j < nkv && !s_abort; ++j) {
-        const int s = j & 1;
-        if (j >= 2 && !mbar_wait_bounded(kv_empty + s, ((j >> 1) - 1) & 1, kWait)) {
+      for (int j = 0; j < nkv_max && !s_abort; ++j) {
+        const int st = j % F_STAGES;
+        if (j >= F_STAGES && !mbar_wait_bounded(kv_empty + st, ((j / F_STAGES) - 1) & 1, kWait)) {
           fail(err, &s_abort, 21u);
           break;
         }
-        mbar_arrive_expect_tx(k_full + s, TILE);
-        tma_load_2d(smem + F_K + s * TILE, &tm_qkv, k_full + s, C + h * HD, row0 + j * BKV);
-        mbar_arrive_expect_tx(v_full + s, TILE);
-        tma_load_2d(smem + F_V + s * TILE, &tm_qkv, v_full + s, 2 * C + h * HD, row0 + j * BKV);
+        mbar_arrive_expect_tx(k_full + st, TILE);
+        tma_load_2d(smem + F_K + st * TILE, &tm_qkv, k_full + st, C + h * HD, row0 + j * BKV);
+        mbar_arrive_expect_tx(v_full + st, TILE);
+        tma_load_2d(smem + F_V + st * TILE, &tm_qkv, v_full + st, 2 * C + h * HD, row0 + j * BKV);
+        trace(tron, 1536 + j);
         issued = j + 1;
       }
       // No TMA write may still be landing when the CTA exits.
       mbar_wait_bounded(q_full, 0, kWait >> 4);
-      for (int j = issued > 2 ? issued - 2 : 0; j < issued; ++j) {
-        mbar_wait_bounded(k_full + (j & 1), (j >> 1) & 1, kWait >> 4);
-        mbar_wait_bounded(v_full + (j & 1), (j >> 1) & 1, kWait >> 4);
+      for (int j = issued > F_STAGES ? issued - F_STAGES : 0; j < issued; ++j) {
+        mbar_wait_bounded(k_full + j % F_STAGES, (j / F_STAGES) & 1, kWait >> 4);
+        mbar_wait_bounded(v_full + j % F_STAGES, (j / F_STAGES) & 1, kWait >> 4);
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
+      // Descriptors are computed once: a K step of 16 elements advances a
+      // K-major operand by 32 bytes (start-address field + 2) and an
+      // MN-major one by 16 rows of 128 bytes (+ 128); stages and tiles are
+      // TILE bytes apart (+ TILE / 16).
       constexpr uint32_t idS = umma_idesc_bf16_f32(BQ, BKV);
       constexpr uint32_t idO = umma_idesc_bf16_f32(BQ, HD, false, true);
-      const uint32_t q_addr = smem_u32(smem + F_Q);
-      bool ok = mbar_wait_bounded(q_full, 0, kWait);
+      constexpr uint64_t kTileStep = TILE >> 4;
+      const uint64_t dq0 = umma_desc_sw128_kmajor(smem_u32(smem + F_QA));
+      const uint64_t dk0 = umma_desc_sw128_kmajor(smem_u32(smem + F_K));
+      const uint64_t dp0 = umma_desc_sw128_kmajor(smem_u32(smem + F_P));
+      const uint64_t dv0 = desc_mn(smem_u32(smem + F_V), 8192);
+      auto issue_s = [&](int t, int j) {
+        const uint64_t da = dq0 + (uint64_t)t * kTileStep;
+        const uint64_t db = dk0 + (uint64_t)(j % F_STAGES) * kTileStep;
+        const uint32_t d = tbase + T_S + t * BKV;
+#pragma unroll
+        for (int k = 0; k < HD / 16; ++k) umma_f16(d, da + 2 * k, db + 2 * k, idS, k > 0 ? 1u : 0u);
+        umma_commit(s_full + t);
+      };
+      bool ok = mbar_wait_bounded(q_full, 0, kWait) && mbar_wait_bounded(k_full, 0, kWait);
       if (!ok) fail(err, &s_abort, 22u);
-      for (int j = 0; ok && j <= nkv && !s_abort; ++j) {
-        if (j < nkv) {
-          const int s = j & 1;
-          if (!mbar_wait_bounded(k_full + s, (j >> 1) & 1, kWait)) {
-            fail(err, &s_abort, 23u);
-            break;
+      if (ok) {
+        tc_fence_after();
+        for (int t = 0; t < ntile; ++t) issue_s(t, 0);
+      }
+      // Event-driven issue: poll every pending MMA's inputs and issue whichever
+      // is ready, so one tile's late softmax never holds back the other's
+      // MMAs. ns[t] / np[t]: next S / PV block of tile t; `rel`: next K / V
+      // block whose stage can be released.
+      int ns[2] = {1, 1}, np[2] = {0, 0};
+      int rel = 0;
+      unsigned long long idle_since = 0;
+      while (ok && !s_abort) {
+        bool done = true, progressed = false;
+        for (int t = 0; t < ntile; ++t) {
+          if (np[t] < nkv[t]) done = false;
+          const int js = ns[t];
+          if (js < nkv[t] && mbar_test(s_free + t, (js - 1) & 1) &&
+              mbar_test(k_full + js % F_STAGES, (js / F_STAGES) & 1)) {
+            tc_fence_after();
+            issue_s(t, js);
+            trace(tron, 1024 + 8 * (js - 1) + 4 * t);
+            ns[t] = js + 1;
+            progressed = true;
           }
-          tc_fence_after();
-          // S buffer s was read by the softmax of block j - 2, which this
-          // thread saw finish (p_full) before issuing O_{j-2}.
-          const uint32_t k_addr = smem_u32(smem + F_K + s * TILE);
+          const int jp = np[t];
+          if (jp < nkv[t] && mbar_test(p_full + t, jp & 1) &&
+              mbar_test(v_full + jp % F_STAGES, (jp / F_STAGES) & 1)) {
+            tc_fence_after();
+            const uint64_t da = dp0 + (uint64_t)(2 * t) * kTileStep;
+            const uint64_t db = dv0 + (uint64_t)(jp % F_STAGES) * kTileStep;
+            const uint32_t d = tbase + T_O + t * HD;
 #pragma unroll
-          for (int k = 0; k < HD / 16; ++k)
-            umma_f16(tbase + T_S + s * BKV, umma_desc_sw128_kmajor(q_addr + k * 32),
-                     umma_desc_sw128_kmajor(k_addr + k * 32), idS, k > 0 ? 1u : 0u);
-          umma_commit(s_full + s);
+            for (int k = 0; k < BKV / 16; ++k)
+              umma_f16(d, da + (uint64_t)((k >> 2) * kTileStep + (k & 3) * 2), db + 128 * k, idO,
+                       (jp > 0 || k > 0) ? 1u : 0u);
+            umma_commit(o_done + t);
+            trace(tron, 1024 + 8 * jp + 4 * t + 1);
+            np[t] = jp + 1;
+            progressed = true;
+          }
         }
-        if (j >= 1) {
-          const int jj = j - 1, s = jj & 1;
-          const uint32_t u = (uint32_t)(jj >> 1);
-          if (!mbar_wait_bounded(p_full + s, u & 1, kWait) || !mbar_wait_bounded(v_full + s, u & 1, kWait) ||
-              (jj >= 2 && !mbar_wait_bounded(o_empty + s, (u - 1) & 1, kWait))) {
-            fail(err, &s_abort, 24u);
-            break;
+        // K_j and V_j are free once every tile that uses block j has issued
+        // its S and PV MMAs of it.
+        while (rel < nkv_max) {
+          bool used = true;
+          for (int t = 0; t < ntile; ++t)
+            if (rel < nkv[t] && (ns[t] <= rel || np[t] <= rel)) used = false;
+          if (!used) break;
+          umma_commit(kv_empty + rel % F_STAGES);
+          ++rel;
+        }
+        if (done) break;
+        if (progressed) {
+          idle_since = 0;
+        } else {
+          const unsigned long long now = globaltimer_ns();
+          if (idle_since == 0) {
+            idle_since = now;
+          } else if (now - idle_since > kWait) {
+            fail(err, &s_abort, 23u);
+            ok = false;
           }
-          tc_fence_after();
-          const uint32_t p_addr = smem_u32(smem + F_P + s * 2 * TILE);
-          const uint32_t v_addr = smem_u32(smem + F_V + s * TILE);
-#pragma unroll
-          for (int k = 0; k < BKV / 16; ++k)
-            umma_f16(tbase + T_O + s * HD, umma_desc_sw128_kmajor(p_addr + (k >> 2) * TILE + (k & 3) * 32),
-                     desc_mn(v_addr + k * 2048, 8192), idO, k > 0 ? 1u : 0u);
-          umma_commit(o_full + s);
-          umma_commit(kv_empty + s);
         }
       }
       // Every issued MMA has finished before TMEM is released.
@@ -268,97 +439,126 @@ k_attn_fwd(const __grid_constant__ CUtensorMap tm_qkv, __nv_bfloat16* __restrict
       mbar_wait_bounded(mma_done, 0, kWait);
     }
   } else if (warp >= 4) {
-    const int quarter = warp & 3;
-    const int r = quarter * 32 + lane;  // query row in the block = TMEM lane
-    const uint32_t lane_base = tbase + ((uint32_t)(quarter * 32) << 16);
-    const int qrow = qb * BQ + r;
-    float m = -INFINITY, l = 0.f, alpha_pend = 0.f;
-    float o[HD];
-#pragma unroll
-    for (int i = 0; i < HD; ++i) o[i] = 0.f;
-    bool ok = true;
-
-    auto fold = [&](int jj, float a) -> bool {
-      const int s = jj & 1;
-      if (!warp_wait(o_full + s, (uint32_t)(jj >> 1) & 1, lane)) return false;
-      tc_fence_after();
-      uint32_t ot[HD];
-      tmem_ld_x32(lane_base + T_O + s * HD, ot);
-      tmem_ld_x32(lane_base + T_O + s * HD + 32, ot + 32);
-      tmem_ld_wait();
-      tc_fence_before();
-      mbar_arrive(o_empty + s);
-#pragma unroll
-      for (int i = 0; i < HD; ++i) o[i] = o[i] * a + __uint_as_float(ot[i]);
-      return true;
-    };
-
-    for (int j = 0; j < nkv; ++j) {
-      const int s = j & 1;
-      if (!warp_wait(s_full + s, (uint32_t)(j >> 1) & 1, lane) || s_abort) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      uint32_t x[BKV];
-#pragma unroll
-      for (int c0 = 0; c0 < BKV; c0 += 32) tmem_ld_x32(lane_base + T_S + s * BKV + c0, x + c0);
-      tmem_ld_wait();
-      const bool diag = causal && j == qb;
-      float mx = -INFINITY;
-#pragma unroll
-      for (int c = 0; c < BKV; ++c) {
-        float v = __uint_as_float(x[c]) * scale_log2;
-        if (diag && c > r) v = -INFINITY;
-        x[c] = __float_as_uint(v);
-        mx = fmaxf(mx, v);
-      }
-      const float m_new = fmaxf(m, mx);
-      const float alpha = exp2f(m - m_new);
-      float sum = 0.f;
-      uint8_t* pbuf = smem + F_P + s * 2 * TILE;
-#pragma unroll
-      for (int ch = 0; ch < BKV / 8; ++ch) {
-        float p[8];
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          p[e] = exp2f(__uint_as_float(x[ch * 8 + e]) - m_new);
-          sum += p[e];
+    const int t = (warp >> 2) - 1;        // tile of this warpgroup
+    const int quarter = warp & 3;         // TMEM lane quarter of this warp
+    const int r = quarter * 32 + lane;    // query row in the tile = TMEM lane
+    if (t < ntile) {
+      const uint32_t lane_base = tbase + ((uint32_t)(quarter * 32) << 16);
+      const uint32_t s_col = T_S + t * BKV, o_col = T_O + t * HD;
+      const int qt = 2 * pr + t;
+      const int qrow = qt * BQ + r;
+      uint8_t* pbuf = smem + F_P + t * 2 * TILE;
+      float m = -INFINITY, l = 0.f;
+      bool ok = true;
+      const bool tr = tron && r == 0;
+      for (int j = 0; j < nkv[t]; ++j) {
+        if (!warp_wait(s_full + t, (uint32_t)j & 1, lane) || s_abort) {
+          ok = false;
+          break;
         }
-        uint4 pk;
-        pk.x = pack_bf16(p[0], p[1]);
-        pk.y = pack_bf16(p[2], p[3]);
-        pk.z = pack_bf16(p[4], p[5]);
-        pk.w = pack_bf16(p[6], p[7]);
-        *reinterpret_cast<uint4*>(pbuf + (ch >> 3) * TILE + sw128(r, ch & 7)) = pk;
-      }
-      l = l * alpha + sum;
-      m = m_new;
-      fence_proxy_async_smem();  // P (generic-proxy writes) -> the tensor cores
-      tc_fence_before();
-      mbar_arrive(p_full + s);
-      if (j >= 1 && !fold(j - 1, alpha_pend)) {
-        ok = false;
-        break;
-      }
-      alpha_pend = alpha;
-    }
-    if (ok && nkv > 0) ok = fold(nkv - 1, alpha_pend);
-    if (ok) {
-      const float inv = 1.f / l;
-      __nv_bfloat16* yr = y + (size_t)(row0 + qrow) * C + h * HD;
+        if (tr) trace(true, 512 * t + 8 * j);
+        tc_fence_after();
+        uint32_t x[BKV];
 #pragma unroll
-      for (int ch = 0; ch < HD / 8; ++ch) {
-        uint4 pk;
-        pk.x = pack_bf16(o[ch * 8 + 0] * inv, o[ch * 8 + 1] * inv);
-        pk.y = pack_bf16(o[ch * 8 + 2] * inv, o[ch * 8 + 3] * inv);
-        pk.z = pack_bf16(o[ch * 8 + 4] * inv, o[ch * 8 + 5] * inv);
-        pk.w = pack_bf16(o[ch * 8 + 6] * inv, o[ch * 8 + 7] * inv);
-        reinterpret_cast<uint4*>(yr)[ch] = pk;
+        for (int c0 = 0; c0 < BKV; c0 += 32) tmem_ld_x32(lane_base + s_col + c0, x + c0);
+        tmem_ld_wait();
+        tc_fence_before();
+        mbar_arrive(s_free + t);
+        if (tr) trace(true, 512 * t + 8 * j + 1);
+        if (causal && j == qt) {
+#pragma unroll
+          for (int c = 0; c < BKV; ++c)
+            if (c > r) x[c] = __float_as_uint(-INFINITY);
+        }
+        float mx0 = __uint_as_float(x[0]), mx1 = __uint_as_float(x[1]);
+        float mx2 = __uint_as_float(x[2]), mx3 = __uint_as_float(x[3]);
+#pragma unroll
+        for (int c = 4; c < BKV; c += 8) {
+          mx0 = fmax3(mx0, __uint_as_float(x[c + 0]), __uint_as_float(x[c + 1]));
+          mx1 = fmax3(mx1, __uint_as_float(x[c + 2]), __uint_as_float(x[c + 3]));
+          mx2 = fmax3(mx2, __uint_as_float(x[c + 4]), __uint_as_float(x[c + 5]));
+          mx3 = fmax3(mx3, __uint_as_float(x[c + 6]), __uint_as_float(x[c + 7]));
+        }
+        const float m_blk = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * scale_log2;
+        const bool raise = m_blk > m + kRescaleLog2;
+        const float m_new = raise ? m_blk : m;
+        const float alpha = raise ? ex2(m - m_new) : 1.f;
+        if (tr) trace(true, 512 * t + 8 * j + 2);
+        if (j >= 1) {
+          // P_t and O_t are free once O_t += P_{j-1} V_{j-1} has completed.
+          if (!warp_wait(o_done + t, (uint32_t)(j - 1) & 1, lane)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+        }
+        if (tr) trace(true, 512 * t + 8 * j + 3);
+        // Probabilities straight into the swizzled P tile, 8 columns (16 bytes)
+        // at a time: 6 of every 8 exponentials on the MUFU unit, 2 on the FMA
+        // pipe (exp2_poly2), which balances the two for this loop.
+        const float neg = -m_new;
+        float sum0 = 0.f, sum1 = 0.f;
+#pragma unroll
+        for (int ch = 0; ch < BKV / 8; ++ch) {
+          float p[8];
+#pragma unroll
+          for (int e = 0; e < 8; e += 2)
+            ffma2(p[e], p[e + 1], __uint_as_float(x[ch * 8 + e]), __uint_as_float(x[ch * 8 + e + 1]), scale_log2,
+                  scale_log2, neg, neg);
+#pragma unroll
+          for (int e = 0; e < 6; ++e) p[e] = ex2(p[e]);
+          exp2_poly2(p[6], p[7], p[6], p[7]);
+          sum0 += (p[0] + p[2]) + (p[4] + p[6]);
+          sum1 += (p[1] + p[3]) + (p[5] + p[7]);
+          uint4 v;
+          v.x = pack_bf16(p[0], p[1]);
+          v.y = pack_bf16(p[2], p[3]);
+          v.z = pack_bf16(p[4], p[5]);
+          v.w = pack_bf16(p[6], p[7]);
+          *reinterpret_cast<uint4*>(pbuf + (ch >> 3) * TILE + sw128(r, ch & 7)) = v;
+        }
+        l = l * alpha + (sum0 + sum1);
+        m = m_new;
+        if (j >= 1 && __any_sync(0xffffffffu, raise)) {
+          // The maximum rose: scale the accumulated output to it before P_j V_j is added.
+          uint32_t o[HD];
+          tmem_ld_x32(lane_base + o_col, o);
+          tmem_ld_x32(lane_base + o_col + 32, o + 32);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < HD; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+          tmem_st_x32(lane_base + o_col, o);
+          tmem_st_x32(lane_base + o_col + 32, o + 32);
+          tmem_st_wait();
+        }
+        fence_proxy_async_smem();  // P (generic-proxy writes) -> the tensor cores
+        tc_fence_before();
+        mbar_arrive(p_full + t);
+        if (tr) trace(true, 512 * t + 8 * j + 4);
       }
-      lse[(size_t)bh * T + qrow] = (m + log2f(l)) * kLn2;
-    } else if (lane == 0) {
-      fail(err, &s_abort, 25u);
+      if (ok && nkv[t] > 0) ok = warp_wait(o_done + t, (uint32_t)(nkv[t] - 1) & 1, lane);
+      if (ok) {
+        tc_fence_after();
+        uint32_t o[HD];
+        tmem_ld_x32(lane_base + o_col, o);
+        tmem_ld_x32(lane_base + o_col + 32, o + 32);
+        tmem_ld_wait();
+        const float inv = 1.f / l;
+        __nv_bfloat16* yr = y + (size_t)(row0 + qrow) * C + h * HD;
+#pragma unroll
+        for (int ch = 0; ch < HD / 8; ++ch) {
+          const float* f = reinterpret_cast<const float*>(o + ch * 8);
+          uint4 pk;
+          pk.x = pack_bf16(f[0] * inv, f[1] * inv);
+          pk.y = pack_bf16(f[2] * inv, f[3] * inv);
+          pk.z = pack_bf16(f[4] * inv, f[5] * inv);
+          pk.w = pack_bf16(f[6] * inv, f[7] * inv);
+          reinterpret_cast<uint4*>(yr)[ch] = pk;
+        }
+        lse[(size_t)bh * T + qrow] = (m + log2f(l)) * kLn2;
+      } else if (lane == 0) {
+        fail(err, &s_abort, 25u);
+      }
     }
   }
   tc_fence_before();
@@ -370,15 +570,24 @@ k_attn_fwd(const __grid_constant__ CUtensorMap tm_qkv, __nv_bfloat16* __restrict
 }
 
 // ============================================================ backward
+// One CTA per (128-key block, batch, head), looping over the query blocks
+// that see it. Every query block is processed as two halves of 64 queries
+// ("half-steps"): the scores S^T and dP^T of a half go to one of two TMEM
+// buffers, so the tensor cores compute the next halves' scores and the
+// previous half's dV / dK updates while the softmax warps work on this one.
 constexpr int G_K = 0, G_V = TILE, G_Q = 2 * TILE, G_DO = 4 * TILE;  // Q / dO: 2 stages each
-constexpr int G_PT = 6 * TILE, G_DST = 8 * TILE;                      // two [128][64] halves each
-constexpr int G_DQS = 10 * TILE;                                      // fp32 [128][64] staging: 32 KB
+constexpr int G_PT = 6 * TILE;                                        // P^T: one [128][64] tile per half buffer
+constexpr int G_DST = 8 * TILE;                                       // dS^T of the query block: two [128][64] halves
+constexpr int G_DQS = 10 * TILE;                                      // fp32 [128][64] dQ staging: 32 KB
 constexpr int G_LSE = 12 * TILE, G_DEL = G_LSE + 1024;                // [2][128] fp32 each
 constexpr int G_BAR = G_DEL + 1024;
 constexpr int G_SMEM = G_BAR + 256 + 1024;
-constexpr int G_THREADS = 384;
-// TMEM columns: S^T 0, dP^T 128, dV 256, dK 320, dQ buffers 384 / 448.
-constexpr uint32_t T_ST = 0, T_DPT = 128, T_DV = 256, T_DK = 320, T_DQ = 384;
+// Warp 0 TMA, 1 MMA, 2-3 idle, 4-11 softmax (warps 4-7: columns 0-31 of a
+// half, 8-11: columns 32-63), 12-15 dQ drain. 128 registers per thread.
+constexpr int G_THREADS = 512;
+// TMEM columns: half buffers b at 128 b (S^T half: +0, dP^T half: +64), dV
+// 256, dK 320, dQ buffers 384 / 448.
+constexpr uint32_t T_SP = 0, T_DV = 256, T_DK = 320, T_DQ = 384;
 
 __global__ void __launch_bounds__(G_THREADS, 1)
 k_attn_bwd(const __grid_constant__ CUtensorMap tm_qkv, const __grid_constant__ CUtensorMap tm_do,
@@ -388,19 +597,22 @@ k_attn_bwd(const __grid_constant__ CUtensorMap tm_qkv, const __grid_constant__ C
   uint8_t* smem = align1024(smem_raw);
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem + G_BAR);
   uint64_t* kv_full = bar;
-  uint64_t* q_full = bar + 1;     // [2]
+  uint64_t* q_full = bar + 1;     // [2] Q, dO, lse, Delta of a query block
   uint64_t* q_empty = bar + 3;    // [2]
-  uint64_t* sp_full = bar + 5;
-  uint64_t* pds_full = bar + 6;
-  uint64_t* pds_empty = bar + 7;
-  uint64_t* dq_full = bar + 8;    // [2]
-  uint64_t* dq_empty = bar + 10;  // [2]
-  uint64_t* acc_full = bar + 12;
-  uint64_t* mma_done = bar + 13;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 14);
+  uint64_t* sp_full = bar + 5;    // [2] per half buffer: S^T, dP^T complete
+  uint64_t* sp_free = bar + 7;    // [2] per half buffer: read into registers
+  uint64_t* pds_full = bar + 9;   // [2] per half buffer: P^T, dS^T in shared memory
+  uint64_t* dq_full = bar + 11;   // [2]
+  uint64_t* dq_empty = bar + 13;  // [2]
+  uint64_t* dq_read = bar + 15;   // dQ of the query block done (dS^T half 0, P^T buffer 0 free)
+  uint64_t* h1_read = bar + 16;   // second half's dV / dK done (dS^T half 1, P^T buffer 1 free)
+  uint64_t* acc_full = bar + 17;
+  uint64_t* mma_done = bar + 18;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 19);
   __shared__ volatile int s_abort;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const bool tron = (int)blockIdx.x == g_trace_cta;
   const int nq = T / BQ;
   const int BH = B * H;
   const int kb = (int)(blockIdx.x / BH);  // key block; the earliest see the most query blocks
@@ -409,6 +621,7 @@ k_attn_bwd(const __grid_constant__ CUtensorMap tm_qkv, const __grid_constant__ C
   const int C = H * HD;
   const int i0 = causal ? kb : 0;
   const int nsteps = nq - i0;
+  const int U = 2 * nsteps;  // half-steps
   const int row0 = b * T;
   const float scale_log2 = scale * kLog2e;
 
@@ -417,12 +630,14 @@ k_attn_bwd(const __grid_constant__ CUtensorMap tm_qkv, const __grid_constant__ C
     for (int s = 0; s < 2; ++s) {
       mbar_init(q_full + s, 1);
       mbar_init(q_empty + s, 1);
+      mbar_init(sp_full + s, 1);
+      mbar_init(sp_free + s, 256);
+      mbar_init(pds_full + s, 256);
       mbar_init(dq_full + s, 1);
       mbar_init(dq_empty + s, 128);
     }
-    mbar_init(sp_full, 1);
-    mbar_init(pds_full, 128);
-    mbar_init(pds_empty, 1);
+    mbar_init(dq_read, 1);
+    mbar_init(h1_read, 1);
     mbar_init(acc_full, 1);
     mbar_init(mma_done, 1);
     s_abort = 0;
@@ -465,148 +680,204 @@ k_attn_bwd(const __grid_constant__ CUtensorMap tm_qkv, const __grid_constant__ C
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      constexpr uint32_t idS = umma_idesc_bf16_f32(BKV, BQ);
+      // Descriptors computed once (see the forward kernel): K-major operands
+      // advance 2 per K step of 16, MN-major ones 128; tiles TILE / 16 apart.
+      constexpr uint32_t idS = umma_idesc_bf16_f32(BKV, 64);                 // S^T / dP^T half: N = 64 queries
       constexpr uint32_t idKV = umma_idesc_bf16_f32(BKV, HD, false, true);  // dV, dK: B MN-major
       constexpr uint32_t idQ = umma_idesc_bf16_f32(BQ, HD, true, true);     // dQ: A and B MN-major
-      const uint32_t k_addr = smem_u32(smem + G_K), v_addr = smem_u32(smem + G_V);
-      const uint32_t pt_addr = smem_u32(smem + G_PT), dst_addr = smem_u32(smem + G_DST);
-      bool ok = mbar_wait_bounded(kv_full, 0, kWait);
-      if (!ok) fail(err, &s_abort, 32u);
-      for (int t = 0; ok && t < nsteps && !s_abort; ++t) {
-        const int s = t & 1;
-        const uint32_t u = (uint32_t)(t >> 1);
-        if (!mbar_wait_bounded(q_full + s, u & 1, kWait)) {
-          fail(err, &s_abort, 33u);
-          break;
-        }
+      constexpr uint64_t kTileStep = TILE >> 4, kHalf = 8192 >> 4;
+      const uint64_t dk = umma_desc_sw128_kmajor(smem_u32(smem + G_K));
+      const uint64_t dv = umma_desc_sw128_kmajor(smem_u32(smem + G_V));
+      const uint64_t dq0 = umma_desc_sw128_kmajor(smem_u32(smem + G_Q));
+      const uint64_t ddo0 = umma_desc_sw128_kmajor(smem_u32(smem + G_DO));
+      const uint64_t dqm0 = desc_mn(smem_u32(smem + G_Q), 8192);    // Q as an MN-major B operand
+      const uint64_t ddom0 = desc_mn(smem_u32(smem + G_DO), 8192);  // dO as an MN-major B operand
+      const uint64_t dpt = umma_desc_sw128_kmajor(smem_u32(smem + G_PT));
+      const uint64_t dst = umma_desc_sw128_kmajor(smem_u32(smem + G_DST));
+      const uint64_t dstm = desc_mn(smem_u32(smem + G_DST), TILE);   // dS^T as an MN-major A operand
+      const uint64_t dkm = desc_mn(smem_u32(smem + G_K), 8192);      // K as an MN-major B operand
+      // S^T and dP^T of half-step u into half buffer u & 1.
+      auto issue_sp = [&](int u) -> bool {
+        const int t = u >> 1, hh = u & 1, s = t & 1;
+        if (!mbar_wait_bounded(q_full + s, (t >> 1) & 1, kWait)) return false;
         tc_fence_after();
-        // S^T / dP^T of step t - 1 were read before pds_full of t - 1 (waited below).
-        const uint32_t q_addr = smem_u32(smem + G_Q + s * TILE), do_addr = smem_u32(smem + G_DO + s * TILE);
+        const uint64_t off = (uint64_t)s * kTileStep + (uint64_t)hh * kHalf;
+        const uint64_t bq = dq0 + off, bdo = ddo0 + off;
+        const uint32_t d = tbase + T_SP + (u & 1) * 128;
 #pragma unroll
-        for (int k = 0; k < HD / 16; ++k)
-          umma_f16(tbase + T_ST, umma_desc_sw128_kmajor(k_addr + k * 32), umma_desc_sw128_kmajor(q_addr + k * 32),
-                   idS, k > 0 ? 1u : 0u);
+        for (int k = 0; k < HD / 16; ++k) umma_f16(d, dk + 2 * k, bq + 2 * k, idS, k > 0 ? 1u : 0u);
 #pragma unroll
-        for (int k = 0; k < HD / 16; ++k)
-          umma_f16(tbase + T_DPT, umma_desc_sw128_kmajor(v_addr + k * 32), umma_desc_sw128_kmajor(do_addr + k * 32),
-                   idS, k > 0 ? 1u : 0u);
-        umma_commit(sp_full);
-        if (!mbar_wait_bounded(pds_full, (uint32_t)t & 1, kWait) ||
-            (t >= 2 && !mbar_wait_bounded(dq_empty + s, (u - 1) & 1, kWait))) {
+        for (int k = 0; k < HD / 16; ++k) umma_f16(d + 64, dv + 2 * k, bdo + 2 * k, idS, k > 0 ? 1u : 0u);
+        umma_commit(sp_full + (u & 1));
+        return true;
+      };
+      bool ok = mbar_wait_bounded(kv_full, 0, kWait);
+      if (ok) {
+        tc_fence_after();
+        ok = issue_sp(0) && (U < 2 || issue_sp(1));
+      }
+      if (!ok) fail(err, &s_abort, 32u);
+      for (int u = 0; ok && u < U && !s_abort; ++u) {
+        const int t = u >> 1, hh = u & 1, s = t & 1, bf = u & 1;
+        const uint32_t ph = (uint32_t)(u >> 1) & 1;
+        // Next scores into this half buffer once the softmax has read it.
+        if (u + 2 < U) {
+          if (!mbar_wait_bounded(sp_free + bf, ph, kWait) || !issue_sp(u + 2)) {
+            fail(err, &s_abort, 33u);
+            break;
+          }
+        }
+        trace(tron, 3072 + 4 * u);
+        if (!mbar_wait_bounded(pds_full + bf, ph, kWait)) {
           fail(err, &s_abort, 34u);
           break;
         }
+        trace(tron, 3072 + 4 * u + 1);
         tc_fence_after();
+        if (hh == 1) {
+          // dQ_i = dS K first (A = dS^T read MN-major, the two 64-query halves
+          // TILE apart): the next block's softmax waits on it to reuse dS^T.
+          if (t >= 2 && !mbar_wait_bounded(dq_empty + s, ((t >> 1) - 1) & 1, kWait)) {
+            fail(err, &s_abort, 35u);
+            break;
+          }
+          tc_fence_after();
 #pragma unroll
-        for (int k = 0; k < BQ / 16; ++k)
-          umma_f16(tbase + T_DV, umma_desc_sw128_kmajor(pt_addr + (k >> 2) * TILE + (k & 3) * 32),
-                   desc_mn(do_addr + k * 2048, 8192), idKV, (t > 0 || k > 0) ? 1u : 0u);
+          for (int k = 0; k < BKV / 16; ++k)
+            umma_f16(tbase + T_DQ + s * HD, dstm + 128 * k, dkm + 128 * k, idQ, k > 0 ? 1u : 0u);
+          umma_commit(dq_full + s);
+          umma_commit(dq_read);
+        }
+        // dV += P^T dO_half, dK += dS^T Q_half (K = 64 queries).
+        const uint64_t off = (uint64_t)s * kTileStep + (uint64_t)hh * kHalf;
+        const uint64_t a_pt = dpt + (uint64_t)bf * kTileStep, a_ds = dst + (uint64_t)hh * kTileStep;
+        const uint64_t b_do = ddom0 + off, b_q = dqm0 + off;
 #pragma unroll
-        for (int k = 0; k < BQ / 16; ++k)
-          umma_f16(tbase + T_DK, umma_desc_sw128_kmajor(dst_addr + (k >> 2) * TILE + (k & 3) * 32),
-                   desc_mn(q_addr + k * 2048, 8192), idKV, (t > 0 || k > 0) ? 1u : 0u);
-        // dQ_i = dS K: A = dS^T read MN-major (query blocks of 64 are the two halves, TILE apart).
+        for (int k = 0; k < 4; ++k)
+          umma_f16(tbase + T_DV, a_pt + 2 * k, b_do + 128 * k, idKV, (u > 0 || k > 0) ? 1u : 0u);
 #pragma unroll
-        for (int k = 0; k < BKV / 16; ++k)
-          umma_f16(tbase + T_DQ + s * HD, desc_mn(dst_addr + k * 2048, TILE), desc_mn(k_addr + k * 2048, 8192), idQ,
-                   k > 0 ? 1u : 0u);
-        umma_commit(dq_full + s);
-        umma_commit(q_empty + s);
-        umma_commit(pds_empty);
+        for (int k = 0; k < 4; ++k)
+          umma_f16(tbase + T_DK, a_ds + 2 * k, b_q + 128 * k, idKV, (u > 0 || k > 0) ? 1u : 0u);
+        if (hh == 1) {
+          umma_commit(h1_read);
+          umma_commit(q_empty + s);
+          trace(tron, 3072 + 4 * u + 2);
+        }
       }
       if (ok && !s_abort) umma_commit(acc_full);
       umma_commit(mma_done);
       mbar_wait_bounded(mma_done, 0, kWait);
     }
-  } else if (warp >= 4 && warp < 8) {
-    // ---- P^T and dS^T, one key row per thread
+  } else if (warp >= 4 && warp < 12) {
+    // ---- P^T and dS^T: one key row per thread, 32 query columns of each half per warp
+    const int wg = (warp >> 2) - 1;     // column group within a half
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;  // key row in the block = TMEM lane
     const uint32_t lane_base = tbase + ((uint32_t)(quarter * 32) << 16);
+    const bool tr = tron && wg == 0 && r == 0;
     bool ok = true;
-    for (int t = 0; t < nsteps; ++t) {
-      const int i = i0 + t, s = t & 1;
-      if (!warp_wait(sp_full, (uint32_t)t & 1, lane) || !warp_wait(q_full + s, (uint32_t)(t >> 1) & 1, lane) ||
-          (t >= 1 && !warp_wait(pds_empty, (uint32_t)(t - 1) & 1, lane)) || s_abort) {
+    for (int u = 0; u < U; ++u) {
+      const int t = u >> 1, hh = u & 1, s = t & 1, bf = u & 1;
+      const int i = i0 + t;
+      if (!warp_wait(sp_full + bf, (uint32_t)(u >> 1) & 1, lane) ||
+          !warp_wait(q_full + s, (uint32_t)(t >> 1) & 1, lane) || s_abort) {
         ok = false;
         break;
       }
+      if (tr) trace(true, 2048 + 4 * u);
       tc_fence_after();
-      const float* lse_s = reinterpret_cast<const float*>(smem + G_LSE + s * 512);
-      const float* del_s = reinterpret_cast<const float*>(smem + G_DEL + s * 512);
+      uint32_t sr[32], dr[32];
+      tmem_ld_x32(lane_base + T_SP + bf * 128 + wg * 32, sr);
+      tmem_ld_x32(lane_base + T_SP + bf * 128 + 64 + wg * 32, dr);
+      tmem_ld_wait();
+      tc_fence_before();
+      mbar_arrive(sp_free + bf);
+      if (tr) trace(true, 2048 + 4 * u + 1);
+      // The previous query block's MMAs must be done with this half's P^T
+      // buffer and dS^T half (its dQ for half 0, its second dV / dK for half 1).
+      if (t >= 1 && !warp_wait(hh == 0 ? dq_read : h1_read, (uint32_t)(t - 1) & 1, lane)) {
+        ok = false;
+        break;
+      }
+      if (tr) trace(true, 2048 + 4 * u + 2);
+      const int cbase = hh * 64 + wg * 32;  // first query column of this thread's 32
+      const float* lse_s = reinterpret_cast<const float*>(smem + G_LSE + s * 512) + cbase;
+      const float* del_s = reinterpret_cast<const float*>(smem + G_DEL + s * 512) + cbase;
       const bool diag = causal && i == kb;
-#pragma unroll 1
-      for (int c0 = 0; c0 < BQ; c0 += 32) {
-        uint32_t sr[32], dr[32];
-        tmem_ld_x32(lane_base + T_ST + c0, sr);
-        tmem_ld_x32(lane_base + T_DPT + c0, dr);
-        tmem_ld_wait();
-        float p[32], ds[32];
 #pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          const int c = c0 + e;  // query column
-          float pv = exp2f(__uint_as_float(sr[e]) * scale_log2 - lse_s[c] * kLog2e);
-          if (diag && c < r) pv = 0.f;  // key r is later than query c
+      for (int ch = 0; ch < 4; ++ch) {
+        const float4 l0 = reinterpret_cast<const float4*>(lse_s)[2 * ch];
+        const float4 l1 = reinterpret_cast<const float4*>(lse_s)[2 * ch + 1];
+        const float4 d0 = reinterpret_cast<const float4*>(del_s)[2 * ch];
+        const float4 d1 = reinterpret_cast<const float4*>(del_s)[2 * ch + 1];
+        const float lv[8] = {l0.x, l0.y, l0.z, l0.w, l1.x, l1.y, l1.z, l1.w};
+        const float dv[8] = {d0.x, d0.y, d0.z, d0.w, d1.x, d1.y, d1.z, d1.w};
+        float p[8], ds[8];
+        // p = 2^(s * scale * log2e - lse * log2e), dS = p (dP - Delta), in packed pairs.
+#pragma unroll
+        for (int e = 0; e < 8; e += 2) {
+          const int c = ch * 8 + e;
+          float n0, n1;
+          fmul2(n0, n1, lv[e], lv[e + 1], -kLog2e, -kLog2e);
+          ffma2(p[e], p[e + 1], __uint_as_float(sr[c]), __uint_as_float(sr[c + 1]), scale_log2, scale_log2, n0, n1);
+          fadd2(ds[e], ds[e + 1], __uint_as_float(dr[c]), __uint_as_float(dr[c + 1]), -dv[e], -dv[e + 1]);
+        }
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          float pv = ex2(p[e]);
+          if (diag && cbase + ch * 8 + e < r) pv = 0.f;  // key r is later than query cbase + c
           p[e] = pv;
-          ds[e] = pv * (__uint_as_float(dr[e]) - del_s[c]);
         }
-        const int half = c0 >> 6;
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const int ch = ((c0 & 63) >> 3) + q;
-          uint4 pk, dk;
-          pk.x = pack_bf16(p[q * 8 + 0], p[q * 8 + 1]);
-          pk.y = pack_bf16(p[q * 8 + 2], p[q * 8 + 3]);
-          pk.z = pack_bf16(p[q * 8 + 4], p[q * 8 + 5]);
-          pk.w = pack_bf16(p[q * 8 + 6], p[q * 8 + 7]);
-          dk.x = pack_bf16(ds[q * 8 + 0], ds[q * 8 + 1]);
-          dk.y = pack_bf16(ds[q * 8 + 2], ds[q * 8 + 3]);
-          dk.z = pack_bf16(ds[q * 8 + 4], ds[q * 8 + 5]);
-          dk.w = pack_bf16(ds[q * 8 + 6], ds[q * 8 + 7]);
-          *reinterpret_cast<uint4*>(smem + G_PT + half * TILE + sw128(r, ch)) = pk;
-          *reinterpret_cast<uint4*>(smem + G_DST + half * TILE + sw128(r, ch)) = dk;
-        }
+        for (int e = 0; e < 8; e += 2) fmul2(ds[e], ds[e + 1], ds[e], ds[e + 1], p[e], p[e + 1]);
+        uint4 pk, dk;
+        pk.x = pack_bf16(p[0], p[1]);
+        pk.y = pack_bf16(p[2], p[3]);
+        pk.z = pack_bf16(p[4], p[5]);
+        pk.w = pack_bf16(p[6], p[7]);
+        dk.x = pack_bf16(ds[0], ds[1]);
+        dk.y = pack_bf16(ds[2], ds[3]);
+        dk.z = pack_bf16(ds[4], ds[5]);
+        dk.w = pack_bf16(ds[6], ds[7]);
+        *reinterpret_cast<uint4*>(smem + G_PT + bf * TILE + sw128(r, wg * 4 + ch)) = pk;
+        *reinterpret_cast<uint4*>(smem + G_DST + hh * TILE + sw128(r, wg * 4 + ch)) = dk;
       }
       fence_proxy_async_smem();
       tc_fence_before();
-      mbar_arrive(pds_full);
+      mbar_arrive(pds_full + bf);
+      if (tr) trace(true, 2048 + 4 * u + 3);
     }
+    // dV (warps 4-7) and dK (warps 8-11) out of TMEM once every step is accumulated.
     if (ok && warp_wait(acc_full, 0, lane)) {
       tc_fence_after();
-      uint32_t dv[HD], dk[HD];
-      tmem_ld_x32(lane_base + T_DV, dv);
-      tmem_ld_x32(lane_base + T_DV + 32, dv + 32);
-      tmem_ld_x32(lane_base + T_DK, dk);
-      tmem_ld_x32(lane_base + T_DK + 32, dk + 32);
-      tmem_ld_wait();
+      const float sc = wg == 0 ? 1.f : scale;
       const size_t row = (size_t)(row0 + kb * BKV + r) * (3 * C);
-      uint4* gk = reinterpret_cast<uint4*>(dqkv + row + C + h * HD);
-      uint4* gv = reinterpret_cast<uint4*>(dqkv + row + 2 * C + h * HD);
+      uint4* g = reinterpret_cast<uint4*>(dqkv + row + (wg == 0 ? 2 * C : C) + h * HD);
 #pragma unroll
-      for (int ch = 0; ch < HD / 8; ++ch) {
-        const float* fk = reinterpret_cast<const float*>(dk + ch * 8);
-        const float* fv = reinterpret_cast<const float*>(dv + ch * 8);
-        uint4 pk, pv;
-        pk.x = pack_bf16(fk[0] * scale, fk[1] * scale);
-        pk.y = pack_bf16(fk[2] * scale, fk[3] * scale);
-        pk.z = pack_bf16(fk[4] * scale, fk[5] * scale);
-        pk.w = pack_bf16(fk[6] * scale, fk[7] * scale);
-        pv.x = pack_bf16(fv[0], fv[1]);
-        pv.y = pack_bf16(fv[2], fv[3]);
-        pv.z = pack_bf16(fv[4], fv[5]);
-        pv.w = pack_bf16(fv[6], fv[7]);
-        gk[ch] = pk;
-        gv[ch] = pv;
+      for (int half = 0; half < 2; ++half) {
+        uint32_t a[32];
+        tmem_ld_x32(lane_base + (wg == 0 ? T_DV : T_DK) + half * 32, a);
+        tmem_ld_wait();
+#pragma unroll
+        for (int ch = 0; ch < 4; ++ch) {
+          const float* f = reinterpret_cast<const float*>(a + ch * 8);
+          uint4 pk;
+          pk.x = pack_bf16(f[0] * sc, f[1] * sc);
+          pk.y = pack_bf16(f[2] * sc, f[3] * sc);
+          pk.z = pack_bf16(f[4] * sc, f[5] * sc);
+          pk.w = pack_bf16(f[6] * sc, f[7] * sc);
+          g[half * 4 + ch] = pk;
+        }
       }
     } else if (lane == 0) {
-      fail(err, &s_abort, 35u);
+      fail(err, &s_abort, 36u);
     }
-  } else if (warp >= 8) {
+  } else if (warp >= 12) {
     // ---- dQ_i: TMEM -> swizzled shared staging -> tensor bulk fp32 adds into the accumulator
     const int quarter = warp & 3;
     const int rq = quarter * 32 + lane;  // query row in the block = TMEM lane
     const uint32_t lane_base = tbase + ((uint32_t)(quarter * 32) << 16);
-    const bool issuer = (warp == 8 && lane == 0);
+    const bool issuer = (warp == 12 && lane == 0);
     uint8_t* stage = smem + G_DQS;
     for (int t = 0; t < nsteps; ++t) {
       const int i = i0 + t, s = t & 1;
@@ -655,9 +926,10 @@ k_attn_bwd(const __grid_constant__ CUtensorMap tm_qkv, const __grid_constant__ C
   }
 }
 
-// Delta[b, h, t] = sum_d dO[b*T + t, h*64 + d] * O[b*T + t, h*64 + d] (fp32).
-__global__ void k_attn_delta(const __nv_bfloat16* __restrict__ y, const __nv_bfloat16* __restrict__ dy,
-                             float* __restrict__ delta, int BT, int T, int H) {
+// Delta[b, h, t] = sum_d dO[b*T + t, h*64 + d] * O[b*T + t, h*64 + d] (fp32),
+// and the fp32 dQ accumulator row [b, h, t, :] cleared (one launch for both).
+__global__ void k_attn_prep(const __nv_bfloat16* __restrict__ y, const __nv_bfloat16* __restrict__ dy,
+                            float* __restrict__ delta, float* __restrict__ dq_acc, int BT, int T, int H) {
   const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   if (idx >= (long long)BT * H) return;
   const int row = (int)(idx / H), h = (int)(idx % H);
@@ -677,7 +949,11 @@ __global__ void k_attn_delta(const __nv_bfloat16* __restrict__ y, const __nv_bfl
     }
   }
   const int bb = row / T, t = row % T;
-  delta[((size_t)bb * H + h) * T + t] = acc;
+  const size_t rh = ((size_t)bb * H + h) * T + t;
+  delta[rh] = acc;
+  float4* z = reinterpret_cast<float4*>(dq_acc + rh * HD);
+#pragma unroll
+  for (int k = 0; k < HD / 4; ++k) z[k] = make_float4(0.f, 0.f, 0.f, 0.f);
 }
 
 // dqkv[b*T + t, h*64 + d] = bf16(scale * dq_acc[b, h, t, d]).
@@ -704,6 +980,18 @@ __global__ void k_attn_dq_out(const float* __restrict__ dq_acc, __nv_bfloat16* _
 }  // namespace attn
 
 // ------------------------------------------------------------ host
+cudaError_t attention_trace_select(int cta) {
+  cudaError_t e = cudaMemcpyToSymbol(attn::g_trace_cta, &cta, sizeof(int));
+  if (e != cudaSuccess) return e;
+  static const unsigned long long zeros[attn::kTraceSlots] = {};
+  return cudaMemcpyToSymbol(attn::g_trace, zeros, sizeof(zeros));
+}
+
+cudaError_t attention_trace_read(unsigned long long* host, int n) {
+  if (n > attn::kTraceSlots) n = attn::kTraceSlots;
+  return cudaMemcpyFromSymbol(host, attn::g_trace, (size_t)n * sizeof(unsigned long long));
+}
+
 bool attention_supported(int B, int T, int H, int head_dim) {
   return B > 0 && H > 0 && head_dim == attn::HD && T > 0 && T % attn::BQ == 0;
 }
@@ -727,7 +1015,7 @@ cudaError_t attention_fwd(const __nv_bfloat16* qkv, __nv_bfloat16* y, float* lse
     attr_set = true;
   }
   const float scale_log2 = kLog2e / sqrtf((float)HD);
-  const unsigned grid = (unsigned)((T / BQ) * B * H);
+  const unsigned grid = (unsigned)(((T / BQ + 1) / 2) * B * H);
   k_attn_fwd<<<grid, F_THREADS, F_SMEM, s>>>(tm, y, lse, B, T, H, causal ? 1 : 0, scale_log2, gemm_err_word());
   return cudaGetLastError();
 }
@@ -754,10 +1042,8 @@ cudaError_t attention_bwd(const __nv_bfloat16* qkv, const __nv_bfloat16* y, cons
     if (e != cudaSuccess) return e;
     attr_set = true;
   }
-  e = cudaMemsetAsync(dq_acc, 0, (size_t)B * H * T * HD * sizeof(float), s);
-  if (e != cudaSuccess) return e;
   const long long rows = (long long)B * T * H;
-  k_attn_delta<<<(unsigned)((rows + 255) / 256), 256, 0, s>>>(y, dy, delta, B * T, T, H);
+  k_attn_prep<<<(unsigned)((rows + 255) / 256), 256, 0, s>>>(y, dy, delta, dq_acc, B * T, T, H);
   const float scale = 1.f / sqrtf((float)HD);
   const unsigned grid = (unsigned)((T / BKV) * B * H);
   k_attn_bwd<<<grid, G_THREADS, G_SMEM, s>>>(tq, tdo, tdq, lse, delta, dqkv, B, T, H, causal ? 1 : 0, scale,

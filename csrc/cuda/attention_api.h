@@ -22,4 +22,9 @@ cudaError_t attention_bwd(const __nv_bfloat16* qkv, const __nv_bfloat16* y, cons
                           const float* lse, __nv_bfloat16* dqkv, float* ws, int B, int T, int H, bool causal,
                           cudaStream_t s);
 
+// Tuning aid: record the event timeline (SM clock) of CTA `cta` of the
+// following launches (-1: off), and read the 4096 recorded slots back.
+cudaError_t attention_trace_select(int cta);
+cudaError_t attention_trace_read(unsigned long long* host, int n);
+
 }  // namespace nexar

@@ -410,6 +410,13 @@ void register_gemm_ops(py::module& m) {
   m.def("attn_supported", [](int64_t B, int64_t T, int64_t H, int64_t hd) {
     return attention_supported((int)B, (int)T, (int)H, (int)hd);
   });
+  m.def("attn_trace_select", [](int64_t cta) { chk(attention_trace_select((int)cta), "attn_trace_select"); });
+  m.def("attn_trace_read", []() {
+    at::Tensor out = at::empty({4096}, at::TensorOptions().dtype(at::kLong));
+    chk(attention_trace_read(reinterpret_cast<unsigned long long*>(out.data_ptr<int64_t>()), 4096),
+        "attn_trace_read");
+    return out;
+  });
   m.def("attn_bwd_workspace_floats", [](int64_t B, int64_t T, int64_t H) {
     return (int64_t)attention_bwd_workspace_floats((int)B, (int)T, (int)H);
   });

@@ -27,7 +27,7 @@ def _reference(qkv, B, T, H, causal):
 
 
 @pytest.mark.parametrize("causal", [True, False])
-@pytest.mark.parametrize("B,T,H", [(2, 256, 2), (1, 384, 3)])
+@pytest.mark.parametrize("B,T,H", [(1, 128, 1), (2, 256, 2), (1, 384, 3), (2, 1024, 4), (1, 2048, 2)])
 def test_attention_matches_fp32_reference(cuda0, B, T, H, causal):
     from nexar_b200 import _native, ops
     g = torch.Generator(device="cuda").manual_seed(3)
@@ -59,3 +59,23 @@ def test_gpt2_step_with_own_attention_tracks_sdpa(cuda0):
         losses[own] = [tr.step(idx, tgt) for _ in range(3)]
     for a, b in zip(losses[False], losses[True]):
         assert abs(a - b) < 2e-2 * max(1.0, abs(a)), losses
+
+
+@pytest.mark.parametrize("causal", [True, False])
+def test_attention_lse_matches_logsumexp(cuda0, causal):
+    """The saved per-row statistic is the natural-log softmax normaliser of the scaled scores."""
+    from nexar_b200 import _native
+    B, T, H = 2, 640, 3
+    g = torch.Generator(device="cuda").manual_seed(4)
+    qkv = torch.randn(B * T, 3 * H * 64, device=cuda0, generator=g).to(torch.bfloat16)
+    y = torch.empty(B * T, H * 64, device=cuda0, dtype=torch.bfloat16)
+    lse = torch.empty(B * H * T, device=cuda0)
+    _native.cuda().attn_fwd(qkv, y, lse, B, T, H, causal)
+    torch.cuda.synchronize()
+    x = qkv.float().view(B, T, 3, H, 64)
+    q, k = x[:, :, 0].transpose(1, 2), x[:, :, 1].transpose(1, 2)
+    s = q @ k.transpose(-1, -2) / 8.0
+    if causal:
+        s = s.masked_fill(torch.ones(T, T, dtype=torch.bool, device=cuda0).triu(1), float("-inf"))
+    ref = torch.logsumexp(s, dim=-1).reshape(-1)
+    torch.testing.assert_close(lse, ref, rtol=1e-3, atol=1e-2)
