@@ -14,8 +14,8 @@
 //   warp 1      allocates 512 TMEM columns; lane 0 issues S_t = Q_t K_j^T
 //               (M = N = 128, K = 64) for the next key block of tile t as
 //               soon as tile t's softmax holds the current scores, and
-//               O_t += P_t V_j (M = 128, N = 64, K = 128) once P_t is in
-//               shared memory, polling both tiles' inputs and issuing
+//               O_t += P_t V_j (M = 128, N = 64, K = 128, P read from TMEM)
+//               once P_t is written, polling both tiles' inputs and issuing
 //               whichever MMA is ready (the tensor pipe takes an MMA only as
 //               fast as it runs them, so a fixed issue order would serialise
 //               the tiles); O_A and O_B accumulate in TMEM;
@@ -25,8 +25,8 @@
 //               it by more than 2^8), so the accumulated output is rescaled
 //               in TMEM only on those blocks. A quarter of the exponentials
 //               run on the FMA pipe (exp2_poly2), the rest on the MUFU unit.
-//               P goes to 128-byte-swizzled shared memory as bf16 (the A
-//               operand of the next MMA).
+//               P goes to TMEM as packed bf16 (tcgen05.st), where the next
+//               MMA reads it as its A operand.
 // Backward (k_attn_bwd): one CTA per (128-key block, batch, head), looping
 // over the query blocks that see it, each as two halves of 64 queries.
 //   warp 0      K_j, V_j once; Q_i, dO_i, lse_i, Delta_i per block (2-deep);
@@ -126,9 +126,22 @@ NEXAR_D uint8_t* align1024(uint8_t* p) {
   return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
 }
 
+// Non-blocking phase test (never suspends the thread).
+NEXAR_D bool mbar_test(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity) : "memory");
+  return ok != 0;
+}
+
 // Bounded wait by lane 0 of a warp; every lane then observes the completed
 // phase itself (acquire) before touching the data the phase publishes.
 NEXAR_D bool warp_wait(uint64_t* bar, uint32_t parity, int lane) {
+  // Fast path: one warp-wide test (the phase is usually complete already).
+  if (mbar_test(bar, parity)) return true;
   int ok = 1;
   if (lane == 0) ok = mbar_wait_bounded(bar, parity, kWait) ? 1 : 0;
   ok = __shfl_sync(0xffffffffu, ok, 0);
@@ -143,17 +156,6 @@ NEXAR_D void fail(unsigned int* err, volatile int* abort_flag, unsigned int code
 
 NEXAR_D void tmem_ld_x32(uint32_t taddr, uint32_t* r) {
   tmem_ld_32x32b_x32(taddr, *reinterpret_cast<uint32_t(*)[32]>(r));
-}
-
-// Non-blocking phase test (never suspends the thread).
-NEXAR_D bool mbar_test(uint64_t* bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity) : "memory");
-  return ok != 0;
 }
 
 // Event timeline of one CTA (SM clock, %clock64) for tuning the pipelines:
@@ -237,6 +239,17 @@ NEXAR_D void tmem_st_x32(uint32_t taddr, const uint32_t* r) {
 }
 NEXAR_D void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
+// kind::f16 MMA whose A operand is read from tensor memory (M = 128 rows in
+// the 128 lanes, K along the columns, two bf16 per 32-bit column) and B from
+// shared memory: no shared-memory traffic for A.
+NEXAR_D void umma_f16_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}"
+      :: "r"(tmem_d), "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate) : "memory");
+}
+
 // ============================================================ forward
 // One CTA per pair of adjacent 128-query tiles (A = 2p, B = 2p + 1) of one
 // (batch, head): the two tiles share every K / V load, and their softmax
@@ -246,15 +259,16 @@ constexpr int F_STAGES = 3;
 constexpr int F_QA = 0;                             // Q_A, Q_B: 2 tiles
 constexpr int F_K = 2 * TILE;                       // K ring
 constexpr int F_V = F_K + F_STAGES * TILE;          // V ring
-constexpr int F_P = F_V + F_STAGES * TILE;          // P_A, P_B: [128][128] bf16 each (two swizzled halves)
-constexpr int F_BAR = F_P + 4 * TILE;
+constexpr int F_BAR = F_V + F_STAGES * TILE;
 constexpr int F_SMEM = F_BAR + 256 + 1024;
 // Warpgroup 0: TMA (warp 0), MMA (warp 1); warpgroup 1: softmax of tile A;
 // warpgroup 2: softmax of tile B. 168 registers per thread (3 warps per SM
 // sub-partition: 3 x 32 x 168 = 16,128 of its 16,384).
 constexpr int F_THREADS = 384;
-// TMEM columns: S_A 0, S_B 128 (fp32 scores), O_A 256, O_B 320 (fp32 output accumulators).
-constexpr uint32_t T_S = 0, T_O = 256;
+// TMEM columns: S_A 0, S_B 128 (fp32 scores), O_A 256, O_B 320 (fp32 output
+// accumulators), P_A 384, P_B 448 (bf16 probabilities, two per column: the A
+// operand of O += P V, read by the tensor cores straight from TMEM).
+constexpr uint32_t T_S = 0, T_O = 256, T_P = 384;
 // The running maximum is raised only when a block's maximum exceeds it by
 // more than 2^8: between raises the probabilities stay below 256 (exact in
 // fp32, ample range in bf16) and the output accumulator needs no rescaling.
@@ -358,7 +372,6 @@ k_attn_fwd(const __grid_constant__ CUtensorMap tm_qkv, __nv_bfloat16* __restrict
       constexpr uint64_t kTileStep = TILE >> 4;
       const uint64_t dq0 = umma_desc_sw128_kmajor(smem_u32(smem + F_QA));
       const uint64_t dk0 = umma_desc_sw128_kmajor(smem_u32(smem + F_K));
-      const uint64_t dp0 = umma_desc_sw128_kmajor(smem_u32(smem + F_P));
       const uint64_t dv0 = desc_mn(smem_u32(smem + F_V), 8192);
       auto issue_s = [&](int t, int j) {
         const uint64_t da = dq0 + (uint64_t)t * kTileStep;
@@ -398,13 +411,12 @@ k_attn_fwd(const __grid_constant__ CUtensorMap tm_qkv, __nv_bfloat16* __restrict
           if (jp < nkv[t] && mbar_test(p_full + t, jp & 1) &&
               mbar_test(v_full + jp % F_STAGES, (jp / F_STAGES) & 1)) {
             tc_fence_after();
-            const uint64_t da = dp0 + (uint64_t)(2 * t) * kTileStep;
+            const uint32_t pa = tbase + T_P + t * 64;  // K step of 16 = 8 columns
             const uint64_t db = dv0 + (uint64_t)(jp % F_STAGES) * kTileStep;
             const uint32_t d = tbase + T_O + t * HD;
 #pragma unroll
             for (int k = 0; k < BKV / 16; ++k)
-              umma_f16(d, da + (uint64_t)((k >> 2) * kTileStep + (k & 3) * 2), db + 128 * k, idO,
-                       (jp > 0 || k > 0) ? 1u : 0u);
+              umma_f16_ts(d, pa + 8 * k, db + 128 * k, idO, (jp > 0 || k > 0) ? 1u : 0u);
             umma_commit(o_done + t);
             trace(tron, 1024 + 8 * jp + 4 * t + 1);
             np[t] = jp + 1;
@@ -447,7 +459,6 @@ k_attn_fwd(const __grid_constant__ CUtensorMap tm_qkv, __nv_bfloat16* __restrict
       const uint32_t s_col = T_S + t * BKV, o_col = T_O + t * HD;
       const int qt = 2 * pr + t;
       const int qrow = qt * BQ + r;
-      uint8_t* pbuf = smem + F_P + t * 2 * TILE;
       float m = -INFINITY, l = 0.f;
       bool ok = true;
       const bool tr = tron && r == 0;
@@ -485,7 +496,7 @@ k_attn_fwd(const __grid_constant__ CUtensorMap tm_qkv, __nv_bfloat16* __restrict
         const float alpha = raise ? ex2(m - m_new) : 1.f;
         if (tr) trace(true, 512 * t + 8 * j + 2);
         if (j >= 1) {
-          // P_t and O_t are free once O_t += P_{j-1} V_{j-1} has completed.
+          // P_t (TMEM) and O_t are free once O_t += P_{j-1} V_{j-1} has completed.
           if (!warp_wait(o_done + t, (uint32_t)(j - 1) & 1, lane)) {
             ok = false;
             break;
@@ -493,11 +504,12 @@ k_attn_fwd(const __grid_constant__ CUtensorMap tm_qkv, __nv_bfloat16* __restrict
           tc_fence_after();
         }
         if (tr) trace(true, 512 * t + 8 * j + 3);
-        // Probabilities straight into the swizzled P tile, 8 columns (16 bytes)
-        // at a time: 6 of every 8 exponentials on the MUFU unit, 2 on the FMA
-        // pipe (exp2_poly2), which balances the two for this loop.
+        // Probabilities into the row's P columns of TMEM, 32 columns (64
+        // values) at a time: 6 of every 8 exponentials on the MUFU unit, 2 on
+        // the FMA pipe (exp2_poly2), which balances the two for this loop.
         const float neg = -m_new;
         float sum0 = 0.f, sum1 = 0.f;
+        uint32_t pk[32];
 #pragma unroll
         for (int ch = 0; ch < BKV / 8; ++ch) {
           float p[8];
@@ -510,13 +522,14 @@ k_attn_fwd(const __grid_constant__ CUtensorMap tm_qkv, __nv_bfloat16* __restrict
           exp2_poly2(p[6], p[7], p[6], p[7]);
           sum0 += (p[0] + p[2]) + (p[4] + p[6]);
           sum1 += (p[1] + p[3]) + (p[5] + p[7]);
-          uint4 v;
-          v.x = pack_bf16(p[0], p[1]);
-          v.y = pack_bf16(p[2], p[3]);
-          v.z = pack_bf16(p[4], p[5]);
-          v.w = pack_bf16(p[6], p[7]);
-          *reinterpret_cast<uint4*>(pbuf + (ch >> 3) * TILE + sw128(r, ch & 7)) = v;
+          const int q = (ch & 7) * 4;
+          pk[q + 0] = pack_bf16(p[0], p[1]);
+          pk[q + 1] = pack_bf16(p[2], p[3]);
+          pk[q + 2] = pack_bf16(p[4], p[5]);
+          pk[q + 3] = pack_bf16(p[6], p[7]);
+          if ((ch & 7) == 7) tmem_st_x32(lane_base + T_P + t * 64 + (ch >> 3) * 32, pk);
         }
+        tmem_st_wait();
         l = l * alpha + (sum0 + sum1);
         m = m_new;
         if (j >= 1 && __any_sync(0xffffffffu, raise)) {
@@ -531,8 +544,7 @@ k_attn_fwd(const __grid_constant__ CUtensorMap tm_qkv, __nv_bfloat16* __restrict
           tmem_st_x32(lane_base + o_col + 32, o + 32);
           tmem_st_wait();
         }
-        fence_proxy_async_smem();  // P (generic-proxy writes) -> the tensor cores
-        tc_fence_before();
+        tc_fence_before();  // P (and a rescaled O) in TMEM before the MMA warp reads it
         mbar_arrive(p_full + t);
         if (tr) trace(true, 512 * t + 8 * j + 4);
       }
@@ -780,7 +792,7 @@ k_attn_bwd(const __grid_constant__ CUtensorMap tm_qkv, const __grid_constant__ C
       const int t = u >> 1, hh = u & 1, s = t & 1, bf = u & 1;
       const int i = i0 + t;
       if (!warp_wait(sp_full + bf, (uint32_t)(u >> 1) & 1, lane) ||
-          !warp_wait(q_full + s, (uint32_t)(t >> 1) & 1, lane) || s_abort) {
+          (hh == 0 && !warp_wait(q_full + s, (uint32_t)(t >> 1) & 1, lane)) || s_abort) {
         ok = false;
         break;
       }

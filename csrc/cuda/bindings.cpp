@@ -487,6 +487,16 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
       .def_property_readonly("connected", &DeviceComm::connected)
       .def_property("timeout_us", &DeviceComm::timeout_us, &DeviceComm::set_timeout_us)
       .def_readwrite("max_blocks", &DeviceComm::max_blocks)
+      .def_property("checks", &DeviceComm::checks, &DeviceComm::set_checks)
+      .def("debug_set_call_counter", &DeviceComm::debug_set_call_counter)
+      .def("debug_broadcast_raw_root", [](DeviceComm& c, const at::Tensor& in, const at::Tensor& out, int root) {
+        TORCH_CHECK(in.is_cuda() && out.is_cuda() && in.numel() == out.numel() &&
+                        in.scalar_type() == out.scalar_type(),
+                    "debug_broadcast_raw_root: matching CUDA tensors");
+        c10::cuda::CUDAGuard g(c.device());
+        c.debug_broadcast_raw_root(in.data_ptr(), out.data_ptr(), dtype_code(in.scalar_type()), in.numel(), root,
+                                   at::cuda::getCurrentCUDAStream(c.device()).stream());
+      })
       .def_readwrite("nvls_min_bytes", &DeviceComm::nvls_min_bytes)
       .def_readonly("last_allreduce_algo", &DeviceComm::last_allreduce_algo)
       .def_readwrite("nvls_min_rs_bytes", &DeviceComm::nvls_min_rs_bytes)

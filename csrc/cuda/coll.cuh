@@ -38,12 +38,67 @@ NEXAR_D void record_timeout(const CommDev& c, int peer, int op, unsigned long lo
   __threadfence_system();
 }
 
+NEXAR_D void record_check(const CommDev& c, int op, unsigned int id, unsigned long long value,
+                          unsigned long long limit) {
+  volatile DeviceStatus* s = c.status;
+  s->rank = (unsigned)value;
+  s->op = (unsigned)op;
+  s->block = id;
+  s->epoch = limit;
+  __threadfence_system();
+  s->code = kStatusCheckFailed;
+  __threadfence_system();
+}
+
+// Entry checks of a collective kernel (when c.checks is set): every block
+// evaluates the same launch arguments, so all blocks agree and return
+// together before touching memory. `bytes` must not exceed `limit`.
+NEXAR_D bool entry_ok(const CommDev& c, int op, int root = 0, unsigned long long bytes = 0,
+                      unsigned long long limit = ~0ull) {
+#ifndef NEXAR_NO_DEVICE_CHECKS
+  if (!c.checks) return true;
+  unsigned int id = 0;
+  unsigned long long v = 0, lim = 0;
+  if (c.world < 1 || c.world > kMaxRanks || c.rank < 0 || c.rank >= c.world) {
+    id = kCheckComm;
+    v = (unsigned long long)c.rank;
+    lim = (unsigned long long)c.world;
+  } else if (root < 0 || root >= c.world) {
+    id = kCheckRoot;
+    v = (unsigned long long)(long long)root;
+    lim = (unsigned long long)c.world;
+  } else if (bytes > limit) {
+    id = kCheckBytes;
+    v = bytes;
+    lim = limit;
+  }
+  if (id != 0) {
+    if (blockIdx.x == 0 && threadIdx.x == 0) record_check(c, op, id, v, lim);
+    return false;
+  }
+#endif
+  return true;
+}
+
 // Block-wide barrier with every peer's block of the same index. Returns false
-// (uniformly across the block) if any wait timed out.
+// (uniformly across the block) if any wait timed out (or, with device checks
+// on, if the epoch is not above the one this block stored last time).
 NEXAR_D bool block_barrier(const CommDev& c, unsigned long long epoch, int op) {
   __syncthreads();
   int ok = 1;
   const int p = threadIdx.x;
+#ifndef NEXAR_NO_DEVICE_CHECKS
+  if (c.checks) {
+    __shared__ int s_epoch_ok;
+    if (threadIdx.x == 0) {
+      const unsigned long long prev = ld_acquire_sys(flag_ptr(c, c.rank, blockIdx.x, c.rank));
+      s_epoch_ok = prev < epoch;
+      if (!s_epoch_ok) record_check(c, op, kCheckEpoch, prev, epoch);
+    }
+    __syncthreads();
+    if (!s_epoch_ok) return false;
+  }
+#endif
   if (p < c.world) {
     fence_sys();
     st_release_sys(flag_ptr(c, p, blockIdx.x, c.rank), epoch);

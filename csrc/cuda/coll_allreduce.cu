@@ -15,6 +15,10 @@ __global__ void __launch_bounds__(kThreads) k_ar_oneshot(CommDev c, const T* in,
                                                          unsigned long long n, float scale,
                                                          bool vec, long long sym_off) {
   const unsigned long long call = call_index(c);
+  if (!entry_ok(c, kOpAllReduce, 0, n * sizeof(T), (sym_off >= 0 ? c.heap_bytes - (unsigned long long)sym_off : c.slot_bytes))) {
+    finish_call(c, call);
+    return;
+  }
   constexpr int V = PackOf<T>::V;
   unsigned long long lo, hi;
   block_range(n, gridDim.x, blockIdx.x, V, &lo, &hi);
@@ -42,6 +46,10 @@ __global__ void __launch_bounds__(kThreads) k_ar_twoshot(CommDev c, const T* in,
                                                          unsigned long long n, float scale,
                                                          bool vec, long long sym_off) {
   const unsigned long long call = call_index(c);
+  if (!entry_ok(c, kOpAllReduce, 0, n * (sizeof(T) > sizeof(TO) ? sizeof(T) : sizeof(TO)), (sym_off >= 0 ? c.heap_bytes - (unsigned long long)sym_off : c.slot_bytes))) {
+    finish_call(c, call);
+    return;
+  }
   constexpr int V = PackOf<T>::V;
   const int N = c.world;
   unsigned long long chunk = (n + N - 1) / N;

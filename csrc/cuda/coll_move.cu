@@ -9,6 +9,10 @@ __global__ void __launch_bounds__(kThreads) k_all_gather(CommDev c, const T* in,
                                                          unsigned long long count,
                                                          unsigned long long out_ld, bool vec) {
   const unsigned long long call = call_index(c);
+  if (!entry_ok(c, kOpAllGather, 0, count * sizeof(T), c.slot_bytes)) {
+    finish_call(c, call);
+    return;
+  }
   constexpr int V = PackOf<T>::V;
   const int N = c.world;
   unsigned long long lo, hi;
@@ -32,6 +36,10 @@ __global__ void __launch_bounds__(kThreads) k_all_to_all(CommDev c, const T* in,
                                                          unsigned long long in_ld,
                                                          unsigned long long out_ld, bool vec) {
   const unsigned long long call = call_index(c);
+  if (!entry_ok(c, kOpAllToAll, 0, (unsigned long long)c.world * count * sizeof(T), c.slot_bytes)) {
+    finish_call(c, call);
+    return;
+  }
   constexpr int V = PackOf<T>::V;
   const int N = c.world;
   unsigned long long lo, hi;
@@ -54,6 +62,10 @@ template <typename T>
 __global__ void __launch_bounds__(kThreads) k_broadcast(CommDev c, const T* in, T* out,
                                                         unsigned long long n, int root, bool vec) {
   const unsigned long long call = call_index(c);
+  if (!entry_ok(c, kOpBroadcast, root, n * sizeof(T), c.slot_bytes)) {
+    finish_call(c, call);
+    return;
+  }
   constexpr int V = PackOf<T>::V;
   unsigned long long lo, hi;
   block_range(n, gridDim.x, blockIdx.x, V, &lo, &hi);
@@ -74,6 +86,10 @@ __global__ void __launch_bounds__(kThreads) k_gather(CommDev c, const T* in, T* 
                                                      unsigned long long count,
                                                      unsigned long long out_ld, int root, bool vec) {
   const unsigned long long call = call_index(c);
+  if (!entry_ok(c, kOpGather, root, count * sizeof(T), c.slot_bytes)) {
+    finish_call(c, call);
+    return;
+  }
   constexpr int V = PackOf<T>::V;
   unsigned long long lo, hi;
   block_range(count, gridDim.x, blockIdx.x, V, &lo, &hi);
@@ -93,6 +109,10 @@ __global__ void __launch_bounds__(kThreads) k_scatter(CommDev c, const T* in, T*
                                                       unsigned long long count,
                                                       unsigned long long in_ld, int root, bool vec) {
   const unsigned long long call = call_index(c);
+  if (!entry_ok(c, kOpScatter, root, (unsigned long long)c.world * count * sizeof(T), c.slot_bytes)) {
+    finish_call(c, call);
+    return;
+  }
   constexpr int V = PackOf<T>::V;
   unsigned long long lo, hi;
   block_range(count, gridDim.x, blockIdx.x, V, &lo, &hi);
@@ -111,6 +131,10 @@ __global__ void __launch_bounds__(kThreads) k_scatter(CommDev c, const T* in, T*
 // ============================================================ barrier
 __global__ void k_barrier(CommDev c) {
   const unsigned long long call = call_index(c);
+  if (!entry_ok(c, kOpBarrier, 0, 0, c.slot_bytes)) {
+    finish_call(c, call);
+    return;
+  }
   block_barrier(c, epoch_of(call, 0), kOpBarrier);
   finish_call(c, call);
 }
@@ -146,6 +170,10 @@ template <typename T>
 __global__ void __launch_bounds__(kThreads) k_broadcast_sag(CommDev c, const T* in, T* out,
                                                             unsigned long long n, int root, bool vec) {
   const unsigned long long call = call_index(c);
+  if (!entry_ok(c, kOpBroadcast, root, n * sizeof(T), c.slot_bytes)) {
+    finish_call(c, call);
+    return;
+  }
   constexpr int V = PackOf<T>::V;
   const int N = c.world;
   unsigned long long chunk = (n + N - 1) / N;

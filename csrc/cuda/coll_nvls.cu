@@ -212,6 +212,9 @@ template <typename T>
 __global__ void __launch_bounds__(kNvlsThreads) k_allreduce_nvls(CommDev c, const T* in, T* out,
                                                                  unsigned long long nbytes, float scale,
                                                                  long long sym_off) {
+  if (!entry_ok(c, kOpAllReduce, 0, sym_off >= 0 ? (unsigned long long)sym_off + nbytes : 0,
+                sym_off >= 0 ? c.nvls_bytes : ~0ull))
+    return;
   __shared__ unsigned int s_seq;
   if (threadIdx.x == 0) s_seq = c.nvls_seq[blockIdx.x];
   __syncthreads();
@@ -256,6 +259,7 @@ template <typename T>
 __global__ void __launch_bounds__(kNvlsThreads) k_reduce_scatter_nvls(CommDev c, const T* in, T* out,
                                                                       unsigned long long count_bytes,
                                                                       float scale, long long in_sym) {
+  if (!entry_ok(c, kOpReduceScatter)) return;
   __shared__ unsigned int s_seq;
   if (threadIdx.x == 0) s_seq = c.nvls_seq[blockIdx.x];
   __syncthreads();
@@ -300,6 +304,7 @@ __global__ void __launch_bounds__(kNvlsThreads) k_reduce_scatter_nvls(CommDev c,
 __global__ void __launch_bounds__(kNvlsThreads) k_gather_bcast_nvls(CommDev c, const void* in, void* out,
                                                                     unsigned long long count_bytes, int root,
                                                                     long long out_sym) {
+  if (!entry_ok(c, root < 0 ? kOpAllGather : kOpBroadcast, root < 0 ? 0 : root)) return;
   __shared__ unsigned int s_seq;
   if (threadIdx.x == 0) s_seq = c.nvls_seq[blockIdx.x];
   __syncthreads();

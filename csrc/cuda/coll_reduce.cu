@@ -13,6 +13,10 @@ __global__ void __launch_bounds__(kThreads) k_reduce_scatter(CommDev c, const T*
                                                              unsigned long long in_ld, float scale,
                                                              bool vec) {
   const unsigned long long call = call_index(c);
+  if (!entry_ok(c, kOpReduceScatter, 0, (unsigned long long)c.world * count * sizeof(T), c.slot_bytes)) {
+    finish_call(c, call);
+    return;
+  }
   constexpr int V = PackOf<T>::V;
   const int N = c.world;
   unsigned long long lo, hi;
@@ -38,6 +42,10 @@ __global__ void __launch_bounds__(kThreads) k_reduce(CommDev c, const T* in, TO*
                                                      unsigned long long n, int root, float scale,
                                                      bool vec) {
   const unsigned long long call = call_index(c);
+  if (!entry_ok(c, kOpReduce, root, n * (sizeof(T) > sizeof(TO) ? sizeof(T) : sizeof(TO)), c.slot_bytes)) {
+    finish_call(c, call);
+    return;
+  }
   constexpr int V = PackOf<T>::V;
   const int N = c.world;
   unsigned long long chunk = (n + N - 1) / N;

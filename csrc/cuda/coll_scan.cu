@@ -10,6 +10,10 @@ template <typename T, int OP>
 __global__ void __launch_bounds__(kThreads) k_scan(CommDev c, const T* in, T* out,
                                                    unsigned long long n, bool exclusive, bool vec) {
   const unsigned long long call = call_index(c);
+  if (!entry_ok(c, kOpScan, 0, n * sizeof(T), c.slot_bytes)) {
+    finish_call(c, call);
+    return;
+  }
   constexpr int V = PackOf<T>::V;
   unsigned long long lo, hi;
   block_range(n, gridDim.x, blockIdx.x, V, &lo, &hi);

@@ -31,6 +31,16 @@ enum StatusCode : unsigned int {
   kStatusOk = 0,
   kStatusWaitTimeout = 1,
   kStatusBadArgument = 2,
+  // A device argument check (CommDev::checks) refused a launch before any
+  // memory access: `block` holds the CheckId, `rank` the offending value and
+  // `epoch` the limit it broke.
+  kStatusCheckFailed = 3,
+};
+enum CheckId : unsigned int {
+  kCheckComm = 1,   // rank / world of the communicator out of range
+  kCheckRoot = 2,   // root or peer index >= world
+  kCheckBytes = 3,  // staged or symmetric extent beyond its buffer
+  kCheckEpoch = 4,  // barrier epoch not above the one this block stored last
 };
 
 constexpr int kMaxRanks = 8;
@@ -66,6 +76,13 @@ struct CommDev {
   char* nvls_mc;
   unsigned long long nvls_bytes;
   unsigned int* nvls_seq;       // local per-block round counters
+  // Device argument checks (NEXAR_DEVICE_CHECKS=1; compiled out with
+  // -DNEXAR_NO_DEVICE_CHECKS): root / peer < world, staged and symmetric
+  // extents inside their buffers, barrier epochs strictly increasing. A
+  // failed check records kStatusCheckFailed and the kernel returns before
+  // touching any buffer.
+  int checks;
+  unsigned long long heap_bytes;
 };
 
 constexpr unsigned long long kNvlsSignalBytes = 1ull << 20;

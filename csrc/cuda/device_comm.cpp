@@ -1,4 +1,5 @@
 #include "device_comm.h"
+#include "coll_api.h"
 
 #include <cstring>
 #include <unistd.h>
@@ -63,7 +64,23 @@ DeviceComm::DeviceComm(int rank, int world, int device, uint64_t heap_bytes, uin
   dev_.nvls_uc = dev_.nvls_mc = nullptr;
   dev_.nvls_bytes = 0;
   dev_.nvls_seq = nullptr;
+  dev_.checks = 0;
+  dev_.heap_bytes = heap_bytes_;
   if (world_ == 1) connected_ = true;
+}
+
+void DeviceComm::debug_set_call_counter(unsigned long long v) {
+  DeviceGuard g(device_);
+  check_cuda(cudaDeviceSynchronize(), "cudaDeviceSynchronize");
+  check_cuda(cudaMemcpy(ctrl_, &v, sizeof(v), cudaMemcpyHostToDevice), "cudaMemcpy(call counter)");
+}
+
+void DeviceComm::debug_broadcast_raw_root(const void* in, void* out, int dt, unsigned long long n, int root,
+                                          cudaStream_t s) {
+  if (!dev_.checks) throw std::runtime_error("debug_broadcast_raw_root needs device checks on (set_checks)");
+  if ((unsigned long long)n * 16 > slot_bytes_) throw std::invalid_argument("debug_broadcast_raw_root: n too large");
+  DeviceGuard g(device_);
+  check_cuda(launch_broadcast(dev_, in, out, dt, n, root, 1, s), "debug broadcast");
 }
 
 DeviceComm::~DeviceComm() {

@@ -60,6 +60,16 @@ class DeviceComm {
   DeviceStatus status() const;
   void clear_status();
   void set_timeout_us(uint64_t us) { dev_.timeout_ns = us * 1000ull; }
+  // Device argument checks in every collective kernel (see CommDev::checks).
+  bool checks() const { return dev_.checks != 0; }
+  void set_checks(bool on) { dev_.checks = on ? 1 : 0; }
+  // Test hooks for the checks: overwrite the device call counter (a stale
+  // counter makes the next barrier epoch not increase); launch a broadcast
+  // kernel with an unvalidated root (refused unless checks are on, so the
+  // kernel's entry check always stands between the root and any access).
+  void debug_set_call_counter(unsigned long long v);
+  void debug_broadcast_raw_root(const void* in, void* out, int dt, unsigned long long n, int root,
+                                cudaStream_t s);
   uint64_t timeout_us() const { return dev_.timeout_ns / 1000ull; }
 
   unsigned int max_blocks = 148;

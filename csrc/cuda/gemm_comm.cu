@@ -84,6 +84,7 @@ struct EpiPeerRS {
   __device__ __forceinline__ int slot() const { return (int)(s_call() & 1ull); }
 
   __device__ bool prologue() const {
+    if (!entry_ok(c, op_id)) return false;  // uniform: every thread checks the same arguments
     if (threadIdx.x == 0) {
       s_call() = call_index(c);
       s_tile_arrivals() = 0u;
@@ -242,6 +243,7 @@ struct GateAG {
   __device__ __forceinline__ int slot() const { return (int)(s_call() & 1ull); }
 
   __device__ bool prologue() const {
+    if (!entry_ok(c, op_id)) return false;  // uniform: every thread checks the same arguments
     if (threadIdx.x == 0) s_call() = call_index(c);
     __syncthreads();
     // Stage the local shard: symmetric slot (peers read it) + gather buffer.

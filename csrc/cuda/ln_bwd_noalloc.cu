@@ -8,9 +8,8 @@
 
 namespace {
 
-// Layout: [0, 256) ticket counter (uint32 at offset 0), then fp32 partials.
+// fp32 partial column sums: [blocks][2][C] (dgamma, dbeta per row block).
 static __device__ __align__(256) unsigned char g_ln_noalloc_scratch[NEXAR_LN_NOALLOC_SCRATCH_BYTES];
-constexpr size_t kCounterBytes = 256;
 
 constexpr int kMaxDevices = 64;
 std::mutex g_setup_mu;
@@ -40,22 +39,18 @@ extern "C" __attribute__((visibility("default"))) int nexar_ln_bwd_noalloc(
     return NEXAR_LN_NOALLOC_BAD_ARGUMENT;
   if (C > NEXAR_LN_NOALLOC_MAX_C) return NEXAR_LN_NOALLOC_TOO_LARGE;
   const int blocks = nexar::ln_bwd_blocks(R);
-  const size_t need = kCounterBytes + nexar::ln_bwd_scratch_floats(C, blocks) * sizeof(float);
+  const size_t need = nexar::ln_bwd_scratch_floats(C, blocks) * sizeof(float);
   if (need > NEXAR_LN_NOALLOC_SCRATCH_BYTES) return NEXAR_LN_NOALLOC_TOO_LARGE;
   int device = -1;
   if (cudaGetDevice(&device) != cudaSuccess) return NEXAR_LN_NOALLOC_SETUP_FAILED;
   unsigned char* base = nullptr;
   const int st = scratch_address(device, &base);
   if (st != NEXAR_LN_NOALLOC_OK) return st;
-  unsigned int* counter = reinterpret_cast<unsigned int*>(base);
-  float* partials = reinterpret_cast<float*>(base + kCounterBytes);
-  // The kernel's ticket counter must start at zero.
-  if (cudaMemsetAsync(counter, 0, sizeof(unsigned int), stream) != cudaSuccess)
-    return NEXAR_LN_NOALLOC_LAUNCH_FAILED;
+  float* partials = reinterpret_cast<float*>(base);
   using bf = __nv_bfloat16;
   const cudaError_t e = nexar::ln_bwd(static_cast<const bf*>(dy), static_cast<const bf*>(x), mean, rstd,
                                       static_cast<const bf*>(w), static_cast<const bf*>(dres),
                                       static_cast<bf*>(dx), static_cast<bf*>(dw), static_cast<bf*>(db),
-                                      partials, counter, R, C, blocks, stream);
+                                      partials, nullptr, R, C, blocks, stream);
   return e == cudaSuccess ? NEXAR_LN_NOALLOC_OK : NEXAR_LN_NOALLOC_LAUNCH_FAILED;
 }

@@ -3,12 +3,13 @@
 // This entry point has no counterpart in the reference (ml-rust/nexar has no
 // LayerNorm and no device kernels at all). It exists for callers that may not
 // allocate device memory at the point where they run the backward pass: code
-// running inside a memory pool owned by another framework or runtime, or a
-// latency-critical path where cudaMalloc (which can synchronize the whole
+// running inside a memory pool owned by another framework or runtime (which
+// owns every byte of the device and does not expect a library to take more),
+// or a latency-critical path where cudaMalloc (which can synchronize the whole
 // device) is not acceptable. Such callers still pass every input and output
-// buffer; the kernel's temporary storage (per-block partial sums of dgamma and
-// dbeta plus a ticket counter) comes from a fixed static device array instead
-// of a caller-provided or freshly allocated scratch buffer.
+// buffer; the kernel's temporary storage (per-block partial column sums of
+// dgamma and dbeta) comes from a fixed static device array instead of a
+// caller-provided or freshly allocated scratch buffer.
 //
 // Limits and behaviour:
 //   * The static array holds NEXAR_LN_NOALLOC_SCRATCH_BYTES (2.5 MiB) on every
@@ -20,9 +21,10 @@
 //     (cudaGetSymbolAddress) with that device current. Make that first call
 //     before any CUDA stream capture begins.
 //   * All calls on a device share the one array and it keeps the last call's
-//     contents. The ticket counter is cleared on the stream before every
-//     launch. Calls that can overlap on the GPU (different streams without
-//     ordering between them) race on the array and must not be issued.
+//     contents. Nothing in it needs clearing: the first launch writes every
+//     partial sum that the second launch reads. Calls that can overlap on the
+//     GPU (different streams without ordering between them) race on the array
+//     and must not be issued.
 #pragma once
 
 #include <cuda_runtime.h>

@@ -115,6 +115,10 @@ __global__ void __launch_bounds__(kMoeThreads) k_moe_dispatch(CommDev c, const _
                                                               unsigned long long recv_off, int capacity,
                                                               unsigned int* ticket) {
   const unsigned long long call = call_index(c);
+  if (!entry_ok(c, kOpMoeDispatch)) {
+    finish_call(c, call);
+    return;
+  }
   const unsigned long long epoch = epoch_of(call, 0);
   __shared__ int base[kMaxRanks];
   const int E = c.world;
@@ -180,6 +184,10 @@ __global__ void __launch_bounds__(kMoeThreads) k_moe_dispatch_rows(CommDev c, co
                                                                    unsigned long long dst_off, int capacity,
                                                                    unsigned int* ticket) {
   const unsigned long long call = call_index(c);
+  if (!entry_ok(c, kOpMoeDispatch)) {
+    finish_call(c, call);
+    return;
+  }
   const unsigned long long epoch = epoch_of(call, 0);
   const int lane = threadIdx.x & 31;
   const int warps = gridDim.x * (kMoeThreads / 32);
@@ -234,6 +242,10 @@ __global__ void __launch_bounds__(kMoeThreads) k_moe_combine(CommDev c, __nv_bfl
                                                              const float* __restrict__ slot_gate,
                                                              unsigned long long eout_off) {
   const unsigned long long call = call_index(c);
+  if (!entry_ok(c, kOpMoeCombine)) {
+    finish_call(c, call);
+    return;
+  }
   const unsigned long long epoch = epoch_of(call, 0);
   // Handshake: every rank's expert outputs are complete before anyone reads.
   int ok = 1;

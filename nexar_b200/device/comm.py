@@ -39,6 +39,10 @@ _OP_NAMES = {1: "all_reduce", 2: "reduce_scatter", 3: "all_gather", 4: "all_to_a
              14: "all_gather_gemm", 15: "compressed_all_reduce"}
 
 
+_CHECK_NAMES = {1: "rank / world out of range", 2: "root or peer >= world", 3: "extent beyond its buffer",
+                4: "barrier epoch not increasing"}
+
+
 def _env_int(name: str, default: int) -> int:
     v = os.environ.get(name)
     return int(v) if v not in (None, "") else default
@@ -207,6 +211,10 @@ class DeviceCommunicator:
             "NEXAR_AR_ONESHOT_MAX", 512 << 10 if world_size <= 4 else 256 << 10)
         self._comm = C.DeviceComm(rank, world_size, device, heap, slot, tmo)
         self._comm.max_blocks = _env_int("NEXAR_MAX_BLOCKS", 148)
+        # Device argument checks in every collective kernel (root / peer <
+        # world, staged and symmetric extents, increasing barrier epochs); a
+        # failed check is reported by check() and the kernel touches nothing.
+        self._comm.checks = os.environ.get("NEXAR_DEVICE_CHECKS", "0") == "1"
         handles = exchange(self._comm.export_handle())
         if world_size > 1:
             self._comm.connect(list(handles))
@@ -369,9 +377,25 @@ class DeviceCommunicator:
     def closed(self) -> bool:
         return self._comm is None
 
+    @property
+    def device_checks(self) -> bool:
+        """Whether the collective kernels verify their arguments on the device."""
+        return bool(self._comm.checks)
+
+    @device_checks.setter
+    def device_checks(self, on: bool):
+        self._comm.checks = bool(on)
+
     def check(self):
-        """Raise CollectiveFailed if any device wait of this communicator timed out."""
+        """Raise CollectiveFailed if any device wait of this communicator timed
+        out or (with device checks on) a kernel refused its arguments."""
         st = self._comm.status()
+        if st["code"] == 3:
+            op = _OP_NAMES.get(st["op"], str(st["op"]))
+            what = _CHECK_NAMES.get(st["block"], str(st["block"]))
+            raise CollectiveFailed(
+                f"{op} refused at rank {self.rank}: device check '{what}' failed "
+                f"(value {st['rank']}, limit {st['epoch']}); the kernel stopped at the check")
         if st["code"] != 0:
             op = _OP_NAMES.get(st["op"], str(st["op"]))
             raise CollectiveFailed(

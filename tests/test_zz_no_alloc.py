@@ -5,9 +5,10 @@ where they run (inside a memory pool owned by another runtime, or on a path
 where cudaMalloc's implicit device synchronisation is unacceptable); its
 scratch is a fixed static device array. This test calls it with ctypes, the
 way such a caller would, and checks it against the regular entry point
-(`_cuda.ln_bwd`, which takes a caller-allocated scratch buffer) on two calls
-in a row, so the second call also shows the shared array is reset correctly.
-This file is collected last on purpose.
+(`_cuda.ln_bwd`, which takes a caller-allocated scratch buffer) and against a
+plain PyTorch fp32 LayerNorm backward, on two calls in a row, so the second
+call also shows that the contents the shared array keeps from the first call
+do not leak into its result. This file is collected last on purpose.
 """
 import ctypes
 
@@ -53,6 +54,14 @@ def test_noalloc_matches_regular_entry_point(cuda0, R, C, with_dres):
     counter = torch.zeros(1, dtype=torch.int32, device=cuda0)
     Cx.ln_bwd(dy, x, mean, rstd, w, dres, dx_ref, dw_ref, db_ref, scratch, counter)
 
+    # plain PyTorch fp32 reference of the same op
+    xf = x.float().requires_grad_(True)
+    wf = w.float().requires_grad_(True)
+    bf32 = b.float().requires_grad_(True)
+    torch.nn.functional.layer_norm(xf, (C,), wf, bf32, 1e-5).backward(dy.float())
+    dx32 = xf.grad + (dres.float() if dres is not None else 0)
+    dw32, db32 = wf.grad, bf32.grad
+
     stream = torch.cuda.current_stream().cuda_stream
     for _ in range(2):
         dx, dw, db = torch.full_like(x, 7.0), torch.full_like(w, 7.0), torch.full_like(w, 7.0)
@@ -63,6 +72,9 @@ def test_noalloc_matches_regular_entry_point(cuda0, R, C, with_dres):
         torch.testing.assert_close(dx.float(), dx_ref.float(), atol=1e-2, rtol=1e-2)
         torch.testing.assert_close(dw.float(), dw_ref.float(), atol=0.25, rtol=3e-2)
         torch.testing.assert_close(db.float(), db_ref.float(), atol=0.25, rtol=3e-2)
+        torch.testing.assert_close(dx.float(), dx32, atol=3e-2, rtol=2e-2)
+        torch.testing.assert_close(dw.float(), dw32, atol=2e-2 * dw32.abs().max().item(), rtol=2e-2)
+        torch.testing.assert_close(db.float(), db32, atol=2e-2 * db32.abs().max().item(), rtol=2e-2)
 
 
 def test_noalloc_rejects_oversized_rows(cuda0):
