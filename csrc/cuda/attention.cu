@@ -11,14 +11,14 @@
 //   warp 0      TMA loads: both Q tiles once, then K and V tiles of 128 keys
 //               into a 3-deep ring (every load reads this GPU's memory; no
 //               multicast);
-//   warp 1      allocates 512 TMEM columns; lane 0 issues S_t = Q_t K_j^T
-//               (M = N = 128, K = 64) for the next key block of tile t as
-//               soon as tile t's softmax holds the current scores, and
-//               O_t += P_t V_j (M = 128, N = 64, K = 128, P read from TMEM)
-//               once P_t is written, polling both tiles' inputs and issuing
-//               whichever MMA is ready (the tensor pipe takes an MMA only as
-//               fast as it runs them, so a fixed issue order would serialise
-//               the tiles); O_A and O_B accumulate in TMEM;
+//   warps 1-2   warp 1 allocates 512 TMEM columns; lane 0 of warp 1 (tile A)
+//               and of warp 2 (tile B) issues S_t = Q_t K_j^T (M = N = 128,
+//               K = 64) for the next key block as soon as the tile's softmax
+//               holds the current scores, and O_t += P_t V_j (M = 128,
+//               N = 64, K = 128, P read from TMEM) once P_t is written. One
+//               issuer per tile: the tensor pipe takes an MMA only as fast as
+//               it runs them, so a single issuer would serialise the tiles;
+//               O_A and O_B accumulate in TMEM;
 //   warps 4-7   softmax of tile A, warps 8-11 of tile B, one query row per
 //               thread (TMEM lane = row), in the exp2 domain. The running
 //               maximum is raised lazily (only when a block's maximum exceeds
@@ -288,7 +288,7 @@ k_attn_fwd(const __grid_constant__ CUtensorMap tm_qkv, __nv_bfloat16* __restrict
   uint64_t* s_free = bar + 12;    // [2] per tile: S read into registers
   uint64_t* p_full = bar + 14;    // [2] per tile: P in shared memory, O rescaled
   uint64_t* o_done = bar + 16;    // [2] per tile: O += P V complete
-  uint64_t* mma_done = bar + 18;
+  uint64_t* mma_done = bar + 18;  // [2] per MMA issuer
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 20);
   __shared__ volatile int s_abort;
 
@@ -313,7 +313,7 @@ k_attn_fwd(const __grid_constant__ CUtensorMap tm_qkv, __nv_bfloat16* __restrict
     for (int s = 0; s < F_STAGES; ++s) {
       mbar_init(k_full + s, 1);
       mbar_init(v_full + s, 1);
-      mbar_init(kv_empty + s, 1);
+      mbar_init(kv_empty + s, ntile);  // one commit per tile's MMA issuer
     }
     for (int t = 0; t < 2; ++t) {
       mbar_init(s_full + t, 1);
@@ -322,6 +322,7 @@ k_attn_fwd(const __grid_constant__ CUtensorMap tm_qkv, __nv_bfloat16* __restrict
       mbar_init(o_done + t, 1);
     }
     mbar_init(mma_done, 1);
+    mbar_init(mma_done + 1, 1);
     s_abort = 0;
     mbar_fence_init();
     tma_prefetch_desc(&tm_qkv);
@@ -361,7 +362,11 @@ k_attn_fwd(const __grid_constant__ CUtensorMap tm_qkv, __nv_bfloat16* __restrict
         mbar_wait_bounded(v_full + j % F_STAGES, (j / F_STAGES) & 1, kWait >> 4);
       }
     }
-  } else if (warp == 1) {
+  } else if (warp == 1 || warp == 2) {
+    // One MMA issuer per tile (warp 1: tile A, warp 2: tile B), each in its
+    // tile's own order with blocking waits: the tensor pipe interleaves the
+    // two tiles' MMAs, so one tile's late softmax never holds back the other.
+    const int t = warp - 1;
     if (lane == 0) {
       // Descriptors are computed once: a K step of 16 elements advances a
       // K-major operand by 32 bytes (start-address field + 2) and an
@@ -370,85 +375,62 @@ k_attn_fwd(const __grid_constant__ CUtensorMap tm_qkv, __nv_bfloat16* __restrict
       constexpr uint32_t idS = umma_idesc_bf16_f32(BQ, BKV);
       constexpr uint32_t idO = umma_idesc_bf16_f32(BQ, HD, false, true);
       constexpr uint64_t kTileStep = TILE >> 4;
-      const uint64_t dq0 = umma_desc_sw128_kmajor(smem_u32(smem + F_QA));
+      const uint64_t dq = umma_desc_sw128_kmajor(smem_u32(smem + F_QA)) + (uint64_t)t * kTileStep;
       const uint64_t dk0 = umma_desc_sw128_kmajor(smem_u32(smem + F_K));
       const uint64_t dv0 = desc_mn(smem_u32(smem + F_V), 8192);
-      auto issue_s = [&](int t, int j) {
-        const uint64_t da = dq0 + (uint64_t)t * kTileStep;
+      const uint32_t d_s = tbase + T_S + t * BKV, d_o = tbase + T_O + t * HD, pa = tbase + T_P + t * 64;
+      const int nk = t < ntile ? nkv[t] : 0;
+      auto issue_s = [&](int j) {
         const uint64_t db = dk0 + (uint64_t)(j % F_STAGES) * kTileStep;
-        const uint32_t d = tbase + T_S + t * BKV;
 #pragma unroll
-        for (int k = 0; k < HD / 16; ++k) umma_f16(d, da + 2 * k, db + 2 * k, idS, k > 0 ? 1u : 0u);
+        for (int k = 0; k < HD / 16; ++k) umma_f16(d_s, dq + 2 * k, db + 2 * k, idS, k > 0 ? 1u : 0u);
         umma_commit(s_full + t);
       };
-      bool ok = mbar_wait_bounded(q_full, 0, kWait) && mbar_wait_bounded(k_full, 0, kWait);
-      if (!ok) fail(err, &s_abort, 22u);
-      if (ok) {
-        tc_fence_after();
-        for (int t = 0; t < ntile; ++t) issue_s(t, 0);
-      }
-      // Event-driven issue: poll every pending MMA's inputs and issue whichever
-      // is ready, so one tile's late softmax never holds back the other's
-      // MMAs. ns[t] / np[t]: next S / PV block of tile t; `rel`: next K / V
-      // block whose stage can be released.
-      int ns[2] = {1, 1}, np[2] = {0, 0};
-      int rel = 0;
-      unsigned long long idle_since = 0;
-      while (ok && !s_abort) {
-        bool done = true, progressed = false;
-        for (int t = 0; t < ntile; ++t) {
-          if (np[t] < nkv[t]) done = false;
-          const int js = ns[t];
-          if (js < nkv[t] && mbar_test(s_free + t, (js - 1) & 1) &&
-              mbar_test(k_full + js % F_STAGES, (js / F_STAGES) & 1)) {
-            tc_fence_after();
-            issue_s(t, js);
-            trace(tron, 1024 + 8 * (js - 1) + 4 * t);
-            ns[t] = js + 1;
-            progressed = true;
-          }
-          const int jp = np[t];
-          if (jp < nkv[t] && mbar_test(p_full + t, jp & 1) &&
-              mbar_test(v_full + jp % F_STAGES, (jp / F_STAGES) & 1)) {
-            tc_fence_after();
-            const uint32_t pa = tbase + T_P + t * 64;  // K step of 16 = 8 columns
-            const uint64_t db = dv0 + (uint64_t)(jp % F_STAGES) * kTileStep;
-            const uint32_t d = tbase + T_O + t * HD;
-#pragma unroll
-            for (int k = 0; k < BKV / 16; ++k)
-              umma_f16_ts(d, pa + 8 * k, db + 128 * k, idO, (jp > 0 || k > 0) ? 1u : 0u);
-            umma_commit(o_done + t);
-            trace(tron, 1024 + 8 * jp + 4 * t + 1);
-            np[t] = jp + 1;
-            progressed = true;
-          }
-        }
-        // K_j and V_j are free once every tile that uses block j has issued
-        // its S and PV MMAs of it.
-        while (rel < nkv_max) {
-          bool used = true;
-          for (int t = 0; t < ntile; ++t)
-            if (rel < nkv[t] && (ns[t] <= rel || np[t] <= rel)) used = false;
-          if (!used) break;
-          umma_commit(kv_empty + rel % F_STAGES);
-          ++rel;
-        }
-        if (done) break;
-        if (progressed) {
-          idle_since = 0;
+      bool ok = true;
+      if (nk > 0) {
+        ok = mbar_wait_bounded(q_full, 0, kWait) && mbar_wait_bounded(k_full, 0, kWait);
+        if (ok) {
+          tc_fence_after();
+          issue_s(0);
         } else {
-          const unsigned long long now = globaltimer_ns();
-          if (idle_since == 0) {
-            idle_since = now;
-          } else if (now - idle_since > kWait) {
-            fail(err, &s_abort, 23u);
-            ok = false;
-          }
+          fail(err, &s_abort, 22u);
         }
+      }
+      for (int j = 0; ok && j < (t < ntile ? nkv_max : 0) && !s_abort; ++j) {
+        if (j < nk) {
+          // The next scores as soon as the softmax holds the current ones.
+          if (j + 1 < nk) {
+            if (!mbar_wait_bounded(s_free + t, j & 1, kWait) ||
+                !mbar_wait_bounded(k_full + (j + 1) % F_STAGES, ((j + 1) / F_STAGES) & 1, kWait)) {
+              fail(err, &s_abort, 23u);
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            issue_s(j + 1);
+            trace(tron, 1024 + 8 * j + 4 * t);
+          }
+          // O_t += P_t V_j (P read from TMEM) once the softmax has written P_t.
+          if (!mbar_wait_bounded(p_full + t, j & 1, kWait) ||
+              !mbar_wait_bounded(v_full + j % F_STAGES, (j / F_STAGES) & 1, kWait)) {
+            fail(err, &s_abort, 24u);
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t db = dv0 + (uint64_t)(j % F_STAGES) * kTileStep;
+#pragma unroll
+          for (int k = 0; k < BKV / 16; ++k)  // K step of 16 = 8 TMEM columns of packed P
+            umma_f16_ts(d_o, pa + 8 * k, db + 128 * k, idO, (j > 0 || k > 0) ? 1u : 0u);
+          umma_commit(o_done + t);
+          trace(tron, 1024 + 8 * j + 4 * t + 1);
+        }
+        // This tile is done with K_j and V_j (the stage frees after both tiles).
+        umma_commit(kv_empty + j % F_STAGES);
       }
       // Every issued MMA has finished before TMEM is released.
-      umma_commit(mma_done);
-      mbar_wait_bounded(mma_done, 0, kWait);
+      umma_commit(mma_done + t);
+      mbar_wait_bounded(mma_done + t, 0, kWait);
     }
   } else if (warp >= 4) {
     const int t = (warp >> 2) - 1;        // tile of this warpgroup

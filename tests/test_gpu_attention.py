@@ -1,19 +1,11 @@
 """tcgen05 self-attention (head dimension 64) against a plain PyTorch fp32
-reference: forward output and the gradient of qkv, causal and full, and one
-GPT-2 training step with it against the same step on torch SDPA.
-
-Opt-in (NEXAR_TEST_ATTENTION=1) until the kernels have been validated on a
-B200: the default GPT-2 path keeps torch SDPA."""
-import os
-
+reference: forward output, the per-row log-sum-exp and the gradient of qkv,
+causal and full, T from 128 to 2048 (odd and even tile counts), and one GPT-2
+training step with it against the same step on torch SDPA."""
 import pytest
 import torch
 
-pytestmark = [
-    pytest.mark.gpu,
-    pytest.mark.skipif(os.environ.get("NEXAR_TEST_ATTENTION") != "1",
-                       reason="tcgen05 attention is opt-in until validated on a B200 (NEXAR_TEST_ATTENTION=1)"),
-]
+pytestmark = pytest.mark.gpu
 
 
 def _reference(qkv, B, T, H, causal):

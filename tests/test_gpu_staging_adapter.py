@@ -2,7 +2,6 @@
 device communicator attached, ``*_device`` calls and raw-pointer collectives
 on CUDA buffers go device -> host -> host collective -> device. Two ranks in
 one process share cuda:0; expected values are PyTorch fp32 sums."""
-import os
 
 import pytest
 import torch
@@ -13,13 +12,6 @@ from nexar_b200.core import DataType, ReduceOp
 
 pytestmark = pytest.mark.gpu
 
-# Paths that have not yet run on a B200: opt-in until their first validation
-# run (NEXAR_TEST_UNVALIDATED=1), so the validated suite runs unchanged.
-UNVALIDATED = pytest.mark.skipif(os.environ.get("NEXAR_TEST_UNVALIDATED") != "1",
-                                 reason="not yet validated on B200s (NEXAR_TEST_UNVALIDATED=1)")
-
-
-@UNVALIDATED
 def test_cuda_adapter_stages_device_buffers(cuda0):
     cs = NexarClient.bootstrap_local(2, adapter="cuda")
     try:

@@ -1,7 +1,6 @@
 """Checkpoint / resume of the data-parallel GPT-2 trainer: a trainer restored
 from another trainer's checkpoint takes the same next step (same loss, same
 fp32 master weights after AdamW) as the original."""
-import os
 
 import pytest
 import torch
@@ -11,12 +10,6 @@ from nexar_b200.parallel.dp import DataParallelTrainer
 
 pytestmark = pytest.mark.gpu
 
-# Paths that have not yet run on a B200: opt-in until their first validation
-# run (NEXAR_TEST_UNVALIDATED=1), so the validated suite runs unchanged.
-UNVALIDATED = pytest.mark.skipif(os.environ.get("NEXAR_TEST_UNVALIDATED") != "1",
-                                 reason="not yet validated on B200s (NEXAR_TEST_UNVALIDATED=1)")
-
-
 def _batch(cfg, seed):
     g = torch.Generator().manual_seed(seed)
     idx = torch.randint(0, cfg.vocab_size, (2, cfg.block_size), generator=g)
@@ -24,7 +17,6 @@ def _batch(cfg, seed):
     return idx, tgt
 
 
-@UNVALIDATED
 def test_resume_matches_uninterrupted_run(cuda0, tmp_path):
     cfg = GPT2Config.tiny()
     a = DataParallelTrainer(cfg, micro_batch=2, seq_len=cfg.block_size, use_cuda_graph=False, seed=0)
