@@ -405,7 +405,7 @@ void gemm_rs(const CommPtr& c, const at::Tensor& A, const at::Tensor& B, const a
   TORCH_CHECK(B.size(1) == K && out.size(0) * c->world() == M && out.size(1) == N, "gemm_reduce_scatter: shape mismatch");
   c10::cuda::CUDAGuard g(c->device());
   check_launch(gemm_reduce_scatter(c->dev(), cbf(A), cbf(B), mbf(out), M, N, K, A.stride(0), B.stride(0), out.stride(0),
-                                   bias ? cbf(*bias) : nullptr, (float)alpha, cur_stream(*c)),
+                                   bias ? cbf(*bias) : nullptr, (float)alpha, c->rs_maps(M, N), cur_stream(*c)),
                "gemm_reduce_scatter");
   count_launch(1);
 }
@@ -426,7 +426,7 @@ void gemm_fp8_rs(const CommPtr& c, const at::Tensor& A, const at::Tensor& sa, co
   check_launch(gemm_fp8_reduce_scatter(c->dev(), reinterpret_cast<const uint8_t*>(A.data_ptr()), sa.data_ptr<float>(),
                                        reinterpret_cast<const uint8_t*>(B.data_ptr()), sb.data_ptr<float>(), mbf(out), M,
                                        N, K, A.stride(0), B.stride(0), out.stride(0), bias ? cbf(*bias) : nullptr,
-                                       (float)alpha, cur_stream(*c)),
+                                       (float)alpha, c->rs_maps(M, N), cur_stream(*c)),
                "gemm_fp8_reduce_scatter");
   count_launch(1);
 }

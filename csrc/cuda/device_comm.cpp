@@ -1,5 +1,6 @@
 #include "device_comm.h"
 #include "coll_api.h"
+#include "gemm_api.h"
 
 #include <cstring>
 #include <unistd.h>
@@ -69,6 +70,30 @@ DeviceComm::DeviceComm(int rank, int world, int device, uint64_t heap_bytes, uin
   if (world_ == 1) connected_ = true;
 }
 
+const CUtensorMap* DeviceComm::rs_maps(int M, int N) {
+  if (rs_maps_dev_ && rs_maps_m_ == M && rs_maps_n_ == N) return rs_maps_dev_;
+  DeviceGuard g(device_);
+  if (!rs_maps_dev_)
+    check_cuda(cudaMalloc(&rs_maps_dev_, 2 * kMaxRanks * sizeof(CUtensorMap)), "cudaMalloc(rs tensor maps)");
+  std::vector<CUtensorMap> maps(2 * kMaxRanks);
+  std::memset(maps.data(), 0, maps.size() * sizeof(CUtensorMap));
+  for (int s = 0; s < 2; ++s)
+    for (int o = 0; o < world_; ++o) {
+      char* base = dev_.peer_base[o];
+      if (!base) throw std::runtime_error("rs_maps: peer heaps not connected");
+      check_cuda(make_tmap_bf16(&maps[s * kMaxRanks + o], base + dev_.stage_off + (uint64_t)s * slot_bytes_, M, N,
+                                N, 32, 64),
+                 "tensor map (reduce-scatter staging)");
+    }
+  // In-flight kernels may still read the previous maps.
+  check_cuda(cudaDeviceSynchronize(), "cudaDeviceSynchronize");
+  check_cuda(cudaMemcpy(rs_maps_dev_, maps.data(), maps.size() * sizeof(CUtensorMap), cudaMemcpyHostToDevice),
+             "cudaMemcpy(rs tensor maps)");
+  rs_maps_m_ = M;
+  rs_maps_n_ = N;
+  return rs_maps_dev_;
+}
+
 void DeviceComm::debug_set_call_counter(unsigned long long v) {
   DeviceGuard g(device_);
   check_cuda(cudaDeviceSynchronize(), "cudaDeviceSynchronize");
@@ -92,6 +117,7 @@ DeviceComm::~DeviceComm() {
   for (char* p : opened_) cudaIpcCloseMemHandle(p);
   if (base_) cudaFree(base_);
   if (ctrl_) cudaFree(ctrl_);
+  if (rs_maps_dev_) cudaFree(rs_maps_dev_);
   if (status_host_) cudaFreeHost(status_host_);
   if (cur >= 0) cudaSetDevice(cur);
 }

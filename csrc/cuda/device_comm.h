@@ -11,6 +11,7 @@
 #include <mutex>
 #include <stdexcept>
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include "comm_types.h"
 
@@ -68,6 +69,12 @@ class DeviceComm {
   // kernel with an unvalidated root (refused unless checks are on, so the
   // kernel's entry check always stands between the root and any access).
   void debug_set_call_counter(unsigned long long v);
+  // Tensor maps over every rank's staging slots as an [M, N] bf16 matrix
+  // (boxes of 32 x 64; [2 slots][kMaxRanks owners], in device memory) for
+  // the GEMM -> reduce-scatter epilogue's TMA stores. Rebuilt when (M, N)
+  // changes; the rebuild synchronises the device, so it must not happen
+  // while a stream is captured (call once per shape before capturing).
+  const CUtensorMap* rs_maps(int M, int N);
   void debug_broadcast_raw_root(const void* in, void* out, int dt, unsigned long long n, int root,
                                 cudaStream_t s);
   uint64_t timeout_us() const { return dev_.timeout_ns / 1000ull; }
@@ -120,6 +127,8 @@ class DeviceComm {
   std::vector<char*> opened_;  // IPC-opened peer bases (to close)
   bool connected_ = false;
   CommDev dev_{};
+  CUtensorMap* rs_maps_dev_ = nullptr;
+  int rs_maps_m_ = -1, rs_maps_n_ = -1;
 };
 
 void check_cuda(cudaError_t e, const char* what);

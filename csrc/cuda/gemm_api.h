@@ -66,9 +66,13 @@ namespace nexar {
 struct CommDev;
 // Row-parallel linear fused with reduce-scatter: out[M/W, N] on rank r =
 // sum over ranks of (A_r . B_r^T)[rows of r] (+ bias). M % (W*128) == 0.
+// `maps`: device array of 2 x kMaxRanks tensor maps over every owner's staging
+// slot ([M, N] bf16, boxes 32 x 64; DeviceComm::rs_maps): the epilogue writes
+// each finished tile into its owner's slot with a TMA store.
 cudaError_t gemm_reduce_scatter(const CommDev& c, const __nv_bfloat16* A, const __nv_bfloat16* B,
                                 __nv_bfloat16* out, int M, int N, int K, long long lda, long long ldb,
-                                long long ldo, const __nv_bfloat16* bias, float alpha, cudaStream_t s);
+                                long long ldo, const __nv_bfloat16* bias, float alpha, const CUtensorMap* maps,
+                                cudaStream_t s);
 // Column-parallel linear fused with all-gather: out[M, N] = act(AG(x) . B^T + bias)
 // with x the local [M/W, K] shard; afull [M, K] is a local gather workspace and
 // cnt a zeroed uint32 array of M/128 + 2 entries (left zeroed on exit).
@@ -77,7 +81,7 @@ cudaError_t gemm_reduce_scatter(const CommDev& c, const __nv_bfloat16* A, const 
 cudaError_t gemm_fp8_reduce_scatter(const CommDev& c, const uint8_t* A, const float* sa, const uint8_t* B,
                                     const float* sb, __nv_bfloat16* out, int M, int N, int K, long long lda,
                                     long long ldb, long long ldo, const __nv_bfloat16* bias, float alpha,
-                                    cudaStream_t s);
+                                    const CUtensorMap* maps, cudaStream_t s);
 cudaError_t all_gather_gemm(const CommDev& c, const __nv_bfloat16* x, long long ldx, const __nv_bfloat16* B,
                             __nv_bfloat16* out, __nv_bfloat16* afull, unsigned int* cnt, int M, int N, int K,
                             long long ldb, long long ldo, const __nv_bfloat16* bias, int act, __nv_bfloat16* pre,

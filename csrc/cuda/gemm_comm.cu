@@ -4,8 +4,9 @@
 //   every rank computes a full partial C_r = A_r . B_r^T; rank o must end
 //   with sum_r C_r[rows of o]. The epilogue writes each finished 128x256 tile
 //   straight into the owner's symmetric staging slot (slot index = source
-//   rank) with coalesced peer stores and publishes a per-tile flag
-//   (st.release.sys). Tiles are produced owner by owner starting at
+//   rank) with TMA stores (a tensor map per owner's slot, in device memory;
+//   a plain store to a peer's memory, no multicast) and publishes a per-tile
+//   flag (st.release.sys) once they have completed. Tiles are produced owner by owner starting at
 //   rank+1, so at any moment the ranks write to different peers and the
 //   NVLink traffic overlaps the MMAs of the following tiles. After its GEMM
 //   tiles every CTA reduces the tiles this rank owns as soon as all sources
@@ -78,6 +79,7 @@ struct EpiPeerRS {
   long long ldo;
   int op_id;
   int arrivals;   // epilogue warps that store each tile (4 bf16 kernel, 8 fp8 kernel)
+  const CUtensorMap* maps;  // [2 slots][kMaxRanks owners] in device memory
   static constexpr int has_pre = 0;
 
   __device__ __forceinline__ unsigned long long epoch() const { return epoch_of(s_call(), 0); }
@@ -108,24 +110,23 @@ struct EpiPeerRS {
 #pragma unroll
     for (int i = 0; i < 64; ++i) v[i] *= alpha;
   }
-  // Copy the staged 32x64 block into the owner's slot for this source rank.
+  // TMA-store the staged 32x64 block into the owner's slot, at this source
+  // rank's rows (the store clips columns past N).
   __device__ void store_block(const CUtensorMap*, const uint8_t* buf, int row0, int col0, int lane) const {
     const int owner = row0 / rpr;
-    const long long lrow0 = (long long)c.rank * rpr + (row0 - owner * rpr);
-    char* base = c.peer_base[owner] + c.stage_off + (unsigned long long)slot() * c.slot_bytes;
-    __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(base) + lrow0 * N + col0;
-    const int ch = lane & 7;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const int r = i * 4 + (lane >> 3);
-      const uint4 v = *reinterpret_cast<const uint4*>(buf + r * 128 + ((ch ^ (r & 7)) << 4));
-      if (col0 + ch * 8 < N) *reinterpret_cast<uint4*>(dst + (long long)r * N + ch * 8) = v;
-    }
+    const int lrow0 = c.rank * rpr + (row0 - owner * rpr);
+    if (lane == 0) sm100::tma_store_2d(maps + slot() * kMaxRanks + owner, buf, col0, lrow0);
   }
   // Publish the tile once all epilogue warps have stored their rows. A
   // shared counter (not a named barrier) joins the warps so that a warp that
   // gave up on an earlier wait can never leave the others blocked forever.
   __device__ void end_tile(int tm, int tn, int lane) const {
+    if (lane == 0) {
+      // This warp's stores of the tile have completed; order them (async
+      // proxy) before the generic release chain that publishes the flag.
+      sm100::tma_store_wait_all<0>();
+      fence_proxy_async_global();
+    }
     __syncwarp();
     if (lane == 0) {
       // CTA-scope release is enough here: the flag writer below issues the
@@ -362,8 +363,10 @@ struct GateAG {
 // ------------------------------------------------------------ launchers
 cudaError_t gemm_reduce_scatter(const CommDev& c, const __nv_bfloat16* A, const __nv_bfloat16* B,
                                 __nv_bfloat16* out, int M, int N, int K, long long lda, long long ldb,
-                                long long ldo, const __nv_bfloat16* bias, float alpha, cudaStream_t s) {
+                                long long ldo, const __nv_bfloat16* bias, float alpha, const CUtensorMap* maps,
+                                cudaStream_t s) {
   using namespace gemm;
+  if (!maps) return cudaErrorInvalidValue;
   const int W = c.world;
   if (M % (W * BM) != 0 || N % 8 != 0) return cudaErrorInvalidValue;
   const int rpr = M / W;
@@ -373,7 +376,7 @@ cudaError_t gemm_reduce_scatter(const CommDev& c, const __nv_bfloat16* A, const 
   CUtensorMap dummy;
   cudaError_t e = make_tmap_bf16(&dummy, A, M, K, lda, 32, 64);
   if (e != cudaSuccess) return e;
-  EpiPeerRS epi{c, rpr, N, tiles_n, alpha, bias, out, ldo, kOpGemmRs, EPI_WARPS};
+  EpiPeerRS epi{c, rpr, N, tiles_n, alpha, bias, out, ldo, kOpGemmRs, EPI_WARPS, maps};
   const int m_rotate = ((c.rank + 1) % W) * (rpr / BM);
   return launch_gemm_generic<EpiPeerRS, NoGate, 0>(A, B, M, N, K, lda, ldb, dummy, dummy, m_rotate, epi, NoGate{},
                                                    gemm_sm_count(), s);
@@ -385,8 +388,9 @@ cudaError_t gemm_reduce_scatter(const CommDev& c, const __nv_bfloat16* A, const 
 cudaError_t gemm_fp8_reduce_scatter(const CommDev& c, const uint8_t* A, const float* sa, const uint8_t* B,
                                     const float* sb, __nv_bfloat16* out, int M, int N, int K, long long lda,
                                     long long ldb, long long ldo, const __nv_bfloat16* bias, float alpha,
-                                    cudaStream_t s) {
+                                    const CUtensorMap* maps, cudaStream_t s) {
   using namespace gemm;
+  if (!maps) return cudaErrorInvalidValue;
   static_assert(gemm8::BM == BM && gemm8::BN == BN, "tile geometry shared with EpiPeerRS");
   const int W = c.world;
   if (M % (W * BM) != 0 || N % 8 != 0 || K % 16 != 0) return cudaErrorInvalidValue;
@@ -400,7 +404,7 @@ cudaError_t gemm_fp8_reduce_scatter(const CommDev& c, const uint8_t* A, const fl
   e = make_tmap_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, B, N, K, ldb, gemm8::BN, gemm8::BK);
   if (e != cudaSuccess) return e;
   dummy = ta;
-  EpiPeerRS epi{c, rpr, N, tiles_n, alpha, bias, out, ldo, kOpGemmRs, gemm8::PROMO_WARPS};
+  EpiPeerRS epi{c, rpr, N, tiles_n, alpha, bias, out, ldo, kOpGemmRs, gemm8::PROMO_WARPS, maps};
   const int m_rotate = ((c.rank + 1) % W) * (rpr / BM);
   static bool attr_set = false;
   if (!attr_set) {
