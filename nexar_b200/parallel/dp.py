@@ -82,7 +82,9 @@ class DataParallelTrainer:
             timeline = os.environ.get("NEXAR_DP_TIMELINE", "0") == "1"
         self._tl = None
         if timeline and self.world > 1:
-            ev = lambda: torch.cuda.Event(enable_timing=True)  # noqa: E731
+            # external: recorded as event nodes when the step is captured in a
+            # CUDA graph, so the replayed step still timestamps them.
+            ev = lambda: torch.cuda.Event(enable_timing=True, external=True)  # noqa: E731
             self._tl = {"step0": ev(), "bwd_end": ev(), "step_end": ev(),
                         "ready": [ev() for _ in self.buckets], "start": [ev() for _ in self.buckets],
                         "end": [ev() for _ in self.buckets], "order": []}

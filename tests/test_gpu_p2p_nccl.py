@@ -4,7 +4,6 @@ one-rank communicator: results equal the inputs, self send / recv is a copy),
 and ring send / recv plus all-reduce over two GPUs when the box has them.
 The expected values are plain PyTorch fp32 computations."""
 import os
-import threading
 
 import pytest
 import torch
@@ -79,39 +78,104 @@ def test_nccl_group_one_gpu(cuda0):
         g.all_reduce(x)
 
 
+# Two-GPU cases: one process per GPU (the deployment model), each joining the
+# host mesh through a seed in this process. Two ranks as threads of one
+# process are avoided: NCCL communicators of one clique inside one process
+# share intra-process state, and tearing them down from two threads at once
+# crashed the process on a B200 box.
+def _spawn_ranks(target, world=2, timeout=180):
+    import multiprocessing as mp
+
+    from nexar_b200 import _host as H
+    seed = H.SeedNode.bind("127.0.0.1:0", b"nccl-test")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    ps = [ctx.Process(target=_rank_main, args=(target, seed.local_addr(), q)) for _ in range(world)]
+    try:
+        for p_ in ps:
+            p_.start()
+        seed.with_formation_timeout(60.0).form_cluster(world)
+        res = {}
+        for _ in range(world):
+            rank, out, err = q.get(timeout=timeout)
+            if err:
+                raise AssertionError(f"rank {rank}: {err}")
+            res[rank] = out
+    finally:
+        for p_ in ps:
+            p_.join(30)
+            if p_.is_alive():
+                p_.kill()
+        seed.close()
+    return [res[r] for r in range(world)]
+
+
+def _rank_main(target, seed_addr, q):
+    import traceback
+
+    from nexar_b200.client import NexarClient
+    c = NexarClient.bootstrap(seed_addr, b"nccl-test")
+    try:
+        if torch.cuda.is_available():
+            torch.cuda.set_device(c.rank)
+        q.put((c.rank, target(c), None))
+    except BaseException:  # noqa: BLE001
+        q.put((c.rank, None, traceback.format_exc()[-2000:]))
+    finally:
+        c.close()
+
+
+def _ring_rank(c):
+    g = nccl.nccl_group_for_client(c, device=c.rank)
+    dev = torch.device("cuda", c.rank)
+    n = 1 << 16
+    xs = [torch.randn(n, generator=torch.Generator().manual_seed(10 + r)) for r in range(2)]
+    x = xs[c.rank].to(dev)
+    got = torch.empty_like(x)
+    peer = 1 - c.rank
+    g.send_recv(x, peer, got, peer)
+    s = x.clone()
+    g.all_reduce(s)
+    torch.cuda.synchronize(dev)
+    g.destroy()
+    return got.cpu(), s.cpu(), xs[peer], xs[0] + xs[1]
+
+
 @UNVALIDATED
 def test_nccl_group_two_gpus_ring():
     if gpu_count() < 2:
         pytest.skip("needs two GPUs")
-    from helpers_host import bootstrap, run_collective
-    clients = bootstrap(2)
-    n = 1 << 16
+    for got, s, want_got, want_s in _spawn_ranks(_ring_rank):
+        torch.testing.assert_close(got, want_got, rtol=0, atol=0)
+        torch.testing.assert_close(s, want_s, rtol=1e-6, atol=1e-6)
 
-    def go(c):
-        torch.cuda.set_device(c.rank)
-        g = nccl.nccl_group_for_client(c, device=c.rank)
-        dev = torch.device("cuda", c.rank)
-        gen = torch.Generator(device=dev).manual_seed(10 + c.rank)
-        x = torch.randn(n, device=dev, generator=gen)
-        got = torch.empty_like(x)
-        peer = 1 - c.rank
-        g.send_recv(x, peer, got, peer)
-        s = x.clone()
-        g.all_reduce(s)
-        torch.cuda.synchronize(dev)
-        g.destroy()
-        return x.cpu(), got.cpu(), s.cpu()
 
-    try:
-        res = run_collective(clients, go, timeout=120)
-    finally:
-        for c in clients:
-            c.close()
-    (x0, got0, s0), (x1, got1, s1) = res
-    torch.testing.assert_close(got0, x1, rtol=0, atol=0)
-    torch.testing.assert_close(got1, x0, rtol=0, atol=0)
-    torch.testing.assert_close(s0, x0 + x1, rtol=1e-6, atol=1e-6)
-    torch.testing.assert_close(s1, s0, rtol=0, atol=0)
+_D, _ROWS, _M = 64, 16, 5
+
+
+def _pipeline_setup():
+    torch.manual_seed(0)
+    stages = [torch.nn.Sequential(torch.nn.Linear(_D, _D), torch.nn.Tanh()) for _ in range(2)]
+    g = torch.Generator().manual_seed(1)
+    mbs = [torch.randn(_ROWS, _D, generator=g) for _ in range(_M)]
+    tgts = [torch.randn(_ROWS, _D, generator=g) for _ in range(_M)]
+    return stages, mbs, tgts
+
+
+def _pipeline_rank(c):
+    from nexar_b200.parallel.pipeline import NcclP2P, run_1f1b
+    stages, mbs, tgts = _pipeline_setup()
+    dev = torch.device("cuda", c.rank)
+    grp = nccl.nccl_group_for_client(c, device=c.rank)
+    mod = stages[c.rank].to(dev)
+    inputs = [x.to(dev) for x in mbs] if c.rank == 0 else [None] * _M
+    tg = [t.to(dev) for t in tgts]
+    losses = run_1f1b(mod, NcclP2P(grp), inputs, (_ROWS, _D), torch.float32,
+                      loss_fn=lambda y, i: ((y - tg[i]) ** 2).mean())
+    torch.cuda.synchronize(dev)
+    grads = [p.grad.cpu() for p in mod.parameters()]
+    grp.destroy()
+    return losses, grads
 
 
 @UNVALIDATED
@@ -120,45 +184,14 @@ def test_pipeline_1f1b_two_gpus():
     against the whole model on the CPU (fp32)."""
     if gpu_count() < 2:
         pytest.skip("needs two GPUs")
-    import copy
-
-    from helpers_host import bootstrap, run_collective
-    from nexar_b200.parallel.pipeline import NcclP2P, run_1f1b
-    d, rows, M = 64, 16, 5
-    torch.manual_seed(0)
-    stages = [torch.nn.Sequential(torch.nn.Linear(d, d), torch.nn.Tanh()) for _ in range(2)]
-    ref = copy.deepcopy(stages)
-    g = torch.Generator().manual_seed(1)
-    mbs = [torch.randn(rows, d, generator=g) for _ in range(M)]
-    tgts = [torch.randn(rows, d, generator=g) for _ in range(M)]
+    ref, mbs, tgts = _pipeline_setup()
     whole = torch.nn.Sequential(*ref)
     ref_losses = []
     for x, t in zip(mbs, tgts):
         loss = ((whole(x) - t) ** 2).mean()
         loss.backward()
         ref_losses.append(float(loss.detach()))
-
-    clients = bootstrap(2)
-
-    def go(c):
-        torch.cuda.set_device(c.rank)
-        dev = torch.device("cuda", c.rank)
-        grp = nccl.nccl_group_for_client(c, device=c.rank)
-        mod = stages[c.rank].to(dev)
-        inputs = [x.to(dev) for x in mbs] if c.rank == 0 else [None] * M
-        tg = [t.to(dev) for t in tgts]
-        losses = run_1f1b(mod, NcclP2P(grp), inputs, (rows, d), torch.float32,
-                          loss_fn=lambda y, i: ((y - tg[i]) ** 2).mean())
-        torch.cuda.synchronize(dev)
-        grads = [p.grad.cpu() for p in mod.parameters()]
-        grp.destroy()
-        return losses, grads
-
-    try:
-        out = run_collective(clients, go, timeout=120)
-    finally:
-        for c in clients:
-            c.close()
+    out = _spawn_ranks(_pipeline_rank)
     assert out[1][0] == pytest.approx(ref_losses, rel=1e-4, abs=1e-5)
     for s in range(2):
         for got, p in zip(out[s][1], ref[s].parameters()):
