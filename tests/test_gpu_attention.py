@@ -1,6 +1,8 @@
 """tcgen05 self-attention (head dimension 64) against a plain PyTorch fp32
 reference: forward output, the per-row log-sum-exp and the gradient of qkv,
-causal and full, T from 128 to 2048 (odd and even tile counts), and one GPT-2
+causal and full, T from 128 to 2048 (odd and even tile counts; more
+(key block, head) items than SMs, so that every persistent backward CTA
+walks several items of different lengths), and one GPT-2
 training step with it against the same step on torch SDPA."""
 import pytest
 import torch
@@ -19,7 +21,8 @@ def _reference(qkv, B, T, H, causal):
 
 
 @pytest.mark.parametrize("causal", [True, False])
-@pytest.mark.parametrize("B,T,H", [(1, 128, 1), (2, 256, 2), (1, 384, 3), (2, 1024, 4), (1, 2048, 2)])
+@pytest.mark.parametrize("B,T,H", [(1, 128, 1), (2, 256, 2), (1, 384, 3), (2, 1024, 4), (1, 2048, 2),
+                                   (3, 1024, 20)])
 def test_attention_matches_fp32_reference(cuda0, B, T, H, causal):
     from nexar_b200 import _native, ops
     g = torch.Generator(device="cuda").manual_seed(3)

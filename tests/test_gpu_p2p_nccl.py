@@ -22,7 +22,6 @@ UNVALIDATED = pytest.mark.skipif(os.environ.get("NEXAR_TEST_UNVALIDATED") != "1"
                                  reason="not yet validated on B200s (NEXAR_TEST_UNVALIDATED=1)")
 
 
-@UNVALIDATED
 def test_nccl_group_one_gpu(cuda0):
     g = nccl.NcclGroup(0, 1, nccl.unique_id(), device=0)
     assert (g.local_rank, g.local_world, g.device) == (0, 1, 0) and not g.closed
