@@ -60,12 +60,12 @@ def tables(records) -> str:
 
 
 def main(argv=None) -> int:
-    paths = (argv if argv is not None else sys.argv[1:])
-    if not paths:
-        print(__doc__)
-        return 2
+    import argparse
+    ap = argparse.ArgumentParser(description="markdown tables from collective sweep JSONL records")
+    ap.add_argument("jsonl", nargs="+", help="files written by nexar_b200.bench.collectives --out")
+    args = ap.parse_args(argv)
     recs = []
-    for p in paths:
+    for p in args.jsonl:
         with open(p) as f:
             recs.extend(json.loads(line) for line in f if line.strip())
     print(tables(recs))
