@@ -59,6 +59,9 @@ def main(argv=None):
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=dev)
+    # Every arm runs on (and is timed on) one non-default stream: the raw
+    # NcclGroup calls go to the stream it was given, which must have a handle.
+    torch.cuda.set_stream(torch.cuda.Stream(dev))
     from nexar_b200.device import DeviceCommunicator
     comm = DeviceCommunicator.from_torch()
     dtype = {"bf16": torch.bfloat16, "f32": torch.float32, "f16": torch.float16}[args.dtype]

@@ -207,8 +207,11 @@ class DeviceCommunicator:
         user = _env_int("NEXAR_SYMM_USER_BYTES", 1 << 30)
         heap = heap_bytes or (1 << 20) + 2 * slot + user  # 1 MiB signal area first
         tmo = timeout_us if timeout_us is not None else _env_int("NEXAR_DEVICE_WAIT_TIMEOUT_US", 10_000_000)
+        # One-shot (one barrier, every rank reads every peer's whole buffer)
+        # beats two-shot up to larger sizes at 2 ranks, where both move the
+        # same bytes per rank (2-GPU sweep: two-shot 30 us at 1-2 MB).
         self.oneshot_max_bytes = _env_int(
-            "NEXAR_AR_ONESHOT_MAX", 512 << 10 if world_size <= 4 else 256 << 10)
+            "NEXAR_AR_ONESHOT_MAX", (2 << 20) if world_size == 2 else (512 << 10 if world_size <= 4 else 256 << 10))
         self._comm = C.DeviceComm(rank, world_size, device, heap, slot, tmo)
         self._comm.max_blocks = _env_int("NEXAR_MAX_BLOCKS", 148)
         # Device argument checks in every collective kernel (root / peer <

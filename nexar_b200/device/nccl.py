@@ -151,14 +151,30 @@ def id_from_bytes(data: bytes) -> bytes:
 class NcclHandle:
     """Completion of a non-blocking NCCL operation. ``wait()`` orders the
     caller's current stream after it (no host block); ``synchronize()`` blocks
-    the host; ``is_finished()`` polls."""
+    the host; ``is_finished()`` polls.
 
-    def __init__(self, group: "NcclGroup", event: torch.cuda.Event, keep: tuple):
-        self._group, self._event, self._keep = group, event, keep
+    The handle holds the operation's tensors. The caching allocator may hand
+    their memory out again on the caller's stream once they are freed, so the
+    caller's stream is ordered after the operation (an event wait) before the
+    handle lets them go, also when it is dropped without ``wait()``. No
+    ``record_stream`` ties them to the group's own stream, which a torn-down
+    group destroys."""
+
+    def __init__(self, group: "NcclGroup", event: torch.cuda.Event, keep: tuple, stream: torch.cuda.Stream):
+        self._group, self._event, self._keep, self._stream = group, event, keep, stream
+        self._ordered = False
 
     def wait(self):
-        torch.cuda.current_stream(self._group.device).wait_event(self._event)
+        self._stream.wait_event(self._event)
+        self._ordered = True
         return self._keep[-1] if self._keep else None
+
+    def __del__(self):
+        try:
+            if not self._ordered and self._keep:
+                self._stream.wait_event(self._event)
+        except Exception:  # noqa: BLE001  (interpreter teardown)
+            pass
 
     def synchronize(self):
         """Block the host until the operation has finished; raises if the communicator reports an error."""
@@ -186,8 +202,9 @@ class NcclGroup:
 
     Every rank constructs it with the same ``uid`` (from :func:`unique_id` on
     one rank, shared out of band) and its own ``local_rank``; construction
-    blocks until all ranks have joined. ``stream`` (a ``torch.cuda.Stream``)
-    is used as is; by default the group makes a private non-blocking stream.
+    blocks until all ranks have joined. ``stream`` (a ``torch.cuda.Stream``
+    other than the legacy default stream) is used as is; by default the group
+    makes a private non-blocking stream.
     """
 
     def __init__(self, local_rank: int, local_world: int, uid: bytes, device: Optional[int] = None,
@@ -195,6 +212,9 @@ class NcclGroup:
         lib = _lib()
         dev = torch.cuda.current_device() if device is None else int(device)
         handle = 0 if stream is None else int(stream.cuda_stream)
+        if stream is not None and handle == 0:
+            # the legacy default stream has handle 0, which the native group reads as "make a private stream"
+            raise NcclCommError("NcclGroup needs a non-default stream (the legacy default stream has no handle)")
         try:
             self._g = lib.NcclGroup(int(local_rank), int(local_world), id_to_bytes(uid), dev, handle)
         except RuntimeError as e:
@@ -320,11 +340,9 @@ class NcclGroup:
         cur = torch.cuda.current_stream(self.device)
         self._stream.wait_stream(cur)
         fn()
-        for t in tensors:
-            t.record_stream(self._stream)
         ev = torch.cuda.Event()
         ev.record(self._stream)
-        h = NcclHandle(self, ev, tuple(tensors) + (result,))
+        h = NcclHandle(self, ev, tuple(tensors) + (result,), cur)
         if blocking:
             h.wait()
             return result

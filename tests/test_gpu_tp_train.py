@@ -1,6 +1,5 @@
 """TP Llama-MLP training step (forward + backward on the fused kernels)
 against the NCCL + cuBLAS formulation of the same step, on >= 2 GPUs."""
-import os
 import socket
 
 import pytest
@@ -10,13 +9,6 @@ import torch.multiprocessing as mp
 from conftest import gpu_count
 
 pytestmark = [pytest.mark.gpu, pytest.mark.multigpu]
-
-# Multi-GPU paths that have not yet run on B200s: opt-in until their first
-# validation run (NEXAR_TEST_UNVALIDATED=1), so that a box with several GPUs
-# runs the validated suite unchanged.
-UNVALIDATED = pytest.mark.skipif(os.environ.get("NEXAR_TEST_UNVALIDATED") != "1",
-                                 reason="not yet validated on B200s (NEXAR_TEST_UNVALIDATED=1)")
-
 
 
 def _free_port():
@@ -59,7 +51,6 @@ def _worker(rank, world, port, results):
     dist.destroy_process_group()
 
 
-@UNVALIDATED
 def test_tp_train_step_matches_nccl_cublas():
     if gpu_count() < 2:
         pytest.skip("needs two GPUs")
