@@ -61,8 +61,6 @@
 // GPT-2 training path.
 #include "attention_api.h"
 
-#include <cstdlib>
-
 #include "common.cuh"
 #include "gemm_api.h"
 #include "sm100.cuh"
@@ -310,8 +308,6 @@ constexpr uint32_t F_TMEM_COLS = 256;
 // fp32, ample range in bf16) and the output accumulator needs no rescaling.
 constexpr float kRescaleLog2 = 8.f;
 
-// NPOLY: pairs of exponentials per 8 on the FMA pipe (1: 6 MUFU + 2 FMA, 2: 4 + 4).
-template <int NPOLY>
 __global__ void __launch_bounds__(F_THREADS, 2)
 k_attn_fwd(const __grid_constant__ CUtensorMap tm_qkv, __nv_bfloat16* __restrict__ y, float* __restrict__ lse, int B,
            int T, int H, int causal, float scale_log2, unsigned int* err) {
@@ -512,8 +508,9 @@ k_attn_fwd(const __grid_constant__ CUtensorMap tm_qkv, __nv_bfloat16* __restrict
       }
       if (tr) trace(true, 8 * j + 3);
       // Probabilities into the row's P columns of TMEM, 32 columns (64
-      // values) at a time: 8 - 2 NPOLY of every 8 exponentials on the MUFU
-      // unit, 2 NPOLY on the FMA pipe (exp2_poly2).
+      // values) at a time: 6 of every 8 exponentials on the MUFU unit, 2 on
+      // the FMA pipe (exp2_poly2); 4 + 4 measured slower (44.4 against
+      // 41.5 us per GPT-2 layer).
       const float neg = -m_new;
       float sum0 = 0.f, sum1 = 0.f;
       uint32_t pk[32];
@@ -525,9 +522,8 @@ k_attn_fwd(const __grid_constant__ CUtensorMap tm_qkv, __nv_bfloat16* __restrict
           ffma2(p[e], p[e + 1], __uint_as_float(x[ch * 8 + e]), __uint_as_float(x[ch * 8 + e + 1]), scale_log2,
                 scale_log2, neg, neg);
 #pragma unroll
-        for (int e = 0; e < 8 - 2 * NPOLY; ++e) p[e] = ex2(p[e]);
-#pragma unroll
-        for (int e = 8 - 2 * NPOLY; e < 8; e += 2) exp2_poly2(p[e], p[e + 1], p[e], p[e + 1]);
+        for (int e = 0; e < 6; ++e) p[e] = ex2(p[e]);
+        exp2_poly2(p[6], p[7], p[6], p[7]);
         sum0 += (p[0] + p[2]) + (p[4] + p[6]);
         sum1 += (p[1] + p[3]) + (p[5] + p[7]);
         const int q = (ch & 7) * 4;
@@ -1118,24 +1114,15 @@ cudaError_t attention_fwd(const __nv_bfloat16* qkv, __nv_bfloat16* y, float* lse
   CUtensorMap tm;
   cudaError_t e = make_tmap_bf16(&tm, qkv, (long long)B * T, 3LL * C, 3LL * C, BQ, HD);
   if (e != cudaSuccess) return e;
-  // NEXAR_ATTN_FWD_POLY=2 puts half the exponentials on the FMA pipe (default 1: a quarter).
-  static const int npoly = [] {
-    const char* v = getenv("NEXAR_ATTN_FWD_POLY");
-    return (v && v[0] == '2') ? 2 : 1;
-  }();
   static bool attr_set = false;
   if (!attr_set) {
-    e = cudaFuncSetAttribute(k_attn_fwd<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, F_SMEM);
-    if (e == cudaSuccess) e = cudaFuncSetAttribute(k_attn_fwd<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, F_SMEM);
+    e = cudaFuncSetAttribute(k_attn_fwd, cudaFuncAttributeMaxDynamicSharedMemorySize, F_SMEM);
     if (e != cudaSuccess) return e;
     attr_set = true;
   }
   const float scale_log2 = kLog2e / sqrtf((float)HD);
   const unsigned grid = (unsigned)((T / BQ) * B * H);
-  if (npoly == 2)
-    k_attn_fwd<2><<<grid, F_THREADS, F_SMEM, s>>>(tm, y, lse, B, T, H, causal ? 1 : 0, scale_log2, gemm_err_word());
-  else
-    k_attn_fwd<1><<<grid, F_THREADS, F_SMEM, s>>>(tm, y, lse, B, T, H, causal ? 1 : 0, scale_log2, gemm_err_word());
+  k_attn_fwd<<<grid, F_THREADS, F_SMEM, s>>>(tm, y, lse, B, T, H, causal ? 1 : 0, scale_log2, gemm_err_word());
   return cudaGetLastError();
 }
 
