@@ -48,11 +48,11 @@ def _worker(rank, world, port, results, graph):
             tgt = torch.randint(0, cfg.vocab_size, (2, 256), generator=g)
             tr.step(idx, tgt)
             torch.cuda.synchronize()
-            p = tr.model.flat.param_bf16.view(torch.int16).cpu()
+            p = tr.model.flat.param_bf16.view(torch.int32).cpu()  # bit patterns (gloo has no 16-bit ints)
             gathered = [torch.empty_like(p) for _ in range(world)]
             dist.all_gather(gathered, p)
             if not torch.equal(gathered[0], gathered[1]):
-                diff = (gathered[0] != gathered[1]).nonzero().flatten()
+                diff = (gathered[0] != gathered[1]).nonzero().flatten() * 2  # bf16 index of each differing pair
                 names = sorted({e.name for e in tr.model.flat.entries
                                 for i in diff[:64].tolist() if e.offset <= i < e.offset + e.numel})
                 errs.append(f"step {step}: {diff.numel()} parameters differ across ranks, e.g. in {names[:8]}")

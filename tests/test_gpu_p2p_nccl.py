@@ -99,7 +99,7 @@ def _spawn_ranks(target, world=2, timeout=180):
             rank, out, err = q.get(timeout=timeout)
             if err:
                 raise AssertionError(f"rank {rank}: {err}")
-            res[rank] = out
+            res[rank] = _tensors(out)
     finally:
         for p_ in ps:
             p_.join(30)
@@ -107,6 +107,25 @@ def _spawn_ranks(target, world=2, timeout=180):
                 p_.kill()
         seed.close()
     return [res[r] for r in range(world)]
+
+
+def _plain(obj):
+    """Tensors as numpy arrays (pickled by value: a shared-memory tensor would
+    need this process alive when the parent unpickles it)."""
+    if isinstance(obj, torch.Tensor):
+        return obj.detach().cpu().numpy()
+    if isinstance(obj, (list, tuple)):
+        return type(obj)(_plain(o) for o in obj)
+    return obj
+
+
+def _tensors(obj):
+    import numpy as np
+    if isinstance(obj, np.ndarray):
+        return torch.from_numpy(obj)
+    if isinstance(obj, (list, tuple)):
+        return type(obj)(_tensors(o) for o in obj)
+    return obj
 
 
 def _rank_main(target, seed_addr, q):
@@ -117,7 +136,7 @@ def _rank_main(target, seed_addr, q):
     try:
         if torch.cuda.is_available():
             torch.cuda.set_device(c.rank)
-        q.put((c.rank, target(c), None))
+        q.put((c.rank, _plain(target(c)), None))
     except BaseException:  # noqa: BLE001
         q.put((c.rank, None, traceback.format_exc()[-2000:]))
     finally:
