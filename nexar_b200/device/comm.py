@@ -247,6 +247,8 @@ class DeviceCommunicator:
         self._nccl = None
         self._timer = DeviceTimeHistogram() if _TIMING else None
         self._last_stream = None
+        self._last_raw = None
+        self._dev_index = torch.device(self.device).index if torch.device(self.device).index is not None else 0
 
     # ----------------------------------------------------------- construction
     @classmethod
@@ -335,6 +337,11 @@ class DeviceCommunicator:
         call-time tags keep concurrent non-blocking collectives apart
         (nexar/src/client/collectives_nb.rs:33-47). The fused kernels and the
         MoE dispatch / combine call this too."""
+        # The raw handle is a cheap check on every call; Stream objects are
+        # made only when the stream changed.
+        raw = torch._C._cuda_getCurrentRawStream(self._dev_index)
+        if raw == self._last_raw:
+            return
         cur = torch.cuda.current_stream(self.device)
         last = self._last_stream
         if last is not None and last != cur:
@@ -346,6 +353,7 @@ class DeviceCommunicator:
             if cap_now == cap_last:
                 cur.wait_stream(last)
         self._last_stream = cur
+        self._last_raw = raw
 
     @contextlib.contextmanager
     def block_limit(self, max_blocks: int):
