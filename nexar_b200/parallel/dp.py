@@ -120,6 +120,13 @@ class DataParallelTrainer:
 
     def _make_acc_hook(self, name):
         def hook(_param):
+            # PyTorch runs this after the parameter's AccumulateGrad node even
+            # when every backward op returned None for it (the kernels wrote
+            # the sink and reported ready themselves): count it only when
+            # autograd really accumulated a gradient, or the bucket would be
+            # reduced before its other parameters' gradients exist.
+            if name in self._seen:
+                return
             # autograd accumulated into the flat view: only valid over a zeroed buffer
             self._zero_grads = True
             self._make_hook(name)()

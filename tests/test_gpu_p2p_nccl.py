@@ -3,7 +3,6 @@
 one-rank communicator: results equal the inputs, self send / recv is a copy),
 and ring send / recv plus all-reduce over two GPUs when the box has them.
 The expected values are plain PyTorch fp32 computations."""
-import os
 
 import pytest
 import torch
@@ -14,12 +13,6 @@ from nexar_b200.device import DeviceCommunicator
 from nexar_b200.device import nccl
 
 pytestmark = pytest.mark.gpu
-
-# Multi-GPU paths that have not yet run on B200s: opt-in until their first
-# validation run (NEXAR_TEST_UNVALIDATED=1), so that a box with several GPUs
-# runs the validated suite unchanged.
-UNVALIDATED = pytest.mark.skipif(os.environ.get("NEXAR_TEST_UNVALIDATED") != "1",
-                                 reason="not yet validated on B200s (NEXAR_TEST_UNVALIDATED=1)")
 
 
 def test_nccl_group_one_gpu(cuda0):
@@ -159,7 +152,6 @@ def _ring_rank(c):
     return got.cpu(), s.cpu(), xs[peer], xs[0] + xs[1]
 
 
-@UNVALIDATED
 def test_nccl_group_two_gpus_ring():
     if gpu_count() < 2:
         pytest.skip("needs two GPUs")
@@ -196,7 +188,6 @@ def _pipeline_rank(c):
     return losses, grads
 
 
-@UNVALIDATED
 def test_pipeline_1f1b_two_gpus():
     """Two pipeline stages on two GPUs, activations and gradients over NCCL p2p,
     against the whole model on the CPU (fp32)."""
