@@ -2,12 +2,15 @@
 
 One process per GPU. Gradients live in one flat bf16 buffer inside the
 symmetric heap, split into ~25 MB buckets (contiguous ranges). A
-post-accumulate hook counts finished parameters per bucket; when a bucket is
+parameter's ready callback (called by the backward kernel that wrote its
+gradient, or autograd's post-accumulate hook when autograd did) counts
+finished parameters per bucket, each once per step; when a bucket is
 complete its all-reduce (two-shot over NVLink, averaging scale 1/world fused
 into the kernel, in place, no staging copies) is launched on the
 communicator's side stream, overlapping the rest of backward. Buckets that
 overlap backward run on a small grid (``overlap_blocks`` CTAs,
-``NEXAR_DP_AR_BLOCKS``) so the persistent GEMM kernels keep their SMs; the
+``NEXAR_DP_AR_BLOCKS``, default 64: 2-GPU step 10.35 ms against 10.52 ms
+with 32) so the persistent GEMM kernels keep most of their SMs; the
 last buckets, which run after backward has finished, take the whole GPU.
 With ``timeline=True`` (``NEXAR_DP_TIMELINE=1``) CUDA events mark, per
 bucket, when it became ready on the compute stream and when its all-reduce
@@ -76,7 +79,7 @@ class DataParallelTrainer:
         self._bucket_left: List[int] = list(self._bucket_need)
         self._launched: List[bool] = [False] * len(self.buckets)
         self.overlap_blocks = int(overlap_blocks if overlap_blocks is not None
-                                  else os.environ.get("NEXAR_DP_AR_BLOCKS", "32"))
+                                  else os.environ.get("NEXAR_DP_AR_BLOCKS", "64"))
         self.tail_buckets = 2  # launched once backward has (nearly) finished: full grid
         if timeline is None:
             timeline = os.environ.get("NEXAR_DP_TIMELINE", "0") == "1"
