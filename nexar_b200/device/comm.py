@@ -208,10 +208,13 @@ class DeviceCommunicator:
         heap = heap_bytes or (1 << 20) + 2 * slot + user  # 1 MiB signal area first
         tmo = timeout_us if timeout_us is not None else _env_int("NEXAR_DEVICE_WAIT_TIMEOUT_US", 10_000_000)
         # One-shot (one barrier, every rank reads every peer's whole buffer)
-        # beats two-shot up to larger sizes at 2 ranks, where both move the
-        # same bytes per rank (2-GPU sweep: two-shot 30 us at 1-2 MB).
+        # against two-shot (two barriers, a staging round trip): in the sweeps
+        # two-shot cost 30-42 us from 512 KB to 2 MB at every world size while
+        # one-shot grew by about 1.5 us per doubling from 256 KB (18-20 us),
+        # so one-shot runs to 2 MB up to 4 ranks and to 1 MB at 8, where every
+        # rank reads seven peers.
         self.oneshot_max_bytes = _env_int(
-            "NEXAR_AR_ONESHOT_MAX", (2 << 20) if world_size == 2 else (512 << 10 if world_size <= 4 else 256 << 10))
+            "NEXAR_AR_ONESHOT_MAX", (2 << 20) if world_size <= 4 else (1 << 20))
         self._comm = C.DeviceComm(rank, world_size, device, heap, slot, tmo)
         # Grid cap of a standalone collective: two CTAs per SM (the kernels'
         # limit), so one CTA copies while the other waits on a signal; the
