@@ -123,7 +123,7 @@ cudaError_t launch_all_reduce(const CommDev& c, const void* in, void* out, int d
   if (n == 0) return cudaSuccess;
   const int es = dtype_size(dt_in);
   const bool vec = aligned16(in) && aligned16(out) && (n * es) % 16 == 0;
-  const unsigned int g = pick_blocks(n * es, max_blocks);  // total bytes: enough CTAs in flight for NVLink
+  const unsigned int g = pick_blocks(n * es / (algo == kAlgoTwoShot ? c.world : 1), max_blocks);
   NEXAR_DISPATCH_OUT_OP(dt_in, dt_out, op, {
     if (algo == kAlgoTwoShot) {
       k_ar_twoshot<T, TO, OP><<<g, kThreads, 0, s>>>(c, (const T*)in, (TO*)out, n, scale, vec, sym_off);

@@ -205,10 +205,8 @@ NEXAR_D T* heap_ptr(const CommDev& c, int owner, unsigned long long off) {
 
 // ---------------------------------------------------------------- launch helpers
 inline unsigned int pick_blocks(unsigned long long bytes, unsigned int max_blocks) {
-  // ~32 KiB of the collective's total bytes per block keeps enough NVLink
-  // requests in flight; small messages use few blocks so the barrier is
-  // cheap. (Sizing by the per-rank chunk instead gave a 1 MB collective at
-  // 8 ranks 4 CTAs, and 0.7x of NCCL from 256 KB to 2 MB.)
+  // ~32 KiB per block keeps enough loads in flight; small messages use few
+  // blocks so the barrier is cheap.
   unsigned long long b = (bytes + 32767) / 32768;
   if (b < 1) b = 1;
   if (b > max_blocks) b = max_blocks;

@@ -145,7 +145,7 @@ cudaError_t launch_all_gather(const CommDev& c, const void* in, void* out, int d
   if (count == 0) return cudaSuccess;
   const int es = dtype_size(dt);
   const bool vec = aligned16(in) && aligned16(out) && (count * es) % 16 == 0 && (out_ld * es) % 16 == 0;
-  const unsigned int g = pick_blocks(count * es * c.world, max_blocks);
+  const unsigned int g = pick_blocks(count * es, max_blocks);
   NEXAR_DISPATCH_ALL(dt, k_all_gather<T><<<g, kThreads, 0, s>>>(c, (const T*)in, (T*)out, count, out_ld, vec));
   return cudaGetLastError();
 }
@@ -157,7 +157,7 @@ cudaError_t launch_all_to_all(const CommDev& c, const void* in, void* out, int d
   const int es = dtype_size(dt);
   const bool vec = aligned16(in) && aligned16(out) && (count * es) % 16 == 0 &&
                    (in_ld * es) % 16 == 0 && (out_ld * es) % 16 == 0;
-  const unsigned int g = pick_blocks(count * es * c.world, max_blocks);
+  const unsigned int g = pick_blocks(count * es, max_blocks);
   NEXAR_DISPATCH_ALL(dt, k_all_to_all<T><<<g, kThreads, 0, s>>>(c, (const T*)in, (T*)out, count, in_ld, out_ld, vec));
   return cudaGetLastError();
 }
@@ -228,7 +228,7 @@ cudaError_t launch_broadcast(const CommDev& c, const void* in, void* out, int dt
   const int es = dtype_size(dt);
   const bool vec = aligned16(in) && aligned16(out) && (n * es) % 16 == 0;
   if (c.world >= 3 && n * es >= (256ull << 10)) {
-    const unsigned int g = pick_blocks(n * es, max_blocks);
+    const unsigned int g = pick_blocks(n * es / c.world, max_blocks);
     NEXAR_DISPATCH_ALL(dt, k_broadcast_sag<T><<<g, kThreads, 0, s>>>(c, (const T*)in, (T*)out, n, root, vec));
     return cudaGetLastError();
   }

@@ -88,7 +88,7 @@ cudaError_t launch_reduce_scatter(const CommDev& c, const void* in, void* out, i
   if (count == 0) return cudaSuccess;
   const int es = dtype_size(dt_in);
   const bool vec = aligned16(in) && aligned16(out) && (count * es) % 16 == 0 && (in_ld * es) % 16 == 0;
-  const unsigned int g = pick_blocks(count * es * c.world, max_blocks);
+  const unsigned int g = pick_blocks(count * es, max_blocks);
   NEXAR_DISPATCH_OUT_OP(dt_in, dt_out, op, {
     k_reduce_scatter<T, TO, OP><<<g, kThreads, 0, s>>>(c, (const T*)in, (TO*)out, count, in_ld, scale, vec);
   });
@@ -101,7 +101,7 @@ cudaError_t launch_reduce(const CommDev& c, const void* in, void* out, int dt_in
   if (n == 0) return cudaSuccess;
   const int es = dtype_size(dt_in);
   const bool vec = aligned16(in) && aligned16(out) && (n * es) % 16 == 0;
-  const unsigned int g = pick_blocks(n * es, max_blocks);
+  const unsigned int g = pick_blocks(n * es / c.world, max_blocks);
   NEXAR_DISPATCH_OUT_OP(dt_in, dt_out, op, {
     k_reduce<T, TO, OP><<<g, kThreads, 0, s>>>(c, (const T*)in, (TO*)out, n, root, scale, vec);
   });
