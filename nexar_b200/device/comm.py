@@ -216,12 +216,10 @@ class DeviceCommunicator:
         self.oneshot_max_bytes = _env_int(
             "NEXAR_AR_ONESHOT_MAX", (2 << 20) if world_size <= 4 else (1 << 20))
         self._comm = C.DeviceComm(rank, world_size, device, heap, slot, tmo)
-        # Grid cap of a standalone collective: two CTAs per SM (the kernels'
-        # limit), so one CTA copies while the other waits on a signal; the
-        # in-place NVLS all-reduce at 8 GPUs ran at 637 GB/s bus bandwidth
-        # (1 GiB) capped at 148 CTAs, 770 GB/s with 256. Collectives that
-        # overlap compute take a smaller grid through block_limit().
-        self._comm.max_blocks = _env_int("NEXAR_MAX_BLOCKS", 256)
+        # Grid cap of a standalone collective (`NEXAR_MAX_BLOCKS`); the 2-, 4-
+        # and 8-GPU sweeps ran with 148. Collectives that overlap compute
+        # take a smaller grid through block_limit().
+        self._comm.max_blocks = _env_int("NEXAR_MAX_BLOCKS", 148)
         # Device argument checks in every collective kernel (root / peer <
         # world, staged and symmetric extents, increasing barrier epochs); a
         # failed check is reported by check() and the kernel touches nothing.
