@@ -46,7 +46,8 @@ def _run(clients, fn):
 
 
 def check_config(clients, n=1024):
-    """The BASELINE correctness configuration."""
+    """Correctness check of the CPU ring configuration: all-reduce, all-gather and reduce-scatter of
+    1024 f32 per rank against the float64 elementwise sum."""
     W = len(clients)
     data = [np.random.RandomState(r).uniform(-1, 1, n).astype(np.float32) for r in range(W)]
     want = np.sum(np.stack(data).astype(np.float64), axis=0)
