@@ -46,8 +46,8 @@ def _run(clients, fn):
 
 
 def check_config(clients, n=1024):
-    """Correctness check of the CPU ring configuration: all-reduce, all-gather and reduce-scatter of
-    1024 f32 per rank against the float64 elementwise sum."""
+    """Correctness check of the CPU ring configuration, 1024 f32 per rank: all-reduce and
+    reduce-scatter against the float64 elementwise sum, all-gather against the concatenation."""
     W = len(clients)
     data = [np.random.RandomState(r).uniform(-1, 1, n).astype(np.float32) for r in range(W)]
     want = np.sum(np.stack(data).astype(np.float64), axis=0)
